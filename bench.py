@@ -1,0 +1,431 @@
+"""Decode-step benchmark of the paged KV-cache data plane on B200.
+
+A step = one decode step of every request of this GPU's shard: the host KVManager appends one token per
+request (slots, copy-on-write pairs, new table entries), the append-scatter kernel writes every layer's new
+K/V into its slot, and paged decode attention runs for every layer.  Default workload: the Llama-3-8B-shaped
+request-sharded config (32 query / 8 kv heads, head_dim 128, 32 layers, block 16, bf16, 256 requests per
+GPU, context lengths log-normal with median 4096 clipped to 32768, a pool of about 150 GB per GPU).
+Inputs are synthetic, seeded N(0,1).
+
+  value : decode tokens/s over all GPUs with every input already resident in HBM (device timed)
+  e2e   : the same step through the C ABI with host buffers: per-layer queries and new K/V copied from pinned
+          host memory, the host KVManager step, and the attention output copied back, inside the timed region
+  roofline : the attention kernel's algorithmic bytes (unique K/V bytes of the contexts) per launch / its
+          average CUDA-event duration, against the measured HBM copy peak
+  cpu_baseline : the reference's own CPU paged_attention_cpu (oracle/_ref) on a bounded sample, all host cores
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config llama3-8b|...]
+Multi-GPU: launched under torch.distributed.run, one process per GPU, requests sharded with no collective
+on the data path (weak scaling); timings are the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import math
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    # name: heads, kv heads, head_dim, layers, block, requests per GPU, kv dtype, length sampler, pool target
+    "llama3-8b": dict(nh=32, kvh=8, D=128, L=32, B=16, ns=256, dtype="bf16", lens=("lognormal", 4096, 0.35, 32768),
+                      pool_gb=150.0),
+    "qwen2.5-0.5b": dict(nh=14, kvh=2, D=64, L=24, B=16, ns=64, dtype="f16", lens=("uniform", 512, 4096),
+                         pool_blocks=65536),
+    "tinyllama-1.1b": dict(nh=32, kvh=4, D=64, L=22, B=16, ns=256, dtype="bf16", lens=("lognormal", 1024, 0.5, 2048),
+                           pool_gb=None),
+}
+DEFAULT = "llama3-8b"
+
+
+def sample_lens(cfg, ns, seed):
+    rng = np.random.default_rng(seed)
+    kind = cfg["lens"][0]
+    if kind == "uniform":
+        return rng.integers(cfg["lens"][1], cfg["lens"][2] + 1, size=ns).astype(np.int64)
+    _, med, sigma, cap = cfg["lens"]
+    x = np.round(rng.lognormal(math.log(med), sigma, size=ns))
+    return np.clip(x, 1, cap).astype(np.int64)
+
+
+def block_bytes_all_layers(cfg):
+    return 2 * cfg["L"] * cfg["B"] * cfg["kvh"] * cfg["D"] * 2
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.p = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.p is not None:
+            time.sleep(0.25)
+            self.p.terminate()
+            try:
+                out, _ = self.p.communicate(timeout=5)
+            except Exception:
+                self.p.kill()
+                out, _ = self.p.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+def cpu_baseline(cfg, lens, target_s=12.0, kind_pref="reference"):
+    """Times the reference's paged_attention_cpu (the reference library built here, else the oracle's
+    restatement) on a bounded sample of this workload: a few sequences of one layer, drawn from the same
+    length distribution, K/V as fp32 copies of bf16/fp16 N(0,1) values; all host cores.  Returns the rate
+    scaled to the workload's decode tok/s."""
+    import oracle
+    kind = "reference" if (kind_pref == "reference" and oracle.have_ref()) else "port"
+    nh, kvh, D, B = cfg["nh"], cfg["kvh"], cfg["D"], cfg["B"]
+    cores = os.cpu_count() or 1
+    rng = np.random.default_rng(77)
+    ns = max(cores, 8)
+    sl = rng.choice(lens, size=ns, replace=True).astype(np.int32)
+    nblk = (sl + B - 1) // B
+    pool = int(nblk.sum())
+    K = rng.standard_normal((pool, B, kvh, D), dtype=np.float32)
+    V = rng.standard_normal((pool, B, kvh, D), dtype=np.float32)
+    Q = rng.standard_normal((ns, nh, D), dtype=np.float32)
+    perm = rng.permutation(pool).astype(np.int32)
+    T = np.zeros((ns, int(nblk.max())), np.int32)
+    o = 0
+    for i in range(ns):
+        T[i, : nblk[i]] = perm[o: o + nblk[i]]
+        o += int(nblk[i])
+    impl = "ref" if kind == "reference" else "c"
+    oracle.paged_attention_cpu(nh, kvh, D, B, Q, K, V, T, sl, partitions=1, nthreads=cores, impl=impl)  # warm
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        oracle.paged_attention_cpu(nh, kvh, D, B, Q, K, V, T, sl, partitions=1, nthreads=cores, impl=impl)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= target_s or reps >= 1000:
+            break
+    per_call = el / reps
+    elem = 2
+    sample_bytes = float(sl.sum()) * kvh * D * 2 * elem  # same byte formula as the GPU (one layer)
+    gbs = sample_bytes / per_call / 1e9
+    step_bytes = float(lens.sum()) * kvh * D * 2 * elem * cfg["L"]
+    step_s = step_bytes / (gbs * 1e9)
+    return {"value": len(lens) / step_s, "unit": "tok/s", "cores": cores, "kind": kind,
+            "gb_s": round(gbs, 3),
+            "sample": f"{ns} sequences x 1 layer ({int(sl.sum())} tokens, lengths drawn from the workload), "
+                      f"{reps} timed calls over {el:.1f}s, scaled to {len(lens)} requests x {cfg['L']} layers"}
+
+
+# ----------------------------------------------------------------------------- GPU workload
+def setup_shard(kvb, cfg, lens, steps_total, dev, seed):
+    """Pool, manager and fragmented block tables for one GPU's shard."""
+    import torch
+    B, L, kvh, D = cfg["B"], cfg["L"], cfg["kvh"], cfg["D"]
+    ns = len(lens)
+    need_blocks = int(((lens + steps_total + B) // B + 1).sum()) + 64
+    free, _ = torch.cuda.mem_get_info(dev)
+    bb = block_bytes_all_layers(cfg)
+    if cfg.get("pool_blocks"):
+        nb = int(cfg["pool_blocks"])
+    elif cfg.get("pool_gb"):
+        nb = int(cfg["pool_gb"] * 1e9 // bb)
+    else:
+        nb = need_blocks
+    nb = max(nb, need_blocks)
+    cap = int((free - 14e9) // bb)
+    if nb > cap:
+        nb = cap
+    if nb < need_blocks:
+        raise RuntimeError(f"pool of {nb} blocks cannot hold the shard ({need_blocks} needed)")
+    tdt = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float16
+    kc = torch.empty((L, nb, B, kvh, D), dtype=tdt, device=dev)
+    vc = torch.empty((L, nb, B, kvh, D), dtype=tdt, device=dev)
+    # Fill the pools with N(0,1): a 2 GiB random chunk, tiled (generating 150 GB with the RNG would dominate).
+    g = torch.Generator(device=dev).manual_seed(seed)
+    chunk = torch.randn(1 << 30, generator=g, device=dev, dtype=torch.float32).to(tdt)
+    for t in (kc, vc):
+        flat = t.view(-1)
+        for o in range(0, flat.numel(), chunk.numel()):
+            n = min(chunk.numel(), flat.numel() - o)
+            flat[o: o + n].copy_(chunk[:n])
+    del chunk
+    # Manager: requests admitted empty, then grown block by block in a random interleaving, so tables are
+    # fragmented the way a long-running server's are.
+    mgr = kvb.KVManager(nb, B)
+    for r in range(ns):
+        assert mgr.admit(r, 0)
+    rng = np.random.default_rng(seed + 1)
+    remaining = lens.copy()
+    while remaining.max() > 0:
+        order = rng.permutation(np.nonzero(remaining > 0)[0])
+        rids = []
+        for r in order:
+            k = int(min(B, remaining[r]))
+            rids.extend([int(r)] * k)
+            remaining[r] -= k
+        done, _, _ = mgr.append_batch(rids)
+        assert done == len(rids)
+    return mgr, kc, vc, nb
+
+
+def run_ours(args, cfg, rank, world, dev):
+    import torch
+    import torch.distributed as dist
+    kvb = importlib.import_module("paged-kv-cache-manager_b200")
+    kvb.lib()
+    nh, kvh, D, L, B = cfg["nh"], cfg["kvh"], cfg["D"], cfg["L"], cfg["B"]
+    ns = cfg["ns"]
+    lens = sample_lens(cfg, ns, seed=1000 + rank)
+    W, K = args.warmup, args.steps
+    steps_total = W + K + 2 * (W + K)  # value run, then e2e run
+    mgr, kc, vc, nb = setup_shard(kvb, cfg, lens, steps_total, dev, seed=rank * 7 + 1)
+    tdt = kc.dtype
+    rids = list(range(ns))
+    max_len = int(lens.max()) + steps_total + 1
+    max_blocks = (max_len + B - 1) // B
+
+    # Device-resident inputs for the value run: per-step slots and lengths precomputed by the host
+    # manager (the table after all steps serves every step: entries past a sequence are never read).
+    n_value = W + K
+    slots_all = np.empty((n_value, ns), np.int32)
+    lens_all = np.empty((n_value, ns), np.int32)
+    for s in range(n_value):
+        done, slots, pairs = mgr.append_batch(rids)
+        assert done == ns and len(pairs) == 0
+        slots_all[s] = slots
+        lens_all[s] = [mgr.num_tokens(r) for r in rids]
+    tables, _ = mgr.dense_tables(rids, max_blocks, pad=0)
+    d_tables = torch.from_numpy(tables).to(dev)
+    d_slots = torch.from_numpy(slots_all).to(dev)
+    d_lens = torch.from_numpy(lens_all).to(dev)
+    g = torch.Generator(device=dev).manual_seed(99 + rank)
+    q = torch.randn((L, ns, nh, D), generator=g, device=dev).to(tdt)
+    knew = torch.randn((L, ns, kvh, D), generator=g, device=dev).to(tdt)
+    vnew = torch.randn((L, ns, kvh, D), generator=g, device=dev).to(tdt)
+    out = torch.empty((L, ns, nh, D), device=dev, dtype=tdt)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    # context split: about 8 CTA waves over this shard's actual tiles
+    total_tiles = int(((lens + 15) // 16).sum())
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    split = max(8, -(-total_tiles // (sms * 8)))
+    a0 = kvb.attention_args(q[0], kc[0], vc[0], d_tables, d_lens[0], out[0], nh, kvh, num_blocks=nb,
+                            split_tiles=split)
+    ws = torch.empty(max(kvb.workspace_bytes(a0), 256), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step_device(s, ev=None):
+        kvb.append_scatter(knew, vnew, kc, vc, d_slots[s], status=status)
+        for l in range(L):
+            if ev is not None:
+                ev[l][0].record(stream)
+            kvb.paged_attention(q[l], kc[l], vc[l], d_tables, d_lens[s], nh, kvh, out=out[l], workspace=ws,
+                                split_tiles=split, status=status, num_blocks=nb)
+            if ev is not None:
+                ev[l][1].record(stream)
+
+    for s in range(W):
+        step_device(s)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
+           for _ in range(K)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device() if dev.index is None else dev.index) as clk:
+        t_start.record(stream)
+        for s in range(K):
+            step_device(W + s, evs[s])
+        t_end.record(stream)
+        torch.cuda.synchronize(dev)
+    ms_total = t_start.elapsed_time(t_end)
+    attn_ms = [e0.elapsed_time(e1) for row in evs for (e0, e1) in row]
+    assert int(status.item()) == 0, f"device status {int(status.item())}"
+    # algorithmic bytes per attention launch: unique K/V bytes of every context, averaged over the steps
+    elem = 2
+    bytes_per_launch = float(lens_all[W:].astype(np.float64).sum(axis=1).mean()) * kvh * D * 2 * elem
+
+    # ---------------------------------------------------------------- e2e through the C ABI, host buffers
+    h_q = torch.randn((L, ns, nh, D), generator=torch.Generator().manual_seed(5)).to(tdt).pin_memory()
+    h_k = torch.randn((L, ns, kvh, D), generator=torch.Generator().manual_seed(6)).to(tdt).pin_memory()
+    h_v = torch.randn((L, ns, kvh, D), generator=torch.Generator().manual_seed(7)).to(tdt).pin_memory()
+    h_out = torch.empty((L, ns, nh, D), dtype=tdt).pin_memory()
+    h_tables = torch.from_numpy(tables.copy()).pin_memory()
+    h_slots = torch.empty(ns, dtype=torch.int32).pin_memory()
+    h_lens = torch.empty(ns, dtype=torch.int32).pin_memory()
+    e_slots = torch.empty(ns, dtype=torch.int32, device=dev)
+    e_lens = torch.empty(ns, dtype=torch.int32, device=dev)
+    np_tables = h_tables.numpy()
+
+    def step_e2e():
+        done, slots, pairs = mgr.append_batch(rids)
+        assert done == ns
+        h_slots.numpy()[:] = slots
+        h_lens.numpy()[:] = [mgr.num_tokens(r) for r in rids]
+        # new table entries (a block boundary was crossed): patch the pinned host table
+        for i in np.nonzero((h_lens.numpy() - 1) % B == 0)[0]:
+            np_tables[i, (h_lens.numpy()[i] - 1) // B] = slots[i] // B
+        d_tables.copy_(h_tables, non_blocking=True)
+        e_slots.copy_(h_slots, non_blocking=True)
+        e_lens.copy_(h_lens, non_blocking=True)
+        knew.copy_(h_k, non_blocking=True)
+        vnew.copy_(h_v, non_blocking=True)
+        kvb.append_scatter(knew, vnew, kc, vc, e_slots, status=status)
+        for l in range(L):
+            q[l].copy_(h_q[l], non_blocking=True)
+            kvb.paged_attention(q[l], kc[l], vc[l], d_tables, e_lens, nh, kvh, out=out[l], workspace=ws,
+                                split_tiles=split, status=status, num_blocks=nb)
+        h_out.copy_(out, non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+
+    for _ in range(W):
+        step_e2e()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(K):
+        step_e2e()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1)
+    assert int(status.item()) == 0
+
+    # max over ranks (device-timed)
+    vals = torch.tensor([ms_total, e2e_ms, float(np.mean(attn_ms))], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    ms_total, e2e_ms, attn_avg = [float(x) for x in vals.cpu()]
+    clocks = clk.summary()
+    gpu_launches = K * (1 + L * (2 if split < (max_blocks * B + 15) // 16 else 1))
+    res = dict(ms_total=ms_total, e2e_ms=e2e_ms, attn_avg_ms=attn_avg, bytes_per_launch=bytes_per_launch,
+               clocks=clocks, ns=ns, nb=nb, split=split, gpu_launches=gpu_launches,
+               h2d=int(h_q.numel() * 2 + h_k.numel() * 2 + h_v.numel() * 2 + h_tables.numel() * 4 + 2 * ns * 4),
+               d2h=int(h_out.numel() * 2), lens_mean=float(lens.mean()))
+    return res, lens
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=60)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default=DEFAULT, choices=sorted(CONFIGS))
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    assert args.warmup >= 3, "at least 3 warm-up steps"
+    cfg = CONFIGS[args.config]
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    metric = "paged decode-attn achieved HBM TB/s & % peak; decode tok/s at 1/2/4/8 GPUs"
+    config = {"workload": f"{args.config}-shaped decode step: append scatter + paged decode attention, all layers",
+              "heads": cfg["nh"], "kv_heads": cfg["kvh"], "head_dim": cfg["D"], "layers": cfg["L"],
+              "block_size": cfg["B"], "requests_per_gpu": cfg["ns"], "lengths": list(cfg["lens"]),
+              "kv_dtype": cfg["dtype"], "l2": "inputs larger than L2 (every step reads the whole context)",
+              "parallelism": f"request-sharded x{args.gpus}, no collective"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        lens = sample_lens(cfg, cfg["ns"], seed=1000)
+        for _ in range(args.warmup):
+            cpu_baseline(cfg, lens, target_s=0.5)
+        vals = [cpu_baseline(cfg, lens, target_s=max(0.5, args.cpu_seconds / max(1, args.steps)))
+                for _ in range(args.steps)]
+        v = float(np.mean([x["value"] for x in vals]))
+        cb = dict(vals[-1])
+        cb["value"] = v
+        line = {"metric": metric, "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": 1000.0 * cfg["ns"] / v, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1)",
+                "config": config, "impl": "reference", "cpu_baseline": cb,
+                "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    res, lens = run_ours(args, cfg, rank, world, dev)
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    peak_gbs = float(peaks.get("hbm_gbs", 6650.0))
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+    ns_total = cfg["ns"] * world
+    ms_step = res["ms_total"] / args.steps
+    value = ns_total / (ms_step / 1e3)
+    achieved = res["bytes_per_launch"] / (res["attn_avg_ms"] / 1e3) / 1e9
+    e2e_ms_step = res["e2e_ms"] / args.steps
+    line = {"metric": metric, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": cfg["dtype"], "data": "synthetic N(0,1), seeded", "config": config,
+            "hbm_tb_s": round(achieved / 1e3, 3), "pct_of_measured_peak": round(100 * achieved / peak_gbs, 1),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
+                         "frac": round(achieved / peak_gbs, 4), "traffic": None,
+                         "kernel": "paged_decode_kernel (+ split merge)", "peak_source": peak_src},
+            "e2e": {"value": round(ns_total / (e2e_ms_step / 1e3), 1), "unit": "tok/s",
+                    "h2d_bytes_per_step": res["h2d"], "d2h_bytes_per_step": res["d2h"]},
+            "gpu_launches": res["gpu_launches"], "clocks": res["clocks"],
+            "shard": {"pool_blocks": res["nb"], "split_tiles": res["split"], "mean_context": res["lens_mean"]}}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg, lens, target_s=args.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,202 @@
+/*
+ * kvp_b200.h -- C ABI of the B200 paged KV-cache data plane.
+ *
+ * Plain pointers and sizes only.  Device buffers are caller-owned and stay caller-owned; no entry point
+ * allocates device memory.  Every function returns an int status (KVP_OK == 0) and never throws or aborts;
+ * kvp_last_error() gives the message of the last failure on the calling thread.  Launch functions are
+ * asynchronous on the given stream (a cudaStream_t passed as void*, NULL = legacy default stream) and do
+ * not synchronize.  Problems that only device data can reveal (a block id outside the pool, a sequence
+ * longer than its table row, a pipeline wait that gave up) cannot be returned synchronously: kernels OR a
+ * KVP_STATUS_* bit into the optional caller-provided device word `status`.
+ *
+ * Cache layout, identical to the reference (include/kvpage/paged_attention.h:8-21 of
+ * prathameshpranjale/paged-kv-cache-manager):
+ *   q, out        [num_seqs][num_heads][head_dim]
+ *   k/v pool      [num_blocks][block_size][kv_heads][head_dim]   (one pool per layer)
+ *   block_tables  [num_seqs][max_blocks] int32; entries past a sequence are never read
+ *   seq_lens      [num_seqs] int32 >= 1
+ * Query head h uses kv head h / (num_heads / kv_heads).  Multi-layer calls address layer l's pool at
+ * base + l * layer_stride elements (layer_stride 0 = num_blocks * block_size * kv_heads * head_dim, i.e.
+ * a contiguous [layers][num_blocks][block_size][kv_heads][head_dim] array as in python/paged_model.py:25).
+ */
+#ifndef KVP_B200_H
+#define KVP_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define KVP_API __attribute__((visibility("default")))
+#else
+#define KVP_API
+#endif
+
+/* ---- status codes returned by every entry point ---- */
+#define KVP_OK 0
+#define KVP_EINVAL 1   /* bad argument (the reference throws std::invalid_argument here) */
+#define KVP_ECUDA 2    /* a CUDA runtime/driver call failed */
+#define KVP_EBOUNDS 3  /* a host-visible id or size is outside its range */
+#define KVP_ENOSPACE 4 /* caller-provided workspace or capacity too small */
+#define KVP_ESTATE 5   /* host control-plane misuse (the reference throws std::logic_error here) */
+
+/* ---- bits kernels OR into the optional device status word ---- */
+#define KVP_STATUS_BAD_BLOCK 1 /* a table / slot / pair block id outside [0, num_blocks); access skipped */
+#define KVP_STATUS_BAD_LEN 2   /* seq_len < 1 or ceil(seq_len / block_size) > max_blocks; sequence skipped */
+#define KVP_STATUS_TIMEOUT 4   /* a pipeline wait gave up after ~1 s; the kernel returned early */
+
+typedef enum kvp_dtype { KVP_DTYPE_F32 = 0, KVP_DTYPE_F16 = 1, KVP_DTYPE_BF16 = 2 } kvp_dtype;
+
+/* Message of the last failure on this thread ("" if none). */
+KVP_API const char* kvp_last_error(void);
+/* Library version string. */
+KVP_API const char* kvp_version(void);
+
+/* ======================================================================== paged decode attention
+ * Replaces the reference's GPU entry point launch_paged_attention (cuda/paged_attention.cuh:16-19) and is
+ * the device form of paged_attention_cpu / reference_attention (include/kvpage/paged_attention.h:25-35,
+ * src/paged_attention.cpp:25-114): one query token per sequence, softmax(q.K^T * scale) V over the
+ * sequence's context, read in place through its block table.  fp32 accumulation; K/V fp16 or bf16;
+ * q and out fp32, fp16 or bf16.  Requirements: head_dim in {32, 64, 96, 128, 256}; num_heads % kv_heads
+ * == 0; num_heads / kv_heads <= 16; block_size >= 1; 16-byte aligned pools. */
+typedef struct kvp_attn_args {
+    const void* q;
+    int32_t q_dtype;
+    const void* k_cache; /* this layer's pools */
+    const void* v_cache;
+    int32_t kv_dtype;
+    int64_t num_blocks; /* blocks in each pool; bounds every table entry (0: unchecked) */
+    const int32_t* block_tables;
+    const int32_t* seq_lens;
+    void* out;
+    int32_t out_dtype;
+    int32_t num_seqs, num_heads, kv_heads, head_dim, block_size, max_blocks;
+    float scale;         /* <= 0: 1/sqrt(head_dim) */
+    int32_t split_tiles; /* 16-token tiles per context split; 0: automatic; < 0: never split */
+    int32_t kv_heads_per_cta; /* tuning, 0: automatic */
+    int32_t stages;           /* tuning, 0: automatic */
+    void* workspace;          /* split-K partials; kvp_attention_workspace_size() bytes, 256-B aligned */
+    size_t workspace_bytes;
+    int32_t* status; /* optional device word for KVP_STATUS_* bits */
+} kvp_attn_args;
+
+/* Bytes of workspace kvp_paged_attention needs for these arguments (0 when no context is split). */
+KVP_API size_t kvp_attention_workspace_size(const kvp_attn_args* a);
+KVP_API int kvp_paged_attention(const kvp_attn_args* a, void* stream);
+
+/* ======================================================================== KV-cache mutations
+ * The device data plane of the reference's KVManager decisions (src/kv_manager.cpp:211-242), whose bytes
+ * the reference moves only in Python (python/paged_model.py:54-55, 92-95, 113-117, 145-146). */
+
+/* Append scatter: writes each sequence's new token K/V, for every layer, into its slot
+ * (slot = block * block_size + offset, i.e. (table[pos / B], pos % B) for pos = tokens before the append;
+ * a negative slot skips the sequence).  k_new / v_new: [num_layers][num_seqs][kv_heads][head_dim] in the
+ * pool dtype.  Slots must be distinct. */
+typedef struct kvp_append_args {
+    const void* k_new;
+    const void* v_new;
+    void* k_cache;
+    void* v_cache;
+    int64_t layer_stride; /* elements between layer pools; 0: contiguous */
+    const int32_t* slots; /* [num_seqs] device */
+    int32_t kv_dtype, num_layers, num_seqs, kv_heads, head_dim, block_size;
+    int64_t num_blocks;
+    int32_t* status;
+} kvp_append_args;
+KVP_API int kvp_append_scatter(const kvp_append_args* a, void* stream);
+
+/* Copy-on-write: for each (src, dst) pair copies the whole block, every layer, K and V
+ * (python/paged_model.py:92-95).  pairs: device int32 [n_pairs][2].  All pairs of one call run
+ * concurrently, so no dst may equal another pair's src or dst. */
+typedef struct kvp_cow_args {
+    void* k_cache;
+    void* v_cache;
+    int64_t layer_stride; /* elements; 0: contiguous */
+    const int32_t* pairs;
+    int32_t n_pairs, kv_dtype, num_layers, kv_heads, head_dim, block_size;
+    int64_t num_blocks;
+    int32_t* status;
+} kvp_cow_args;
+KVP_API int kvp_cow_copy(const kvp_cow_args* a, void* stream);
+
+/* Swap between the device pools and a pinned host pool.  A host slot holds one block of every layer:
+ * [K: num_layers x block_bytes][V: num_layers x block_bytes], block_bytes = block_size*kv_heads*head_dim*elem.
+ * blocks / host_slots are HOST arrays of length n; host_pool is pinned (cudaHostAlloc / registered) memory
+ * of at least (max slot + 1) * 2 * num_layers * block_bytes bytes.  Asynchronous on `stream`; the caller
+ * orders it against compute with events.  Swap-out copies data only: the caller then frees the request in
+ * its KVManager.  Swap-in copies into the fresh ids that re-admission returned (src/simulator.cpp:193, 231-241). */
+typedef struct kvp_swap_args {
+    void* k_cache;
+    void* v_cache;
+    int64_t layer_stride; /* elements; 0: contiguous */
+    int32_t kv_dtype, num_layers, kv_heads, head_dim, block_size;
+    int64_t num_blocks;
+    const int32_t* blocks;     /* host */
+    const int64_t* host_slots; /* host */
+    int32_t n;
+    void* host_pool;
+    int64_t host_pool_slots; /* slots the host pool holds; every host_slots[i] must be below it */
+} kvp_swap_args;
+KVP_API int kvp_swap_out(const kvp_swap_args* a, void* stream);
+KVP_API int kvp_swap_in(const kvp_swap_args* a, void* stream);
+
+/* ======================================================================== host control plane
+ * C view of kvp::KVManager (include/kvpage/kv_manager.h; reference include/kvpage/kv_manager.h:26-77).
+ * Bool results come back as 1/0; a thrown std::logic_error becomes -KVP_ESTATE and std::invalid_argument
+ * -KVP_EINVAL (message in kvp_last_error()). */
+typedef struct kvp_mgr kvp_mgr;
+KVP_API kvp_mgr* kvp_mgr_create(int32_t num_blocks, int32_t block_size);
+KVP_API void kvp_mgr_destroy(kvp_mgr* m);
+KVP_API void kvp_mgr_set_check_each_op(kvp_mgr* m, int32_t on);
+KVP_API int kvp_mgr_admit(kvp_mgr* m, int64_t r, int32_t prompt_tokens);
+KVP_API int kvp_mgr_admit_with_prefix(kvp_mgr* m, int64_t r, int64_t parent, int32_t shared_tokens,
+                                      int32_t prompt_tokens);
+KVP_API int kvp_mgr_fork(kvp_mgr* m, int64_t r, int64_t parent);
+KVP_API int kvp_mgr_append_token(kvp_mgr* m, int64_t r);
+KVP_API int kvp_mgr_free(kvp_mgr* m, int64_t r);
+KVP_API int kvp_mgr_contains(kvp_mgr* m, int64_t r);
+KVP_API int kvp_mgr_num_tokens(kvp_mgr* m, int64_t r);
+/* Copies up to cap block ids of r into out; returns the table length. */
+KVP_API int kvp_mgr_table(kvp_mgr* m, int64_t r, int32_t* out, int32_t cap);
+KVP_API int kvp_mgr_refcount(kvp_mgr* m, int32_t block);
+KVP_API int kvp_mgr_free_blocks(kvp_mgr* m);
+KVP_API int kvp_mgr_total_blocks(kvp_mgr* m);
+KVP_API int kvp_mgr_available_blocks(kvp_mgr* m);
+KVP_API int kvp_mgr_can_admit(kvp_mgr* m, int32_t prompt_tokens);
+KVP_API int kvp_mgr_blocks_needed_to_admit(kvp_mgr* m, int64_t parent, int32_t shared_tokens, int32_t prompt_tokens);
+/* out[10] = requests, used_tokens, allocated_blocks, allocated_slots, internal_waste, logical_blocks,
+ * blocks_saved, cow_copies, cached_blocks, cache_evictions. */
+KVP_API void kvp_mgr_stats(kvp_mgr* m, int64_t* out);
+KVP_API void kvp_mgr_recompute_stats(kvp_mgr* m, int64_t* out);
+/* Writes validate()'s message ("" when consistent) into buf; returns its length. */
+KVP_API int kvp_mgr_validate(kvp_mgr* m, char* buf, int32_t cap);
+KVP_API int kvp_mgr_cache_prefix(kvp_mgr* m, int32_t key, int64_t owner, int32_t tokens);
+KVP_API int kvp_mgr_has_cached_prefix(kvp_mgr* m, int32_t key);
+KVP_API int kvp_mgr_cached_prefix_tokens(kvp_mgr* m, int32_t key);
+KVP_API int kvp_mgr_blocks_needed_to_admit_cached(kvp_mgr* m, int32_t key, int32_t shared_tokens, int32_t prompt_tokens);
+KVP_API int kvp_mgr_admit_with_cached_prefix(kvp_mgr* m, int64_t r, int32_t key, int32_t shared_tokens,
+                                             int32_t prompt_tokens);
+KVP_API int kvp_mgr_evictable_blocks(kvp_mgr* m, int32_t key, int32_t shared_blocks);
+KVP_API int kvp_mgr_shared_blocks_with_cached(kvp_mgr* m, int32_t key, int32_t shared_tokens, int32_t prompt_tokens);
+KVP_API int kvp_mgr_clear_cache(kvp_mgr* m);
+
+/* Batched append for a decode step: append_token for rids[0..n) in order, as the reference's Python
+ * harness does per request (python/paged_model.py:105-118).  For each i, slots[i] receives the write slot
+ * (block * block_size + offset) of the new token; when the append was a copy-on-write, the pair
+ * (old block, new block) goes to cow_pairs[2k], cow_pairs[2k+1] (k counts copies; total in *n_cow;
+ * cow_pairs needs room for 2n ints).  Returns the number of successful appends: n on success; on the first
+ * append that found no block the batch stops there, that request's slot is -1 and later slots are -1. */
+KVP_API int kvp_mgr_append_batch(kvp_mgr* m, const int64_t* rids, int32_t n, int32_t* slots, int32_t* cow_pairs,
+                                 int32_t* n_cow);
+/* Dense table rows for a batch: row i = table of rids[i], padded with `pad` up to max_blocks; lens[i] =
+ * tokens.  Returns KVP_EBOUNDS if a table is longer than max_blocks. */
+KVP_API int kvp_mgr_dense_tables(kvp_mgr* m, const int64_t* rids, int32_t n, int32_t max_blocks, int32_t pad,
+                                 int32_t* tables, int32_t* lens);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KVP_B200_H */

@@ -1,0 +1,41 @@
+// Decode attention over a paged KV cache -- the C++ entry point of this library.
+//
+// The reference declares its CPU implementations here (include/kvpage/paged_attention.h:8-35:
+// AttnShape, reference_attention, paged_attention_cpu).  This library keeps AttnShape and the layout
+// contract unchanged and provides the device implementation behind the same shape description; it runs
+// only on the GPU (there is no CPU fallback) and forwards to kvp_paged_attention in kvp_b200.h.
+//
+// Layouts (row-major, contiguous), unchanged from the reference:
+//   q, out        [num_seqs][num_heads][head_dim]
+//   k_cache,
+//   v_cache       [num_blocks][block_size][kv_heads][head_dim]
+//   block_tables  [num_seqs][max_blocks]   int32 physical block ids; entries past a sequence are ignored
+//   seq_lens      [num_seqs]               >= 1
+// Query head h uses kv head h / (num_heads / kv_heads); scale = 1/sqrt(head_dim).
+#pragma once
+#include <cstddef>
+#include <cstdint>
+
+#include "kvpage/types.h"
+
+namespace kvp {
+
+struct AttnShape {
+    int num_heads = 8;
+    int kv_heads = 2;
+    int head_dim = 64;
+    int block_size = 16;
+};
+
+enum class DType : int32_t { F32 = 0, F16 = 1, BF16 = 2 };
+
+// Device pointers throughout; asynchronous on `stream` (a cudaStream_t).  Throws std::invalid_argument
+// for shapes the kernel does not support or that the reference rejects (num_heads % kv_heads != 0), and
+// std::runtime_error when a CUDA call fails.  `workspace` (kvp_attention_workspace_size bytes) enables
+// splitting long contexts across CTAs; pass nullptr to run one CTA per sequence.
+KVPAGE_EXPORT void paged_attention(const AttnShape& s, int num_seqs, int max_blocks, const void* q, DType q_dtype,
+                     const void* k_cache, const void* v_cache, DType kv_dtype, int64_t num_blocks,
+                     const int32_t* block_tables, const int32_t* seq_lens, void* out, DType out_dtype,
+                     void* workspace = nullptr, size_t workspace_bytes = 0, void* stream = nullptr);
+
+}  // namespace kvp

@@ -1,0 +1,432 @@
+"""kvpage-b200: B200-native paged KV cache data plane.
+
+Python mirror of the library's C ABI (include/kvp_b200.h), loaded with ctypes from the in-tree
+libkvpage_b200.so.  It mirrors the reference's Python binding (python/kvpage_py.cpp:12-66 of
+prathameshpranjale/paged-kv-cache-manager: KVManager with block_table / num_tokens / refcount / stats /
+validate) and adds the device entry points: paged_attention, append_scatter, cow_copy, swap_out/in.
+Device buffers are torch CUDA tensors (torch supplies device memory and streams); every computation runs
+in this library's CUDA kernels.  There is no CPU fallback: without the shared library, or for CPU
+tensors, the device calls raise.
+
+The directory name contains dashes, so import it with importlib:
+    kvb = importlib.import_module("paged-kv-cache-manager_b200")
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from typing import Optional, Sequence
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libkvpage_b200.so")
+
+KVP_OK, KVP_EINVAL, KVP_ECUDA, KVP_EBOUNDS, KVP_ENOSPACE, KVP_ESTATE = 0, 1, 2, 3, 4, 5
+KVP_STATUS_BAD_BLOCK, KVP_STATUS_BAD_LEN, KVP_STATUS_TIMEOUT = 1, 2, 4
+F32, F16, BF16 = 0, 1, 2
+NO_REQUEST = -1
+STATS_FIELDS = ("requests", "used_tokens", "allocated_blocks", "allocated_slots", "internal_waste",
+                "logical_blocks", "blocks_saved", "cow_copies", "cached_blocks", "cache_evictions")
+
+_i32, _i64, _vp, _f32, _sz = C.c_int32, C.c_int64, C.c_void_p, C.c_float, C.c_size_t
+_pi32, _pi64 = C.POINTER(C.c_int32), C.POINTER(C.c_int64)
+
+
+class AttnArgs(C.Structure):
+    _fields_ = [("q", _vp), ("q_dtype", _i32), ("k_cache", _vp), ("v_cache", _vp), ("kv_dtype", _i32),
+                ("num_blocks", _i64), ("block_tables", _vp), ("seq_lens", _vp), ("out", _vp), ("out_dtype", _i32),
+                ("num_seqs", _i32), ("num_heads", _i32), ("kv_heads", _i32), ("head_dim", _i32),
+                ("block_size", _i32), ("max_blocks", _i32), ("scale", _f32), ("split_tiles", _i32),
+                ("kv_heads_per_cta", _i32), ("stages", _i32), ("workspace", _vp), ("workspace_bytes", _sz),
+                ("status", _vp)]
+
+
+class AppendArgs(C.Structure):
+    _fields_ = [("k_new", _vp), ("v_new", _vp), ("k_cache", _vp), ("v_cache", _vp), ("layer_stride", _i64),
+                ("slots", _vp), ("kv_dtype", _i32), ("num_layers", _i32), ("num_seqs", _i32), ("kv_heads", _i32),
+                ("head_dim", _i32), ("block_size", _i32), ("num_blocks", _i64), ("status", _vp)]
+
+
+class CowArgs(C.Structure):
+    _fields_ = [("k_cache", _vp), ("v_cache", _vp), ("layer_stride", _i64), ("pairs", _vp), ("n_pairs", _i32),
+                ("kv_dtype", _i32), ("num_layers", _i32), ("kv_heads", _i32), ("head_dim", _i32),
+                ("block_size", _i32), ("num_blocks", _i64), ("status", _vp)]
+
+
+class SwapArgs(C.Structure):
+    _fields_ = [("k_cache", _vp), ("v_cache", _vp), ("layer_stride", _i64), ("kv_dtype", _i32),
+                ("num_layers", _i32), ("kv_heads", _i32), ("head_dim", _i32), ("block_size", _i32),
+                ("num_blocks", _i64), ("blocks", _pi32), ("host_slots", _pi64), ("n", _i32), ("host_pool", _vp),
+                ("host_pool_slots", _i64)]
+
+
+# (name, restype, argtypes) of every C-ABI entry point in include/kvp_b200.h.
+_SIGNATURES = [
+    ("kvp_last_error", C.c_char_p, []),
+    ("kvp_version", C.c_char_p, []),
+    ("kvp_attention_workspace_size", _sz, [C.POINTER(AttnArgs)]),
+    ("kvp_paged_attention", C.c_int, [C.POINTER(AttnArgs), _vp]),
+    ("kvp_append_scatter", C.c_int, [C.POINTER(AppendArgs), _vp]),
+    ("kvp_cow_copy", C.c_int, [C.POINTER(CowArgs), _vp]),
+    ("kvp_swap_out", C.c_int, [C.POINTER(SwapArgs), _vp]),
+    ("kvp_swap_in", C.c_int, [C.POINTER(SwapArgs), _vp]),
+    ("kvp_mgr_create", _vp, [_i32, _i32]),
+    ("kvp_mgr_destroy", None, [_vp]),
+    ("kvp_mgr_set_check_each_op", None, [_vp, _i32]),
+    ("kvp_mgr_admit", C.c_int, [_vp, _i64, _i32]),
+    ("kvp_mgr_admit_with_prefix", C.c_int, [_vp, _i64, _i64, _i32, _i32]),
+    ("kvp_mgr_fork", C.c_int, [_vp, _i64, _i64]),
+    ("kvp_mgr_append_token", C.c_int, [_vp, _i64]),
+    ("kvp_mgr_free", C.c_int, [_vp, _i64]),
+    ("kvp_mgr_contains", C.c_int, [_vp, _i64]),
+    ("kvp_mgr_num_tokens", C.c_int, [_vp, _i64]),
+    ("kvp_mgr_table", C.c_int, [_vp, _i64, _pi32, _i32]),
+    ("kvp_mgr_refcount", C.c_int, [_vp, _i32]),
+    ("kvp_mgr_free_blocks", C.c_int, [_vp]),
+    ("kvp_mgr_total_blocks", C.c_int, [_vp]),
+    ("kvp_mgr_available_blocks", C.c_int, [_vp]),
+    ("kvp_mgr_can_admit", C.c_int, [_vp, _i32]),
+    ("kvp_mgr_blocks_needed_to_admit", C.c_int, [_vp, _i64, _i32, _i32]),
+    ("kvp_mgr_stats", None, [_vp, _pi64]),
+    ("kvp_mgr_recompute_stats", None, [_vp, _pi64]),
+    ("kvp_mgr_validate", C.c_int, [_vp, C.c_char_p, _i32]),
+    ("kvp_mgr_cache_prefix", C.c_int, [_vp, _i32, _i64, _i32]),
+    ("kvp_mgr_has_cached_prefix", C.c_int, [_vp, _i32]),
+    ("kvp_mgr_cached_prefix_tokens", C.c_int, [_vp, _i32]),
+    ("kvp_mgr_blocks_needed_to_admit_cached", C.c_int, [_vp, _i32, _i32, _i32]),
+    ("kvp_mgr_admit_with_cached_prefix", C.c_int, [_vp, _i64, _i32, _i32, _i32]),
+    ("kvp_mgr_evictable_blocks", C.c_int, [_vp, _i32, _i32]),
+    ("kvp_mgr_shared_blocks_with_cached", C.c_int, [_vp, _i32, _i32, _i32]),
+    ("kvp_mgr_clear_cache", C.c_int, [_vp]),
+    ("kvp_mgr_append_batch", C.c_int, [_vp, _pi64, _i32, _pi32, _pi32, _pi32]),
+    ("kvp_mgr_dense_tables", C.c_int, [_vp, _pi64, _i32, _i32, _i32, _pi32, _pi32]),
+]
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """The loaded libkvpage_b200.so (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing; build it with build_lib.py (no CPU fallback exists)")
+        L = C.CDLL(LIB_PATH)
+        for name, res, args in _SIGNATURES:
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = L
+    return _lib
+
+
+def exported_symbols() -> list:
+    return [n for n, _, _ in _SIGNATURES]
+
+
+def last_error() -> str:
+    return lib().kvp_last_error().decode()
+
+
+class KVPError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"kvp error {code}: {msg}")
+        self.code = code
+
+
+def _check(rc: int) -> int:
+    if rc != KVP_OK:
+        msg = last_error()
+        if rc in (KVP_EINVAL,):
+            raise ValueError(msg)
+        raise KVPError(rc, msg)
+    return rc
+
+
+def _bool(rc: int) -> bool:
+    """Maps a bool-returning C entry point: 1/0, or -code when the C++ side threw."""
+    if rc < 0:
+        code = -rc
+        msg = last_error()
+        if code == KVP_EINVAL:
+            raise ValueError(msg)
+        raise RuntimeError(msg)  # std::logic_error in the reference
+    return bool(rc)
+
+
+# ============================================================================ host control plane
+class KVManager:
+    """kvp::KVManager through the C ABI; method names follow the reference's Python binding."""
+
+    def __init__(self, num_blocks: int, block_size: int):
+        self._L = lib()
+        h = self._L.kvp_mgr_create(num_blocks, block_size)
+        if not h:
+            raise ValueError(last_error())
+        self._h = C.c_void_p(h)
+        self._B = block_size
+
+    def __del__(self):
+        try:
+            if getattr(self, "_h", None):
+                self._L.kvp_mgr_destroy(self._h)
+                self._h = None
+        except Exception:
+            pass
+
+    @property
+    def handle(self):
+        return self._h
+
+    def set_check_each_op(self, on: bool):
+        self._L.kvp_mgr_set_check_each_op(self._h, 1 if on else 0)
+
+    def block_size(self) -> int:
+        return self._B
+
+    def admit(self, r: int, prompt: int) -> bool:
+        return _bool(self._L.kvp_mgr_admit(self._h, r, prompt))
+
+    def admit_with_prefix(self, r: int, parent: int, shared: int, prompt: int) -> bool:
+        return _bool(self._L.kvp_mgr_admit_with_prefix(self._h, r, parent, shared, prompt))
+
+    def fork(self, r: int, parent: int) -> bool:
+        return _bool(self._L.kvp_mgr_fork(self._h, r, parent))
+
+    def append_token(self, r: int) -> bool:
+        return _bool(self._L.kvp_mgr_append_token(self._h, r))
+
+    def free(self, r: int):
+        _bool(self._L.kvp_mgr_free(self._h, r))
+
+    def contains(self, r: int) -> bool:
+        return bool(self._L.kvp_mgr_contains(self._h, r))
+
+    def num_tokens(self, r: int) -> int:
+        v = self._L.kvp_mgr_num_tokens(self._h, r)
+        if v < 0:
+            _bool(v)
+        return v
+
+    def block_table(self, r: int) -> list:
+        n = self._L.kvp_mgr_table(self._h, r, None, 0)
+        if n < 0:
+            _bool(n)
+        buf = (C.c_int32 * max(n, 1))()
+        self._L.kvp_mgr_table(self._h, r, buf, n)
+        return list(buf[:n])
+
+    def refcount(self, b: int) -> int:
+        v = self._L.kvp_mgr_refcount(self._h, b)
+        if v < 0:
+            _bool(v)
+        return v
+
+    def free_blocks(self) -> int:
+        return self._L.kvp_mgr_free_blocks(self._h)
+
+    def total_blocks(self) -> int:
+        return self._L.kvp_mgr_total_blocks(self._h)
+
+    def available_blocks(self) -> int:
+        return self._L.kvp_mgr_available_blocks(self._h)
+
+    def can_admit(self, prompt: int) -> bool:
+        return _bool(self._L.kvp_mgr_can_admit(self._h, prompt))
+
+    def blocks_needed_to_admit(self, parent: int, shared: int, prompt: int) -> int:
+        v = self._L.kvp_mgr_blocks_needed_to_admit(self._h, parent, shared, prompt)
+        if v < 0 and last_error():
+            _bool(v)
+        return v
+
+    def stats(self) -> dict:
+        buf = (C.c_int64 * 10)()
+        self._L.kvp_mgr_stats(self._h, buf)
+        return dict(zip(STATS_FIELDS, list(buf)))
+
+    def recompute_stats(self) -> dict:
+        buf = (C.c_int64 * 10)()
+        self._L.kvp_mgr_recompute_stats(self._h, buf)
+        return dict(zip(STATS_FIELDS, list(buf)))
+
+    def validate(self) -> str:
+        buf = C.create_string_buffer(1024)
+        self._L.kvp_mgr_validate(self._h, buf, 1024)
+        return buf.value.decode()
+
+    def cache_prefix(self, key: int, owner: int, tokens: int) -> bool:
+        return _bool(self._L.kvp_mgr_cache_prefix(self._h, key, owner, tokens))
+
+    def has_cached_prefix(self, key: int) -> bool:
+        return bool(self._L.kvp_mgr_has_cached_prefix(self._h, key))
+
+    def cached_prefix_tokens(self, key: int) -> int:
+        return self._L.kvp_mgr_cached_prefix_tokens(self._h, key)
+
+    def blocks_needed_to_admit_cached(self, key: int, shared: int, prompt: int) -> int:
+        return self._L.kvp_mgr_blocks_needed_to_admit_cached(self._h, key, shared, prompt)
+
+    def admit_with_cached_prefix(self, r: int, key: int, shared: int, prompt: int) -> bool:
+        return _bool(self._L.kvp_mgr_admit_with_cached_prefix(self._h, r, key, shared, prompt))
+
+    def evictable_blocks(self, key: int = -1, shared_blocks: int = 0) -> int:
+        return self._L.kvp_mgr_evictable_blocks(self._h, key, shared_blocks)
+
+    def shared_blocks_with_cached(self, key: int, shared: int, prompt: int) -> int:
+        return self._L.kvp_mgr_shared_blocks_with_cached(self._h, key, shared, prompt)
+
+    def clear_cache(self):
+        _bool(self._L.kvp_mgr_clear_cache(self._h))
+
+    # ---- decode-step helpers (native loops) ----
+    def append_batch(self, rids: Sequence[int]):
+        """append_token for each request in order; returns (done, slots[n], cow_pairs[k][2])."""
+        import numpy as np
+        n = len(rids)
+        r = np.ascontiguousarray(np.asarray(rids, dtype=np.int64))
+        slots = np.empty(max(n, 1), dtype=np.int32)
+        pairs = np.empty(max(2 * n, 2), dtype=np.int32)
+        ncow = C.c_int32(0)
+        done = self._L.kvp_mgr_append_batch(self._h, r.ctypes.data_as(_pi64), n, slots.ctypes.data_as(_pi32),
+                                            pairs.ctypes.data_as(_pi32), C.byref(ncow))
+        if done < 0:
+            _bool(done)
+        return done, slots[:n], pairs[: 2 * ncow.value].reshape(-1, 2)
+
+    def dense_tables(self, rids: Sequence[int], max_blocks: int, pad: int = 0):
+        """Padded [n][max_blocks] int32 tables and int32 lengths of the given requests."""
+        import numpy as np
+        n = len(rids)
+        r = np.ascontiguousarray(np.asarray(rids, dtype=np.int64))
+        tables = np.empty((max(n, 1), max_blocks), dtype=np.int32)
+        lens = np.empty(max(n, 1), dtype=np.int32)
+        _check(self._L.kvp_mgr_dense_tables(self._h, r.ctypes.data_as(_pi64), n, max_blocks, pad,
+                                            tables.ctypes.data_as(_pi32), lens.ctypes.data_as(_pi32)))
+        return tables[:n], lens[:n]
+
+
+# ============================================================================ device entry points
+def _dtype_code(t) -> int:
+    import torch
+    m = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
+    if t.dtype not in m:
+        raise ValueError(f"unsupported dtype {t.dtype}")
+    return m[t.dtype]
+
+
+def _dev(t, name):
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (the library has no CPU path)")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    return t.data_ptr()
+
+
+def _stream_ptr(stream):
+    import torch
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return C.c_void_p(stream.cuda_stream)
+
+
+def attention_args(q, k_cache, v_cache, block_tables, seq_lens, out, num_heads, kv_heads, *, num_blocks=None,
+                   workspace=None, split_tiles=0, kv_heads_per_cta=0, stages=0, status=None, scale=0.0) -> AttnArgs:
+    """AttnArgs for one layer; k_cache/v_cache are [num_blocks][B][kv_heads][D] (or views of them)."""
+    nb, B, kvh, D = k_cache.shape[-4:]
+    assert kvh == kv_heads
+    a = AttnArgs()
+    a.q, a.q_dtype = _dev(q, "q"), _dtype_code(q)
+    a.k_cache, a.v_cache, a.kv_dtype = _dev(k_cache, "k_cache"), _dev(v_cache, "v_cache"), _dtype_code(k_cache)
+    a.num_blocks = nb if num_blocks is None else num_blocks
+    a.block_tables, a.seq_lens = _dev(block_tables, "block_tables"), _dev(seq_lens, "seq_lens")
+    a.out, a.out_dtype = _dev(out, "out"), _dtype_code(out)
+    a.num_seqs, a.num_heads, a.kv_heads, a.head_dim = q.shape[0], num_heads, kv_heads, D
+    a.block_size, a.max_blocks = B, block_tables.shape[1]
+    a.scale, a.split_tiles, a.kv_heads_per_cta, a.stages = scale, split_tiles, kv_heads_per_cta, stages
+    if workspace is not None:
+        a.workspace, a.workspace_bytes = _dev(workspace, "workspace"), workspace.numel() * workspace.element_size()
+    a.status = _dev(status, "status") if status is not None else None
+    return a
+
+
+def workspace_bytes(args: AttnArgs) -> int:
+    return int(lib().kvp_attention_workspace_size(C.byref(args)))
+
+
+def paged_attention(q, k_cache, v_cache, block_tables, seq_lens, num_heads: int, kv_heads: int, *, out=None,
+                    out_dtype=None, workspace=None, split_tiles: int = 0, kv_heads_per_cta: int = 0, stages: int = 0,
+                    status=None, stream=None, num_blocks: Optional[int] = None):
+    """Decode attention through the C ABI (kvp_paged_attention).  Allocates `out` (and a workspace when
+    none is given and the context will be split) with torch if not provided."""
+    import torch
+    if out is None:
+        out = torch.empty(q.shape, dtype=out_dtype or q.dtype, device=q.device)
+    a = attention_args(q, k_cache, v_cache, block_tables, seq_lens, out, num_heads, kv_heads, num_blocks=num_blocks,
+                       workspace=workspace, split_tiles=split_tiles, kv_heads_per_cta=kv_heads_per_cta,
+                       stages=stages, status=status)
+    if workspace is None and split_tiles >= 0:
+        need = workspace_bytes(a)
+        if need:
+            workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+            a.workspace, a.workspace_bytes = workspace.data_ptr(), need
+    _check(lib().kvp_paged_attention(C.byref(a), _stream_ptr(stream)))
+    return out
+
+
+def append_scatter(k_new, v_new, k_cache, v_cache, slots, *, status=None, stream=None):
+    """k_new/v_new: [L][num_seqs][kvh][D]; k_cache/v_cache: [L][num_blocks][B][kvh][D]; slots int32 [num_seqs]."""
+    L, nb, B, kvh, D = k_cache.shape
+    a = AppendArgs()
+    a.k_new, a.v_new = _dev(k_new, "k_new"), _dev(v_new, "v_new")
+    a.k_cache, a.v_cache = _dev(k_cache, "k_cache"), _dev(v_cache, "v_cache")
+    a.layer_stride, a.slots = nb * B * kvh * D, _dev(slots, "slots")
+    a.kv_dtype, a.num_layers, a.num_seqs = _dtype_code(k_cache), L, slots.shape[0]
+    a.kv_heads, a.head_dim, a.block_size, a.num_blocks = kvh, D, B, nb
+    a.status = _dev(status, "status") if status is not None else None
+    _check(lib().kvp_append_scatter(C.byref(a), _stream_ptr(stream)))
+
+
+def cow_copy(k_cache, v_cache, pairs, *, status=None, stream=None):
+    """pairs: int32 [n][2] device tensor of (src, dst) blocks."""
+    L, nb, B, kvh, D = k_cache.shape
+    a = CowArgs()
+    a.k_cache, a.v_cache = _dev(k_cache, "k_cache"), _dev(v_cache, "v_cache")
+    a.layer_stride, a.pairs, a.n_pairs = nb * B * kvh * D, _dev(pairs, "pairs"), pairs.shape[0]
+    a.kv_dtype, a.num_layers, a.kv_heads, a.head_dim, a.block_size, a.num_blocks = (
+        _dtype_code(k_cache), L, kvh, D, B, nb)
+    a.status = _dev(status, "status") if status is not None else None
+    _check(lib().kvp_cow_copy(C.byref(a), _stream_ptr(stream)))
+
+
+def _swap(fn, k_cache, v_cache, blocks, host_slots, host_pool, stream):
+    import numpy as np
+    L, nb, B, kvh, D = k_cache.shape
+    b = np.ascontiguousarray(np.asarray(blocks, dtype=np.int32))
+    s = np.ascontiguousarray(np.asarray(host_slots, dtype=np.int64))
+    a = SwapArgs()
+    a.k_cache, a.v_cache = _dev(k_cache, "k_cache"), _dev(v_cache, "v_cache")
+    a.layer_stride, a.kv_dtype, a.num_layers = nb * B * kvh * D, _dtype_code(k_cache), L
+    a.kv_heads, a.head_dim, a.block_size, a.num_blocks = kvh, D, B, nb
+    a.blocks, a.host_slots, a.n = b.ctypes.data_as(_pi32), s.ctypes.data_as(_pi64), len(b)
+    if host_pool.is_cuda or not host_pool.is_pinned():
+        raise ValueError("host_pool must be pinned host memory")
+    a.host_pool = host_pool.data_ptr()
+    a.host_pool_slots = host_pool.numel() * host_pool.element_size() // host_slot_bytes(L, B, kvh, D,
+                                                                                         k_cache.element_size())
+    _check(fn(C.byref(a), _stream_ptr(stream)))
+
+
+def swap_out(k_cache, v_cache, blocks, host_slots, host_pool, *, stream=None):
+    """Copies the given blocks (all layers, K and V) into host slots of a pinned pool."""
+    _swap(lib().kvp_swap_out, k_cache, v_cache, blocks, host_slots, host_pool, stream)
+
+
+def swap_in(k_cache, v_cache, blocks, host_slots, host_pool, *, stream=None):
+    """Copies host slots back into the given (freshly admitted) blocks."""
+    _swap(lib().kvp_swap_in, k_cache, v_cache, blocks, host_slots, host_pool, stream)
+
+
+def host_slot_bytes(num_layers: int, block_size: int, kv_heads: int, head_dim: int, elem: int = 2) -> int:
+    return 2 * num_layers * block_size * kv_heads * head_dim * elem

@@ -1,0 +1,723 @@
+// Paged decode attention for sm_100a: split-K ("flash-decoding") over 16-token tiles of the context.
+//
+// Work unit: one CTA per (sequence, group of kv heads, context split).  A producer warp walks the split's
+// tiles, reads block ids from the sequence's table row (32 entries per coalesced load) and issues TMA tiled
+// loads of the K and V rows of every kv head in the group into a ring of shared-memory stages (128B/64B
+// swizzled, completion counted on an mbarrier).  One consumer warp per kv head computes, per tile,
+//     S^T[16 tokens x 8 heads] = K_tile[16 x D] . Q^T[D x 8]      (mma.sync m16n8k16, fp32 accumulate)
+// so the GQA group of query heads (up to 8 per n-tile) shares every K/V byte; an online softmax in the
+// log2 domain with warp-shuffle reductions; then
+//     O^T[D x 8] += V_tile^T[D x 16] . P^T[16 x 8]
+// with P^T obtained from the S^T accumulator by movmatrix.  P (and an fp32 query) are split into a
+// 16-bit high part plus a 16-bit residual, so the result keeps close to fp32 accuracy.
+// A sequence handled by one split is normalised and written directly; otherwise the CTA writes
+// (m, l, unnormalised O) partials and merge_splits combines them.
+//
+// Numerics follow the reference's paged_attention_cpu (src/paged_attention.cpp:68-114): per-partition
+// running (m, l, acc) with rescaling by exp(m_old - m_new), partitions merged by exp(m_p - M).
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <type_traits>
+
+#include "kvp_device.cuh"
+#include "kvp_internal.h"
+
+namespace kvpd {
+
+constexpr int kMaxStages = 12;
+constexpr int kMaxKvhPerCta = 8;
+
+struct AttnParams {
+    const void* q;
+    const int32_t* tables;
+    const int32_t* lens;
+    void* out;
+    float2* ws_ml;  // [num_seqs][max_splits][num_heads] (m in log2 units, l)
+    float* ws_o;    // [num_seqs][max_splits][num_heads][D]
+    int32_t* status;
+    long long num_blocks;  // 0: unchecked
+    int q_dtype, out_dtype;
+    int num_seqs, nh, g, max_blocks, B, R, nruns;
+    int kvh_cta, groups, stages, split_tiles, max_splits, per_head;
+    uint32_t head_stride, box_slot, stage_half, box_tx;
+    int oob_row;  // a row coordinate outside the tensor map (zero fill) used for skipped blocks
+    float sl2;    // scale * log2(e)
+};
+
+// Length of sequence `seq` in 16-token tiles, or 0 (with a status bit) if its length is invalid.
+__device__ __forceinline__ int seq_tiles(const AttnParams& p, int seq, int* len_out) {
+    const int len = p.lens[seq];
+    const long long nblk = (static_cast<long long>(len) + p.B - 1) / p.B;
+    if (len < 1 || nblk > p.max_blocks) {
+        *len_out = 0;
+        return 0;
+    }
+    *len_out = len;
+    return (len + 15) >> 4;
+}
+
+template <int D, int NT, class KV>
+__global__ void __launch_bounds__((kMaxKvhPerCta + 1) * 32, 1)
+    paged_decode_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                        const AttnParams p) {
+    constexpr int W = (D % 64 == 0) ? 64 : 32;  // elements per smem row
+    constexpr int ROWB = W * 2;                  // bytes per smem row
+    constexpr int NCH = D / W;
+    constexpr int KS = D / 16;                   // k-steps of the score MMA / m-tiles of the PV MMA
+    constexpr uint32_t SWM = (ROWB == 128) ? 7u : 3u;
+    using Tr = F16Traits<KV>;
+
+    __shared__ __align__(8) uint64_t full_bar[kMaxStages];
+    __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
+    extern __shared__ uint8_t dyn_smem[];
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int seq = blockIdx.x / p.groups;
+    const int grp = blockIdx.x - seq * p.groups;
+    const int split = blockIdx.y;
+
+    int len = 0;
+    const int ntiles = seq_tiles(p, seq, &len);
+    const int nsplit = (ntiles + p.split_tiles - 1) / p.split_tiles;
+    if (ntiles == 0) {
+        // Invalid length: report once and write zeros so the output is deterministic.
+        if (split == 0) {
+            if (threadIdx.x == 0) report(p.status, KVP_STATUS_BAD_LEN);
+            const int heads = p.kvh_cta * p.g;
+            for (int i = threadIdx.x; i < heads * D; i += blockDim.x) {
+                const int hq = grp * heads + i / D;
+                store_any(p.out, (static_cast<size_t>(seq) * p.nh + hq) * D + i % D, p.out_dtype, 0.f);
+            }
+        }
+        return;
+    }
+    if (split >= nsplit) return;
+    const int t0 = split * p.split_tiles;
+    const int n = min(ntiles - t0, p.split_tiles);
+
+    const uint32_t smem_base = (smem_u32(dyn_smem) + 1023u) & ~1023u;
+    const int S = p.stages;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(smem_u32(&full_bar[s]), 1);
+            mbar_init(smem_u32(&empty_bar[s]), static_cast<uint32_t>(p.kvh_cta));
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    if (warp == p.kvh_cta) {
+        // ------------------------------------------------------------ producer warp
+        if (lane == 0) {
+            prefetch_tensormap(&kmap);
+            prefetch_tensormap(&vmap);
+        }
+        const int32_t* trow = p.tables + static_cast<size_t>(seq) * p.max_blocks;
+        const int kvh0 = grp * p.kvh_cta;
+        int cache_lo = -(1 << 30);
+        int32_t cached = 0;
+        for (int i = 0; i < n; ++i) {
+            const int s = i % S;
+            if (i >= S && !mbar_wait(smem_u32(&empty_bar[s]), static_cast<uint32_t>((i / S - 1) & 1))) {
+                if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
+                break;
+            }
+            const int tb = (t0 + i) * 16;
+            const int nr = min(p.nruns, (len - tb + p.R - 1) / p.R);
+            const uint32_t fb = smem_u32(&full_bar[s]);
+            if (lane == 0) mbar_arrive_expect_tx(fb, static_cast<uint32_t>(nr) * NCH * 2u * p.box_tx);
+            const uint32_t kst = smem_base + static_cast<uint32_t>(s) * 2u * p.stage_half;
+            const uint32_t vst = kst + p.stage_half;
+            for (int j = 0; j < nr; ++j) {
+                const int tok = tb + j * p.R;
+                const int bi = tok / p.B;
+                if (bi < cache_lo || bi >= cache_lo + 32) {
+                    cache_lo = bi;
+                    cached = (bi + lane < p.max_blocks) ? __ldg(trow + bi + lane) : 0;
+                }
+                const int32_t blk = __shfl_sync(0xffffffffu, cached, bi - cache_lo);
+                int row = blk * p.B + (tok - bi * p.B);
+                if (p.num_blocks > 0 && (blk < 0 || blk >= p.num_blocks)) {
+                    if (lane == 0) report(p.status, KVP_STATUS_BAD_BLOCK);
+                    row = p.oob_row;
+                }
+                if (lane == 0) {
+#pragma unroll
+                    for (int c = 0; c < NCH; ++c) {
+                        const uint32_t off = static_cast<uint32_t>(j * NCH + c) * p.box_slot;
+                        if (!p.per_head) {
+                            tma_load_3d(kst + off, &kmap, fb, c * W, row, kvh0);
+                            tma_load_3d(vst + off, &vmap, fb, c * W, row, kvh0);
+                        } else {
+                            for (int w = 0; w < p.kvh_cta; ++w) {
+                                const uint32_t ho = off + static_cast<uint32_t>(w) * p.head_stride;
+                                tma_load_3d(kst + ho, &kmap, fb, c * W, kvh0 + w, row);
+                                tma_load_3d(vst + ho, &vmap, fb, c * W, kvh0 + w, row);
+                            }
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+        }
+        return;
+    }
+    if (warp >= p.kvh_cta) return;
+
+    // ---------------------------------------------------------------- consumer warp: one kv head
+    const int gid = lane >> 2;  // MMA group id: token row (scores) / head column (P^T) / dim row (O^T)
+    const int c4 = lane & 3;
+    const int kvh_global = grp * p.kvh_cta + warp;
+
+    // Query fragments (B operand of the score MMA): head nt*8+gid, dims ks*16 + 2*c4 (+1, +8, +9).
+    uint32_t qhi[NT][KS][2], qlo[NT][KS][2];
+    const int kv_dt = std::is_same<KV, __half>::value ? KVP_DTYPE_F16 : KVP_DTYPE_BF16;
+    const bool use_qlo = p.q_dtype != kv_dt;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        const int j = nt * 8 + gid;
+        const bool live = j < p.g;
+        const size_t qbase = (static_cast<size_t>(seq) * p.nh + kvh_global * p.g + (live ? j : 0)) * D;
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int d = ks * 16 + 2 * c4 + h * 8;
+                const float x0 = live ? load_any(p.q, qbase + d, p.q_dtype) : 0.f;
+                const float x1 = live ? load_any(p.q, qbase + d + 1, p.q_dtype) : 0.f;
+                const uint32_t hi = Tr::pack(x0, x1);
+                qhi[nt][ks][h] = hi;
+                qlo[nt][ks][h] = Tr::pack(x0 - Tr::unpack_lo(hi), x1 - Tr::unpack_hi(hi));
+            }
+        }
+    }
+
+    // Per-lane shared-memory geometry.  For ldmatrix matrix index jm = lane >> 3 and row rr = lane & 7:
+    //   score operand (K, non-transposed): token (jm & 1) * 8 + rr, dim offset (jm >> 1) * 8
+    //   PV operand    (V, transposed):     token (jm >> 1) * 8 + rr, dim offset (jm & 1) * 8
+    const int jm = lane >> 3, rr = lane & 7;
+    uint32_t k_row_off, v_row_off, k_x, v_x;
+    int k_doff, v_doff;
+    {
+        const int tk = (jm & 1) * 8 + rr;
+        const int tv = (jm >> 1) * 8 + rr;
+        const uint32_t hoff = static_cast<uint32_t>(warp) * p.head_stride;
+        const uint32_t ko = static_cast<uint32_t>(tk / p.R) * NCH * p.box_slot + hoff +
+                            static_cast<uint32_t>(tk % p.R) * ROWB;
+        const uint32_t vo = static_cast<uint32_t>(tv / p.R) * NCH * p.box_slot + hoff +
+                            static_cast<uint32_t>(tv % p.R) * ROWB;
+        k_row_off = ko;
+        v_row_off = vo;
+        k_x = (ko >> 7) & SWM;  // swizzle phase of this row (box slots are 1024-byte aligned)
+        v_x = (vo >> 7) & SWM;
+        k_doff = (jm >> 1) * 8;
+        v_doff = (jm & 1) * 8;
+    }
+
+    float o[NT][KS][4];
+    float m_run[NT][2], l_run[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        m_run[nt][0] = m_run[nt][1] = -INFINITY;
+        l_run[nt][0] = l_run[nt][1] = 0.f;
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) o[nt][ks][0] = o[nt][ks][1] = o[nt][ks][2] = o[nt][ks][3] = 0.f;
+    }
+
+    bool aborted = false;
+    for (int i = 0; i < n; ++i) {
+        const int s = i % S;
+        if (!mbar_wait(smem_u32(&full_bar[s]), static_cast<uint32_t>((i / S) & 1))) {
+            if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
+            aborted = true;
+            break;
+        }
+        const uint32_t kst = smem_base + static_cast<uint32_t>(s) * 2u * p.stage_half;
+        const uint32_t vst = kst + p.stage_half;
+        const int tb = (t0 + i) * 16;
+        const int valid = min(16, len - tb);
+
+        // ---- scores S^T = K . Q^T
+        float sacc[NT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+            const int d = ks * 16 + k_doff;
+            const uint32_t addr = kst + k_row_off + static_cast<uint32_t>(d / W) * p.box_slot +
+                                  ((static_cast<uint32_t>((d % W) >> 3) ^ k_x) << 4);
+            uint32_t a[4];
+            ldsm_x4(addr, a);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                mma16816<KV>(sacc[nt], a, qhi[nt][ks][0], qhi[nt][ks][1]);
+                if (use_qlo) mma16816<KV>(sacc[nt], a, qlo[nt][ks][0], qlo[nt][ks][1]);
+            }
+        }
+
+        // ---- online softmax (log2 domain); rows gid / gid+8 are tokens, columns 2*c4, 2*c4+1 heads
+        uint32_t pb_hi[NT][2], pb_lo[NT][2];
+        const bool row0_ok = gid < valid, row1_ok = gid + 8 < valid;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            float sv[4];
+            sv[0] = row0_ok ? sacc[nt][0] * p.sl2 : -INFINITY;
+            sv[1] = row0_ok ? sacc[nt][1] * p.sl2 : -INFINITY;
+            sv[2] = row1_ok ? sacc[nt][2] * p.sl2 : -INFINITY;
+            sv[3] = row1_ok ? sacc[nt][3] * p.sl2 : -INFINITY;
+            float mx0 = fmaxf(sv[0], sv[2]), mx1 = fmaxf(sv[1], sv[3]);
+#pragma unroll
+            for (int off = 4; off < 32; off <<= 1) {
+                mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+            }
+            const float mn0 = fmaxf(m_run[nt][0], mx0), mn1 = fmaxf(m_run[nt][1], mx1);
+            const float corr0 = fast_exp2(m_run[nt][0] - mn0), corr1 = fast_exp2(m_run[nt][1] - mn1);
+            m_run[nt][0] = mn0;
+            m_run[nt][1] = mn1;
+            const float p0 = fast_exp2(sv[0] - mn0), p1 = fast_exp2(sv[1] - mn1);
+            const float p2 = fast_exp2(sv[2] - mn0), p3 = fast_exp2(sv[3] - mn1);
+            l_run[nt][0] = l_run[nt][0] * corr0 + (p0 + p2);
+            l_run[nt][1] = l_run[nt][1] * corr1 + (p1 + p3);
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) {
+                o[nt][ks][0] *= corr0;
+                o[nt][ks][1] *= corr1;
+                o[nt][ks][2] *= corr0;
+                o[nt][ks][3] *= corr1;
+            }
+            const uint32_t h01 = Tr::pack(p0, p1), h23 = Tr::pack(p2, p3);
+            const uint32_t l01 = Tr::pack(p0 - Tr::unpack_lo(h01), p1 - Tr::unpack_hi(h01));
+            const uint32_t l23 = Tr::pack(p2 - Tr::unpack_lo(h23), p3 - Tr::unpack_hi(h23));
+            pb_hi[nt][0] = movmatrix_trans(h01);
+            pb_hi[nt][1] = movmatrix_trans(h23);
+            pb_lo[nt][0] = movmatrix_trans(l01);
+            pb_lo[nt][1] = movmatrix_trans(l23);
+        }
+
+        // ---- rows past the end of the context: zero this head's V rows so stale bytes cannot turn
+        // 0 * garbage into NaN in the PV product.
+        if (valid < 16) {
+            const int units = (16 - valid) * NCH * (W / 8);
+            for (int u = lane; u < units; u += 32) {
+                const int t = valid + u / (NCH * (W / 8));
+                const int rem = u % (NCH * (W / 8));
+                const int c = rem / (W / 8), cu = rem % (W / 8);
+                const uint32_t ro = static_cast<uint32_t>(t / p.R) * NCH * p.box_slot +
+                                    static_cast<uint32_t>(c) * p.box_slot + static_cast<uint32_t>(warp) * p.head_stride +
+                                    static_cast<uint32_t>(t % p.R) * ROWB;
+                const uint32_t a = vst + ro + ((static_cast<uint32_t>(cu) ^ ((ro >> 7) & SWM)) << 4);
+                asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0u) : "memory");
+            }
+            __syncwarp();
+        }
+
+        // ---- O^T += V^T . P^T
+#pragma unroll
+        for (int mt = 0; mt < KS; ++mt) {
+            const int d = mt * 16 + v_doff;
+            const uint32_t addr = vst + v_row_off + static_cast<uint32_t>(d / W) * p.box_slot +
+                                  ((static_cast<uint32_t>((d % W) >> 3) ^ v_x) << 4);
+            uint32_t a[4];
+            ldsm_x4_trans(addr, a);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                mma16816<KV>(o[nt][mt], a, pb_hi[nt][0], pb_hi[nt][1]);
+                mma16816<KV>(o[nt][mt], a, pb_lo[nt][0], pb_lo[nt][1]);
+            }
+        }
+        if (valid < 16) fence_proxy_async_smem();  // generic writes above precede the next TMA into this stage
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&empty_bar[s]));
+    }
+    if (aborted) return;
+
+    // ---------------------------------------------------------------- epilogue
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            float l = l_run[nt][e];
+#pragma unroll
+            for (int off = 4; off < 32; off <<= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+            l_run[nt][e] = l;
+        }
+    }
+    const bool single = nsplit == 1;
+    const size_t part_row = (static_cast<size_t>(seq) * p.max_splits + split) * p.nh;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int j = nt * 8 + 2 * c4 + e;
+            if (j >= p.g) continue;
+            const int hq = kvh_global * p.g + j;
+            if (single) {
+                const float inv = 1.f / l_run[nt][e];
+                const size_t ob = (static_cast<size_t>(seq) * p.nh + hq) * D;
+#pragma unroll
+                for (int mt = 0; mt < KS; ++mt) {
+                    store_any(p.out, ob + mt * 16 + gid, p.out_dtype, o[nt][mt][e] * inv);
+                    store_any(p.out, ob + mt * 16 + gid + 8, p.out_dtype, o[nt][mt][2 + e] * inv);
+                }
+            } else {
+                float* wo = p.ws_o + (part_row + hq) * D;
+#pragma unroll
+                for (int mt = 0; mt < KS; ++mt) {
+                    wo[mt * 16 + gid] = o[nt][mt][e];
+                    wo[mt * 16 + gid + 8] = o[nt][mt][2 + e];
+                }
+                if (gid == 0) p.ws_ml[part_row + hq] = make_float2(m_run[nt][e], l_run[nt][e]);
+            }
+        }
+    }
+}
+
+// Combines the split partials of every (sequence, head) whose context was split: one warp each.
+template <int D>
+__global__ void __launch_bounds__(128) merge_splits_kernel(const AttnParams p) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long idx = static_cast<long long>(blockIdx.x) * 4 + warp;
+    if (idx >= static_cast<long long>(p.num_seqs) * p.nh) return;
+    const int seq = static_cast<int>(idx / p.nh), hq = static_cast<int>(idx % p.nh);
+    int len = 0;
+    const int ntiles = seq_tiles(p, seq, &len);
+    const int nsplit = (ntiles + p.split_tiles - 1) / p.split_tiles;
+    if (nsplit <= 1) return;
+    const size_t row0 = static_cast<size_t>(seq) * p.max_splits * p.nh + hq;  // split stride: nh
+    float M = -INFINITY;
+    for (int i = lane; i < nsplit; i += 32) M = fmaxf(M, p.ws_ml[row0 + static_cast<size_t>(i) * p.nh].x);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    float L = 0.f;
+    for (int i = lane; i < nsplit; i += 32) {
+        const float2 ml = p.ws_ml[row0 + static_cast<size_t>(i) * p.nh];
+        L += ml.y * fast_exp2(ml.x - M);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+    const float invL = 1.f / L;
+    float acc[(D + 31) / 32];
+#pragma unroll
+    for (int k = 0; k < (D + 31) / 32; ++k) acc[k] = 0.f;
+    for (int i = 0; i < nsplit; ++i) {
+        const size_t r = row0 + static_cast<size_t>(i) * p.nh;
+        const float w = fast_exp2(p.ws_ml[r].x - M);
+        const float* src = p.ws_o + r * D;
+#pragma unroll
+        for (int k = 0; k < (D + 31) / 32; ++k) {
+            const int d = k * 32 + lane;
+            if (d < D) acc[k] += src[d] * w;
+        }
+    }
+    const size_t ob = (static_cast<size_t>(seq) * p.nh + hq) * D;
+#pragma unroll
+    for (int k = 0; k < (D + 31) / 32; ++k) {
+        const int d = k * 32 + lane;
+        if (d < D) store_any(p.out, ob + d, p.out_dtype, acc[k] * invL);
+    }
+}
+
+}  // namespace kvpd
+
+// ============================================================================ host side
+namespace kvpi {
+
+namespace {
+
+int gcd_int(int a, int b) {
+    while (b) {
+        const int t = a % b;
+        a = b;
+        b = t;
+    }
+    return a;
+}
+size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// Tensor map over one layer's pool.  per_head == 0: dims (head_dim, rows = num_blocks*B, kv_heads), box
+// (W, R, kvh_cta) -> smem [kvh][R][W].  per_head == 1: dims (head_dim, kv_heads, rows), box (W, 1, R).
+int encode_pool_map(CUtensorMap* map, const void* base, int kv_dtype, const kvp_attn_args& a, const AttnPlan& pl,
+                    long long rows, int per_head) {
+    auto fn = encode_fn();
+    if (!fn) return fail(KVP_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const CUtensorMapDataType dt =
+        kv_dtype == KVP_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const uint64_t D = static_cast<uint64_t>(a.head_dim), H = static_cast<uint64_t>(a.kv_heads);
+    cuuint64_t dims[3];
+    cuuint64_t strides[2];
+    cuuint32_t box[3];
+    const cuuint32_t estr[3] = {1, 1, 1};
+    if (!per_head) {
+        dims[0] = D;
+        dims[1] = static_cast<cuuint64_t>(rows);
+        dims[2] = H;
+        strides[0] = H * D * 2;
+        strides[1] = D * 2;
+        box[0] = static_cast<cuuint32_t>(pl.W);
+        box[1] = static_cast<cuuint32_t>(pl.R);
+        box[2] = static_cast<cuuint32_t>(pl.kvh_cta);
+    } else {
+        dims[0] = D;
+        dims[1] = H;
+        dims[2] = static_cast<cuuint64_t>(rows);
+        strides[0] = D * 2;
+        strides[1] = H * D * 2;
+        box[0] = static_cast<cuuint32_t>(pl.W);
+        box[1] = 1;
+        box[2] = static_cast<cuuint32_t>(pl.R);
+    }
+    const CUtensorMapSwizzle sw = pl.W == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+    const CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(KVP_ECUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string(r));
+    return KVP_OK;
+}
+
+// Which tensor-map shape the driver accepts: the 3-D (D, rows, heads) form with one box for all heads of
+// a CTA, or the per-head fallback.  Probed once per process with a dummy (host-only) encode.
+int pool_map_mode() {
+    static int mode = -1;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        auto fn = encode_fn();
+        mode = 1;
+        if (!fn) return;
+        alignas(64) CUtensorMap m;
+        static __align__(256) unsigned char dummy[1 << 16];
+        cuuint64_t dims[3] = {128, 64, 8};
+        cuuint64_t strides[2] = {8 * 128 * 2, 128 * 2};
+        cuuint32_t box[3] = {64, 16, 8};
+        cuuint32_t estr[3] = {1, 1, 1};
+        if (fn(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dummy, dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
+            mode = 0;
+    });
+    return mode;
+}
+
+}  // namespace
+
+int plan_attention(const kvp_attn_args& a, bool have_workspace, AttnPlan* out) {
+    AttnPlan pl;
+    const int D = a.head_dim;
+    if (!(D == 32 || D == 64 || D == 96 || D == 128 || D == 256))
+        return fail(KVP_EINVAL, "head_dim must be one of 32, 64, 96, 128, 256");
+    if (a.kv_heads <= 0 || a.num_heads <= 0 || a.num_heads % a.kv_heads != 0)
+        return fail(KVP_EINVAL, "num_heads % kv_heads != 0");
+    const int g = a.num_heads / a.kv_heads;
+    if (g > 16) return fail(KVP_EINVAL, "more than 16 query heads per kv head are not supported");
+    if (a.block_size < 1 || a.max_blocks < 1 || a.num_seqs < 0) return fail(KVP_EINVAL, "bad block_size / max_blocks / num_seqs");
+    pl.R = gcd_int(a.block_size, 16);
+    pl.nruns = 16 / pl.R;
+    pl.W = (D % 64 == 0) ? 64 : 32;
+    pl.nch = D / pl.W;
+    pl.per_head = pool_map_mode();
+    const size_t rowb = static_cast<size_t>(pl.W) * 2;
+    // kv heads per CTA: largest divisor of kv_heads <= 8 whose stage fits 64 KB (or the caller's choice).
+    int kc = a.kv_heads_per_cta;
+    if (kc <= 0 || kc > kvpd::kMaxKvhPerCta || a.kv_heads % kc != 0) {
+        kc = 1;
+        for (int d = 1; d <= std::min(a.kv_heads, kvpd::kMaxKvhPerCta); ++d)
+            if (a.kv_heads % d == 0 && static_cast<size_t>(d) * 16 * D * 2 * 2 <= (64u << 10)) kc = d;
+    }
+    pl.kvh_cta = kc;
+    pl.groups = a.kv_heads / kc;
+    if (!pl.per_head) {
+        pl.head_stride = static_cast<uint32_t>(pl.R * rowb);
+        pl.box_slot = static_cast<uint32_t>(round_up(static_cast<size_t>(kc) * pl.R * rowb, 1024));
+    } else {
+        pl.head_stride = static_cast<uint32_t>(round_up(pl.R * rowb, 1024));
+        pl.box_slot = static_cast<uint32_t>(kc) * pl.head_stride;
+    }
+    pl.box_tx = static_cast<uint32_t>(static_cast<size_t>(kc) * pl.R * rowb);
+    pl.stage_half = static_cast<uint32_t>(pl.nruns) * pl.nch * pl.box_slot;
+    const size_t stage = 2ull * pl.stage_half;
+    const size_t smem_cap = 227u << 10;
+    int st = a.stages;
+    if (st <= 0) st = static_cast<int>(std::max<size_t>(2, std::min<size_t>(8, (96u << 10) / stage)));
+    st = std::min(st, kvpd::kMaxStages);
+    while (st > 2 && stage * st + 1024 > smem_cap) --st;
+    if (stage * st + 1024 > smem_cap) return fail(KVP_EINVAL, "shape needs more shared memory than a CTA has");
+    pl.stages = st;
+    pl.smem = stage * st + 1024;
+    pl.max_tiles = static_cast<int>((static_cast<long long>(a.max_blocks) * a.block_size + 15) / 16);
+    // Context split: tiles per CTA.
+    int split = pl.max_tiles;
+    if (a.split_tiles > 0) {
+        split = std::min(a.split_tiles, pl.max_tiles);
+    } else if (a.split_tiles == 0 && have_workspace) {
+        // Aim for ~8 waves of CTAs assuming sequences average half of max_blocks.
+        const long long est = static_cast<long long>(a.num_seqs) * std::max(1, pl.max_tiles / 2) * pl.groups;
+        const int per_sm = std::max(1, static_cast<int>(smem_cap / pl.smem));
+        const long long target = static_cast<long long>(sm_count()) * per_sm * 8;
+        split = static_cast<int>(std::max<long long>(8, (est + target - 1) / std::max<long long>(1, target)));
+        split = std::min(split, pl.max_tiles);
+    }
+    pl.split_tiles = std::max(1, split);
+    pl.max_splits = (pl.max_tiles + pl.split_tiles - 1) / pl.split_tiles;
+    if (pl.max_splits > 65535) return fail(KVP_EINVAL, "too many context splits; raise split_tiles");
+    pl.ws_bytes = 0;
+    if (pl.max_splits > 1) {
+        const size_t rows = static_cast<size_t>(a.num_seqs) * pl.max_splits * a.num_heads;
+        pl.ws_bytes = round_up(rows * sizeof(float2), 256) + rows * static_cast<size_t>(D) * sizeof(float);
+    }
+    *out = pl;
+    return KVP_OK;
+}
+
+namespace {
+
+template <int D, int NT, class KV>
+int launch_typed(const kvp_attn_args& a, const AttnPlan& pl, const kvpd::AttnParams& prm, const CUtensorMap& km,
+                 const CUtensorMap& vm, cudaStream_t stream) {
+    auto kern = kvpd::paged_decode_kernel<D, NT, KV>;
+    static int configured[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return fail(KVP_ECUDA, "device index out of range");
+    if (configured[dev] < static_cast<int>(pl.smem)) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 << 10);
+        if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(attention)");
+        configured[dev] = 227 << 10;
+    }
+    if (a.num_seqs == 0) return KVP_OK;
+    dim3 grid(static_cast<unsigned>(a.num_seqs * pl.groups), static_cast<unsigned>(pl.max_splits));
+    dim3 block(static_cast<unsigned>((pl.kvh_cta + 1) * 32));
+    kern<<<grid, block, pl.smem, stream>>>(km, vm, prm);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_status(e, "attention kernel launch");
+    if (pl.max_splits > 1) {
+        const long long pairs = static_cast<long long>(a.num_seqs) * a.num_heads;
+        kvpd::merge_splits_kernel<D><<<static_cast<unsigned>((pairs + 3) / 4), 128, 0, stream>>>(prm);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return cuda_status(e, "split merge kernel launch");
+    }
+    return KVP_OK;
+}
+
+template <int D, class KV>
+int launch_nt(const kvp_attn_args& a, const AttnPlan& pl, const kvpd::AttnParams& prm, const CUtensorMap& km,
+              const CUtensorMap& vm, cudaStream_t s) {
+    if (prm.g <= 8) return launch_typed<D, 1, KV>(a, pl, prm, km, vm, s);
+    if constexpr (D <= 128) return launch_typed<D, 2, KV>(a, pl, prm, km, vm, s);
+    return fail(KVP_EINVAL, "head_dim 256 supports at most 8 query heads per kv head");
+}
+
+template <class KV>
+int launch_d(const kvp_attn_args& a, const AttnPlan& pl, const kvpd::AttnParams& prm, const CUtensorMap& km,
+             const CUtensorMap& vm, cudaStream_t s) {
+    switch (a.head_dim) {
+        case 32: return launch_nt<32, KV>(a, pl, prm, km, vm, s);
+        case 64: return launch_nt<64, KV>(a, pl, prm, km, vm, s);
+        case 96: return launch_nt<96, KV>(a, pl, prm, km, vm, s);
+        case 128: return launch_nt<128, KV>(a, pl, prm, km, vm, s);
+        case 256: return launch_nt<256, KV>(a, pl, prm, km, vm, s);
+        default: return fail(KVP_EINVAL, "unsupported head_dim");
+    }
+}
+
+}  // namespace
+
+}  // namespace kvpi
+
+extern "C" KVP_API size_t kvp_attention_workspace_size(const kvp_attn_args* a) {
+    if (!a) return 0;
+    kvpi::AttnPlan pl;
+    if (kvpi::plan_attention(*a, true, &pl) != KVP_OK) return 0;
+    return pl.ws_bytes;
+}
+
+extern "C" KVP_API int kvp_paged_attention(const kvp_attn_args* a, void* stream) {
+    using namespace kvpi;
+    clear_error();
+    if (!a) return fail(KVP_EINVAL, "null arguments");
+    if (!valid_dtype(a->q_dtype) || !valid_dtype(a->out_dtype) ||
+        !(a->kv_dtype == KVP_DTYPE_F16 || a->kv_dtype == KVP_DTYPE_BF16))
+        return fail(KVP_EINVAL, "unsupported dtype (K/V must be fp16 or bf16)");
+    if (a->num_seqs > 0 && (!a->q || !a->k_cache || !a->v_cache || !a->block_tables || !a->seq_lens || !a->out))
+        return fail(KVP_EINVAL, "null buffer");
+    if (!aligned16(a->k_cache) || !aligned16(a->v_cache)) return fail(KVP_EINVAL, "K/V pools must be 16-byte aligned");
+    AttnPlan pl;
+    int rc = plan_attention(*a, a->workspace != nullptr, &pl);
+    if (rc != KVP_OK) return rc;
+    if (pl.max_splits > 1) {
+        if (!a->workspace || a->workspace_bytes < pl.ws_bytes)
+            return fail(KVP_ENOSPACE, "workspace smaller than kvp_attention_workspace_size()");
+        if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0) return fail(KVP_EINVAL, "workspace must be 256-byte aligned");
+    }
+    // Rows of the tensor map: the whole pool when its size is known (TMA then zero-fills anything
+    // outside it); otherwise the largest extent a 32-bit row coordinate can address.
+    long long rows;
+    if (a->num_blocks > 0) {
+        rows = a->num_blocks * static_cast<long long>(a->block_size);
+        if (rows > 0x7fffffffLL) return fail(KVP_EINVAL, "num_blocks * block_size must stay below 2^31");
+    } else {
+        rows = 0x7fffffffLL / a->block_size * a->block_size;
+    }
+    alignas(64) CUtensorMap km, vm;
+    rc = encode_pool_map(&km, a->k_cache, a->kv_dtype, *a, pl, rows, pl.per_head);
+    if (rc != KVP_OK) return rc;
+    rc = encode_pool_map(&vm, a->v_cache, a->kv_dtype, *a, pl, rows, pl.per_head);
+    if (rc != KVP_OK) return rc;
+
+    kvpd::AttnParams prm;
+    std::memset(&prm, 0, sizeof(prm));
+    prm.q = a->q;
+    prm.tables = a->block_tables;
+    prm.lens = a->seq_lens;
+    prm.out = a->out;
+    if (pl.max_splits > 1) {
+        const size_t rows_ml = static_cast<size_t>(a->num_seqs) * pl.max_splits * a->num_heads;
+        prm.ws_ml = static_cast<float2*>(a->workspace);
+        prm.ws_o = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + ((rows_ml * sizeof(float2) + 255) / 256 * 256));
+    }
+    prm.status = a->status;
+    prm.num_blocks = a->num_blocks > 0 ? a->num_blocks : 0;
+    prm.q_dtype = a->q_dtype;
+    prm.out_dtype = a->out_dtype;
+    prm.num_seqs = a->num_seqs;
+    prm.nh = a->num_heads;
+    prm.g = a->num_heads / a->kv_heads;
+    prm.max_blocks = a->max_blocks;
+    prm.B = a->block_size;
+    prm.R = pl.R;
+    prm.nruns = pl.nruns;
+    prm.kvh_cta = pl.kvh_cta;
+    prm.groups = pl.groups;
+    prm.stages = pl.stages;
+    prm.split_tiles = pl.split_tiles;
+    prm.max_splits = pl.max_splits;
+    prm.per_head = pl.per_head;
+    prm.head_stride = pl.head_stride;
+    prm.box_slot = pl.box_slot;
+    prm.stage_half = pl.stage_half;
+    prm.box_tx = pl.box_tx;
+    prm.oob_row = static_cast<int>(std::min<long long>(rows, 0x7fffffffLL));
+    const float scale = a->scale > 0.f ? a->scale : 1.0f / std::sqrt(static_cast<float>(a->head_dim));
+    prm.sl2 = scale * 1.4426950408889634f;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (a->kv_dtype == KVP_DTYPE_F16) return launch_d<__half>(*a, pl, prm, km, vm, s);
+    return launch_d<__nv_bfloat16>(*a, pl, prm, km, vm, s);
+}

@@ -1,0 +1,229 @@
+// Device data plane of the KVManager decisions: append scatter, copy-on-write block copies, swap.
+//
+// All three are pure byte movement and HBM-bound (swap: host-link bound).  Copies use 16-byte vectors with
+// several loads in flight per thread; grids are sized in multiples of the SM count.  Results are bit-exact
+// copies, as in the reference's Python data plane (python/paged_model.py:54-55, 92-95, 113-117, 145-146).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <vector>
+
+#include "kvp_device.cuh"
+#include "kvp_internal.h"
+
+namespace kvpd {
+
+// ---------------------------------------------------------------- append scatter
+// One 16-byte unit per thread-iteration: unit u of (layer, seq, K|V).  Row of a token = kv_heads*D elems.
+struct AppendParams {
+    const uint4* k_new;
+    const uint4* v_new;
+    uint4* k_cache;
+    uint4* v_cache;
+    const int32_t* slots;
+    int32_t* status;
+    long long layer_stride_u;  // 16-byte units between layer pools
+    long long num_slots;       // num_blocks * block_size (0: unchecked)
+    int num_layers, num_seqs, row_u;  // row_u: 16-byte units per token row
+};
+
+__global__ void __launch_bounds__(256) append_scatter_kernel(const AppendParams p) {
+    const long long per_layer = static_cast<long long>(p.num_seqs) * p.row_u;
+    const long long total = per_layer * p.num_layers;
+    for (long long u = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; u < total;
+         u += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int layer = static_cast<int>(u / per_layer);
+        const long long r = u - layer * per_layer;
+        const int seq = static_cast<int>(r / p.row_u);
+        const int e = static_cast<int>(r - static_cast<long long>(seq) * p.row_u);
+        const int slot = __ldg(p.slots + seq);
+        if (slot < 0) continue;
+        if (p.num_slots > 0 && slot >= p.num_slots) {
+            if (e == 0 && layer == 0) report(p.status, KVP_STATUS_BAD_BLOCK);
+            continue;
+        }
+        const long long dst = layer * p.layer_stride_u + static_cast<long long>(slot) * p.row_u + e;
+        const uint4 kx = __ldg(p.k_new + u);
+        const uint4 vx = __ldg(p.v_new + u);
+        p.k_cache[dst] = kx;
+        p.v_cache[dst] = vx;
+    }
+}
+
+// ---------------------------------------------------------------- copy-on-write
+// Work item = (pair, layer, K|V): copies block_u 16-byte units.  Each thread moves UNROLL units per round
+// so several loads are in flight before the stores.
+struct CowParams {
+    uint4* k_cache;
+    uint4* v_cache;
+    const int32_t* pairs;
+    int32_t* status;
+    long long layer_stride_u;
+    long long num_blocks;  // 0: unchecked
+    int n_pairs, num_layers, block_u;
+};
+
+template <int UNROLL>
+__global__ void __launch_bounds__(256) cow_copy_kernel(const CowParams p) {
+    const long long items = static_cast<long long>(p.n_pairs) * p.num_layers * 2;
+    for (long long it = blockIdx.x; it < items; it += gridDim.x) {
+        const int kv = static_cast<int>(it & 1);
+        const long long pl = it >> 1;
+        const int pair = static_cast<int>(pl / p.num_layers);
+        const int layer = static_cast<int>(pl - static_cast<long long>(pair) * p.num_layers);
+        const int src = __ldg(p.pairs + 2 * pair), dst = __ldg(p.pairs + 2 * pair + 1);
+        if (p.num_blocks > 0 && (src < 0 || dst < 0 || src >= p.num_blocks || dst >= p.num_blocks)) {
+            if (threadIdx.x == 0 && layer == 0 && kv == 0) report(p.status, KVP_STATUS_BAD_BLOCK);
+            continue;
+        }
+        uint4* base = (kv ? p.v_cache : p.k_cache) + layer * p.layer_stride_u;
+        const uint4* s = base + static_cast<long long>(src) * p.block_u;
+        uint4* d = base + static_cast<long long>(dst) * p.block_u;
+        for (int u0 = threadIdx.x; u0 < p.block_u; u0 += blockDim.x * UNROLL) {
+            uint4 buf[UNROLL];
+#pragma unroll
+            for (int k = 0; k < UNROLL; ++k) {
+                const int u = u0 + k * blockDim.x;
+                if (u < p.block_u) buf[k] = s[u];
+            }
+#pragma unroll
+            for (int k = 0; k < UNROLL; ++k) {
+                const int u = u0 + k * blockDim.x;
+                if (u < p.block_u) d[u] = buf[k];
+            }
+        }
+    }
+}
+
+}  // namespace kvpd
+
+namespace kvpi {
+namespace {
+
+long long resolve_layer_stride(long long given, long long num_blocks, int block_size, int kvh, int D) {
+    return given > 0 ? given : num_blocks * block_size * kvh * static_cast<long long>(D);
+}
+
+int grid_for(long long work_units, int threads) {
+    const long long want = (work_units + threads - 1) / threads;
+    const long long cap = static_cast<long long>(sm_count()) * 16;
+    return static_cast<int>(std::max<long long>(1, std::min(want, cap)));
+}
+
+}  // namespace
+}  // namespace kvpi
+
+extern "C" KVP_API int kvp_append_scatter(const kvp_append_args* a, void* stream) {
+    using namespace kvpi;
+    clear_error();
+    if (!a) return fail(KVP_EINVAL, "null arguments");
+    if (!(a->kv_dtype == KVP_DTYPE_F16 || a->kv_dtype == KVP_DTYPE_BF16))
+        return fail(KVP_EINVAL, "pool dtype must be fp16 or bf16");
+    if (a->num_layers < 0 || a->num_seqs < 0 || a->kv_heads < 1 || a->head_dim < 1 || a->block_size < 1 ||
+        a->num_blocks < 0)
+        return fail(KVP_EINVAL, "bad shape");
+    const long long row_bytes = static_cast<long long>(a->kv_heads) * a->head_dim * 2;
+    if (row_bytes % 16 != 0) return fail(KVP_EINVAL, "kv_heads * head_dim * 2 must be a multiple of 16 bytes");
+    if (a->num_layers == 0 || a->num_seqs == 0) return KVP_OK;
+    if (!a->k_new || !a->v_new || !a->k_cache || !a->v_cache || !a->slots) return fail(KVP_EINVAL, "null buffer");
+    if (!aligned16(a->k_new) || !aligned16(a->v_new) || !aligned16(a->k_cache) || !aligned16(a->v_cache))
+        return fail(KVP_EINVAL, "buffers must be 16-byte aligned");
+    const long long ls = resolve_layer_stride(a->layer_stride, a->num_blocks, a->block_size, a->kv_heads, a->head_dim);
+    if ((ls * 2) % 16 != 0) return fail(KVP_EINVAL, "layer stride must be a multiple of 16 bytes");
+    if (a->num_layers > 1 && ls <= 0) return fail(KVP_EINVAL, "layer_stride or num_blocks required for several layers");
+    kvpd::AppendParams p;
+    p.k_new = static_cast<const uint4*>(a->k_new);
+    p.v_new = static_cast<const uint4*>(a->v_new);
+    p.k_cache = static_cast<uint4*>(a->k_cache);
+    p.v_cache = static_cast<uint4*>(a->v_cache);
+    p.slots = a->slots;
+    p.status = a->status;
+    p.layer_stride_u = ls * 2 / 16;
+    p.num_slots = a->num_blocks * static_cast<long long>(a->block_size);
+    p.num_layers = a->num_layers;
+    p.num_seqs = a->num_seqs;
+    p.row_u = static_cast<int>(row_bytes / 16);
+    const long long units = static_cast<long long>(a->num_layers) * a->num_seqs * p.row_u;
+    kvpd::append_scatter_kernel<<<grid_for(units, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+    return cuda_status(cudaGetLastError(), "append scatter launch");
+}
+
+extern "C" KVP_API int kvp_cow_copy(const kvp_cow_args* a, void* stream) {
+    using namespace kvpi;
+    clear_error();
+    if (!a) return fail(KVP_EINVAL, "null arguments");
+    if (!(a->kv_dtype == KVP_DTYPE_F16 || a->kv_dtype == KVP_DTYPE_BF16))
+        return fail(KVP_EINVAL, "pool dtype must be fp16 or bf16");
+    if (a->n_pairs < 0 || a->num_layers < 0 || a->kv_heads < 1 || a->head_dim < 1 || a->block_size < 1 ||
+        a->num_blocks < 0)
+        return fail(KVP_EINVAL, "bad shape");
+    const long long block_bytes = static_cast<long long>(a->block_size) * a->kv_heads * a->head_dim * 2;
+    if (block_bytes % 16 != 0) return fail(KVP_EINVAL, "block bytes must be a multiple of 16");
+    if (a->n_pairs == 0 || a->num_layers == 0) return KVP_OK;
+    if (!a->k_cache || !a->v_cache || !a->pairs) return fail(KVP_EINVAL, "null buffer");
+    if (!aligned16(a->k_cache) || !aligned16(a->v_cache)) return fail(KVP_EINVAL, "pools must be 16-byte aligned");
+    const long long ls = resolve_layer_stride(a->layer_stride, a->num_blocks, a->block_size, a->kv_heads, a->head_dim);
+    if ((ls * 2) % 16 != 0) return fail(KVP_EINVAL, "layer stride must be a multiple of 16 bytes");
+    if (a->num_layers > 1 && ls <= 0) return fail(KVP_EINVAL, "layer_stride or num_blocks required for several layers");
+    kvpd::CowParams p;
+    p.k_cache = static_cast<uint4*>(a->k_cache);
+    p.v_cache = static_cast<uint4*>(a->v_cache);
+    p.pairs = a->pairs;
+    p.status = a->status;
+    p.layer_stride_u = ls * 2 / 16;
+    p.num_blocks = a->num_blocks;
+    p.n_pairs = a->n_pairs;
+    p.num_layers = a->num_layers;
+    p.block_u = static_cast<int>(block_bytes / 16);
+    const long long items = static_cast<long long>(a->n_pairs) * a->num_layers * 2;
+    const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(items, static_cast<long long>(sm_count()) * 8)));
+    kvpd::cow_copy_kernel<4><<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+    return cuda_status(cudaGetLastError(), "copy-on-write launch");
+}
+
+// ---------------------------------------------------------------- swap (host link)
+namespace {
+
+// One cudaMemcpy2DAsync per (block, K|V): rows = layers, width = block bytes, device pitch = layer stride,
+// host pitch = block bytes (the slot layout keeps one layer's block after another).
+int swap_copy(const kvp_swap_args* a, void* stream, bool out) {
+    using namespace kvpi;
+    clear_error();
+    if (!a) return fail(KVP_EINVAL, "null arguments");
+    if (!(a->kv_dtype == KVP_DTYPE_F16 || a->kv_dtype == KVP_DTYPE_BF16))
+        return fail(KVP_EINVAL, "pool dtype must be fp16 or bf16");
+    if (a->n < 0 || a->num_layers < 1 || a->kv_heads < 1 || a->head_dim < 1 || a->block_size < 1 || a->num_blocks < 0)
+        return fail(KVP_EINVAL, "bad shape");
+    if (a->n == 0) return KVP_OK;
+    if (!a->k_cache || !a->v_cache || !a->blocks || !a->host_slots || !a->host_pool) return fail(KVP_EINVAL, "null buffer");
+    const size_t bb = static_cast<size_t>(a->block_size) * a->kv_heads * a->head_dim * 2;
+    const long long ls = resolve_layer_stride(a->layer_stride, a->num_blocks, a->block_size, a->kv_heads, a->head_dim);
+    if (a->num_layers > 1 && ls <= 0) return fail(KVP_EINVAL, "layer_stride or num_blocks required for several layers");
+    const size_t pitch_dev = static_cast<size_t>(ls) * 2;
+    const size_t slot_bytes = 2 * static_cast<size_t>(a->num_layers) * bb;
+    for (int i = 0; i < a->n; ++i) {
+        if (a->blocks[i] < 0 || (a->num_blocks > 0 && a->blocks[i] >= a->num_blocks) || a->host_slots[i] < 0 ||
+            a->host_slots[i] >= a->host_pool_slots)
+            return fail(KVP_EBOUNDS, "swap block id or host slot out of range at index " + std::to_string(i));
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    for (int i = 0; i < a->n; ++i) {
+        const int blk = a->blocks[i];
+        char* host = static_cast<char*>(a->host_pool) + static_cast<size_t>(a->host_slots[i]) * slot_bytes;
+        for (int kv = 0; kv < 2; ++kv) {
+            char* dev = static_cast<char*>(kv ? a->v_cache : a->k_cache) + static_cast<size_t>(blk) * bb;
+            char* h = host + static_cast<size_t>(kv) * a->num_layers * bb;
+            cudaError_t e = out ? cudaMemcpy2DAsync(h, bb, dev, pitch_dev, bb, static_cast<size_t>(a->num_layers),
+                                                    cudaMemcpyDeviceToHost, s)
+                                : cudaMemcpy2DAsync(dev, pitch_dev, h, bb, bb, static_cast<size_t>(a->num_layers),
+                                                    cudaMemcpyHostToDevice, s);
+            if (e != cudaSuccess) return cuda_status(e, out ? "swap-out copy" : "swap-in copy");
+        }
+    }
+    return KVP_OK;
+}
+
+}  // namespace
+
+extern "C" KVP_API int kvp_swap_out(const kvp_swap_args* a, void* stream) { return swap_copy(a, stream, true); }
+extern "C" KVP_API int kvp_swap_in(const kvp_swap_args* a, void* stream) { return swap_copy(a, stream, false); }

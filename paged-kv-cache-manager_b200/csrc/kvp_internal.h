@@ -1,0 +1,43 @@
+// Host-side internals shared by the C-ABI translation units (not part of the public interface).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+#include "kvp_b200.h"
+
+namespace kvpi {
+
+// Records `msg` as this thread's last error and returns `code`.
+int fail(int code, const std::string& msg);
+// Maps a CUDA error to KVP_ECUDA with a message naming `what`; KVP_OK for cudaSuccess.
+int cuda_status(cudaError_t e, const char* what);
+void clear_error();
+
+inline int dtype_bytes(int dt) { return dt == KVP_DTYPE_F32 ? 4 : 2; }
+inline bool valid_dtype(int dt) { return dt == KVP_DTYPE_F32 || dt == KVP_DTYPE_F16 || dt == KVP_DTYPE_BF16; }
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int sm_count();  // SMs of the current device (cached per device)
+
+// Launch plan of the attention kernel, derived only from the arguments (so the workspace query and the
+// launch agree).
+struct AttnPlan {
+    int R = 16;           // tokens per TMA run: gcd(block_size, 16)
+    int nruns = 1;        // runs per 16-token tile
+    int W = 64;           // elements per swizzled smem row (64: 128B swizzle, 32: 64B swizzle)
+    int nch = 1;          // W-wide chunks per head_dim
+    int kvh_cta = 1;      // kv heads per CTA (one consumer warp each)
+    int groups = 1;       // kv_heads / kvh_cta
+    int stages = 2;       // pipeline depth (16-token tiles in flight)
+    int per_head = 0;     // 1: one TMA box per kv head (fallback tensor-map shape)
+    int split_tiles = 1;  // tiles per CTA
+    int max_tiles = 1;    // tiles of the longest possible sequence
+    int max_splits = 1;
+    uint32_t head_stride = 0, box_slot = 0, stage_half = 0, box_tx = 0;
+    size_t smem = 0, ws_bytes = 0;
+};
+int plan_attention(const kvp_attn_args& a, bool have_workspace, AttnPlan* plan);
+
+}  // namespace kvpi

@@ -1,0 +1,91 @@
+"""The C-ABI library loads without a GPU, exports every entry point include/kvp_b200.h declares plus the
+C++ drop-in API, and rejects invalid arguments before touching the device."""
+import ctypes as C
+import os
+import re
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared():
+    src = open(os.path.join(ROOT, "include", "kvp_b200.h")).read()
+    return sorted(set(re.findall(r"KVP_API\s+[\w\s\*]+?\b(kvp_\w+)\s*\(", src)))
+
+
+def test_header_declarations_are_all_exported(kvb):
+    names = _declared()
+    assert len(names) >= 38
+    L = kvb.lib()
+    for n in names:
+        assert hasattr(L, n), n
+    assert sorted(kvb.exported_symbols()) == names
+
+
+def test_cxx_drop_in_symbols_exported(kvb):
+    out = subprocess.run(["nm", "-DC", "--defined-only", kvb.LIB_PATH], capture_output=True, text=True).stdout
+    for sym in ("kvp::KVManager::append_token(long)", "kvp::KVManager::admit_with_prefix(long, long, int, int)",
+                "kvp::KVManager::fork(long, long)", "kvp::KVManager::free(long)",
+                "kvp::BlockAllocator::allocate()", "launch_paged_attention(",
+                "kvp::paged_attention(kvp::AttnShape const&"):
+        assert sym in out, sym
+    # nothing from the statically linked CUDA runtime leaks out of the library
+    assert " cudaMalloc" not in out
+
+
+def test_version_and_error_string(kvb):
+    assert b"sm_100a" in kvb.lib().kvp_version()
+
+
+def _args(kvb, **kw):
+    a = kvb.AttnArgs()
+    a.q_dtype, a.kv_dtype, a.out_dtype = kvb.F32, kvb.F16, kvb.F32
+    a.num_seqs, a.num_heads, a.kv_heads, a.head_dim, a.block_size, a.max_blocks = 2, 8, 2, 64, 16, 4
+    a.num_blocks = 16
+    # fake, 256-byte aligned addresses: validation fails before any device access
+    a.q = a.k_cache = a.v_cache = a.block_tables = a.seq_lens = a.out = 1 << 20
+    for k, v in kw.items():
+        setattr(a, k, v)
+    return a
+
+
+@pytest.mark.parametrize("bad", [dict(head_dim=48), dict(kv_heads=3), dict(num_heads=40, kv_heads=2),
+                                 dict(kv_dtype=0), dict(q_dtype=7), dict(block_size=0), dict(k_cache=(1 << 20) + 2)])
+def test_attention_rejects_invalid_arguments(kvb, bad):
+    L = kvb.lib()
+    rc = L.kvp_paged_attention(C.byref(_args(kvb, **bad)), None)
+    assert rc == kvb.KVP_EINVAL
+    assert kvb.last_error()
+
+
+def test_workspace_needed_only_when_split(kvb):
+    L = kvb.lib()
+    a = _args(kvb, split_tiles=1, max_blocks=8)
+    n = L.kvp_attention_workspace_size(C.byref(a))
+    assert n == pytest.approx(2 * 8 * 8 * (8 + 64 * 4), rel=0.1)
+    a.split_tiles = -1
+    assert L.kvp_attention_workspace_size(C.byref(a)) == 0
+    a = _args(kvb, split_tiles=1, max_blocks=8)
+    assert L.kvp_paged_attention(C.byref(a), None) == kvb.KVP_ENOSPACE  # no workspace given
+
+
+def test_kv_ops_reject_invalid_arguments(kvb):
+    L = kvb.lib()
+    a = kvb.AppendArgs()
+    a.kv_dtype = kvb.F32
+    assert L.kvp_append_scatter(C.byref(a), None) == kvb.KVP_EINVAL
+    c = kvb.CowArgs()
+    c.kv_dtype, c.n_pairs, c.num_layers, c.kv_heads, c.head_dim, c.block_size = kvb.BF16, 1, 1, 1, 4, 1
+    assert L.kvp_cow_copy(C.byref(c), None) == kvb.KVP_EINVAL  # 8-byte blocks
+    s = kvb.SwapArgs()
+    s.kv_dtype, s.num_layers, s.kv_heads, s.head_dim, s.block_size, s.n = kvb.BF16, 1, 1, 8, 1, 1
+    blocks = (C.c_int32 * 1)(-1)
+    slots = (C.c_int64 * 1)(0)
+    s.blocks, s.host_slots = blocks, slots
+    s.k_cache = s.v_cache = s.host_pool = 1 << 20
+    s.host_pool_slots = 4
+    assert L.kvp_swap_out(C.byref(s), None) == kvb.KVP_EBOUNDS  # negative block id
+    blocks[0], slots[0] = 0, 4
+    assert L.kvp_swap_in(C.byref(s), None) == kvb.KVP_EBOUNDS   # host slot beyond the pool
