@@ -441,6 +441,8 @@ int gcd_int(int a, int b) {
     return a;
 }
 size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+// Dynamic shared memory a CTA may use: the 227 KB opt-in limit less 1 KB for the static mbarriers.
+constexpr int kDynSmemCap = (227 << 10) - 1024;
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -554,7 +556,7 @@ int plan_attention(const kvp_attn_args& a, bool have_workspace, AttnPlan* out) {
     pl.box_tx = static_cast<uint32_t>(static_cast<size_t>(kc) * pl.R * rowb);
     pl.stage_half = static_cast<uint32_t>(pl.nruns) * pl.nch * pl.box_slot;
     const size_t stage = 2ull * pl.stage_half;
-    const size_t smem_cap = 227u << 10;
+    const size_t smem_cap = kDynSmemCap;
     int st = a.stages;
     if (st <= 0) st = static_cast<int>(std::max<size_t>(2, std::min<size_t>(8, (96u << 10) / stage)));
     st = std::min(st, kvpd::kMaxStages);
@@ -598,9 +600,10 @@ int launch_typed(const kvp_attn_args& a, const AttnPlan& pl, const kvpd::AttnPar
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return fail(KVP_ECUDA, "device index out of range");
     if (configured[dev] < static_cast<int>(pl.smem)) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 << 10);
+        // The whole opt-in budget minus the kernel's static barriers.
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmemCap);
         if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(attention)");
-        configured[dev] = 227 << 10;
+        configured[dev] = kDynSmemCap;
     }
     if (a.num_seqs == 0) return KVP_OK;
     dim3 grid(static_cast<unsigned>(a.num_seqs * pl.groups), static_cast<unsigned>(pl.max_splits));
