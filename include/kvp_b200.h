@@ -87,6 +87,18 @@ typedef struct kvp_attn_args {
 KVP_API size_t kvp_attention_workspace_size(const kvp_attn_args* a);
 KVP_API int kvp_paged_attention(const kvp_attn_args* a, void* stream);
 
+/* The same attention for callers that cannot allocate device memory -- e.g. a serving engine whose memory
+ * manager reserves nearly all HBM for the KV pool and gives libraries no allocation hook, or a plugin whose
+ * enqueue callback must not allocate.  This entry point has no counterpart in the reference.  It ignores
+ * a->workspace and keeps the split partials in a fixed KVP_NOALLOC_SCRATCH_BYTES device array built into the
+ * library (held by every GPU that loads it, until exit); it calls no allocator.  The array's device address
+ * is looked up on the first call made on each device, so make that first call before any stream capture.
+ * With split_tiles == 0 the splits are coarsened until the partials fit; an explicit split_tiles whose
+ * partials exceed the array returns KVP_ENOSPACE.  All calls share the array: calls that overlap on the GPU
+ * race and must be serialised by the caller. */
+#define KVP_NOALLOC_SCRATCH_BYTES (32u << 20)
+KVP_API int kvp_paged_attention_noalloc(const kvp_attn_args* a, void* stream);
+
 /* ======================================================================== KV-cache mutations
  * The device data plane of the reference's KVManager decisions (src/kv_manager.cpp:211-242), whose bytes
  * the reference moves only in Python (python/paged_model.py:54-55, 92-95, 113-117, 145-146). */

@@ -65,6 +65,7 @@ _SIGNATURES = [
     ("kvp_version", C.c_char_p, []),
     ("kvp_attention_workspace_size", _sz, [C.POINTER(AttnArgs)]),
     ("kvp_paged_attention", C.c_int, [C.POINTER(AttnArgs), _vp]),
+    ("kvp_paged_attention_noalloc", C.c_int, [C.POINTER(AttnArgs), _vp]),
     ("kvp_append_scatter", C.c_int, [C.POINTER(AppendArgs), _vp]),
     ("kvp_cow_copy", C.c_int, [C.POINTER(CowArgs), _vp]),
     ("kvp_swap_out", C.c_int, [C.POINTER(SwapArgs), _vp]),
