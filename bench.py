@@ -183,13 +183,14 @@ def setup_shard(kvb, cfg, lens, steps_total, dev, seed):
     vc = torch.empty((L, nb, B, kvh, D), dtype=tdt, device=dev)
     # Fill the pools with N(0,1): a 2 GiB random chunk, tiled (generating 150 GB with the RNG would dominate).
     g = torch.Generator(device=dev).manual_seed(seed)
-    chunk = torch.randn(1 << 30, generator=g, device=dev, dtype=torch.float32).to(tdt)
+    chunk = torch.randn(min(1 << 30, kc.numel()), generator=g, device=dev, dtype=torch.float32).to(tdt)
     for t in (kc, vc):
         flat = t.view(-1)
         for o in range(0, flat.numel(), chunk.numel()):
             n = min(chunk.numel(), flat.numel() - o)
             flat[o: o + n].copy_(chunk[:n])
     del chunk
+    torch.cuda.empty_cache()
     # Manager: requests admitted empty, then grown block by block in a random interleaving, so tables are
     # fragmented the way a long-running server's are.
     mgr = kvb.KVManager(nb, B)
@@ -215,8 +216,13 @@ def run_ours(args, cfg, rank, world, dev):
     kvb = importlib.import_module("paged-kv-cache-manager_b200")
     kvb.lib()
     nh, kvh, D, L, B = cfg["nh"], cfg["kvh"], cfg["D"], cfg["L"], cfg["B"]
-    ns = cfg["ns"]
-    lens = sample_lens(cfg, ns, seed=1000 + rank)
+    # The whole job's requests (ns per GPU) are sampled once and sharded by context length, longest first
+    # (sharding.assign_requests); each rank serves its shard with its own pool and KVManager.
+    sh = importlib.import_module("paged-kv-cache-manager_b200.sharding")
+    all_lens = sample_lens(cfg, cfg["ns"] * world, seed=1000)
+    rank_of = sh.assign_requests(all_lens.tolist(), world)
+    lens = all_lens[sh.shard_of(rank_of, rank)]
+    ns = len(lens)
     W, K = args.warmup, args.steps
     steps_total = W + K + 2 * (W + K)  # value run, then e2e run
     mgr, kc, vc, nb = setup_shard(kvb, cfg, lens, steps_total, dev, seed=rank * 7 + 1)
@@ -355,14 +361,22 @@ def main():
     ap.add_argument("--config", default=DEFAULT, choices=sorted(CONFIGS))
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--requests", type=int, default=0, help="profiling: requests per GPU (pool sized to need)")
+    ap.add_argument("--layers", type=int, default=0, help="profiling: number of layers (pool sized to need)")
     args = ap.parse_args()
     assert args.warmup >= 3, "at least 3 warm-up steps"
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.requests or args.layers:
+        cfg["ns"] = args.requests or cfg["ns"]
+        cfg["L"] = args.layers or cfg["L"]
+        cfg["pool_gb"], cfg["pool_blocks"] = None, None
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     metric = "paged decode-attn achieved HBM TB/s & % peak; decode tok/s at 1/2/4/8 GPUs"
-    config = {"workload": f"{args.config}-shaped decode step: append scatter + paged decode attention, all layers",
+    reduced = " (reduced profiling case)" if (args.requests or args.layers) else ""
+    config = {"workload": f"{args.config}-shaped decode step: append scatter + paged decode attention, all layers"
+                          + reduced,
               "heads": cfg["nh"], "kv_heads": cfg["kvh"], "head_dim": cfg["D"], "layers": cfg["L"],
               "block_size": cfg["B"], "requests_per_gpu": cfg["ns"], "lengths": list(cfg["lens"]),
               "kv_dtype": cfg["dtype"], "l2": "inputs larger than L2 (every step reads the whole context)",
@@ -402,17 +416,26 @@ def main():
         pass
     peak_gbs = float(peaks.get("hbm_gbs", 6650.0))
     peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
-    ns_total = cfg["ns"] * world
+    ns_total = cfg["ns"] * world  # every rank serves a balanced shard of the job's requests
     ms_step = res["ms_total"] / args.steps
     value = ns_total / (ms_step / 1e3)
     achieved = res["bytes_per_launch"] / (res["attn_avg_ms"] / 1e3) / 1e9
+    # DRAM traffic per launch: the ncu-measured (read + write) / algorithmic ratio of this kernel on a reduced
+    # case of the same workload (profiles/traffic.json), scaled to this launch's algorithmic bytes.
+    traffic = None
+    try:
+        tr = json.load(open(os.path.join(ROOT, "profiles", "traffic.json")))
+        if args.config == DEFAULT:
+            traffic = round(tr["dram_read_plus_write_over_algorithmic"] * res["bytes_per_launch"])
+    except Exception:
+        pass
     e2e_ms_step = res["e2e_ms"] / args.steps
     line = {"metric": metric, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": cfg["dtype"], "data": "synthetic N(0,1), seeded", "config": config,
             "hbm_tb_s": round(achieved / 1e3, 3), "pct_of_measured_peak": round(100 * achieved / peak_gbs, 1),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
-                         "frac": round(achieved / peak_gbs, 4), "traffic": None,
+                         "frac": round(achieved / peak_gbs, 4), "traffic": traffic,
                          "kernel": "paged_decode_kernel (+ split merge)", "peak_source": peak_src},
             "e2e": {"value": round(ns_total / (e2e_ms_step / 1e3), 1), "unit": "tok/s",
                     "h2d_bytes_per_step": res["h2d"], "d2h_bytes_per_step": res["d2h"]},
