@@ -208,6 +208,44 @@ KVP_API int kvp_mgr_append_batch(kvp_mgr* m, const int64_t* rids, int32_t n, int
 KVP_API int kvp_mgr_dense_tables(kvp_mgr* m, const int64_t* rids, int32_t n, int32_t max_blocks, int32_t pad,
                                  int32_t* tables, int32_t* lens);
 
+/* ======================================================================== decode-step runtime
+ * One call per decode step for one GPU shard: the device form of the reference harness's decode_batch
+ * (python/paged_model.py:105-154).  For the given requests, in order: KVManager::append_token (through the
+ * caller's kvp_mgr), the copy-on-write copies those appends decided, the append scatter of every layer's new
+ * K/V, and paged attention for every layer over the updated cache.  The host-buffer form copies the inputs
+ * in and the outputs out on its own streams so that transfers overlap the attention of other layers, and
+ * returns once the outputs are in host memory (pinned host buffers make the copies asynchronous).
+ * Device memory: the caller passes the pools and one workspace of kvp_decoder_workspace_size() bytes; the
+ * decoder allocates no device memory (it allocates pinned host staging for tables and slots). */
+typedef struct kvp_decoder_config {
+    int32_t num_layers, num_heads, kv_heads, head_dim, block_size;
+    int32_t kv_dtype, q_dtype, out_dtype;
+    int64_t num_blocks;          /* blocks in each layer's pool */
+    int64_t layer_stride;        /* elements between layer pools; 0: contiguous [L][num_blocks][B][kvh][D] */
+    int32_t max_seqs;            /* most requests in one step */
+    int32_t max_blocks_per_seq;  /* table row length */
+    int32_t split_tiles;         /* 0: automatic from the step's context lengths; < 0: never split */
+    void* k_cache;
+    void* v_cache;
+    void* workspace; /* device, 256-byte aligned */
+    size_t workspace_bytes;
+} kvp_decoder_config;
+typedef struct kvp_decoder kvp_decoder;
+KVP_API size_t kvp_decoder_workspace_size(const kvp_decoder_config* c);
+KVP_API kvp_decoder* kvp_decoder_create(const kvp_decoder_config* c, kvp_mgr* mgr);
+KVP_API void kvp_decoder_destroy(kvp_decoder* d);
+/* q / out: [num_layers][n][num_heads][head_dim]; k_new / v_new: [num_layers][n][kv_heads][head_dim] (pool
+ * dtype).  Host pointers.  Returns KVP_OK, or KVP_ENOSPACE when an append found no free block (the KVManager
+ * state then reflects the appends that succeeded; nothing was launched). */
+KVP_API int kvp_decoder_step(kvp_decoder* d, const int64_t* rids, int32_t n, const void* q, const void* k_new,
+                             const void* v_new, void* out);
+/* Same with device pointers, asynchronous on `stream` (only the host bookkeeping and the small table / slot
+ * upload are done before returning). */
+KVP_API int kvp_decoder_step_device(kvp_decoder* d, const int64_t* rids, int32_t n, const void* q,
+                                    const void* k_new, const void* v_new, void* out, void* stream);
+/* OR of the KVP_STATUS_* bits the decoder's kernels reported so far (synchronises the decoder's streams). */
+KVP_API int kvp_decoder_status(kvp_decoder* d);
+
 #ifdef __cplusplus
 }
 #endif

@@ -59,6 +59,14 @@ class SwapArgs(C.Structure):
                 ("host_pool_slots", _i64)]
 
 
+class DecoderConfig(C.Structure):
+    _fields_ = [("num_layers", _i32), ("num_heads", _i32), ("kv_heads", _i32), ("head_dim", _i32),
+                ("block_size", _i32), ("kv_dtype", _i32), ("q_dtype", _i32), ("out_dtype", _i32),
+                ("num_blocks", _i64), ("layer_stride", _i64), ("max_seqs", _i32), ("max_blocks_per_seq", _i32),
+                ("split_tiles", _i32), ("k_cache", _vp), ("v_cache", _vp), ("workspace", _vp),
+                ("workspace_bytes", _sz)]
+
+
 # (name, restype, argtypes) of every C-ABI entry point in include/kvp_b200.h.
 _SIGNATURES = [
     ("kvp_last_error", C.c_char_p, []),
@@ -100,6 +108,12 @@ _SIGNATURES = [
     ("kvp_mgr_clear_cache", C.c_int, [_vp]),
     ("kvp_mgr_append_batch", C.c_int, [_vp, _pi64, _i32, _pi32, _pi32, _pi32]),
     ("kvp_mgr_dense_tables", C.c_int, [_vp, _pi64, _i32, _i32, _i32, _pi32, _pi32]),
+    ("kvp_decoder_workspace_size", _sz, [C.POINTER(DecoderConfig)]),
+    ("kvp_decoder_create", _vp, [C.POINTER(DecoderConfig), _vp]),
+    ("kvp_decoder_destroy", None, [_vp]),
+    ("kvp_decoder_step", C.c_int, [_vp, _pi64, _i32, _vp, _vp, _vp, _vp]),
+    ("kvp_decoder_step_device", C.c_int, [_vp, _pi64, _i32, _vp, _vp, _vp, _vp, _vp]),
+    ("kvp_decoder_status", C.c_int, [_vp]),
 ]
 
 _lib = None
@@ -431,3 +445,67 @@ def swap_in(k_cache, v_cache, blocks, host_slots, host_pool, *, stream=None):
 
 def host_slot_bytes(num_layers: int, block_size: int, kv_heads: int, head_dim: int, elem: int = 2) -> int:
     return 2 * num_layers * block_size * kv_heads * head_dim * elem
+
+
+# ============================================================================ decode-step runtime
+class Decoder:
+    """kvp_decoder: one call per decode step for one GPU shard (appends through `mgr`, copy-on-write, append
+    scatter and attention for every layer).  k_cache / v_cache: [L][num_blocks][B][kv_heads][D] device pools.
+    The workspace is allocated here with torch unless one is passed."""
+
+    def __init__(self, mgr: "KVManager", k_cache, v_cache, num_heads: int, max_seqs: int, max_blocks_per_seq: int,
+                 q_dtype=None, out_dtype=None, split_tiles: int = 0, workspace=None):
+        import torch
+        L, nb, B, kvh, D = k_cache.shape
+        c = DecoderConfig()
+        c.num_layers, c.num_heads, c.kv_heads, c.head_dim, c.block_size = L, num_heads, kvh, D, B
+        c.kv_dtype = _dtype_code(k_cache)
+        tq = {None: c.kv_dtype, torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
+        c.q_dtype, c.out_dtype = tq[q_dtype], tq[out_dtype]
+        c.num_blocks, c.layer_stride = nb, nb * B * kvh * D
+        c.max_seqs, c.max_blocks_per_seq, c.split_tiles = max_seqs, max_blocks_per_seq, split_tiles
+        c.k_cache, c.v_cache = _dev(k_cache, "k_cache"), _dev(v_cache, "v_cache")
+        self._L = lib()
+        need = int(self._L.kvp_decoder_workspace_size(C.byref(c)))
+        if need == 0:
+            raise ValueError("invalid decoder configuration")
+        if workspace is None:
+            workspace = torch.empty(need, dtype=torch.uint8, device=k_cache.device)
+        c.workspace, c.workspace_bytes = _dev(workspace, "workspace"), workspace.numel() * workspace.element_size()
+        self._ws, self._k, self._v, self._mgr, self.cfg = workspace, k_cache, v_cache, mgr, c
+        h = self._L.kvp_decoder_create(C.byref(c), mgr.handle)
+        if not h:
+            raise KVPError(KVP_EINVAL, last_error())
+        self._h = C.c_void_p(h)
+
+    def __del__(self):
+        try:
+            if getattr(self, "_h", None):
+                self._L.kvp_decoder_destroy(self._h)
+                self._h = None
+        except Exception:
+            pass
+
+    @staticmethod
+    def _rids(rids):
+        import numpy as np
+        return np.ascontiguousarray(np.asarray(rids, dtype=np.int64))
+
+    def step(self, rids, q, k_new, v_new, out):
+        """Host tensors (pinned for overlap): q/out [L][n][nh][D], k_new/v_new [L][n][kvh][D].  Returns once
+        `out` holds the step's attention outputs."""
+        r = self._rids(rids)
+        for t in (q, k_new, v_new, out):
+            if t.is_cuda or not t.is_contiguous():
+                raise ValueError("decoder.step takes contiguous host tensors")
+        _check(self._L.kvp_decoder_step(self._h, r.ctypes.data_as(_pi64), len(r), q.data_ptr(), k_new.data_ptr(),
+                                         v_new.data_ptr(), out.data_ptr()))
+
+    def step_device(self, rids, q, k_new, v_new, out, stream=None):
+        r = self._rids(rids)
+        _check(self._L.kvp_decoder_step_device(self._h, r.ctypes.data_as(_pi64), len(r), _dev(q, "q"),
+                                                _dev(k_new, "k_new"), _dev(v_new, "v_new"), _dev(out, "out"),
+                                                _stream_ptr(stream)))
+
+    def status(self) -> int:
+        return int(self._L.kvp_decoder_status(self._h))

@@ -9,7 +9,6 @@
 
 #include "kvp_b200.h"
 #include "kvp_internal.h"
-#include "kvpage/kv_manager.h"
 
 namespace kvpi {
 
@@ -44,11 +43,7 @@ int sm_count() {
 extern "C" KVP_API const char* kvp_last_error(void) { return kvpi::g_last_error.c_str(); }
 extern "C" KVP_API const char* kvp_version(void) { return "kvpage-b200 0.1 (sm_100a)"; }
 
-// ------------------------------------------------------------------ KVManager
-struct kvp_mgr {
-    kvp::KVManager m;
-    kvp_mgr(int nb, int bs) : m(nb, bs) {}
-};
+// ------------------------------------------------------------------ KVManager (kvp_mgr is in kvp_internal.h)
 
 namespace {
 

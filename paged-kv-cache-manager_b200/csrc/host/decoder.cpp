@@ -1,0 +1,427 @@
+// Decode-step runtime: one call per step for one GPU shard (the device form of the reference harness's
+// decode_batch, python/paged_model.py:105-154).
+//
+// Per step: host bookkeeping (KVManager::append_token per request -> write slots and copy-on-write pairs,
+// dense table rows, lengths), one upload of that metadata, then on the compute stream: copy-on-write copies,
+// the append scatter of every layer's new K/V, and paged attention per layer.  With host buffers, a copy-in
+// stream feeds the new K/V and each layer's queries and a copy-out stream drains each layer's output as soon as
+// its attention finishes, so transfers overlap the attention of other layers.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <new>
+#include <stdexcept>
+#include <unordered_set>
+#include <vector>
+
+#include "kvp_b200.h"
+#include "kvp_internal.h"
+
+namespace {
+
+constexpr int kMaxSplitsCap = 64;  // bounds the split-K workspace the decoder reserves per sequence and head
+
+size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+int elem(int dt) { return dt == KVP_DTYPE_F32 ? 4 : 2; }
+
+struct Layout {
+    size_t meta = 0;        // [tables max_seqs*max_blocks][lens][slots][pairs 2*max_seqs] int32
+    size_t status = 0;      // int32
+    size_t attn = 0;        // split partials
+    size_t q = 0, k = 0, v = 0, out = 0;  // host-path staging
+    size_t total = 0;
+    size_t attn_bytes = 0;
+};
+
+Layout layout_of(const kvp_decoder_config& c) {
+    Layout L;
+    const size_t ns = static_cast<size_t>(c.max_seqs);
+    size_t o = 0;
+    L.meta = o;
+    o = align256(o + sizeof(int32_t) * (ns * static_cast<size_t>(c.max_blocks_per_seq) + 4 * ns));
+    L.status = o;
+    o = align256(o + sizeof(int32_t));
+    L.attn = o;
+    if (c.split_tiles >= 0) {
+        const size_t max_tiles =
+            (static_cast<size_t>(c.max_blocks_per_seq) * static_cast<size_t>(c.block_size) + 15) / 16;
+        const size_t splits = std::min<size_t>(kMaxSplitsCap, max_tiles);
+        const size_t rows = ns * splits * static_cast<size_t>(c.num_heads);
+        L.attn_bytes = splits > 1 ? align256(rows * 8) + rows * static_cast<size_t>(c.head_dim) * 4 : 0;
+    }
+    o = align256(o + L.attn_bytes);
+    const size_t per_q = ns * c.num_heads * c.head_dim, per_kv = ns * c.kv_heads * c.head_dim;
+    L.q = o;
+    o = align256(o + static_cast<size_t>(c.num_layers) * per_q * elem(c.q_dtype));
+    L.k = o;
+    o = align256(o + static_cast<size_t>(c.num_layers) * per_kv * elem(c.kv_dtype));
+    L.v = o;
+    o = align256(o + static_cast<size_t>(c.num_layers) * per_kv * elem(c.kv_dtype));
+    L.out = o;
+    o = align256(o + static_cast<size_t>(c.num_layers) * per_q * elem(c.out_dtype));
+    L.total = o;
+    return L;
+}
+
+int check_config(const kvp_decoder_config* c) {
+    using kvpi::fail;
+    if (!c) return fail(KVP_EINVAL, "null config");
+    if (c->num_layers < 1 || c->num_heads < 1 || c->kv_heads < 1 || c->head_dim < 1 || c->block_size < 1 ||
+        c->max_seqs < 1 || c->max_blocks_per_seq < 1 || c->num_blocks < 1)
+        return fail(KVP_EINVAL, "bad decoder shape");
+    if (!(c->kv_dtype == KVP_DTYPE_F16 || c->kv_dtype == KVP_DTYPE_BF16) || !kvpi::valid_dtype(c->q_dtype) ||
+        !kvpi::valid_dtype(c->out_dtype))
+        return fail(KVP_EINVAL, "bad decoder dtype");
+    return KVP_OK;
+}
+
+}  // namespace
+
+struct kvp_decoder {
+    kvp_decoder_config cfg{};
+    kvp_mgr* mgr = nullptr;
+    Layout lay;
+    char* ws = nullptr;
+    int32_t* h_meta = nullptr;  // pinned staging with the same layout as the device meta region
+    size_t meta_bytes = 0;
+    int64_t layer_stride = 0;   // elements
+    cudaStream_t s_in = nullptr, s_comp = nullptr, s_out = nullptr;
+    cudaEvent_t ev_meta = nullptr, ev_staged = nullptr, ev_done = nullptr;
+    std::vector<cudaEvent_t> ev_q, ev_att;
+    std::vector<int32_t> pairs;
+    int device = 0;
+
+    ~kvp_decoder() {
+        if (h_meta) cudaFreeHost(h_meta);
+        for (auto e : ev_q) cudaEventDestroy(e);
+        for (auto e : ev_att) cudaEventDestroy(e);
+        for (auto e : {ev_meta, ev_staged, ev_done})
+            if (e) cudaEventDestroy(e);
+        for (auto s : {s_in, s_comp, s_out})
+            if (s) cudaStreamDestroy(s);
+    }
+
+    int32_t* d_meta() const { return reinterpret_cast<int32_t*>(ws + lay.meta); }
+    int32_t* d_status() const { return reinterpret_cast<int32_t*>(ws + lay.status); }
+};
+
+namespace {
+
+// Host bookkeeping of a step: appends, slots, copy-on-write pairs, table rows and lengths into the pinned
+// staging.  Returns KVP_OK or KVP_ENOSPACE (an append found no block).
+int host_step(kvp_decoder* d, const int64_t* rids, int n) {
+    kvp::KVManager& m = d->mgr->m;
+    const kvp_decoder_config& c = d->cfg;
+    const int B = c.block_size, MB = c.max_blocks_per_seq;
+    int32_t* tables = d->h_meta;
+    int32_t* lens = tables + static_cast<size_t>(n) * MB;
+    int32_t* slots = lens + n;
+    d->pairs.clear();
+    for (int i = 0; i < n; ++i) {
+        const kvp::BlockTable& t = m.table(rids[i]);
+        const int pos = t.tokens;
+        const kvp::BlockId old_last = t.blocks.empty() ? kvp::kNoBlock : t.blocks.back();
+        if (!m.append_token(rids[i])) return kvpi::fail(KVP_ENOSPACE, "no free block for request " + std::to_string(rids[i]));
+        if (pos % B != 0 && t.blocks.back() != old_last) {
+            d->pairs.push_back(old_last);
+            d->pairs.push_back(t.blocks.back());
+        }
+        if (static_cast<int>(t.blocks.size()) > MB)
+            return kvpi::fail(KVP_EBOUNDS, "request " + std::to_string(rids[i]) + " outgrew max_blocks_per_seq");
+        slots[i] = t.blocks[static_cast<size_t>(pos / B)] * B + pos % B;
+        lens[i] = t.tokens;
+        std::memcpy(tables + static_cast<size_t>(i) * MB, t.blocks.data(), sizeof(int32_t) * t.blocks.size());
+    }
+    std::memcpy(slots + n, d->pairs.data(), sizeof(int32_t) * d->pairs.size());
+    return KVP_OK;
+}
+
+// Context split for this step: ~8 CTA waves over the real tiles, within the reserved workspace.
+int choose_split(const kvp_decoder* d, int n) {
+    const kvp_decoder_config& c = d->cfg;
+    if (c.split_tiles != 0) return c.split_tiles;
+    const int32_t* lens = d->h_meta + static_cast<size_t>(n) * c.max_blocks_per_seq;
+    long long tiles = 0;
+    for (int i = 0; i < n; ++i) tiles += (lens[i] + 15) / 16;
+    const long long max_tiles = (static_cast<long long>(c.max_blocks_per_seq) * c.block_size + 15) / 16;
+    const long long target = static_cast<long long>(kvpi::sm_count()) * 8;
+    long long split = std::max<long long>(8, (tiles + target - 1) / target);
+    split = std::max<long long>(split, (max_tiles + kMaxSplitsCap - 1) / kMaxSplitsCap);
+    return static_cast<int>(std::min<long long>(split, std::max<long long>(1, max_tiles)));
+}
+
+// Copy-on-write launches in order-preserving chunks: a pair whose destination is the source of an earlier
+// pair of the chunk starts a new chunk, so every block is read before it is overwritten.
+int launch_cow(kvp_decoder* d, const int32_t* d_pairs, cudaStream_t s) {
+    const kvp_decoder_config& c = d->cfg;
+    const int npairs = static_cast<int>(d->pairs.size() / 2);
+    int start = 0;
+    std::unordered_set<int32_t> srcs;
+    auto flush = [&](int end) {
+        if (end <= start) return KVP_OK;
+        kvp_cow_args a{};
+        a.k_cache = c.k_cache;
+        a.v_cache = c.v_cache;
+        a.layer_stride = d->layer_stride;
+        a.pairs = d_pairs + 2 * start;
+        a.n_pairs = end - start;
+        a.kv_dtype = c.kv_dtype;
+        a.num_layers = c.num_layers;
+        a.kv_heads = c.kv_heads;
+        a.head_dim = c.head_dim;
+        a.block_size = c.block_size;
+        a.num_blocks = c.num_blocks;
+        a.status = d->d_status();
+        return kvp_cow_copy(&a, s);
+    };
+    for (int k = 0; k < npairs; ++k) {
+        if (srcs.count(d->pairs[2 * k + 1])) {
+            int rc = flush(k);
+            if (rc != KVP_OK) return rc;
+            start = k;
+            srcs.clear();
+        }
+        srcs.insert(d->pairs[2 * k]);
+    }
+    return flush(npairs);
+}
+
+int enqueue_device(kvp_decoder* d, int n, const void* q, const void* knew, const void* vnew, void* out,
+                   cudaStream_t s_comp, bool per_layer_events) {
+    const kvp_decoder_config& c = d->cfg;
+    const int32_t* meta = d->d_meta();
+    const int32_t* d_tables = meta;
+    const int32_t* d_lens = meta + static_cast<size_t>(n) * c.max_blocks_per_seq;
+    const int32_t* d_slots = d_lens + n;
+    const int32_t* d_pairs = d_slots + n;
+    int rc = launch_cow(d, d_pairs, s_comp);
+    if (rc != KVP_OK) return rc;
+    kvp_append_args ap{};
+    ap.k_new = knew;
+    ap.v_new = vnew;
+    ap.k_cache = c.k_cache;
+    ap.v_cache = c.v_cache;
+    ap.layer_stride = d->layer_stride;
+    ap.slots = d_slots;
+    ap.kv_dtype = c.kv_dtype;
+    ap.num_layers = c.num_layers;
+    ap.num_seqs = n;
+    ap.kv_heads = c.kv_heads;
+    ap.head_dim = c.head_dim;
+    ap.block_size = c.block_size;
+    ap.num_blocks = c.num_blocks;
+    ap.status = d->d_status();
+    rc = kvp_append_scatter(&ap, s_comp);
+    if (rc != KVP_OK) return rc;
+    const int split = choose_split(d, n);
+    const size_t kv_layer_bytes = static_cast<size_t>(d->layer_stride) * 2;
+    const size_t q_layer = static_cast<size_t>(n) * c.num_heads * c.head_dim;
+    for (int l = 0; l < c.num_layers; ++l) {
+        if (per_layer_events) {
+            cudaError_t e = cudaStreamWaitEvent(s_comp, d->ev_q[static_cast<size_t>(l)], 0);
+            if (e != cudaSuccess) return kvpi::cuda_status(e, "decoder wait");
+        }
+        kvp_attn_args a{};
+        a.q = static_cast<const char*>(q) + q_layer * elem(c.q_dtype) * l;
+        a.q_dtype = c.q_dtype;
+        a.k_cache = static_cast<const char*>(c.k_cache) + kv_layer_bytes * l;
+        a.v_cache = static_cast<const char*>(c.v_cache) + kv_layer_bytes * l;
+        a.kv_dtype = c.kv_dtype;
+        a.num_blocks = c.num_blocks;
+        a.block_tables = d_tables;
+        a.seq_lens = d_lens;
+        a.out = static_cast<char*>(out) + q_layer * elem(c.out_dtype) * l;
+        a.out_dtype = c.out_dtype;
+        a.num_seqs = n;
+        a.num_heads = c.num_heads;
+        a.kv_heads = c.kv_heads;
+        a.head_dim = c.head_dim;
+        a.block_size = c.block_size;
+        a.max_blocks = c.max_blocks_per_seq;
+        a.split_tiles = split;
+        a.workspace = d->lay.attn_bytes ? d->ws + d->lay.attn : nullptr;
+        a.workspace_bytes = d->lay.attn_bytes;
+        a.status = d->d_status();
+        rc = kvp_paged_attention(&a, s_comp);
+        if (rc != KVP_OK) return rc;
+        if (per_layer_events) {
+            cudaError_t e = cudaEventRecord(d->ev_att[static_cast<size_t>(l)], s_comp);
+            if (e != cudaSuccess) return kvpi::cuda_status(e, "decoder record");
+        }
+    }
+    return KVP_OK;
+}
+
+int upload_meta(kvp_decoder* d, int n, cudaStream_t s) {
+    const size_t ints = static_cast<size_t>(n) * d->cfg.max_blocks_per_seq + 2 * static_cast<size_t>(n) + d->pairs.size();
+    cudaError_t e = cudaMemcpyAsync(d->d_meta(), d->h_meta, ints * sizeof(int32_t), cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) return kvpi::cuda_status(e, "decoder metadata upload");
+    e = cudaEventRecord(d->ev_staged, s);
+    return kvpi::cuda_status(e, "decoder record");
+}
+
+// The pinned staging may still be read by the previous step's upload.
+int wait_staging(kvp_decoder* d) { return kvpi::cuda_status(cudaEventSynchronize(d->ev_staged), "decoder staging wait"); }
+
+template <class F>
+int guarded(F&& f) {
+    kvpi::clear_error();
+    try {
+        return f();
+    } catch (const std::invalid_argument& e) {
+        return kvpi::fail(KVP_EINVAL, e.what());
+    } catch (const std::exception& e) {
+        return kvpi::fail(KVP_ESTATE, e.what());
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+KVP_API size_t kvp_decoder_workspace_size(const kvp_decoder_config* c) {
+    if (check_config(c) != KVP_OK) return 0;
+    return layout_of(*c).total;
+}
+
+KVP_API kvp_decoder* kvp_decoder_create(const kvp_decoder_config* c, kvp_mgr* mgr) {
+    kvpi::clear_error();
+    if (check_config(c) != KVP_OK) return nullptr;
+    if (!mgr || !c->k_cache || !c->v_cache || !c->workspace) {
+        kvpi::fail(KVP_EINVAL, "null manager, pool or workspace");
+        return nullptr;
+    }
+    if (mgr->m.block_size() != c->block_size || mgr->m.total_blocks() > c->num_blocks) {
+        kvpi::fail(KVP_EINVAL, "manager block size / pool size differ from the decoder's");
+        return nullptr;
+    }
+    if (c->split_tiles > 0) {
+        const long long max_tiles = (static_cast<long long>(c->max_blocks_per_seq) * c->block_size + 15) / 16;
+        if ((max_tiles + c->split_tiles - 1) / c->split_tiles > kMaxSplitsCap) {
+            kvpi::fail(KVP_EINVAL, "split_tiles gives more than 64 splits per sequence; raise it or pass 0");
+            return nullptr;
+        }
+    }
+    Layout lay = layout_of(*c);
+    if (c->workspace_bytes < lay.total || (reinterpret_cast<uintptr_t>(c->workspace) & 255u)) {
+        kvpi::fail(KVP_ENOSPACE, "decoder workspace smaller than kvp_decoder_workspace_size() or not 256-byte aligned");
+        return nullptr;
+    }
+    auto* d = new (std::nothrow) kvp_decoder();
+    if (!d) {
+        kvpi::fail(KVP_ESTATE, "out of host memory");
+        return nullptr;
+    }
+    d->cfg = *c;
+    d->mgr = mgr;
+    d->lay = lay;
+    d->ws = static_cast<char*>(c->workspace);
+    d->layer_stride = c->layer_stride > 0 ? c->layer_stride
+                                          : c->num_blocks * c->block_size * static_cast<int64_t>(c->kv_heads) * c->head_dim;
+    d->meta_bytes = lay.status - lay.meta;
+    cudaGetDevice(&d->device);
+    bool ok = cudaHostAlloc(reinterpret_cast<void**>(&d->h_meta), d->meta_bytes, cudaHostAllocDefault) == cudaSuccess;
+    ok = ok && cudaStreamCreateWithFlags(&d->s_in, cudaStreamNonBlocking) == cudaSuccess;
+    ok = ok && cudaStreamCreateWithFlags(&d->s_comp, cudaStreamNonBlocking) == cudaSuccess;
+    ok = ok && cudaStreamCreateWithFlags(&d->s_out, cudaStreamNonBlocking) == cudaSuccess;
+    ok = ok && cudaEventCreateWithFlags(&d->ev_meta, cudaEventDisableTiming) == cudaSuccess;
+    ok = ok && cudaEventCreateWithFlags(&d->ev_staged, cudaEventDisableTiming) == cudaSuccess;
+    ok = ok && cudaEventCreateWithFlags(&d->ev_done, cudaEventDisableTiming) == cudaSuccess;
+    d->ev_q.resize(static_cast<size_t>(c->num_layers));
+    d->ev_att.resize(static_cast<size_t>(c->num_layers));
+    for (int l = 0; ok && l < c->num_layers; ++l) {
+        ok = cudaEventCreateWithFlags(&d->ev_q[static_cast<size_t>(l)], cudaEventDisableTiming) == cudaSuccess &&
+             cudaEventCreateWithFlags(&d->ev_att[static_cast<size_t>(l)], cudaEventDisableTiming) == cudaSuccess;
+    }
+    ok = ok && cudaMemsetAsync(d->d_status(), 0, sizeof(int32_t), d->s_comp) == cudaSuccess;
+    ok = ok && cudaEventRecord(d->ev_staged, d->s_in) == cudaSuccess;
+    ok = ok && cudaStreamSynchronize(d->s_comp) == cudaSuccess;
+    if (!ok) {
+        kvpi::fail(KVP_ECUDA, std::string("decoder setup: ") + cudaGetErrorString(cudaGetLastError()));
+        delete d;
+        return nullptr;
+    }
+    return d;
+}
+
+KVP_API void kvp_decoder_destroy(kvp_decoder* d) {
+    if (!d) return;
+    cudaStreamSynchronize(d->s_in);
+    cudaStreamSynchronize(d->s_comp);
+    cudaStreamSynchronize(d->s_out);
+    delete d;
+}
+
+KVP_API int kvp_decoder_step_device(kvp_decoder* d, const int64_t* rids, int32_t n, const void* q, const void* k_new,
+                                    const void* v_new, void* out, void* stream) {
+    return guarded([&] {
+        if (!d || (n > 0 && (!rids || !q || !k_new || !v_new || !out))) return kvpi::fail(KVP_EINVAL, "null argument");
+        if (n < 0 || n > d->cfg.max_seqs) return kvpi::fail(KVP_EINVAL, "n outside [0, max_seqs]");
+        if (n == 0) return KVP_OK;
+        int rc = wait_staging(d);
+        if (rc != KVP_OK) return rc;
+        rc = host_step(d, rids, n);
+        if (rc != KVP_OK) return rc;
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        rc = upload_meta(d, n, s);
+        if (rc != KVP_OK) return rc;
+        return enqueue_device(d, n, q, k_new, v_new, out, s, false);
+    });
+}
+
+KVP_API int kvp_decoder_step(kvp_decoder* d, const int64_t* rids, int32_t n, const void* q, const void* k_new,
+                             const void* v_new, void* out) {
+    return guarded([&] {
+        if (!d || (n > 0 && (!rids || !q || !k_new || !v_new || !out))) return kvpi::fail(KVP_EINVAL, "null argument");
+        if (n < 0 || n > d->cfg.max_seqs) return kvpi::fail(KVP_EINVAL, "n outside [0, max_seqs]");
+        if (n == 0) return KVP_OK;
+        const kvp_decoder_config& c = d->cfg;
+        int rc = wait_staging(d);
+        if (rc != KVP_OK) return rc;
+        rc = host_step(d, rids, n);
+        if (rc != KVP_OK) return rc;
+        const size_t q_layer = static_cast<size_t>(n) * c.num_heads * c.head_dim * elem(c.q_dtype);
+        const size_t o_layer = static_cast<size_t>(n) * c.num_heads * c.head_dim * elem(c.out_dtype);
+        const size_t kv_all = static_cast<size_t>(c.num_layers) * n * c.kv_heads * c.head_dim * elem(c.kv_dtype);
+        char* dq = d->ws + d->lay.q;
+        char* dk = d->ws + d->lay.k;
+        char* dv = d->ws + d->lay.v;
+        char* dout = d->ws + d->lay.out;
+        // copy-in stream: metadata, new K/V, then each layer's queries
+        rc = upload_meta(d, n, d->s_in);
+        if (rc != KVP_OK) return rc;
+        cudaError_t e = cudaMemcpyAsync(dk, k_new, kv_all, cudaMemcpyHostToDevice, d->s_in);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(dv, v_new, kv_all, cudaMemcpyHostToDevice, d->s_in);
+        if (e == cudaSuccess) e = cudaEventRecord(d->ev_meta, d->s_in);
+        for (int l = 0; e == cudaSuccess && l < c.num_layers; ++l) {
+            e = cudaMemcpyAsync(dq + q_layer * l, static_cast<const char*>(q) + q_layer * l, q_layer,
+                                cudaMemcpyHostToDevice, d->s_in);
+            if (e == cudaSuccess) e = cudaEventRecord(d->ev_q[static_cast<size_t>(l)], d->s_in);
+        }
+        if (e != cudaSuccess) return kvpi::cuda_status(e, "decoder input copies");
+        e = cudaStreamWaitEvent(d->s_comp, d->ev_meta, 0);
+        if (e != cudaSuccess) return kvpi::cuda_status(e, "decoder wait");
+        rc = enqueue_device(d, n, dq, dk, dv, dout, d->s_comp, true);
+        if (rc != KVP_OK) return rc;
+        // copy-out stream: each layer's output as soon as its attention is done
+        for (int l = 0; e == cudaSuccess && l < c.num_layers; ++l) {
+            e = cudaStreamWaitEvent(d->s_out, d->ev_att[static_cast<size_t>(l)], 0);
+            if (e == cudaSuccess)
+                e = cudaMemcpyAsync(static_cast<char*>(out) + o_layer * l, dout + o_layer * l, o_layer,
+                                    cudaMemcpyDeviceToHost, d->s_out);
+        }
+        if (e == cudaSuccess) e = cudaStreamSynchronize(d->s_out);
+        return kvpi::cuda_status(e, "decoder output copies");
+    });
+}
+
+KVP_API int kvp_decoder_status(kvp_decoder* d) {
+    if (!d) return -KVP_EINVAL;
+    cudaStreamSynchronize(d->s_comp);
+    int32_t v = 0;
+    if (cudaMemcpy(&v, d->d_status(), sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) return -KVP_ECUDA;
+    return v;
+}
+
+}  // extern "C"

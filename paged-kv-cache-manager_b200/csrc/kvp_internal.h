@@ -6,6 +6,13 @@
 #include <string>
 
 #include "kvp_b200.h"
+#include "kvpage/kv_manager.h"
+
+// The C handle of a host control plane: one kvp::KVManager.
+struct kvp_mgr {
+    kvp::KVManager m;
+    kvp_mgr(int nb, int bs) : m(nb, bs) {}
+};
 
 namespace kvpi {
 

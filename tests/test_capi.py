@@ -89,3 +89,17 @@ def test_kv_ops_reject_invalid_arguments(kvb):
     assert L.kvp_swap_out(C.byref(s), None) == kvb.KVP_EBOUNDS  # negative block id
     blocks[0], slots[0] = 0, 4
     assert L.kvp_swap_in(C.byref(s), None) == kvb.KVP_EBOUNDS   # host slot beyond the pool
+
+
+def test_decoder_config_validation(kvb):
+    L = kvb.lib()
+    c = kvb.DecoderConfig()
+    assert L.kvp_decoder_workspace_size(C.byref(c)) == 0  # all-zero shape is invalid
+    c.num_layers, c.num_heads, c.kv_heads, c.head_dim, c.block_size = 2, 8, 2, 64, 16
+    c.kv_dtype, c.q_dtype, c.out_dtype, c.num_blocks, c.max_seqs, c.max_blocks_per_seq = 2, 2, 0, 64, 4, 8
+    n = L.kvp_decoder_workspace_size(C.byref(c))
+    assert n > 2 * 4 * 8 * 64 * 2  # at least the query staging
+    m = kvb.KVManager(64, 16)
+    assert not L.kvp_decoder_create(C.byref(c), m.handle)  # no pools / workspace
+    c.split_tiles = -1
+    assert L.kvp_decoder_workspace_size(C.byref(c)) < n  # no split-K partials reserved

@@ -1,0 +1,100 @@
+"""The decode-step runtime (kvp_decoder_*) produces exactly what the individual entry points produce when
+driven by hand (append batch -> copy-on-write -> append scatter -> attention per layer), with host buffers
+and with device buffers, and its attention output matches the oracle on the updated cache."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _setup(kvb, seed, L=4, nb=192, B=16, kvh=2, D=64, nh=8):
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    k = torch.randn((L, nb, B, kvh, D), generator=g, device="cuda").to(torch.bfloat16)
+    v = torch.randn((L, nb, B, kvh, D), generator=g, device="cuda").to(torch.bfloat16)
+    m = kvb.KVManager(nb, B)
+    assert m.admit(0, 37) and m.fork(1, 0) and m.fork(2, 0) and m.admit(3, 300) and m.admit_with_prefix(4, 3, 160, 170)
+    return k, v, m
+
+
+def _manual_step(kvb, m, k, v, rids, q, kn, vn, split, max_blocks, nh, kvh):
+    import torch
+    done, slots, pairs = m.append_batch(rids)
+    assert done == len(rids)
+    if len(pairs):
+        kvb.cow_copy(k, v, torch.from_numpy(np.ascontiguousarray(pairs)).cuda())
+    kvb.append_scatter(kn, vn, k, v, torch.from_numpy(slots).cuda())
+    tables, lens = m.dense_tables(rids, max_blocks)
+    t, l = torch.from_numpy(tables).cuda(), torch.from_numpy(lens).cuda()
+    out = torch.empty(q.shape, dtype=q.dtype, device="cuda")
+    for layer in range(k.shape[0]):
+        kvb.paged_attention(q[layer], k[layer], v[layer], t, l, nh, kvh, out=out[layer], split_tiles=split)
+    return out
+
+
+@pytest.mark.parametrize("path", ["host", "device"])
+def test_decoder_matches_manual_path(kvb, cuda, path):
+    import torch
+    nh, kvh, D, L, MB = 8, 2, 64, 4, 40
+    k1, v1, m1 = _setup(kvb, 1)
+    k2, v2, m2 = k1.clone(), v1.clone(), None
+    _, _, m2 = _setup(kvb, 1)
+    dec = kvb.Decoder(m1, k1, v1, nh, max_seqs=8, max_blocks_per_seq=MB, split_tiles=2)
+    rids = [0, 1, 2, 3, 4]
+    rng = np.random.default_rng(3)
+    for step in range(6):
+        order = [int(x) for x in rng.permutation(rids)]
+        n = len(order)
+        q = torch.randn((L, n, nh, D)).to(torch.bfloat16)
+        kn = torch.randn((L, n, kvh, D)).to(torch.bfloat16)
+        vn = torch.randn((L, n, kvh, D)).to(torch.bfloat16)
+        if path == "host":
+            out1 = torch.empty((L, n, nh, D), dtype=torch.bfloat16).pin_memory()
+            dec.step(order, q.pin_memory(), kn.pin_memory(), vn.pin_memory(), out1)
+        else:
+            out1 = torch.empty((L, n, nh, D), dtype=torch.bfloat16, device="cuda")
+            dec.step_device(order, q.cuda(), kn.cuda(), vn.cuda(), out1)
+            torch.cuda.synchronize()
+            out1 = out1.cpu()
+        out2 = _manual_step(kvb, m2, k2, v2, order, q.cuda(), kn.cuda(), vn.cuda(), 2, MB, nh, kvh)
+        torch.cuda.synchronize()
+        assert torch.equal(out1, out2.cpu()), step
+        assert torch.equal(k1, k2) and torch.equal(v1, v2), step
+    assert dec.status() == 0
+    assert m1.stats() == m2.stats() and m1.stats()["cow_copies"] == 2
+
+
+def test_decoder_output_matches_oracle(kvb, ora, cuda):
+    import torch
+    nh, kvh, D, L, MB = 8, 2, 64, 4, 40
+    k, v, m = _setup(kvb, 5)
+    dec = kvb.Decoder(m, k, v, nh, max_seqs=8, max_blocks_per_seq=MB, out_dtype=torch.float32)
+    rids = [4, 3, 2, 1, 0]
+    q = torch.randn((L, 5, nh, D)).to(torch.bfloat16)
+    kn = torch.randn((L, 5, kvh, D)).to(torch.bfloat16)
+    vn = torch.randn((L, 5, kvh, D)).to(torch.bfloat16)
+    out = torch.empty((L, 5, nh, D), dtype=torch.float32).pin_memory()
+    dec.step(rids, q.pin_memory(), kn.pin_memory(), vn.pin_memory(), out)
+    tables, lens = m.dense_tables(rids, MB)
+    for layer in (0, 3):
+        ref = ora.reference_attention(nh, kvh, D, 16, q[layer].float().numpy(), k[layer].float().cpu().numpy(),
+                                      v[layer].float().cpu().numpy(), tables, lens)
+        got = out[layer].numpy()
+        assert np.isfinite(got).all()
+        assert (np.abs(got - ref) <= 2e-3 + 2e-3 * np.abs(ref)).all()
+
+
+def test_decoder_reports_exhaustion(kvb, cuda):
+    import torch
+    L, nb, B, kvh, D, nh = 2, 3, 16, 2, 64, 4
+    k = torch.zeros((L, nb, B, kvh, D), dtype=torch.bfloat16, device="cuda")
+    v = torch.zeros_like(k)
+    m = kvb.KVManager(nb, B)
+    assert m.admit(0, 32) and m.admit(1, 16)
+    dec = kvb.Decoder(m, k, v, nh, max_seqs=2, max_blocks_per_seq=4)
+    z = torch.zeros((L, 2, nh, D), dtype=torch.bfloat16).pin_memory()
+    zk = torch.zeros((L, 2, kvh, D), dtype=torch.bfloat16).pin_memory()
+    with pytest.raises(kvb.KVPError) as e:
+        dec.step([0, 1], z, zk, zk, z.clone())  # both need a new block; only one is free
+    assert e.value.code == kvb.KVP_ENOSPACE
+    assert m.num_tokens(0) == 33 and m.num_tokens(1) == 16  # the first append happened, the second did not
