@@ -251,22 +251,41 @@ def run_ours(args, cfg, rank, world, dev):
     vnew = torch.randn((L, ns, kvh, D), generator=g, device=dev).to(tdt)
     out = torch.empty((L, ns, nh, D), device=dev, dtype=tdt)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
-    # context split: about 8 CTA waves over this shard's actual tiles
-    total_tiles = int(((lens + 15) // 16).sum())
-    sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    split = max(8, -(-total_tiles // (sms * 8)))
+    # context schedule: 0 = balanced persistent (stream-K) grid; > 0 = fixed splits of that many tiles
+    split = args.split
     a0 = kvb.attention_args(q[0], kc[0], vc[0], d_tables, d_lens[0], out[0], nh, kvh, num_blocks=nb,
                             split_tiles=split)
     ws = torch.empty(max(kvb.workspace_bytes(a0), 256), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
+    # Launch arguments are built once; a step only repoints the slots / lengths (so the timed loop measures
+    # the kernels, not Python).
+    import ctypes
+    L_lib = kvb.lib()
+    attn_args = []
+    for l in range(L):
+        a = kvb.attention_args(q[l], kc[l], vc[l], d_tables, d_lens[0], out[l], nh, kvh, num_blocks=nb,
+                               split_tiles=split, status=status)
+        a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+        attn_args.append(a)
+    app = kvb.AppendArgs()
+    app.k_new, app.v_new, app.k_cache, app.v_cache = knew.data_ptr(), vnew.data_ptr(), kc.data_ptr(), vc.data_ptr()
+    app.layer_stride, app.kv_dtype, app.num_layers, app.num_seqs = nb * B * kvh * D, kvb._dtype_code(kc), L, ns
+    app.kv_heads, app.head_dim, app.block_size, app.num_blocks, app.status = kvh, D, B, nb, status.data_ptr()
+    sptr = ctypes.c_void_p(stream.cuda_stream)
+    lens_row = d_lens.stride(0) * 4
+    slots_row = d_slots.stride(0) * 4
+
     def step_device(s, ev=None):
-        kvb.append_scatter(knew, vnew, kc, vc, d_slots[s], status=status)
+        app.slots = d_slots.data_ptr() + s * slots_row
+        assert L_lib.kvp_append_scatter(ctypes.byref(app), sptr) == 0
+        lp = d_lens.data_ptr() + s * lens_row
         for l in range(L):
+            a = attn_args[l]
+            a.seq_lens = lp
             if ev is not None:
                 ev[l][0].record(stream)
-            kvb.paged_attention(q[l], kc[l], vc[l], d_tables, d_lens[s], nh, kvh, out=out[l], workspace=ws,
-                                split_tiles=split, status=status, num_blocks=nb)
+            assert L_lib.kvp_paged_attention(ctypes.byref(a), sptr) == 0
             if ev is not None:
                 ev[l][1].record(stream)
 
@@ -327,7 +346,7 @@ def run_ours(args, cfg, rank, world, dev):
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
     ms_total, e2e_ms, attn_avg = [float(x) for x in vals.cpu()]
     clocks = clk.summary()
-    gpu_launches = K * (1 + L * (2 if split < (max_blocks * B + 15) // 16 else 1))
+    gpu_launches = K * (1 + L * (2 if split == 0 or split < (max_blocks * B + 15) // 16 else 1))
     res = dict(ms_total=ms_total, e2e_ms=e2e_ms, attn_avg_ms=attn_avg, bytes_per_launch=bytes_per_launch,
                clocks=clocks, ns=ns, nb=nb, split=split, gpu_launches=gpu_launches,
                h2d=h2d, d2h=int(h_out.numel() * 2), lens_mean=float(lens.mean()))
@@ -342,6 +361,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default=DEFAULT, choices=sorted(CONFIGS))
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--split", type=int, default=0, help="tiles per context split (0: balanced persistent grid)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--requests", type=int, default=0, help="profiling: requests per GPU (pool sized to need)")
     ap.add_argument("--layers", type=int, default=0, help="profiling: number of layers (pool sized to need)")

@@ -1,17 +1,25 @@
-// Paged decode attention for sm_100a: split-K ("flash-decoding") over 16-token tiles of the context.
+// Paged decode attention for sm_100a: flash-decoding over 16-token tiles of the context.
 //
-// Work unit: one CTA per (sequence, group of kv heads, context split).  A producer warp walks the split's
-// tiles, reads block ids from the sequence's table row (32 entries per coalesced load) and issues TMA tiled
-// loads of the K and V rows of every kv head in the group into a ring of shared-memory stages (128B/64B
-// swizzled, completion counted on an mbarrier).  One consumer warp per kv head computes, per tile,
+// Two schedules share the same tile pipeline:
+//   * stream-K (default): a persistent grid of as many CTAs as fit on the GPU; the step's tiles (all
+//     sequences, concatenated) are divided evenly between CTAs regardless of sequence boundaries, so every
+//     CTA streams the same number of bytes with one pipeline ramp per launch.  A CTA's range is cut into
+//     segments at sequence boundaries; a segment that covers a whole sequence is normalised and written
+//     directly, the others leave (m, l, unnormalised O) partials that merge_streamk combines.
+//   * fixed splits: one CTA per (sequence, kv-head group, split of split_tiles tiles); split_tiles large
+//     enough means one CTA per sequence and no workspace at all (the reference's signature).
+//
+// Tile pipeline (per CTA): a producer warp reads block ids from the sequence's table row (32 entries per
+// coalesced load) and issues TMA tiled loads of the K and V rows of every kv head of the CTA's group into a
+// ring of shared-memory stages (128B/64B swizzled; completion counted on an mbarrier); at the start of a
+// stream-K segment it also bulk-copies the sequence's queries into the stage.  One consumer warp per kv head
+// computes, per tile,
 //     S^T[16 tokens x 8 heads] = K_tile[16 x D] . Q^T[D x 8]      (mma.sync m16n8k16, fp32 accumulate)
 // so the GQA group of query heads (up to 8 per n-tile) shares every K/V byte; an online softmax in the
 // log2 domain with warp-shuffle reductions; then
 //     O^T[D x 8] += V_tile^T[D x 16] . P^T[16 x 8]
-// with P^T obtained from the S^T accumulator by movmatrix.  P (and an fp32 query) are split into a
-// 16-bit high part plus a 16-bit residual, so the result keeps close to fp32 accuracy.
-// A sequence handled by one split is normalised and written directly; otherwise the CTA writes
-// (m, l, unnormalised O) partials and merge_splits combines them.
+// with P^T obtained from the S^T accumulator by movmatrix.  P (and an fp32 query) are split into a 16-bit
+// high part plus a 16-bit residual, so the result keeps close to fp32 accuracy.
 //
 // Numerics follow the reference's paged_attention_cpu (src/paged_attention.cpp:68-114): per-partition
 // running (m, l, acc) with rescaling by exp(m_old - m_new), partitions merged by exp(m_p - M).
@@ -24,6 +32,8 @@
 #include <cstring>
 #include <mutex>
 #include <type_traits>
+#include <utility>
+#include <vector>
 
 #include "kvp_device.cuh"
 #include "kvp_internal.h"
@@ -32,227 +42,202 @@ namespace kvpd {
 
 constexpr int kMaxStages = 12;
 constexpr int kMaxKvhPerCta = 8;
+constexpr int kMaxStreamSeqs = 8192;  // stream-K keeps the tile prefix sums of all sequences in smem
 
 struct AttnParams {
     const void* q;
     const int32_t* tables;
     const int32_t* lens;
     void* out;
-    float2* ws_ml;  // [num_seqs][max_splits][num_heads] (m in log2 units, l)
-    float* ws_o;    // [num_seqs][max_splits][num_heads][D]
+    float2* ws_ml;   // partial (m in log2 units, l) rows of nh heads
+    float* ws_o;     // partial unnormalised outputs, D per row
+    int32_t* prefix; // stream-K: [num_seqs + 1] tile prefix sums (written by CTA 0 for the merge)
     int32_t* status;
     long long num_blocks;  // 0: unchecked
     int q_dtype, out_dtype;
     int num_seqs, nh, g, max_blocks, B, R, nruns;
     int kvh_cta, groups, stages, split_tiles, max_splits, per_head;
+    int G;                 // stream-K CTAs per kv-head group
     uint32_t head_stride, box_slot, stage_half, box_tx;
-    int oob_row;  // a row coordinate outside the tensor map (zero fill) used for skipped blocks
-    float sl2;    // scale * log2(e)
+    uint32_t stage_bytes;  // stride between stages (2 * stage_half + query area)
+    uint32_t q_area;       // stream-K: bytes of the per-stage query area (0: queries read from global memory)
+    uint32_t pre_off;      // stream-K: offset of the prefix sums in dynamic smem
+    int oob_row;           // a row coordinate outside the tensor map (zero fill) used for skipped blocks
+    float sl2;             // scale * log2(e)
 };
 
-// Length of sequence `seq` in 16-token tiles, or 0 (with a status bit) if its length is invalid.
-__device__ __forceinline__ int seq_tiles(const AttnParams& p, int seq, int* len_out) {
-    const int len = p.lens[seq];
+// Sequence length in 16-token tiles, or 0 when the length is invalid (len < 1 or more blocks than a
+// table row holds).
+__device__ __forceinline__ int tiles_of_len(const AttnParams& p, int len) {
     const long long nblk = (static_cast<long long>(len) + p.B - 1) / p.B;
-    if (len < 1 || nblk > p.max_blocks) {
-        *len_out = 0;
-        return 0;
-    }
-    *len_out = len;
+    if (len < 1 || nblk > p.max_blocks) return 0;
     return (len + 15) >> 4;
 }
 
-template <int D, int NT, class KV>
-__global__ void __launch_bounds__((kMaxKvhPerCta + 1) * 32, 1)
-    paged_decode_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
-                        const AttnParams p) {
-    constexpr int W = (D % 64 == 0) ? 64 : 32;  // elements per smem row
-    constexpr int ROWB = W * 2;                  // bytes per smem row
-    constexpr int NCH = D / W;
-    constexpr int KS = D / 16;                   // k-steps of the score MMA / m-tiles of the PV MMA
-    constexpr uint32_t SWM = (ROWB == 128) ? 7u : 3u;
-    using Tr = F16Traits<KV>;
+template <int D>
+struct Geo {
+    static constexpr int W = (D % 64 == 0) ? 64 : 32;  // elements per smem row
+    static constexpr int ROWB = W * 2;                  // bytes per smem row
+    static constexpr int NCH = D / W;
+    static constexpr int KS = D / 16;                   // k-steps of the score MMA / m-tiles of the PV MMA
+    static constexpr uint32_t SWM = (ROWB == 128) ? 7u : 3u;
+};
 
-    __shared__ __align__(8) uint64_t full_bar[kMaxStages];
-    __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
-    extern __shared__ uint8_t dyn_smem[];
-
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    const int seq = blockIdx.x / p.groups;
-    const int grp = blockIdx.x - seq * p.groups;
-    const int split = blockIdx.y;
-
-    int len = 0;
-    const int ntiles = seq_tiles(p, seq, &len);
-    const int nsplit = (ntiles + p.split_tiles - 1) / p.split_tiles;
-    if (ntiles == 0) {
-        // Invalid length: report once and write zeros so the output is deterministic.
-        if (split == 0) {
-            if (threadIdx.x == 0) report(p.status, KVP_STATUS_BAD_LEN);
-            const int heads = p.kvh_cta * p.g;
-            for (int i = threadIdx.x; i < heads * D; i += blockDim.x) {
-                const int hq = grp * heads + i / D;
-                store_any(p.out, (static_cast<size_t>(seq) * p.nh + hq) * D + i % D, p.out_dtype, 0.f);
-            }
+// ---------------------------------------------------------------- producer: one tile into one stage
+// All 32 lanes call this (the table cache is a warp-wide register array); lane 0 issues the copies.
+// Returns the transaction bytes the tile adds to the stage's barrier.
+template <int D>
+__device__ __forceinline__ void produce_tile(const AttnParams& p, const CUtensorMap* km, const CUtensorMap* vm,
+                                             uint32_t kst, uint32_t vst, uint32_t fb, int tb, int len,
+                                             const int32_t* trow, int kvh0, int lane, int& cache_lo,
+                                             int32_t& cached, uint32_t extra_tx) {
+    using G_ = Geo<D>;
+    const int nr = min(p.nruns, (len - tb + p.R - 1) / p.R);
+    if (lane == 0) mbar_arrive_expect_tx(fb, static_cast<uint32_t>(nr) * G_::NCH * 2u * p.box_tx + extra_tx);
+    for (int j = 0; j < nr; ++j) {
+        const int tok = tb + j * p.R;
+        const int bi = tok / p.B;
+        if (bi < cache_lo || bi >= cache_lo + 32) {
+            cache_lo = bi;
+            cached = (bi + lane < p.max_blocks) ? __ldg(trow + bi + lane) : 0;
         }
-        return;
-    }
-    if (split >= nsplit) return;
-    const int t0 = split * p.split_tiles;
-    const int n = min(ntiles - t0, p.split_tiles);
-
-    const uint32_t smem_base = (smem_u32(dyn_smem) + 1023u) & ~1023u;
-    const int S = p.stages;
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < S; ++s) {
-            mbar_init(smem_u32(&full_bar[s]), 1);
-            mbar_init(smem_u32(&empty_bar[s]), static_cast<uint32_t>(p.kvh_cta));
+        const int32_t blk = __shfl_sync(0xffffffffu, cached, bi - cache_lo);
+        int row = blk * p.B + (tok - bi * p.B);
+        if (p.num_blocks > 0 && (blk < 0 || blk >= p.num_blocks)) {
+            if (lane == 0) report(p.status, KVP_STATUS_BAD_BLOCK);
+            row = p.oob_row;
         }
-        fence_barrier_init();
-    }
-    __syncthreads();
-
-    if (warp == p.kvh_cta) {
-        // ------------------------------------------------------------ producer warp
         if (lane == 0) {
-            prefetch_tensormap(&kmap);
-            prefetch_tensormap(&vmap);
-        }
-        const int32_t* trow = p.tables + static_cast<size_t>(seq) * p.max_blocks;
-        const int kvh0 = grp * p.kvh_cta;
-        int cache_lo = -(1 << 30);
-        int32_t cached = 0;
-        for (int i = 0; i < n; ++i) {
-            const int s = i % S;
-            if (i >= S && !mbar_wait(smem_u32(&empty_bar[s]), static_cast<uint32_t>((i / S - 1) & 1))) {
-                if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
-                break;
-            }
-            const int tb = (t0 + i) * 16;
-            const int nr = min(p.nruns, (len - tb + p.R - 1) / p.R);
-            const uint32_t fb = smem_u32(&full_bar[s]);
-            if (lane == 0) mbar_arrive_expect_tx(fb, static_cast<uint32_t>(nr) * NCH * 2u * p.box_tx);
-            const uint32_t kst = smem_base + static_cast<uint32_t>(s) * 2u * p.stage_half;
-            const uint32_t vst = kst + p.stage_half;
-            for (int j = 0; j < nr; ++j) {
-                const int tok = tb + j * p.R;
-                const int bi = tok / p.B;
-                if (bi < cache_lo || bi >= cache_lo + 32) {
-                    cache_lo = bi;
-                    cached = (bi + lane < p.max_blocks) ? __ldg(trow + bi + lane) : 0;
-                }
-                const int32_t blk = __shfl_sync(0xffffffffu, cached, bi - cache_lo);
-                int row = blk * p.B + (tok - bi * p.B);
-                if (p.num_blocks > 0 && (blk < 0 || blk >= p.num_blocks)) {
-                    if (lane == 0) report(p.status, KVP_STATUS_BAD_BLOCK);
-                    row = p.oob_row;
-                }
-                if (lane == 0) {
 #pragma unroll
-                    for (int c = 0; c < NCH; ++c) {
-                        const uint32_t off = static_cast<uint32_t>(j * NCH + c) * p.box_slot;
-                        if (!p.per_head) {
-                            tma_load_3d(kst + off, &kmap, fb, c * W, row, kvh0);
-                            tma_load_3d(vst + off, &vmap, fb, c * W, row, kvh0);
-                        } else {
-                            for (int w = 0; w < p.kvh_cta; ++w) {
-                                const uint32_t ho = off + static_cast<uint32_t>(w) * p.head_stride;
-                                tma_load_3d(kst + ho, &kmap, fb, c * W, kvh0 + w, row);
-                                tma_load_3d(vst + ho, &vmap, fb, c * W, kvh0 + w, row);
-                            }
-                        }
+            for (int c = 0; c < G_::NCH; ++c) {
+                const uint32_t off = static_cast<uint32_t>(j * G_::NCH + c) * p.box_slot;
+                if (!p.per_head) {
+                    tma_load_3d(kst + off, km, fb, c * G_::W, row, kvh0);
+                    tma_load_3d(vst + off, vm, fb, c * G_::W, row, kvh0);
+                } else {
+                    for (int w = 0; w < p.kvh_cta; ++w) {
+                        const uint32_t ho = off + static_cast<uint32_t>(w) * p.head_stride;
+                        tma_load_3d(kst + ho, km, fb, c * G_::W, kvh0 + w, row);
+                        tma_load_3d(vst + ho, vm, fb, c * G_::W, kvh0 + w, row);
                     }
                 }
             }
-            __syncwarp();
         }
-        return;
     }
-    if (warp >= p.kvh_cta) return;
+}
 
-    // ---------------------------------------------------------------- consumer warp: one kv head
-    const int gid = lane >> 2;  // MMA group id: token row (scores) / head column (P^T) / dim row (O^T)
-    const int c4 = lane & 3;
-    const int kvh_global = grp * p.kvh_cta + warp;
-
-    // Query fragments (B operand of the score MMA): head nt*8+gid, dims ks*16 + 2*c4 (+1, +8, +9).
+// ---------------------------------------------------------------- consumer: one warp, one kv head
+template <int D, int NT, class KV>
+struct Consumer {
+    using G_ = Geo<D>;
+    using Tr = F16Traits<KV>;
+    static constexpr int KS = G_::KS;
+    uint32_t k_row_off, v_row_off, k_x, v_x;
+    int k_doff, v_doff;
     uint32_t qhi[NT][KS][2], qlo[NT][KS][2];
-    const int kv_dt = std::is_same<KV, __half>::value ? KVP_DTYPE_F16 : KVP_DTYPE_BF16;
-    const bool use_qlo = p.q_dtype != kv_dt;
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-        const int j = nt * 8 + gid;
-        const bool live = j < p.g;
-        const size_t qbase = (static_cast<size_t>(seq) * p.nh + kvh_global * p.g + (live ? j : 0)) * D;
-#pragma unroll
-        for (int ks = 0; ks < KS; ++ks) {
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int d = ks * 16 + 2 * c4 + h * 8;
-                const float x0 = live ? load_any(p.q, qbase + d, p.q_dtype) : 0.f;
-                const float x1 = live ? load_any(p.q, qbase + d + 1, p.q_dtype) : 0.f;
-                const uint32_t hi = Tr::pack(x0, x1);
-                qhi[nt][ks][h] = hi;
-                qlo[nt][ks][h] = Tr::pack(x0 - Tr::unpack_lo(hi), x1 - Tr::unpack_hi(hi));
-            }
-        }
-    }
+    float o[NT][KS][4];
+    float m_run[NT][2], l_run[NT][2];
 
     // Per-lane shared-memory geometry.  For ldmatrix matrix index jm = lane >> 3 and row rr = lane & 7:
     //   score operand (K, non-transposed): token (jm & 1) * 8 + rr, dim offset (jm >> 1) * 8
     //   PV operand    (V, transposed):     token (jm >> 1) * 8 + rr, dim offset (jm & 1) * 8
-    const int jm = lane >> 3, rr = lane & 7;
-    uint32_t k_row_off, v_row_off, k_x, v_x;
-    int k_doff, v_doff;
-    {
+    __device__ __forceinline__ void init_geometry(const AttnParams& p, int warp, int lane) {
+        const int jm = lane >> 3, rr = lane & 7;
         const int tk = (jm & 1) * 8 + rr;
         const int tv = (jm >> 1) * 8 + rr;
         const uint32_t hoff = static_cast<uint32_t>(warp) * p.head_stride;
-        const uint32_t ko = static_cast<uint32_t>(tk / p.R) * NCH * p.box_slot + hoff +
-                            static_cast<uint32_t>(tk % p.R) * ROWB;
-        const uint32_t vo = static_cast<uint32_t>(tv / p.R) * NCH * p.box_slot + hoff +
-                            static_cast<uint32_t>(tv % p.R) * ROWB;
-        k_row_off = ko;
-        v_row_off = vo;
-        k_x = (ko >> 7) & SWM;  // swizzle phase of this row (box slots are 1024-byte aligned)
-        v_x = (vo >> 7) & SWM;
+        k_row_off = static_cast<uint32_t>(tk / p.R) * G_::NCH * p.box_slot + hoff + static_cast<uint32_t>(tk % p.R) * G_::ROWB;
+        v_row_off = static_cast<uint32_t>(tv / p.R) * G_::NCH * p.box_slot + hoff + static_cast<uint32_t>(tv % p.R) * G_::ROWB;
+        k_x = (k_row_off >> 7) & G_::SWM;  // swizzle phase of this row (box slots are 1024-byte aligned)
+        v_x = (v_row_off >> 7) & G_::SWM;
         k_doff = (jm >> 1) * 8;
         v_doff = (jm & 1) * 8;
     }
 
-    float o[NT][KS][4];
-    float m_run[NT][2], l_run[NT][2];
+    __device__ __forceinline__ void reset() {
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-        m_run[nt][0] = m_run[nt][1] = -INFINITY;
-        l_run[nt][0] = l_run[nt][1] = 0.f;
+        for (int nt = 0; nt < NT; ++nt) {
+            m_run[nt][0] = m_run[nt][1] = -INFINITY;
+            l_run[nt][0] = l_run[nt][1] = 0.f;
 #pragma unroll
-        for (int ks = 0; ks < KS; ++ks) o[nt][ks][0] = o[nt][ks][1] = o[nt][ks][2] = o[nt][ks][3] = 0.f;
+            for (int ks = 0; ks < KS; ++ks) o[nt][ks][0] = o[nt][ks][1] = o[nt][ks][2] = o[nt][ks][3] = 0.f;
+        }
     }
 
-    bool aborted = false;
-    for (int i = 0; i < n; ++i) {
-        const int s = i % S;
-        if (!mbar_wait(smem_u32(&full_bar[s]), static_cast<uint32_t>((i / S) & 1))) {
-            if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
-            aborted = true;
-            break;
-        }
-        const uint32_t kst = smem_base + static_cast<uint32_t>(s) * 2u * p.stage_half;
-        const uint32_t vst = kst + p.stage_half;
-        const int tb = (t0 + i) * 16;
-        const int valid = min(16, len - tb);
+    __device__ __forceinline__ void set_q(int nt, int ks, int h, float x0, float x1) {
+        const uint32_t hi = Tr::pack(x0, x1);
+        qhi[nt][ks][h] = hi;
+        qlo[nt][ks][h] = Tr::pack(x0 - Tr::unpack_lo(hi), x1 - Tr::unpack_hi(hi));
+    }
 
-        // ---- scores S^T = K . Q^T
+    // Query fragments (B operand of the score MMA): head nt*8+gid, dims ks*16 + 2*c4 (+1, +8, +9), read from
+    // global memory.
+    __device__ __forceinline__ void load_q_global(const AttnParams& p, int seq, int kvh_global, int lane) {
+        const int gid = lane >> 2, c4 = lane & 3;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const int j = nt * 8 + gid;
+            const bool live = j < p.g;
+            const size_t qbase = (static_cast<size_t>(seq) * p.nh + kvh_global * p.g + (live ? j : 0)) * D;
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int d = ks * 16 + 2 * c4 + h * 8;
+                    set_q(nt, ks, h, live ? load_any(p.q, qbase + d, p.q_dtype) : 0.f,
+                          live ? load_any(p.q, qbase + d + 1, p.q_dtype) : 0.f);
+                }
+        }
+    }
+
+    // Same from the query area of a stage: [kvh_cta * g heads][D] in the query dtype.
+    __device__ __forceinline__ void load_q_smem(const AttnParams& p, uint32_t qsm, int warp, int lane) {
+        const int gid = lane >> 2, c4 = lane & 3;
+        const uint32_t esz = p.q_dtype == KVP_DTYPE_F32 ? 4u : 2u;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const int j = nt * 8 + gid;
+            const bool live = j < p.g;
+            const uint32_t row = qsm + static_cast<uint32_t>((warp * p.g + (live ? j : 0)) * D) * esz;
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const uint32_t a = row + static_cast<uint32_t>(ks * 16 + 2 * c4 + h * 8) * esz;
+                    float x0 = 0.f, x1 = 0.f;
+                    if (live) {
+                        if (p.q_dtype == KVP_DTYPE_F32) {
+                            asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(x0), "=f"(x1) : "r"(a));
+                        } else {
+                            uint32_t v;
+                            asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+                            if (p.q_dtype == KVP_DTYPE_F16) {
+                                x0 = F16Traits<__half>::unpack_lo(v);
+                                x1 = F16Traits<__half>::unpack_hi(v);
+                            } else {
+                                x0 = F16Traits<__nv_bfloat16>::unpack_lo(v);
+                                x1 = F16Traits<__nv_bfloat16>::unpack_hi(v);
+                            }
+                        }
+                    }
+                    set_q(nt, ks, h, x0, x1);
+                }
+        }
+    }
+
+    // One 16-token tile: `valid` rows hold context tokens.
+    __device__ __forceinline__ void tile(const AttnParams& p, uint32_t kst, uint32_t vst, int valid, int warp,
+                                         int lane, bool use_qlo) {
+        const int gid = lane >> 2;
         float sacc[NT][4];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
+        // ---- scores S^T = K . Q^T
 #pragma unroll
         for (int ks = 0; ks < KS; ++ks) {
             const int d = ks * 16 + k_doff;
-            const uint32_t addr = kst + k_row_off + static_cast<uint32_t>(d / W) * p.box_slot +
-                                  ((static_cast<uint32_t>((d % W) >> 3) ^ k_x) << 4);
+            const uint32_t addr = kst + k_row_off + static_cast<uint32_t>(d / G_::W) * p.box_slot +
+                                  ((static_cast<uint32_t>((d % G_::W) >> 3) ^ k_x) << 4);
             uint32_t a[4];
             ldsm_x4(addr, a);
 #pragma unroll
@@ -261,7 +246,6 @@ __global__ void __launch_bounds__((kMaxKvhPerCta + 1) * 32, 1)
                 if (use_qlo) mma16816<KV>(sacc[nt], a, qlo[nt][ks][0], qlo[nt][ks][1]);
             }
         }
-
         // ---- online softmax (log2 domain); rows gid / gid+8 are tokens, columns 2*c4, 2*c4+1 heads
         uint32_t pb_hi[NT][2], pb_lo[NT][2];
         const bool row0_ok = gid < valid, row1_ok = gid + 8 < valid;
@@ -301,30 +285,29 @@ __global__ void __launch_bounds__((kMaxKvhPerCta + 1) * 32, 1)
             pb_lo[nt][0] = movmatrix_trans(l01);
             pb_lo[nt][1] = movmatrix_trans(l23);
         }
-
         // ---- rows past the end of the context: zero this head's V rows so stale bytes cannot turn
         // 0 * garbage into NaN in the PV product.
         if (valid < 16) {
-            const int units = (16 - valid) * NCH * (W / 8);
+            constexpr int UPR = G_::NCH * (G_::W / 8);  // 16-byte units per token row of one head
+            const int units = (16 - valid) * UPR;
             for (int u = lane; u < units; u += 32) {
-                const int t = valid + u / (NCH * (W / 8));
-                const int rem = u % (NCH * (W / 8));
-                const int c = rem / (W / 8), cu = rem % (W / 8);
-                const uint32_t ro = static_cast<uint32_t>(t / p.R) * NCH * p.box_slot +
+                const int t = valid + u / UPR;
+                const int rem = u % UPR;
+                const int c = rem / (G_::W / 8), cu = rem % (G_::W / 8);
+                const uint32_t ro = static_cast<uint32_t>(t / p.R) * G_::NCH * p.box_slot +
                                     static_cast<uint32_t>(c) * p.box_slot + static_cast<uint32_t>(warp) * p.head_stride +
-                                    static_cast<uint32_t>(t % p.R) * ROWB;
-                const uint32_t a = vst + ro + ((static_cast<uint32_t>(cu) ^ ((ro >> 7) & SWM)) << 4);
+                                    static_cast<uint32_t>(t % p.R) * G_::ROWB;
+                const uint32_t a = vst + ro + ((static_cast<uint32_t>(cu) ^ ((ro >> 7) & G_::SWM)) << 4);
                 asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0u) : "memory");
             }
             __syncwarp();
         }
-
         // ---- O^T += V^T . P^T
 #pragma unroll
         for (int mt = 0; mt < KS; ++mt) {
             const int d = mt * 16 + v_doff;
-            const uint32_t addr = vst + v_row_off + static_cast<uint32_t>(d / W) * p.box_slot +
-                                  ((static_cast<uint32_t>((d % W) >> 3) ^ v_x) << 4);
+            const uint32_t addr = vst + v_row_off + static_cast<uint32_t>(d / G_::W) * p.box_slot +
+                                  ((static_cast<uint32_t>((d % G_::W) >> 3) ^ v_x) << 4);
             uint32_t a[4];
             ldsm_x4_trans(addr, a);
 #pragma unroll
@@ -334,95 +317,382 @@ __global__ void __launch_bounds__((kMaxKvhPerCta + 1) * 32, 1)
             }
         }
         if (valid < 16) fence_proxy_async_smem();  // generic writes above precede the next TMA into this stage
+    }
+
+    // Segment epilogue: the final normalised output (`single`) or a partial row `part_row` (nh heads).
+    __device__ __forceinline__ void finish(const AttnParams& p, int lane, int seq, int kvh_global, bool single,
+                                           size_t part_row) {
+        const int gid = lane >> 2, c4 = lane & 3;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                float l = l_run[nt][e];
+#pragma unroll
+                for (int off = 4; off < 32; off <<= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+                l_run[nt][e] = l;
+            }
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int j = nt * 8 + 2 * c4 + e;
+                if (j >= p.g) continue;
+                const int hq = kvh_global * p.g + j;
+                if (single) {
+                    const float inv = 1.f / l_run[nt][e];
+                    const size_t ob = (static_cast<size_t>(seq) * p.nh + hq) * D;
+#pragma unroll
+                    for (int mt = 0; mt < KS; ++mt) {
+                        store_any(p.out, ob + mt * 16 + gid, p.out_dtype, o[nt][mt][e] * inv);
+                        store_any(p.out, ob + mt * 16 + gid + 8, p.out_dtype, o[nt][mt][2 + e] * inv);
+                    }
+                } else {
+                    float* wo = p.ws_o + (part_row + hq) * D;
+#pragma unroll
+                    for (int mt = 0; mt < KS; ++mt) {
+                        wo[mt * 16 + gid] = o[nt][mt][e];
+                        wo[mt * 16 + gid + 8] = o[nt][mt][2 + e];
+                    }
+                    if (gid == 0) p.ws_ml[part_row + hq] = make_float2(m_run[nt][e], l_run[nt][e]);
+                }
+            }
+    }
+};
+
+template <class KV>
+__device__ __forceinline__ bool q_needs_residual(const AttnParams& p) {
+    const int kv_dt = std::is_same<KV, __half>::value ? KVP_DTYPE_F16 : KVP_DTYPE_BF16;
+    return p.q_dtype != kv_dt;
+}
+
+__device__ __forceinline__ void init_barriers(const AttnParams& p, uint64_t* full_bar, uint64_t* empty_bar) {
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < p.stages; ++s) {
+            mbar_init(smem_u32(&full_bar[s]), 1);
+            mbar_init(smem_u32(&empty_bar[s]), static_cast<uint32_t>(p.kvh_cta));
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+}
+
+// ---------------------------------------------------------------- fixed-split schedule
+template <int D, int NT, class KV>
+__global__ void __launch_bounds__((kMaxKvhPerCta + 1) * 32, 1)
+    paged_decode_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                        const AttnParams p) {
+    __shared__ __align__(8) uint64_t full_bar[kMaxStages];
+    __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
+    extern __shared__ uint8_t dyn_smem[];
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int seq = blockIdx.x / p.groups;
+    const int grp = blockIdx.x - seq * p.groups;
+    const int split = blockIdx.y;
+
+    const int len = p.lens[seq];
+    const int ntiles = tiles_of_len(p, len);
+    const int nsplit = (ntiles + p.split_tiles - 1) / p.split_tiles;
+    if (ntiles == 0) {
+        // Invalid length: report once and write zeros so the output is deterministic.
+        if (split == 0) {
+            if (threadIdx.x == 0) report(p.status, KVP_STATUS_BAD_LEN);
+            const int heads = p.kvh_cta * p.g;
+            for (int i = threadIdx.x; i < heads * D; i += blockDim.x) {
+                const int hq = grp * heads + i / D;
+                store_any(p.out, (static_cast<size_t>(seq) * p.nh + hq) * D + i % D, p.out_dtype, 0.f);
+            }
+        }
+        return;
+    }
+    if (split >= nsplit) return;
+    const int t0 = split * p.split_tiles;
+    const int n = min(ntiles - t0, p.split_tiles);
+    const uint32_t smem_base = (smem_u32(dyn_smem) + 1023u) & ~1023u;
+    const int S = p.stages;
+    init_barriers(p, full_bar, empty_bar);
+
+    if (warp == p.kvh_cta) {
+        if (lane == 0) {
+            prefetch_tensormap(&kmap);
+            prefetch_tensormap(&vmap);
+        }
+        const int32_t* trow = p.tables + static_cast<size_t>(seq) * p.max_blocks;
+        int cache_lo = -(1 << 30);
+        int32_t cached = 0;
+        for (int i = 0; i < n; ++i) {
+            const int s = i % S;
+            if (i >= S && !mbar_wait(smem_u32(&empty_bar[s]), static_cast<uint32_t>((i / S - 1) & 1))) {
+                if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
+                break;
+            }
+            const uint32_t kst = smem_base + static_cast<uint32_t>(s) * p.stage_bytes;
+            produce_tile<D>(p, &kmap, &vmap, kst, kst + p.stage_half, smem_u32(&full_bar[s]), (t0 + i) * 16, len,
+                            trow, grp * p.kvh_cta, lane, cache_lo, cached, 0u);
+            __syncwarp();
+        }
+        return;
+    }
+    if (warp >= p.kvh_cta) return;
+
+    Consumer<D, NT, KV> cs;
+    const int kvh_global = grp * p.kvh_cta + warp;
+    cs.init_geometry(p, warp, lane);
+    cs.load_q_global(p, seq, kvh_global, lane);
+    cs.reset();
+    const bool use_qlo = q_needs_residual<KV>(p);
+    for (int i = 0; i < n; ++i) {
+        const int s = i % S;
+        if (!mbar_wait(smem_u32(&full_bar[s]), static_cast<uint32_t>((i / S) & 1))) {
+            if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
+            return;
+        }
+        const uint32_t kst = smem_base + static_cast<uint32_t>(s) * p.stage_bytes;
+        cs.tile(p, kst, kst + p.stage_half, min(16, len - (t0 + i) * 16), warp, lane, use_qlo);
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&empty_bar[s]));
     }
-    if (aborted) return;
+    cs.finish(p, lane, seq, kvh_global, nsplit == 1, (static_cast<size_t>(seq) * p.max_splits + split) * p.nh);
+}
 
-    // ---------------------------------------------------------------- epilogue
+// ---------------------------------------------------------------- stream-K schedule
+// CTA c of G owns tiles [c*T/G, (c+1)*T/G) of the concatenation of all sequences' tiles (T in total).
+__device__ __forceinline__ long long cta_begin(long long c, long long T, int G) { return c * T / G; }
+
+// Tile prefix sums P[0..ns] of all sequences into shared memory (invalid lengths count 0 tiles).
+__device__ __forceinline__ void build_prefix(const AttnParams& p, int32_t* P, int32_t* warp_tot) {
+    const int ns = p.num_seqs, nthr = blockDim.x, tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31, nwarps = (nthr + 31) >> 5;
+    const int per = (ns + nthr - 1) / nthr;
+    const int b = min(tid * per, ns), e = min(b + per, ns);
+    int local = 0;
+    for (int i = b; i < e; ++i) local += tiles_of_len(p, __ldg(p.lens + i));
+    int x = local;
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-            float l = l_run[nt][e];
-#pragma unroll
-            for (int off = 4; off < 32; off <<= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-            l_run[nt][e] = l;
-        }
+    for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, off);
+        if (lane >= off) x += y;
     }
-    const bool single = nsplit == 1;
-    const size_t part_row = (static_cast<size_t>(seq) * p.max_splits + split) * p.nh;
+    if (lane == 31) warp_tot[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int v = lane < nwarps ? warp_tot[lane] : 0;
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-            const int j = nt * 8 + 2 * c4 + e;
-            if (j >= p.g) continue;
-            const int hq = kvh_global * p.g + j;
-            if (single) {
-                const float inv = 1.f / l_run[nt][e];
-                const size_t ob = (static_cast<size_t>(seq) * p.nh + hq) * D;
-#pragma unroll
-                for (int mt = 0; mt < KS; ++mt) {
-                    store_any(p.out, ob + mt * 16 + gid, p.out_dtype, o[nt][mt][e] * inv);
-                    store_any(p.out, ob + mt * 16 + gid + 8, p.out_dtype, o[nt][mt][2 + e] * inv);
-                }
-            } else {
-                float* wo = p.ws_o + (part_row + hq) * D;
-#pragma unroll
-                for (int mt = 0; mt < KS; ++mt) {
-                    wo[mt * 16 + gid] = o[nt][mt][e];
-                    wo[mt * 16 + gid + 8] = o[nt][mt][2 + e];
-                }
-                if (gid == 0) p.ws_ml[part_row + hq] = make_float2(m_run[nt][e], l_run[nt][e]);
-            }
+        for (int off = 1; off < 32; off <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, v, off);
+            if (lane >= off) v += y;
         }
+        if (lane < nwarps) warp_tot[lane] = v;
+    }
+    __syncthreads();
+    int run = (warp > 0 ? warp_tot[warp - 1] : 0) + (x - local);
+    for (int i = b; i < e; ++i) {
+        P[i] = run;
+        run += tiles_of_len(p, __ldg(p.lens + i));
+    }
+    if (tid == nthr - 1) P[ns] = warp_tot[nwarps - 1];
+    __syncthreads();
+}
+
+// First sequence whose tile range ends after tile t (P[s+1] > t).
+__device__ __forceinline__ int seq_of_tile(const int32_t* P, int ns, long long t) {
+    int lo = 0, hi = ns - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (P[mid + 1] > t) hi = mid; else lo = mid + 1;
+    }
+    return lo;
+}
+
+template <int D, int NT, class KV>
+__global__ void __launch_bounds__((kMaxKvhPerCta + 1) * 32, 1)
+    paged_decode_streamk_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                                const AttnParams p) {
+    __shared__ __align__(8) uint64_t full_bar[kMaxStages];
+    __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
+    __shared__ int32_t warp_tot[32];
+    extern __shared__ uint8_t dyn_smem[];
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int c = blockIdx.x, grp = blockIdx.y;
+    const uint32_t base_off = ((smem_u32(dyn_smem) + 1023u) & ~1023u) - smem_u32(dyn_smem);
+    const uint32_t smem_base = smem_u32(dyn_smem) + base_off;
+    int32_t* P = reinterpret_cast<int32_t*>(dyn_smem + base_off + p.pre_off);
+    build_prefix(p, P, warp_tot);
+    const int ns = p.num_seqs;
+    const long long T = P[ns];
+    if (c == 0 && grp == 0)
+        for (int i = threadIdx.x; i <= ns; i += blockDim.x) p.prefix[i] = P[i];
+    // With fewer tiles than CTAs only the first T CTAs work, so every working CTA owns >= 1 tile.
+    const int Ge = static_cast<int>(min(static_cast<long long>(p.G), T));
+    if (c >= Ge) return;
+    const long long b0 = cta_begin(c, T, Ge), b1 = cta_begin(c + 1, T, Ge);
+    const int s_first = seq_of_tile(P, ns, b0);
+    const int S = p.stages;
+    init_barriers(p, full_bar, empty_bar);
+    const uint32_t q_bytes = static_cast<uint32_t>(p.kvh_cta * p.g * D) * (p.q_dtype == KVP_DTYPE_F32 ? 4u : 2u);
+
+    if (warp == p.kvh_cta) {
+        // ------------------------------------------------------------ producer warp
+        if (lane == 0) {
+            prefetch_tensormap(&kmap);
+            prefetch_tensormap(&vmap);
+        }
+        const int kvh0 = grp * p.kvh_cta;
+        int i = 0;  // tile counter of this CTA (stage = i % S)
+        int s = s_first;
+        for (long long t = b0; t < b1;) {
+            while (P[s + 1] <= t) ++s;
+            const long long seg_end = min(b1, static_cast<long long>(P[s + 1]));
+            const int len = __ldg(p.lens + s);
+            const int32_t* trow = p.tables + static_cast<size_t>(s) * p.max_blocks;
+            int cache_lo = -(1 << 30);
+            int32_t cached = 0;
+            for (long long u = t; u < seg_end; ++u, ++i) {
+                const int st = i % S;
+                if (i >= S && !mbar_wait(smem_u32(&empty_bar[st]), static_cast<uint32_t>((i / S - 1) & 1))) {
+                    if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
+                    return;
+                }
+                const uint32_t kst = smem_base + static_cast<uint32_t>(st) * p.stage_bytes;
+                const uint32_t fb = smem_u32(&full_bar[st]);
+                const bool first = (u == t) && p.q_area != 0;
+                produce_tile<D>(p, &kmap, &vmap, kst, kst + p.stage_half, fb, static_cast<int>(u - P[s]) * 16, len,
+                                trow, kvh0, lane, cache_lo, cached, first ? q_bytes : 0u);
+                if (first && lane == 0) {
+                    const char* src = static_cast<const char*>(p.q) +
+                                      (static_cast<size_t>(s) * p.nh + static_cast<size_t>(kvh0) * p.g) * D *
+                                          (p.q_dtype == KVP_DTYPE_F32 ? 4 : 2);
+                    bulk_load(kst + 2u * p.stage_half, src, q_bytes, fb);
+                }
+                __syncwarp();
+            }
+            t = seg_end;
+        }
+        return;
+    }
+    if (warp >= p.kvh_cta) return;
+
+    // ---------------------------------------------------------------- consumer warps
+    Consumer<D, NT, KV> cs;
+    const int kvh_global = grp * p.kvh_cta + warp;
+    cs.init_geometry(p, warp, lane);
+    const bool use_qlo = q_needs_residual<KV>(p);
+    int i = 0;
+    int s = s_first;
+    for (long long t = b0; t < b1;) {
+        while (P[s + 1] <= t) ++s;
+        const long long seg_end = min(b1, static_cast<long long>(P[s + 1]));
+        const int len = __ldg(p.lens + s);
+        if (p.q_area == 0) cs.load_q_global(p, s, kvh_global, lane);
+        cs.reset();
+        for (long long u = t; u < seg_end; ++u, ++i) {
+            const int st = i % S;
+            if (!mbar_wait(smem_u32(&full_bar[st]), static_cast<uint32_t>((i / S) & 1))) {
+                if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
+                return;
+            }
+            const uint32_t kst = smem_base + static_cast<uint32_t>(st) * p.stage_bytes;
+            if (u == t && p.q_area != 0) cs.load_q_smem(p, kst + 2u * p.stage_half, warp, lane);
+            cs.tile(p, kst, kst + p.stage_half, min(16, len - static_cast<int>(u - P[s]) * 16), warp, lane, use_qlo);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&empty_bar[st]));
+        }
+        const bool single = (t == P[s]) && (seg_end == P[s + 1]);
+        cs.finish(p, lane, s, kvh_global, single, static_cast<size_t>(c + s) * p.nh);
+        t = seg_end;
     }
 }
 
-// Combines the split partials of every (sequence, head) whose context was split: one warp each.
+// ---------------------------------------------------------------- merges
+// Combines `n` partial rows of one (sequence, head) -- rows row0 + k * stride -- into the output: one warp.
+// Lane k owns partial k's weight; the output loop's loads are independent, so they overlap.
+template <int D>
+__device__ __forceinline__ void merge_rows(const AttnParams& p, size_t row0, size_t stride, int n, size_t out_off,
+                                           int lane) {
+    float M = -INFINITY;
+    for (int k = lane; k < n; k += 32) M = fmaxf(M, p.ws_ml[row0 + k * stride].x);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    float L = 0.f;
+    for (int k = lane; k < n; k += 32) {
+        const float2 ml = p.ws_ml[row0 + k * stride];
+        L += ml.y * fast_exp2(ml.x - M);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+    const float invL = 1.f / L;
+    constexpr int PER = (D + 31) / 32;
+    float acc[PER];
+#pragma unroll
+    for (int q = 0; q < PER; ++q) acc[q] = 0.f;
+    for (int k0 = 0; k0 < n; k0 += 32) {
+        const int kk = k0 + lane;
+        const float w = kk < n ? fast_exp2(p.ws_ml[row0 + kk * stride].x - M) * invL : 0.f;
+        const int cnt = min(32, n - k0);
+#pragma unroll 4
+        for (int k = 0; k < cnt; ++k) {
+            const float wk = __shfl_sync(0xffffffffu, w, k);
+            const float* src = p.ws_o + (row0 + static_cast<size_t>(k0 + k) * stride) * D;
+#pragma unroll
+            for (int q = 0; q < PER; ++q) {
+                const int d = q * 32 + lane;
+                if (d < D) acc[q] += src[d] * wk;
+            }
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < PER; ++q) {
+        const int d = q * 32 + lane;
+        if (d < D) store_any(p.out, out_off + d, p.out_dtype, acc[q]);
+    }
+}
+
+// Fixed-split schedule: one warp per (sequence, head) whose context was split.
 template <int D>
 __global__ void __launch_bounds__(128) merge_splits_kernel(const AttnParams p) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const long long idx = static_cast<long long>(blockIdx.x) * 4 + warp;
     if (idx >= static_cast<long long>(p.num_seqs) * p.nh) return;
     const int seq = static_cast<int>(idx / p.nh), hq = static_cast<int>(idx % p.nh);
-    int len = 0;
-    const int ntiles = seq_tiles(p, seq, &len);
+    const int ntiles = tiles_of_len(p, p.lens[seq]);
     const int nsplit = (ntiles + p.split_tiles - 1) / p.split_tiles;
     if (nsplit <= 1) return;
-    const size_t row0 = static_cast<size_t>(seq) * p.max_splits * p.nh + hq;  // split stride: nh
-    float M = -INFINITY;
-    for (int i = lane; i < nsplit; i += 32) M = fmaxf(M, p.ws_ml[row0 + static_cast<size_t>(i) * p.nh].x);
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-    float L = 0.f;
-    for (int i = lane; i < nsplit; i += 32) {
-        const float2 ml = p.ws_ml[row0 + static_cast<size_t>(i) * p.nh];
-        L += ml.y * fast_exp2(ml.x - M);
+    merge_rows<D>(p, static_cast<size_t>(seq) * p.max_splits * p.nh + hq, static_cast<size_t>(p.nh), nsplit,
+                  (static_cast<size_t>(seq) * p.nh + hq) * D, lane);
+}
+
+// Stream-K schedule: one warp per (sequence, head).  Sequence s's segments are the CTAs c that own its first
+// to its last tile (every working CTA owns at least one tile); their partial rows are (c + s) * nh + head.
+// Invalid lengths get zeros here.
+template <int D>
+__global__ void __launch_bounds__(128) merge_streamk_kernel(const AttnParams p) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long idx = static_cast<long long>(blockIdx.x) * 4 + warp;
+    if (idx >= static_cast<long long>(p.num_seqs) * p.nh) return;
+    const int seq = static_cast<int>(idx / p.nh), hq = static_cast<int>(idx % p.nh);
+    const size_t out_off = (static_cast<size_t>(seq) * p.nh + hq) * D;
+    if (tiles_of_len(p, p.lens[seq]) == 0) {
+        if (hq == 0 && lane == 0) report(p.status, KVP_STATUS_BAD_LEN);
+        for (int d = lane; d < D; d += 32) store_any(p.out, out_off + d, p.out_dtype, 0.f);
+        return;
     }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-    const float invL = 1.f / L;
-    float acc[(D + 31) / 32];
-#pragma unroll
-    for (int k = 0; k < (D + 31) / 32; ++k) acc[k] = 0.f;
-    for (int i = 0; i < nsplit; ++i) {
-        const size_t r = row0 + static_cast<size_t>(i) * p.nh;
-        const float w = fast_exp2(p.ws_ml[r].x - M);
-        const float* src = p.ws_o + r * D;
-#pragma unroll
-        for (int k = 0; k < (D + 31) / 32; ++k) {
-            const int d = k * 32 + lane;
-            if (d < D) acc[k] += src[d] * w;
-        }
-    }
-    const size_t ob = (static_cast<size_t>(seq) * p.nh + hq) * D;
-#pragma unroll
-    for (int k = 0; k < (D + 31) / 32; ++k) {
-        const int d = k * 32 + lane;
-        if (d < D) store_any(p.out, ob + d, p.out_dtype, acc[k] * invL);
-    }
+    const long long T = p.prefix[p.num_seqs];
+    const int Ge = static_cast<int>(min(static_cast<long long>(p.G), T));
+    const long long t0 = p.prefix[seq], t1 = p.prefix[seq + 1] - 1;
+    auto owner = [&](long long t) {
+        long long c = t * Ge / T;
+        while (c + 1 < Ge && cta_begin(c + 1, T, Ge) <= t) ++c;
+        while (c > 0 && cta_begin(c, T, Ge) > t) --c;
+        return c;
+    };
+    const long long c0 = owner(t0), c1 = owner(t1);
+    if (c0 == c1) return;  // one CTA covered the whole sequence and wrote the output itself
+    merge_rows<D>(p, static_cast<size_t>(c0 + seq) * p.nh + hq, static_cast<size_t>(p.nh), static_cast<int>(c1 - c0 + 1),
+                  out_off, lane);
 }
 
 }  // namespace kvpd
@@ -441,7 +711,7 @@ int gcd_int(int a, int b) {
     return a;
 }
 size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
-// Dynamic shared memory a CTA may use: the 227 KB opt-in limit less 1 KB for the static mbarriers.
+// Dynamic shared memory a CTA may use: the 227 KB opt-in limit less 1 KB for the static barriers.
 constexpr int kDynSmemCap = (227 << 10) - 1024;
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -519,6 +789,83 @@ int pool_map_mode() {
     return mode;
 }
 
+// ---- kernel instantiations by (kv dtype, head_dim, n-tiles)
+template <int D, int NT, class KV>
+struct Kernels {
+    static const void* decode() { return reinterpret_cast<const void*>(&kvpd::paged_decode_kernel<D, NT, KV>); }
+    static const void* streamk() { return reinterpret_cast<const void*>(&kvpd::paged_decode_streamk_kernel<D, NT, KV>); }
+};
+
+template <class KV, int D>
+const void* pick_d(int NT, bool streamk) {
+    if (NT == 1) return streamk ? Kernels<D, 1, KV>::streamk() : Kernels<D, 1, KV>::decode();
+    if constexpr (D <= 128) return streamk ? Kernels<D, 2, KV>::streamk() : Kernels<D, 2, KV>::decode();
+    return nullptr;
+}
+
+template <class KV>
+const void* pick_kv(int D, int NT, bool streamk) {
+    switch (D) {
+        case 32: return pick_d<KV, 32>(NT, streamk);
+        case 64: return pick_d<KV, 64>(NT, streamk);
+        case 96: return pick_d<KV, 96>(NT, streamk);
+        case 128: return pick_d<KV, 128>(NT, streamk);
+        case 256: return pick_d<KV, 256>(NT, streamk);
+        default: return nullptr;
+    }
+}
+
+const void* pick_kernel(int kv_dtype, int D, int g, bool streamk) {
+    const int NT = g <= 8 ? 1 : 2;
+    return kv_dtype == KVP_DTYPE_F16 ? pick_kv<__half>(D, NT, streamk) : pick_kv<__nv_bfloat16>(D, NT, streamk);
+}
+
+// Opts a kernel into the whole dynamic shared-memory budget, once per device.
+int allow_smem(const void* fn) {
+    static std::mutex mu;
+    static std::vector<std::pair<const void*, int>> done;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    for (const auto& d : done)
+        if (d.first == fn && d.second == dev) return KVP_OK;
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmemCap);
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(attention)");
+    done.emplace_back(fn, dev);
+    return KVP_OK;
+}
+
+// Resident CTAs per SM of the stream-K kernel for this launch shape (occupancy API; shared-memory estimate
+// when no device is present, e.g. for a workspace query on a build machine).
+// Cached per (kernel, threads, smem, device): the occupancy query costs far more than a launch.
+int streamk_ctas_per_sm(const void* fn, int threads, size_t smem) {
+    struct Key {
+        const void* fn;
+        int threads;
+        size_t smem;
+        int dev;
+        int n;
+    };
+    static std::mutex mu;
+    static std::vector<Key> cache;
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) dev = -1;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        for (const auto& k : cache)
+            if (k.fn == fn && k.threads == threads && k.smem == smem && k.dev == dev) return k.n;
+    }
+    int n = 0;
+    if (!(fn && dev >= 0 && allow_smem(fn) == KVP_OK &&
+          cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, threads, smem) == cudaSuccess && n > 0)) {
+        cudaGetLastError();
+        n = std::max(1, static_cast<int>((228u << 10) / (smem + 1024)));
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    cache.push_back(Key{fn, threads, smem, dev, n});
+    return n;
+}
+
 }  // namespace
 
 int plan_attention(const kvp_attn_args& a, bool have_workspace, AttnPlan* out) {
@@ -530,6 +877,7 @@ int plan_attention(const kvp_attn_args& a, bool have_workspace, AttnPlan* out) {
         return fail(KVP_EINVAL, "num_heads % kv_heads != 0");
     const int g = a.num_heads / a.kv_heads;
     if (g > 16) return fail(KVP_EINVAL, "more than 16 query heads per kv head are not supported");
+    if (g > 8 && D > 128) return fail(KVP_EINVAL, "head_dim 256 supports at most 8 query heads per kv head");
     if (a.block_size < 1 || a.max_blocks < 1 || a.num_seqs < 0) return fail(KVP_EINVAL, "bad block_size / max_blocks / num_seqs");
     pl.R = gcd_int(a.block_size, 16);
     pl.nruns = 16 / pl.R;
@@ -555,35 +903,48 @@ int plan_attention(const kvp_attn_args& a, bool have_workspace, AttnPlan* out) {
     }
     pl.box_tx = static_cast<uint32_t>(static_cast<size_t>(kc) * pl.R * rowb);
     pl.stage_half = static_cast<uint32_t>(pl.nruns) * pl.nch * pl.box_slot;
-    const size_t stage = 2ull * pl.stage_half;
+    pl.max_tiles = static_cast<int>((static_cast<long long>(a.max_blocks) * a.block_size + 15) / 16);
+
+    // Schedule: stream-K when splitting is automatic and a workspace is available; otherwise fixed splits.
+    pl.streamk = (a.split_tiles == 0 && have_workspace && a.num_seqs > 0 && a.num_seqs <= kvpd::kMaxStreamSeqs) ? 1 : 0;
+    const size_t qelem = a.q_dtype == KVP_DTYPE_F32 ? 4 : 2;
+    if (pl.streamk && (reinterpret_cast<uintptr_t>(a.q) & 15u) == 0)
+        pl.q_area = static_cast<uint32_t>(round_up(static_cast<size_t>(kc) * g * D * qelem, 1024));
+    pl.stage_bytes = 2u * pl.stage_half + pl.q_area;
+    const size_t stage = pl.stage_bytes;
+    const size_t pre = pl.streamk ? round_up((static_cast<size_t>(a.num_seqs) + 1) * 4, 128) : 0;
     const size_t smem_cap = kDynSmemCap;
     int st = a.stages;
     if (st <= 0) st = static_cast<int>(std::max<size_t>(2, std::min<size_t>(8, (96u << 10) / stage)));
     st = std::min(st, kvpd::kMaxStages);
-    while (st > 2 && stage * st + 1024 > smem_cap) --st;
-    if (stage * st + 1024 > smem_cap) return fail(KVP_EINVAL, "shape needs more shared memory than a CTA has");
+    while (st > 2 && stage * st + pre + 1024 > smem_cap) --st;
+    if (stage * st + pre + 1024 > smem_cap) return fail(KVP_EINVAL, "shape needs more shared memory than a CTA has");
     pl.stages = st;
-    pl.smem = stage * st + 1024;
-    pl.max_tiles = static_cast<int>((static_cast<long long>(a.max_blocks) * a.block_size + 15) / 16);
-    // Context split: tiles per CTA.
-    int split = pl.max_tiles;
-    if (a.split_tiles > 0) {
-        split = std::min(a.split_tiles, pl.max_tiles);
-    } else if (a.split_tiles == 0 && have_workspace) {
-        // Aim for ~8 waves of CTAs assuming sequences average half of max_blocks.
-        const long long est = static_cast<long long>(a.num_seqs) * std::max(1, pl.max_tiles / 2) * pl.groups;
-        const int per_sm = std::max(1, static_cast<int>(smem_cap / pl.smem));
-        const long long target = static_cast<long long>(sm_count()) * per_sm * 8;
-        split = static_cast<int>(std::max<long long>(8, (est + target - 1) / std::max<long long>(1, target)));
-        split = std::min(split, pl.max_tiles);
+    pl.pre_off = static_cast<uint32_t>(stage * st);
+    pl.smem = stage * st + pre + 1024;
+
+    if (pl.streamk) {
+        const void* fn = pick_kernel(a.kv_dtype, D, g, true);
+        pl.G = sm_count() * streamk_ctas_per_sm(fn, (kc + 1) * 32, pl.smem);
+        pl.split_tiles = pl.max_tiles;
+        pl.max_splits = 1;
+        const size_t rows = (static_cast<size_t>(pl.G) + a.num_seqs) * a.num_heads;
+        pl.ws_o_off = round_up(rows * sizeof(float2), 256);
+        pl.ws_pre_off = pl.ws_o_off + round_up(rows * static_cast<size_t>(D) * sizeof(float), 256);
+        pl.ws_bytes = pl.ws_pre_off + round_up((static_cast<size_t>(a.num_seqs) + 1) * 4, 256);
+        *out = pl;
+        return KVP_OK;
     }
+    int split = pl.max_tiles;
+    if (a.split_tiles > 0) split = std::min(a.split_tiles, pl.max_tiles);
     pl.split_tiles = std::max(1, split);
     pl.max_splits = (pl.max_tiles + pl.split_tiles - 1) / pl.split_tiles;
     if (pl.max_splits > 65535) return fail(KVP_EINVAL, "too many context splits; raise split_tiles");
     pl.ws_bytes = 0;
     if (pl.max_splits > 1) {
         const size_t rows = static_cast<size_t>(a.num_seqs) * pl.max_splits * a.num_heads;
-        pl.ws_bytes = round_up(rows * sizeof(float2), 256) + rows * static_cast<size_t>(D) * sizeof(float);
+        pl.ws_o_off = round_up(rows * sizeof(float2), 256);
+        pl.ws_bytes = pl.ws_o_off + rows * static_cast<size_t>(D) * sizeof(float);
     }
     *out = pl;
     return KVP_OK;
@@ -591,33 +952,38 @@ int plan_attention(const kvp_attn_args& a, bool have_workspace, AttnPlan* out) {
 
 namespace {
 
+template <int D>
+int launch_merge(const kvp_attn_args& a, const AttnPlan& pl, const kvpd::AttnParams& prm, cudaStream_t stream) {
+    const long long pairs = static_cast<long long>(a.num_seqs) * a.num_heads;
+    if (pairs == 0) return KVP_OK;
+    const unsigned blocks = static_cast<unsigned>((pairs + 3) / 4);
+    if (pl.streamk)
+        kvpd::merge_streamk_kernel<D><<<blocks, 128, 0, stream>>>(prm);
+    else if (pl.max_splits > 1)
+        kvpd::merge_splits_kernel<D><<<blocks, 128, 0, stream>>>(prm);
+    else
+        return KVP_OK;
+    return cuda_status(cudaGetLastError(), "split merge kernel launch");
+}
+
 template <int D, int NT, class KV>
 int launch_typed(const kvp_attn_args& a, const AttnPlan& pl, const kvpd::AttnParams& prm, const CUtensorMap& km,
                  const CUtensorMap& vm, cudaStream_t stream) {
-    auto kern = kvpd::paged_decode_kernel<D, NT, KV>;
-    static int configured[64] = {0};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64) return fail(KVP_ECUDA, "device index out of range");
-    if (configured[dev] < static_cast<int>(pl.smem)) {
-        // The whole opt-in budget minus the kernel's static barriers.
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmemCap);
-        if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(attention)");
-        configured[dev] = kDynSmemCap;
-    }
+    const void* fn = pl.streamk ? Kernels<D, NT, KV>::streamk() : Kernels<D, NT, KV>::decode();
+    int rc = allow_smem(fn);
+    if (rc != KVP_OK) return rc;
     if (a.num_seqs == 0) return KVP_OK;
-    dim3 grid(static_cast<unsigned>(a.num_seqs * pl.groups), static_cast<unsigned>(pl.max_splits));
     dim3 block(static_cast<unsigned>((pl.kvh_cta + 1) * 32));
-    kern<<<grid, block, pl.smem, stream>>>(km, vm, prm);
+    if (pl.streamk) {
+        dim3 grid(static_cast<unsigned>(pl.G), static_cast<unsigned>(pl.groups));
+        kvpd::paged_decode_streamk_kernel<D, NT, KV><<<grid, block, pl.smem, stream>>>(km, vm, prm);
+    } else {
+        dim3 grid(static_cast<unsigned>(a.num_seqs * pl.groups), static_cast<unsigned>(pl.max_splits));
+        kvpd::paged_decode_kernel<D, NT, KV><<<grid, block, pl.smem, stream>>>(km, vm, prm);
+    }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_status(e, "attention kernel launch");
-    if (pl.max_splits > 1) {
-        const long long pairs = static_cast<long long>(a.num_seqs) * a.num_heads;
-        kvpd::merge_splits_kernel<D><<<static_cast<unsigned>((pairs + 3) / 4), 128, 0, stream>>>(prm);
-        e = cudaGetLastError();
-        if (e != cudaSuccess) return cuda_status(e, "split merge kernel launch");
-    }
-    return KVP_OK;
+    return launch_merge<D>(a, pl, prm, stream);
 }
 
 template <int D, class KV>
@@ -665,7 +1031,7 @@ extern "C" KVP_API int kvp_paged_attention(const kvp_attn_args* a, void* stream)
     AttnPlan pl;
     int rc = plan_attention(*a, a->workspace != nullptr, &pl);
     if (rc != KVP_OK) return rc;
-    if (pl.max_splits > 1) {
+    if (pl.ws_bytes > 0) {
         if (!a->workspace || a->workspace_bytes < pl.ws_bytes)
             return fail(KVP_ENOSPACE, "workspace smaller than kvp_attention_workspace_size()");
         if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0) return fail(KVP_EINVAL, "workspace must be 256-byte aligned");
@@ -691,10 +1057,11 @@ extern "C" KVP_API int kvp_paged_attention(const kvp_attn_args* a, void* stream)
     prm.tables = a->block_tables;
     prm.lens = a->seq_lens;
     prm.out = a->out;
-    if (pl.max_splits > 1) {
-        const size_t rows_ml = static_cast<size_t>(a->num_seqs) * pl.max_splits * a->num_heads;
-        prm.ws_ml = static_cast<float2*>(a->workspace);
-        prm.ws_o = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + ((rows_ml * sizeof(float2) + 255) / 256 * 256));
+    if (pl.ws_bytes > 0) {
+        char* ws = static_cast<char*>(a->workspace);
+        prm.ws_ml = reinterpret_cast<float2*>(ws);
+        prm.ws_o = reinterpret_cast<float*>(ws + pl.ws_o_off);
+        if (pl.streamk) prm.prefix = reinterpret_cast<int32_t*>(ws + pl.ws_pre_off);
     }
     prm.status = a->status;
     prm.num_blocks = a->num_blocks > 0 ? a->num_blocks : 0;
@@ -713,10 +1080,14 @@ extern "C" KVP_API int kvp_paged_attention(const kvp_attn_args* a, void* stream)
     prm.split_tiles = pl.split_tiles;
     prm.max_splits = pl.max_splits;
     prm.per_head = pl.per_head;
+    prm.G = pl.G;
     prm.head_stride = pl.head_stride;
     prm.box_slot = pl.box_slot;
     prm.stage_half = pl.stage_half;
     prm.box_tx = pl.box_tx;
+    prm.stage_bytes = pl.stage_bytes;
+    prm.q_area = pl.q_area;
+    prm.pre_off = pl.pre_off;
     prm.oob_row = static_cast<int>(std::min<long long>(rows, 0x7fffffffLL));
     const float scale = a->scale > 0.f ? a->scale : 1.0f / std::sqrt(static_cast<float>(a->head_dim));
     prm.sl2 = scale * 1.4426950408889634f;

@@ -20,7 +20,7 @@
 
 namespace {
 
-constexpr int kMaxSplitsCap = 64;  // bounds the split-K workspace the decoder reserves per sequence and head
+constexpr int kMaxSplitsCap = 64;  // most fixed splits per sequence the decoder reserves workspace for
 
 size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 int elem(int dt) { return dt == KVP_DTYPE_F32 ? 4 : 2; }
@@ -44,11 +44,21 @@ Layout layout_of(const kvp_decoder_config& c) {
     o = align256(o + sizeof(int32_t));
     L.attn = o;
     if (c.split_tiles >= 0) {
-        const size_t max_tiles =
-            (static_cast<size_t>(c.max_blocks_per_seq) * static_cast<size_t>(c.block_size) + 15) / 16;
-        const size_t splits = std::min<size_t>(kMaxSplitsCap, max_tiles);
-        const size_t rows = ns * splits * static_cast<size_t>(c.num_heads);
-        L.attn_bytes = splits > 1 ? align256(rows * 8) + rows * static_cast<size_t>(c.head_dim) * 4 : 0;
+        // The attention workspace of the largest step: the balanced (stream-K) schedule for split_tiles 0,
+        // otherwise the fixed splits.
+        kvp_attn_args a{};
+        a.q_dtype = c.q_dtype;
+        a.kv_dtype = c.kv_dtype;
+        a.out_dtype = c.out_dtype;
+        a.num_blocks = c.num_blocks;
+        a.num_seqs = c.max_seqs;
+        a.num_heads = c.num_heads;
+        a.kv_heads = c.kv_heads;
+        a.head_dim = c.head_dim;
+        a.block_size = c.block_size;
+        a.max_blocks = c.max_blocks_per_seq;
+        a.split_tiles = c.split_tiles;
+        L.attn_bytes = kvp_attention_workspace_size(&a);
     }
     o = align256(o + L.attn_bytes);
     const size_t per_q = ns * c.num_heads * c.head_dim, per_kv = ns * c.kv_heads * c.head_dim;
@@ -137,19 +147,6 @@ int host_step(kvp_decoder* d, const int64_t* rids, int n) {
     return KVP_OK;
 }
 
-// Context split for this step: ~8 CTA waves over the real tiles, within the reserved workspace.
-int choose_split(const kvp_decoder* d, int n) {
-    const kvp_decoder_config& c = d->cfg;
-    if (c.split_tiles != 0) return c.split_tiles;
-    const int32_t* lens = d->h_meta + static_cast<size_t>(n) * c.max_blocks_per_seq;
-    long long tiles = 0;
-    for (int i = 0; i < n; ++i) tiles += (lens[i] + 15) / 16;
-    const long long max_tiles = (static_cast<long long>(c.max_blocks_per_seq) * c.block_size + 15) / 16;
-    const long long target = static_cast<long long>(kvpi::sm_count()) * 8;
-    long long split = std::max<long long>(8, (tiles + target - 1) / target);
-    split = std::max<long long>(split, (max_tiles + kMaxSplitsCap - 1) / kMaxSplitsCap);
-    return static_cast<int>(std::min<long long>(split, std::max<long long>(1, max_tiles)));
-}
 
 // Copy-on-write launches in order-preserving chunks: a pair whose destination is the source of an earlier
 // pair of the chunk starts a new chunk, so every block is read before it is overwritten.
@@ -214,7 +211,7 @@ int enqueue_device(kvp_decoder* d, int n, const void* q, const void* knew, const
     ap.status = d->d_status();
     rc = kvp_append_scatter(&ap, s_comp);
     if (rc != KVP_OK) return rc;
-    const int split = choose_split(d, n);
+    const int split = c.split_tiles;  // 0: balanced schedule over the step's real context lengths
     const size_t kv_layer_bytes = static_cast<size_t>(d->layer_stride) * 2;
     const size_t q_layer = static_cast<size_t>(n) * c.num_heads * c.head_dim;
     for (int l = 0; l < c.num_layers; ++l) {

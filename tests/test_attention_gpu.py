@@ -267,3 +267,34 @@ def test_empty_batch_is_a_no_op(kvb, cuda):
     t = torch.zeros((0, 1), dtype=torch.int32, device="cuda")
     kvb.paged_attention(z, k, k, t, torch.zeros(0, dtype=torch.int32, device="cuda"), 8, 2, out=z)
     torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("lens", [
+    [1, 2, 3, 1, 16],                       # fewer tiles than persistent CTAs
+    [32768] + [17] * 100,                    # one very long context among many short ones
+    [5000] * 3 + [1] * 300 + [700] * 50,     # many sequences, mixed
+])
+def test_balanced_schedule_edge_cases(kvb, ora, cuda, lens):
+    """The persistent balanced schedule (automatic split): CTA ranges cut through sequences anywhere,
+    sequences entirely inside one CTA are written directly, the rest merged."""
+    nb = sum((n + 15) // 16 for n in lens) + 3
+    Q, K, V, T, L = _normal_case(len(lens), len(lens), 32, 8, 128, 16, lens, nb)
+    got, ref = run_attention(kvb, ora, Q, K, V, T, L, 32, 8, kv="bf16", q="bf16", split_tiles=0)
+    check_close(got, ref, what=f"balanced schedule {len(lens)} sequences")
+
+
+def test_balanced_schedule_unaligned_query(kvb, ora, cuda):
+    """A query buffer that is not 16-byte aligned is read from global memory instead of being bulk-copied."""
+    import torch
+    lens = [300, 45, 1000]
+    Q, K, V, T, L = _normal_case(12, 3, 16, 4, 64, 16, lens, 100)
+    kt, kf = _round(K, "f16")
+    vt, vf = _round(V, "f16")
+    ref = ora.reference_attention(16, 4, 64, 16, Q, kf, vf, T, L)
+    buf = torch.empty(Q.size + 1, dtype=torch.float32, device="cuda")
+    qv = buf[1:].view(Q.shape)  # 4-byte aligned only
+    qv.copy_(torch.from_numpy(Q))
+    o = torch.full(Q.shape, float("nan"), dtype=torch.float32, device="cuda")
+    kvb.paged_attention(qv, kt.cuda(), vt.cuda(), torch.from_numpy(T).cuda(), torch.from_numpy(L).cuda(), 16, 4, out=o)
+    torch.cuda.synchronize()
+    check_close(o.cpu().numpy(), ref, what="unaligned query")

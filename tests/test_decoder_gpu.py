@@ -86,7 +86,7 @@ def test_decoder_output_matches_oracle(kvb, ora, cuda):
 
 def test_decoder_reports_exhaustion(kvb, cuda):
     import torch
-    L, nb, B, kvh, D, nh = 2, 3, 16, 2, 64, 4
+    L, nb, B, kvh, D, nh = 2, 4, 16, 2, 64, 4
     k = torch.zeros((L, nb, B, kvh, D), dtype=torch.bfloat16, device="cuda")
     v = torch.zeros_like(k)
     m = kvb.KVManager(nb, B)
