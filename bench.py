@@ -254,8 +254,8 @@ def run_ours(args, cfg, rank, world, dev):
     # context schedule: 0 = balanced persistent (stream-K) grid; > 0 = fixed splits of that many tiles
     split = args.split
     a0 = kvb.attention_args(q[0], kc[0], vc[0], d_tables, d_lens[0], out[0], nh, kvh, num_blocks=nb,
-                            split_tiles=split)
-    ws = torch.empty(max(kvb.workspace_bytes(a0), 256), dtype=torch.uint8, device=dev)
+                            split_tiles=split, warps_per_kv_head=args.wph, stages=args.stages)
+    ws = torch.zeros(max(kvb.workspace_bytes(a0), 256), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
     # Launch arguments are built once; a step only repoints the slots / lengths (so the timed loop measures
@@ -265,8 +265,9 @@ def run_ours(args, cfg, rank, world, dev):
     attn_args = []
     for l in range(L):
         a = kvb.attention_args(q[l], kc[l], vc[l], d_tables, d_lens[0], out[l], nh, kvh, num_blocks=nb,
-                               split_tiles=split, status=status)
+                               split_tiles=split, status=status, warps_per_kv_head=args.wph, stages=args.stages)
         a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+        a.flags = kvb.KVP_ATTN_WORKSPACE_CLEAN  # zero-filled once; every call leaves the counters zero
         attn_args.append(a)
     app = kvb.AppendArgs()
     app.k_new, app.v_new, app.k_cache, app.v_cache = knew.data_ptr(), vnew.data_ptr(), kc.data_ptr(), vc.data_ptr()
@@ -309,6 +310,16 @@ def run_ours(args, cfg, rank, world, dev):
     # algorithmic bytes per attention launch: unique K/V bytes of every context, averaged over the steps
     elem = 2
     bytes_per_launch = float(lens_all[W:].astype(np.float64).sum(axis=1).mean()) * kvh * D * 2 * elem
+
+    if args.no_e2e:
+        vals = torch.tensor([ms_total, ms_total, float(np.mean(attn_ms))], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+        ms_total, e2e_ms, attn_avg = [float(x) for x in vals.cpu()]
+        gpu_launches = K * (1 + L * 2)
+        return dict(ms_total=ms_total, e2e_ms=e2e_ms, attn_avg_ms=attn_avg, bytes_per_launch=bytes_per_launch,
+                    clocks=clk.summary(), ns=ns, nb=nb, split=split, gpu_launches=gpu_launches, h2d=0, d2h=0,
+                    lens_mean=float(lens.mean())), lens
 
     # ---------------------------------------------------------------- e2e through the C ABI, host buffers
     # One kvp_decoder_step per decode step: host KVManager appends, metadata upload, new K/V and per-layer
@@ -362,6 +373,9 @@ def main():
     ap.add_argument("--config", default=DEFAULT, choices=sorted(CONFIGS))
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--split", type=int, default=0, help="tiles per context split (0: balanced persistent grid)")
+    ap.add_argument("--wph", type=int, default=0, help="tuning: consumer warps per kv head (0: automatic)")
+    ap.add_argument("--stages", type=int, default=0, help="tuning: pipeline stages (0: automatic)")
+    ap.add_argument("--no-e2e", action="store_true", help="tuning runs: skip the end-to-end leg")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--requests", type=int, default=0, help="profiling: requests per GPU (pool sized to need)")
     ap.add_argument("--layers", type=int, default=0, help="profiling: number of layers (pool sized to need)")

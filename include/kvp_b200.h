@@ -81,9 +81,19 @@ typedef struct kvp_attn_args {
     void* workspace;          /* split-K partials; kvp_attention_workspace_size() bytes, 256-B aligned */
     size_t workspace_bytes;
     int32_t* status; /* optional device word for KVP_STATUS_* bits */
+    int32_t warps_per_kv_head; /* tuning, 0: automatic (consumer warps sharing one kv head's tiles) */
+    int32_t flags;             /* KVP_ATTN_* bits */
 } kvp_attn_args;
 
-/* Bytes of workspace kvp_paged_attention needs for these arguments (0 when no context is split). */
+/* The caller guarantees the workspace's counter words are zero, so the call skips resetting them: true for
+ * workspace memory that was zero-filled once and has since only been used by completed calls (each call
+ * leaves the counters zero).  Without it every balanced-schedule call first clears them on the stream. */
+#define KVP_ATTN_WORKSPACE_CLEAN 1
+
+/* Bytes of workspace kvp_paged_attention needs for these arguments (0 when no context is split).  With
+ * split_tiles == 0 and a workspace the balanced persistent schedule is used: the step's tiles are divided
+ * evenly between as many CTAs as fit on the GPU, and contexts split between CTAs are merged in the same
+ * kernel. */
 KVP_API size_t kvp_attention_workspace_size(const kvp_attn_args* a);
 KVP_API int kvp_paged_attention(const kvp_attn_args* a, void* stream);
 

@@ -22,6 +22,7 @@ LIB_PATH = os.path.join(_HERE, "libkvpage_b200.so")
 
 KVP_OK, KVP_EINVAL, KVP_ECUDA, KVP_EBOUNDS, KVP_ENOSPACE, KVP_ESTATE = 0, 1, 2, 3, 4, 5
 KVP_STATUS_BAD_BLOCK, KVP_STATUS_BAD_LEN, KVP_STATUS_TIMEOUT = 1, 2, 4
+KVP_ATTN_WORKSPACE_CLEAN = 1
 F32, F16, BF16 = 0, 1, 2
 NO_REQUEST = -1
 STATS_FIELDS = ("requests", "used_tokens", "allocated_blocks", "allocated_slots", "internal_waste",
@@ -37,7 +38,7 @@ class AttnArgs(C.Structure):
                 ("num_seqs", _i32), ("num_heads", _i32), ("kv_heads", _i32), ("head_dim", _i32),
                 ("block_size", _i32), ("max_blocks", _i32), ("scale", _f32), ("split_tiles", _i32),
                 ("kv_heads_per_cta", _i32), ("stages", _i32), ("workspace", _vp), ("workspace_bytes", _sz),
-                ("status", _vp)]
+                ("status", _vp), ("warps_per_kv_head", _i32), ("flags", _i32)]
 
 
 class AppendArgs(C.Structure):
@@ -347,7 +348,8 @@ def _stream_ptr(stream):
 
 
 def attention_args(q, k_cache, v_cache, block_tables, seq_lens, out, num_heads, kv_heads, *, num_blocks=None,
-                   workspace=None, split_tiles=0, kv_heads_per_cta=0, stages=0, status=None, scale=0.0) -> AttnArgs:
+                   workspace=None, split_tiles=0, kv_heads_per_cta=0, stages=0, status=None, scale=0.0,
+                   warps_per_kv_head=0) -> AttnArgs:
     """AttnArgs for one layer; k_cache/v_cache are [num_blocks][B][kv_heads][D] (or views of them)."""
     nb, B, kvh, D = k_cache.shape[-4:]
     assert kvh == kv_heads
@@ -360,6 +362,7 @@ def attention_args(q, k_cache, v_cache, block_tables, seq_lens, out, num_heads, 
     a.num_seqs, a.num_heads, a.kv_heads, a.head_dim = q.shape[0], num_heads, kv_heads, D
     a.block_size, a.max_blocks = B, block_tables.shape[1]
     a.scale, a.split_tiles, a.kv_heads_per_cta, a.stages = scale, split_tiles, kv_heads_per_cta, stages
+    a.warps_per_kv_head = warps_per_kv_head
     if workspace is not None:
         a.workspace, a.workspace_bytes = _dev(workspace, "workspace"), workspace.numel() * workspace.element_size()
     a.status = _dev(status, "status") if status is not None else None
@@ -372,7 +375,7 @@ def workspace_bytes(args: AttnArgs) -> int:
 
 def paged_attention(q, k_cache, v_cache, block_tables, seq_lens, num_heads: int, kv_heads: int, *, out=None,
                     out_dtype=None, workspace=None, split_tiles: int = 0, kv_heads_per_cta: int = 0, stages: int = 0,
-                    status=None, stream=None, num_blocks: Optional[int] = None):
+                    status=None, stream=None, num_blocks: Optional[int] = None, warps_per_kv_head: int = 0):
     """Decode attention through the C ABI (kvp_paged_attention).  Allocates `out` (and a workspace when
     none is given and the context will be split) with torch if not provided."""
     import torch
@@ -380,12 +383,13 @@ def paged_attention(q, k_cache, v_cache, block_tables, seq_lens, num_heads: int,
         out = torch.empty(q.shape, dtype=out_dtype or q.dtype, device=q.device)
     a = attention_args(q, k_cache, v_cache, block_tables, seq_lens, out, num_heads, kv_heads, num_blocks=num_blocks,
                        workspace=workspace, split_tiles=split_tiles, kv_heads_per_cta=kv_heads_per_cta,
-                       stages=stages, status=status)
+                       stages=stages, status=status, warps_per_kv_head=warps_per_kv_head)
     if workspace is None and split_tiles >= 0:
         need = workspace_bytes(a)
         if need:
-            workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+            workspace = torch.zeros(need, dtype=torch.uint8, device=q.device)
             a.workspace, a.workspace_bytes = workspace.data_ptr(), need
+            a.flags |= KVP_ATTN_WORKSPACE_CLEAN
     _check(lib().kvp_paged_attention(C.byref(a), _stream_ptr(stream)))
     return out
 

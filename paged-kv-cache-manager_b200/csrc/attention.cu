@@ -40,7 +40,8 @@
 
 namespace kvpd {
 
-constexpr int kMaxStages = 12;
+constexpr int kMaxStages = 16;
+constexpr int kMaxConsumerWarps = 8;
 constexpr int kMaxKvhPerCta = 8;
 constexpr int kMaxStreamSeqs = 8192;  // stream-K keeps the tile prefix sums of all sequences in smem
 
@@ -51,16 +52,19 @@ struct AttnParams {
     void* out;
     float2* ws_ml;   // partial (m in log2 units, l) rows of nh heads
     float* ws_o;     // partial unnormalised outputs, D per row
-    int32_t* prefix; // stream-K: [num_seqs + 1] tile prefix sums (written by CTA 0 for the merge)
+    int32_t* counters;  // stream-K: [num_seqs][groups] finished-segment counters (zero between calls)
     int32_t* status;
     long long num_blocks;  // 0: unchecked
     int q_dtype, out_dtype;
     int num_seqs, nh, g, max_blocks, B, R, nruns;
     int kvh_cta, groups, stages, split_tiles, max_splits, per_head;
     int G;                 // stream-K CTAs per kv-head group
+    int wph;               // consumer warps per kv head (they take turns over the stages)
     uint32_t head_stride, box_slot, stage_half, box_tx;
-    uint32_t stage_bytes;  // stride between stages (2 * stage_half + query area)
-    uint32_t q_area;       // stream-K: bytes of the per-stage query area (0: queries read from global memory)
+    uint32_t stage_bytes;  // stride between stages (2 * stage_half)
+    uint32_t q_area;       // bytes of one query slot (0: queries read from global memory)
+    uint32_t q_off;        // offset of the two query slots in dynamic smem
+    uint32_t comb_off;     // offset of the warp-combine area in dynamic smem
     uint32_t pre_off;      // stream-K: offset of the prefix sums in dynamic smem
     int oob_row;           // a row coordinate outside the tensor map (zero fill) used for skipped blocks
     float sl2;             // scale * log2(e)
@@ -124,6 +128,64 @@ __device__ __forceinline__ void produce_tile(const AttnParams& p, const CUtensor
             }
         }
     }
+}
+
+// Up to 8 consecutive tiles of one sequence at once, lane k producing tile `tile + k` into stage
+// (i + k) % S: each lane waits for its own stage, arms its own barrier and issues its own copies, so the
+// per-tile issue cost is paid in parallel.  Only for one run per tile (block_size a multiple of 16).
+// Returns false (after reporting) if a wait gave up.
+template <int D>
+__device__ __forceinline__ bool produce_batch(const AttnParams& p, const CUtensorMap* km, const CUtensorMap* vm,
+                                              uint32_t smem_base, uint64_t* full_bar, uint64_t* empty_bar, int i,
+                                              int tile, int nb, int len, const int32_t* trow, int kvh0, int lane,
+                                              int& cache_lo, int32_t& cached) {
+    using G_ = Geo<D>;
+    const int S = p.stages;
+    const int bi_first = tile * 16 / p.B;
+    const int bi_last = (min((tile + nb) * 16, len) - 1) / p.B;
+    if (bi_first < cache_lo || bi_last >= cache_lo + 32) {
+        cache_lo = bi_first;
+        cached = (bi_first + lane < p.max_blocks) ? __ldg(trow + bi_first + lane) : 0;
+    }
+    const bool act = lane < nb;
+    const int tok = (tile + (act ? lane : 0)) * 16;
+    const int bi = tok / p.B;
+    const int32_t blk = __shfl_sync(0xffffffffu, cached, bi - cache_lo);
+    bool ok = true;
+    if (act) {
+        int row = blk * p.B + (tok - bi * p.B);
+        if (p.num_blocks > 0 && (blk < 0 || blk >= p.num_blocks)) {
+            report(p.status, KVP_STATUS_BAD_BLOCK);
+            row = p.oob_row;
+        }
+        const int ii = i + lane;
+        const int st = ii % S;
+        if (ii >= S && !mbar_wait(smem_u32(&empty_bar[st]), static_cast<uint32_t>((ii / S - 1) & 1))) {
+            report(p.status, KVP_STATUS_TIMEOUT);
+            ok = false;
+        }
+        if (ok) {
+            const uint32_t fb = smem_u32(&full_bar[st]);
+            const uint32_t kst = smem_base + static_cast<uint32_t>(st) * p.stage_bytes;
+            const uint32_t vst = kst + p.stage_half;
+            mbar_arrive_expect_tx(fb, static_cast<uint32_t>(G_::NCH) * 2u * p.box_tx);
+#pragma unroll
+            for (int c = 0; c < G_::NCH; ++c) {
+                const uint32_t off = static_cast<uint32_t>(c) * p.box_slot;
+                if (!p.per_head) {
+                    tma_load_3d(kst + off, km, fb, c * G_::W, row, kvh0);
+                    tma_load_3d(vst + off, vm, fb, c * G_::W, row, kvh0);
+                } else {
+                    for (int w = 0; w < p.kvh_cta; ++w) {
+                        const uint32_t ho = off + static_cast<uint32_t>(w) * p.head_stride;
+                        tma_load_3d(kst + ho, km, fb, c * G_::W, kvh0 + w, row);
+                        tma_load_3d(vst + ho, vm, fb, c * G_::W, kvh0 + w, row);
+                    }
+                }
+            }
+        }
+    }
+    return __all_sync(0xffffffffu, ok);
 }
 
 // ---------------------------------------------------------------- consumer: one warp, one kv head
@@ -319,6 +381,51 @@ struct Consumer {
         if (valid < 16) fence_proxy_async_smem();  // generic writes above precede the next TMA into this stage
     }
 
+    // Lane-wise state exchange between the warps of one kv head: NREG floats per lane.
+    static constexpr int NREG = NT * KS * 4 + NT * 4;
+    __device__ __forceinline__ void store_state(float* area, int lane) const {
+        int r = 0;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) area[(r++) * 32 + lane] = o[nt][ks][e];
+            area[(r++) * 32 + lane] = m_run[nt][0];
+            area[(r++) * 32 + lane] = m_run[nt][1];
+            area[(r++) * 32 + lane] = l_run[nt][0];
+            area[(r++) * 32 + lane] = l_run[nt][1];
+        }
+    }
+    // Folds another warp's state (same lane layout) into this one: per head column, rescale both sides to
+    // the larger running max.  A warp that saw no tile has m = -inf and contributes nothing.
+    __device__ __forceinline__ void merge_state(const float* area, int lane) {
+        int r = 0;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const int rm = r + KS * 4;
+            float a[2], b[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const float m2 = area[(rm + e) * 32 + lane];
+                const float l2 = area[(rm + 2 + e) * 32 + lane];
+                const float M = fmaxf(m_run[nt][e], m2);
+                a[e] = M == -INFINITY ? 0.f : fast_exp2(m_run[nt][e] - M);
+                b[e] = M == -INFINITY ? 0.f : fast_exp2(m2 - M);
+                l_run[nt][e] = l_run[nt][e] * a[e] + l2 * b[e];
+                m_run[nt][e] = M;
+            }
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float v = area[(r++) * 32 + lane];
+                    o[nt][ks][e] = o[nt][ks][e] * a[e & 1] + v * b[e & 1];
+                }
+            r += 4;
+        }
+    }
+
     // Segment epilogue: the final normalised output (`single`) or a partial row `part_row` (nh heads).
     __device__ __forceinline__ void finish(const AttnParams& p, int lane, int seq, int kvh_global, bool single,
                                            size_t part_row) {
@@ -366,32 +473,248 @@ __device__ __forceinline__ bool q_needs_residual(const AttnParams& p) {
     return p.q_dtype != kv_dt;
 }
 
-__device__ __forceinline__ void init_barriers(const AttnParams& p, uint64_t* full_bar, uint64_t* empty_bar) {
+__device__ __forceinline__ void named_barrier(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// One attention segment: tiles [tile0, tile1) of sequence `seq`, written as the final output (`single`) or
+// as the partial row `part_row`.
+struct Segment {
+    int seq, tile0, tile1;
+    bool single;
+    size_t part_row;
+    int c0, nseg;  // stream-K: first CTA holding part of the sequence and how many do (0: merged elsewhere)
+};
+
+// Fixed splits: the CTA's one segment.
+struct SplitSegments {
+    Segment seg;
+    bool done;
+    __device__ __forceinline__ bool next(Segment& s) {
+        if (done) return false;
+        s = seg;
+        done = true;
+        return true;
+    }
+};
+
+// CTA c of Ge owns tiles [c*T/Ge, (c+1)*T/Ge) of the concatenation of all sequences' tiles (T in total).
+__device__ __forceinline__ long long cta_begin(long long c, long long T, int G) { return c * T / G; }
+__device__ __forceinline__ int cta_of_tile(long long t, long long T, int G) {
+    long long c = t * G / T;
+    while (c + 1 < G && cta_begin(c + 1, T, G) <= t) ++c;
+    while (c > 0 && cta_begin(c, T, G) > t) --c;
+    return static_cast<int>(c);
+}
+
+// Stream-K: the CTA's tile range [t, end) of the concatenated sequences, cut at sequence boundaries.
+struct StreamSegments {
+    const int32_t* P;  // tile prefix sums in shared memory
+    long long t, end, T;
+    int s, cta, nh, Ge;
+    __device__ __forceinline__ bool next(Segment& sg) {
+        if (t >= end) return false;
+        while (P[s + 1] <= t) ++s;
+        const long long e = min(end, static_cast<long long>(P[s + 1]));
+        sg.seq = s;
+        sg.tile0 = static_cast<int>(t - P[s]);
+        sg.tile1 = static_cast<int>(e - P[s]);
+        sg.single = (t == P[s]) && (e == P[s + 1]);
+        sg.part_row = static_cast<size_t>(cta + s) * nh;
+        sg.c0 = sg.single ? cta : cta_of_tile(P[s], T, Ge);
+        sg.nseg = sg.single ? 1 : cta_of_tile(P[s + 1] - 1, T, Ge) - sg.c0 + 1;
+        t = e;
+        return true;
+    }
+};
+
+__device__ __forceinline__ void init_barriers(const AttnParams& p, uint64_t* full_bar, uint64_t* empty_bar,
+                                              uint64_t* qfull, uint64_t* qempty) {
     if (threadIdx.x == 0) {
         for (int s = 0; s < p.stages; ++s) {
             mbar_init(smem_u32(&full_bar[s]), 1);
             mbar_init(smem_u32(&empty_bar[s]), static_cast<uint32_t>(p.kvh_cta));
+        }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(smem_u32(&qfull[s]), 1);
+            mbar_init(smem_u32(&qempty[s]), static_cast<uint32_t>(p.kvh_cta * p.wph));
         }
         fence_barrier_init();
     }
     __syncthreads();
 }
 
+// The work of one CTA over its segments.  Warp kvh_cta * wph is the producer; consumer warp w serves kv head
+// w % kvh_cta and takes the tiles whose stage index is congruent to w / kvh_cta modulo wph (the stage count
+// is a multiple of wph, so each stage always has the same kvh_cta consumers).  At the end of a segment the
+// wph warps of a head combine their (m, l, O) lane by lane through shared memory.
+//
+// Every wait is bounded: a warp that gives up reports KVP_STATUS_TIMEOUT and then runs through the rest of
+// its control flow without waiting (so the named barriers of its partner warps are still reached).
+template <int D>
+__device__ __forceinline__ void merge_rows(const AttnParams& p, size_t row0, size_t stride, int n, size_t out_off,
+                                           int lane);
+
+template <int D, int NT, class KV, class Segs>
+__device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap* km, const CUtensorMap* vm, Segs segs,
+                                         uint8_t* dyn, uint32_t smem_base, uint64_t* full_bar, uint64_t* empty_bar,
+                                         uint64_t* qfull, uint64_t* qempty, int grp, int* last_flag) {
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int NC = p.kvh_cta * p.wph;
+    const int S = p.stages;
+    const uint32_t qelem = p.q_dtype == KVP_DTYPE_F32 ? 4u : 2u;
+    const uint32_t q_bytes = static_cast<uint32_t>(p.kvh_cta * p.g * D) * qelem;
+    const int kvh0 = grp * p.kvh_cta;
+    Segment sg;
+    if (warp == NC) {
+        // ------------------------------------------------------------ producer warp
+        if (lane == 0) {
+            prefetch_tensormap(km);
+            prefetch_tensormap(vm);
+        }
+        bool ok = true;
+        int i = 0, j = 0;
+        while (segs.next(sg)) {
+            const int len = __ldg(p.lens + sg.seq);
+            const int32_t* trow = p.tables + static_cast<size_t>(sg.seq) * p.max_blocks;
+            int cache_lo = -(1 << 30);
+            int32_t cached = 0;
+            if (p.q_area != 0) {
+                const int slot = j & 1;
+                if (ok && j >= 2 && !mbar_wait(smem_u32(&qempty[slot]), static_cast<uint32_t>(((j >> 1) - 1) & 1))) {
+                    if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
+                    ok = false;
+                }
+                if (ok && lane == 0) {
+                    const uint32_t qb = smem_u32(&qfull[slot]);
+                    mbar_arrive_expect_tx(qb, q_bytes);
+                    const char* src = static_cast<const char*>(p.q) +
+                                      (static_cast<size_t>(sg.seq) * p.nh + static_cast<size_t>(kvh0) * p.g) * D * qelem;
+                    bulk_load(smem_base + p.q_off + static_cast<uint32_t>(slot) * p.q_area, src, q_bytes, qb);
+                }
+            }
+            // One run per tile: issue in batches of up to 8 tiles (one per lane); else one tile at a time.
+            const int nb_max = p.nruns == 1 ? min(8, S) : 1;
+            for (int tile = sg.tile0; tile < sg.tile1;) {
+                const int nb = min(nb_max, sg.tile1 - tile);
+                if (ok) {
+                    if (nb_max > 1) {
+                        ok = produce_batch<D>(p, km, vm, smem_base, full_bar, empty_bar, i, tile, nb, len, trow, kvh0,
+                                              lane, cache_lo, cached);
+                    } else {
+                        const int st = i % S;
+                        if (i >= S && !mbar_wait(smem_u32(&empty_bar[st]), static_cast<uint32_t>((i / S - 1) & 1))) {
+                            if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
+                            ok = false;
+                        } else {
+                            const uint32_t kst = smem_base + static_cast<uint32_t>(st) * p.stage_bytes;
+                            produce_tile<D>(p, km, vm, kst, kst + p.stage_half, smem_u32(&full_bar[st]), tile * 16, len,
+                                            trow, kvh0, lane, cache_lo, cached, 0u);
+                        }
+                    }
+                    __syncwarp();
+                }
+                tile += nb;
+                i += nb;
+            }
+            ++j;
+        }
+        return;
+    }
+    if (warp > NC) return;
+
+    // ---------------------------------------------------------------- consumer warps
+    const int head = warp % p.kvh_cta, sub = warp / p.kvh_cta;
+    const int kvh_global = kvh0 + head;
+    Consumer<D, NT, KV> cs;
+    cs.init_geometry(p, head, lane);
+    const bool use_qlo = q_needs_residual<KV>(p);
+    float* comb = reinterpret_cast<float*>(dyn + p.comb_off);
+    constexpr int NREG = Consumer<D, NT, KV>::NREG;
+    bool ok = true;
+    int i = 0, j = 0;
+    while (segs.next(sg)) {
+        const int len = __ldg(p.lens + sg.seq);
+        if (p.q_area != 0) {
+            const int slot = j & 1;
+            if (ok && !mbar_wait(smem_u32(&qfull[slot]), static_cast<uint32_t>((j >> 1) & 1))) {
+                if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
+                ok = false;
+            }
+            if (ok) cs.load_q_smem(p, smem_base + p.q_off + static_cast<uint32_t>(slot) * p.q_area, head, lane);
+            __syncwarp();
+            if (ok && lane == 0) mbar_arrive(smem_u32(&qempty[slot]));
+        } else {
+            cs.load_q_global(p, sg.seq, kvh_global, lane);
+        }
+        cs.reset();
+        for (int tile = sg.tile0; tile < sg.tile1; ++tile, ++i) {
+            if (!ok || (i % p.wph) != sub) continue;
+            const int st = i % S;
+            if (!mbar_wait(smem_u32(&full_bar[st]), static_cast<uint32_t>((i / S) & 1))) {
+                if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
+                ok = false;
+                continue;
+            }
+            const uint32_t kst = smem_base + static_cast<uint32_t>(st) * p.stage_bytes;
+            cs.tile(p, kst, kst + p.stage_half, min(16, len - tile * 16), head, lane, use_qlo);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&empty_bar[st]));
+        }
+        if (p.wph > 1) {
+            float* area = comb + static_cast<size_t>(head) * NREG * 32;
+            const size_t stride = static_cast<size_t>(p.kvh_cta) * NREG * 32;
+            if (sub > 0) cs.store_state(area + (sub - 1) * stride, lane);
+            named_barrier(1 + head, p.wph * 32);
+            if (sub == 0)
+                for (int k = 1; k < p.wph; ++k) cs.merge_state(area + (k - 1) * stride, lane);
+            named_barrier(1 + head, p.wph * 32);  // the area is rewritten by the next segment
+        }
+        if (sub == 0 && ok) cs.finish(p, lane, sg.seq, kvh_global, sg.single, sg.part_row);
+        // Stream-K, sequence split across CTAs: the last CTA to finish its part merges the partials of every
+        // head of its group (the counter is reset so the workspace stays clean for the next call).
+        if (!sg.single && sg.nseg > 0) {
+            if (sub == 0) __threadfence();  // this warp's partial rows, device-wide
+            named_barrier(kMaxConsumerWarps + 1, NC * 32);
+            if (warp == 0 && lane == 0) {
+                int last = 0;
+                if (ok) {
+                    int* cnt = p.counters + static_cast<size_t>(sg.seq) * p.groups + grp;
+                    last = atomicAdd(cnt, 1) == sg.nseg - 1;
+                    if (last) atomicExch(cnt, 0);
+                }
+                *last_flag = last;
+            }
+            named_barrier(kMaxConsumerWarps + 1, NC * 32);
+            if (*last_flag) {
+                __threadfence();
+                // every consumer warp merges some of the group's query heads
+                for (int jj = warp; jj < p.kvh_cta * p.g; jj += NC) {
+                    const int hq = kvh0 * p.g + jj;
+                    merge_rows<D>(p, static_cast<size_t>(sg.c0 + sg.seq) * p.nh + hq, static_cast<size_t>(p.nh),
+                                  sg.nseg, (static_cast<size_t>(sg.seq) * p.nh + hq) * D, lane);
+                }
+            }
+            named_barrier(kMaxConsumerWarps + 1, NC * 32);  // the flag is rewritten by the next segment
+        }
+        ++j;
+    }
+}
+
 // ---------------------------------------------------------------- fixed-split schedule
 template <int D, int NT, class KV>
-__global__ void __launch_bounds__((kMaxKvhPerCta + 1) * 32, 1)
+__global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
     paged_decode_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                         const AttnParams p) {
     __shared__ __align__(8) uint64_t full_bar[kMaxStages];
     __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
+    __shared__ __align__(8) uint64_t qfull[2], qempty[2];
     extern __shared__ uint8_t dyn_smem[];
 
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
     const int seq = blockIdx.x / p.groups;
     const int grp = blockIdx.x - seq * p.groups;
     const int split = blockIdx.y;
-
     const int len = p.lens[seq];
     const int ntiles = tiles_of_len(p, len);
     const int nsplit = (ntiles + p.split_tiles - 1) / p.split_tiles;
@@ -408,58 +731,22 @@ __global__ void __launch_bounds__((kMaxKvhPerCta + 1) * 32, 1)
         return;
     }
     if (split >= nsplit) return;
-    const int t0 = split * p.split_tiles;
-    const int n = min(ntiles - t0, p.split_tiles);
-    const uint32_t smem_base = (smem_u32(dyn_smem) + 1023u) & ~1023u;
-    const int S = p.stages;
-    init_barriers(p, full_bar, empty_bar);
-
-    if (warp == p.kvh_cta) {
-        if (lane == 0) {
-            prefetch_tensormap(&kmap);
-            prefetch_tensormap(&vmap);
-        }
-        const int32_t* trow = p.tables + static_cast<size_t>(seq) * p.max_blocks;
-        int cache_lo = -(1 << 30);
-        int32_t cached = 0;
-        for (int i = 0; i < n; ++i) {
-            const int s = i % S;
-            if (i >= S && !mbar_wait(smem_u32(&empty_bar[s]), static_cast<uint32_t>((i / S - 1) & 1))) {
-                if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
-                break;
-            }
-            const uint32_t kst = smem_base + static_cast<uint32_t>(s) * p.stage_bytes;
-            produce_tile<D>(p, &kmap, &vmap, kst, kst + p.stage_half, smem_u32(&full_bar[s]), (t0 + i) * 16, len,
-                            trow, grp * p.kvh_cta, lane, cache_lo, cached, 0u);
-            __syncwarp();
-        }
-        return;
-    }
-    if (warp >= p.kvh_cta) return;
-
-    Consumer<D, NT, KV> cs;
-    const int kvh_global = grp * p.kvh_cta + warp;
-    cs.init_geometry(p, warp, lane);
-    cs.load_q_global(p, seq, kvh_global, lane);
-    cs.reset();
-    const bool use_qlo = q_needs_residual<KV>(p);
-    for (int i = 0; i < n; ++i) {
-        const int s = i % S;
-        if (!mbar_wait(smem_u32(&full_bar[s]), static_cast<uint32_t>((i / S) & 1))) {
-            if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
-            return;
-        }
-        const uint32_t kst = smem_base + static_cast<uint32_t>(s) * p.stage_bytes;
-        cs.tile(p, kst, kst + p.stage_half, min(16, len - (t0 + i) * 16), warp, lane, use_qlo);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&empty_bar[s]));
-    }
-    cs.finish(p, lane, seq, kvh_global, nsplit == 1, (static_cast<size_t>(seq) * p.max_splits + split) * p.nh);
+    const uint32_t base_off = ((smem_u32(dyn_smem) + 1023u) & ~1023u) - smem_u32(dyn_smem);
+    init_barriers(p, full_bar, empty_bar, qfull, qempty);
+    SplitSegments segs;
+    segs.seg.seq = seq;
+    segs.seg.tile0 = split * p.split_tiles;
+    segs.seg.tile1 = min(ntiles, segs.seg.tile0 + p.split_tiles);
+    segs.seg.single = nsplit == 1;
+    segs.seg.part_row = (static_cast<size_t>(seq) * p.max_splits + split) * p.nh;
+    segs.seg.c0 = 0;
+    segs.seg.nseg = 0;
+    segs.done = false;
+    cta_body<D, NT, KV>(p, &kmap, &vmap, segs, dyn_smem + base_off, smem_u32(dyn_smem) + base_off, full_bar,
+                        empty_bar, qfull, qempty, grp, nullptr);
 }
 
 // ---------------------------------------------------------------- stream-K schedule
-// CTA c of G owns tiles [c*T/G, (c+1)*T/G) of the concatenation of all sequences' tiles (T in total).
-__device__ __forceinline__ long long cta_begin(long long c, long long T, int G) { return c * T / G; }
 
 // Tile prefix sums P[0..ns] of all sequences into shared memory (invalid lengths count 0 tiles).
 __device__ __forceinline__ void build_prefix(const AttnParams& p, int32_t* P, int32_t* warp_tot) {
@@ -507,131 +794,78 @@ __device__ __forceinline__ int seq_of_tile(const int32_t* P, int ns, long long t
 }
 
 template <int D, int NT, class KV>
-__global__ void __launch_bounds__((kMaxKvhPerCta + 1) * 32, 1)
+__global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
     paged_decode_streamk_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                                 const AttnParams p) {
     __shared__ __align__(8) uint64_t full_bar[kMaxStages];
     __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
+    __shared__ __align__(8) uint64_t qfull[2], qempty[2];
     __shared__ int32_t warp_tot[32];
     extern __shared__ uint8_t dyn_smem[];
 
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
     const int c = blockIdx.x, grp = blockIdx.y;
     const uint32_t base_off = ((smem_u32(dyn_smem) + 1023u) & ~1023u) - smem_u32(dyn_smem);
-    const uint32_t smem_base = smem_u32(dyn_smem) + base_off;
     int32_t* P = reinterpret_cast<int32_t*>(dyn_smem + base_off + p.pre_off);
     build_prefix(p, P, warp_tot);
     const int ns = p.num_seqs;
     const long long T = P[ns];
-    if (c == 0 && grp == 0)
-        for (int i = threadIdx.x; i <= ns; i += blockDim.x) p.prefix[i] = P[i];
+    if (c == 0) {
+        // Sequences with an invalid length own no tile: report them and write zeros for this group's heads.
+        const int heads = p.kvh_cta * p.g;
+        for (int s = 0; s < ns; ++s) {
+            if (P[s + 1] != P[s]) continue;
+            if (threadIdx.x == 0 && grp == 0) report(p.status, KVP_STATUS_BAD_LEN);
+            for (int i = threadIdx.x; i < heads * D; i += blockDim.x)
+                store_any(p.out, (static_cast<size_t>(s) * p.nh + grp * heads + i / D) * D + i % D, p.out_dtype, 0.f);
+        }
+    }
     // With fewer tiles than CTAs only the first T CTAs work, so every working CTA owns >= 1 tile.
     const int Ge = static_cast<int>(min(static_cast<long long>(p.G), T));
     if (c >= Ge) return;
-    const long long b0 = cta_begin(c, T, Ge), b1 = cta_begin(c + 1, T, Ge);
-    const int s_first = seq_of_tile(P, ns, b0);
-    const int S = p.stages;
-    init_barriers(p, full_bar, empty_bar);
-    const uint32_t q_bytes = static_cast<uint32_t>(p.kvh_cta * p.g * D) * (p.q_dtype == KVP_DTYPE_F32 ? 4u : 2u);
-
-    if (warp == p.kvh_cta) {
-        // ------------------------------------------------------------ producer warp
-        if (lane == 0) {
-            prefetch_tensormap(&kmap);
-            prefetch_tensormap(&vmap);
-        }
-        const int kvh0 = grp * p.kvh_cta;
-        int i = 0;  // tile counter of this CTA (stage = i % S)
-        int s = s_first;
-        for (long long t = b0; t < b1;) {
-            while (P[s + 1] <= t) ++s;
-            const long long seg_end = min(b1, static_cast<long long>(P[s + 1]));
-            const int len = __ldg(p.lens + s);
-            const int32_t* trow = p.tables + static_cast<size_t>(s) * p.max_blocks;
-            int cache_lo = -(1 << 30);
-            int32_t cached = 0;
-            for (long long u = t; u < seg_end; ++u, ++i) {
-                const int st = i % S;
-                if (i >= S && !mbar_wait(smem_u32(&empty_bar[st]), static_cast<uint32_t>((i / S - 1) & 1))) {
-                    if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
-                    return;
-                }
-                const uint32_t kst = smem_base + static_cast<uint32_t>(st) * p.stage_bytes;
-                const uint32_t fb = smem_u32(&full_bar[st]);
-                const bool first = (u == t) && p.q_area != 0;
-                produce_tile<D>(p, &kmap, &vmap, kst, kst + p.stage_half, fb, static_cast<int>(u - P[s]) * 16, len,
-                                trow, kvh0, lane, cache_lo, cached, first ? q_bytes : 0u);
-                if (first && lane == 0) {
-                    const char* src = static_cast<const char*>(p.q) +
-                                      (static_cast<size_t>(s) * p.nh + static_cast<size_t>(kvh0) * p.g) * D *
-                                          (p.q_dtype == KVP_DTYPE_F32 ? 4 : 2);
-                    bulk_load(kst + 2u * p.stage_half, src, q_bytes, fb);
-                }
-                __syncwarp();
-            }
-            t = seg_end;
-        }
-        return;
-    }
-    if (warp >= p.kvh_cta) return;
-
-    // ---------------------------------------------------------------- consumer warps
-    Consumer<D, NT, KV> cs;
-    const int kvh_global = grp * p.kvh_cta + warp;
-    cs.init_geometry(p, warp, lane);
-    const bool use_qlo = q_needs_residual<KV>(p);
-    int i = 0;
-    int s = s_first;
-    for (long long t = b0; t < b1;) {
-        while (P[s + 1] <= t) ++s;
-        const long long seg_end = min(b1, static_cast<long long>(P[s + 1]));
-        const int len = __ldg(p.lens + s);
-        if (p.q_area == 0) cs.load_q_global(p, s, kvh_global, lane);
-        cs.reset();
-        for (long long u = t; u < seg_end; ++u, ++i) {
-            const int st = i % S;
-            if (!mbar_wait(smem_u32(&full_bar[st]), static_cast<uint32_t>((i / S) & 1))) {
-                if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
-                return;
-            }
-            const uint32_t kst = smem_base + static_cast<uint32_t>(st) * p.stage_bytes;
-            if (u == t && p.q_area != 0) cs.load_q_smem(p, kst + 2u * p.stage_half, warp, lane);
-            cs.tile(p, kst, kst + p.stage_half, min(16, len - static_cast<int>(u - P[s]) * 16), warp, lane, use_qlo);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&empty_bar[st]));
-        }
-        const bool single = (t == P[s]) && (seg_end == P[s + 1]);
-        cs.finish(p, lane, s, kvh_global, single, static_cast<size_t>(c + s) * p.nh);
-        t = seg_end;
-    }
+    StreamSegments segs;
+    segs.P = P;
+    segs.T = T;
+    segs.Ge = Ge;
+    segs.t = cta_begin(c, T, Ge);
+    segs.end = cta_begin(c + 1, T, Ge);
+    segs.s = seq_of_tile(P, ns, segs.t);
+    segs.cta = c;
+    segs.nh = p.nh;
+    init_barriers(p, full_bar, empty_bar, qfull, qempty);
+    __shared__ int last_flag;
+    cta_body<D, NT, KV>(p, &kmap, &vmap, segs, dyn_smem + base_off, smem_u32(dyn_smem) + base_off, full_bar,
+                        empty_bar, qfull, qempty, grp, &last_flag);
 }
 
 // ---------------------------------------------------------------- merges
 // Combines `n` partial rows of one (sequence, head) -- rows row0 + k * stride -- into the output: one warp.
-// Lane k owns partial k's weight; the output loop's loads are independent, so they overlap.
+// Lane k holds partial k's (m, l) (one L2 round trip), the weights stay in registers and the output loop's
+// loads are independent of each other.  Partials written by other CTAs of the same launch are read through
+// L2 (ld.global.cg).
 template <int D>
 __device__ __forceinline__ void merge_rows(const AttnParams& p, size_t row0, size_t stride, int n, size_t out_off,
                                            int lane) {
-    float M = -INFINITY;
-    for (int k = lane; k < n; k += 32) M = fmaxf(M, p.ws_ml[row0 + k * stride].x);
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-    float L = 0.f;
-    for (int k = lane; k < n; k += 32) {
-        const float2 ml = p.ws_ml[row0 + k * stride];
-        L += ml.y * fast_exp2(ml.x - M);
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-    const float invL = 1.f / L;
     constexpr int PER = (D + 31) / 32;
     float acc[PER];
 #pragma unroll
     for (int q = 0; q < PER; ++q) acc[q] = 0.f;
+    float M = -INFINITY, L = 0.f;
     for (int k0 = 0; k0 < n; k0 += 32) {
         const int kk = k0 + lane;
-        const float w = kk < n ? fast_exp2(p.ws_ml[row0 + kk * stride].x - M) * invL : 0.f;
+        const float2 ml = kk < n ? __ldcg(&p.ws_ml[row0 + kk * stride]) : make_float2(-INFINITY, 0.f);
+        float Mc = ml.x;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) Mc = fmaxf(Mc, __shfl_xor_sync(0xffffffffu, Mc, off));
+        const float Mn = fmaxf(M, Mc);
+        const float rescale = M == -INFINITY ? 0.f : fast_exp2(M - Mn);
+        const float w = kk < n ? fast_exp2(ml.x - Mn) : 0.f;
+        float Lc = ml.y * w;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) Lc += __shfl_xor_sync(0xffffffffu, Lc, off);
+        L = L * rescale + Lc;
+#pragma unroll
+        for (int q = 0; q < PER; ++q) acc[q] *= rescale;
+        M = Mn;
         const int cnt = min(32, n - k0);
 #pragma unroll 4
         for (int k = 0; k < cnt; ++k) {
@@ -640,14 +874,15 @@ __device__ __forceinline__ void merge_rows(const AttnParams& p, size_t row0, siz
 #pragma unroll
             for (int q = 0; q < PER; ++q) {
                 const int d = q * 32 + lane;
-                if (d < D) acc[q] += src[d] * wk;
+                if (d < D) acc[q] += __ldcg(src + d) * wk;
             }
         }
     }
+    const float invL = 1.f / L;
 #pragma unroll
     for (int q = 0; q < PER; ++q) {
         const int d = q * 32 + lane;
-        if (d < D) store_any(p.out, out_off + d, p.out_dtype, acc[q]);
+        if (d < D) store_any(p.out, out_off + d, p.out_dtype, acc[q] * invL);
     }
 }
 
@@ -663,36 +898,6 @@ __global__ void __launch_bounds__(128) merge_splits_kernel(const AttnParams p) {
     if (nsplit <= 1) return;
     merge_rows<D>(p, static_cast<size_t>(seq) * p.max_splits * p.nh + hq, static_cast<size_t>(p.nh), nsplit,
                   (static_cast<size_t>(seq) * p.nh + hq) * D, lane);
-}
-
-// Stream-K schedule: one warp per (sequence, head).  Sequence s's segments are the CTAs c that own its first
-// to its last tile (every working CTA owns at least one tile); their partial rows are (c + s) * nh + head.
-// Invalid lengths get zeros here.
-template <int D>
-__global__ void __launch_bounds__(128) merge_streamk_kernel(const AttnParams p) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const long long idx = static_cast<long long>(blockIdx.x) * 4 + warp;
-    if (idx >= static_cast<long long>(p.num_seqs) * p.nh) return;
-    const int seq = static_cast<int>(idx / p.nh), hq = static_cast<int>(idx % p.nh);
-    const size_t out_off = (static_cast<size_t>(seq) * p.nh + hq) * D;
-    if (tiles_of_len(p, p.lens[seq]) == 0) {
-        if (hq == 0 && lane == 0) report(p.status, KVP_STATUS_BAD_LEN);
-        for (int d = lane; d < D; d += 32) store_any(p.out, out_off + d, p.out_dtype, 0.f);
-        return;
-    }
-    const long long T = p.prefix[p.num_seqs];
-    const int Ge = static_cast<int>(min(static_cast<long long>(p.G), T));
-    const long long t0 = p.prefix[seq], t1 = p.prefix[seq + 1] - 1;
-    auto owner = [&](long long t) {
-        long long c = t * Ge / T;
-        while (c + 1 < Ge && cta_begin(c + 1, T, Ge) <= t) ++c;
-        while (c > 0 && cta_begin(c, T, Ge) > t) --c;
-        return c;
-    };
-    const long long c0 = owner(t0), c1 = owner(t1);
-    if (c0 == c1) return;  // one CTA covered the whole sequence and wrote the output itself
-    merge_rows<D>(p, static_cast<size_t>(c0 + seq) * p.nh + hq, static_cast<size_t>(p.nh), static_cast<int>(c1 - c0 + 1),
-                  out_off, lane);
 }
 
 }  // namespace kvpd
@@ -907,31 +1112,54 @@ int plan_attention(const kvp_attn_args& a, bool have_workspace, AttnPlan* out) {
 
     // Schedule: stream-K when splitting is automatic and a workspace is available; otherwise fixed splits.
     pl.streamk = (a.split_tiles == 0 && have_workspace && a.num_seqs > 0 && a.num_seqs <= kvpd::kMaxStreamSeqs) ? 1 : 0;
+    // Consumer warps per kv head: fill 8 consumer warps per CTA, so small groups still have enough warps in
+    // flight to hide the per-tile latency -- as many as the shared memory of the smallest ring allows.
     const size_t qelem = a.q_dtype == KVP_DTYPE_F32 ? 4 : 2;
-    if (pl.streamk && (reinterpret_cast<uintptr_t>(a.q) & 15u) == 0)
-        pl.q_area = static_cast<uint32_t>(round_up(static_cast<size_t>(kc) * g * D * qelem, 1024));
-    pl.stage_bytes = 2u * pl.stage_half + pl.q_area;
+    if ((reinterpret_cast<uintptr_t>(a.q) & 15u) == 0)
+        pl.q_area = static_cast<uint32_t>(round_up(static_cast<size_t>(kc) * g * D * qelem, 128));
+    pl.stage_bytes = 2u * pl.stage_half;
     const size_t stage = pl.stage_bytes;
+    const int NT = g <= 8 ? 1 : 2;
     const size_t pre = pl.streamk ? round_up((static_cast<size_t>(a.num_seqs) + 1) * 4, 128) : 0;
     const size_t smem_cap = kDynSmemCap;
-    int st = a.stages;
-    if (st <= 0) st = static_cast<int>(std::max<size_t>(2, std::min<size_t>(8, (96u << 10) / stage)));
-    st = std::min(st, kvpd::kMaxStages);
-    while (st > 2 && stage * st + pre + 1024 > smem_cap) --st;
-    if (stage * st + pre + 1024 > smem_cap) return fail(KVP_EINVAL, "shape needs more shared memory than a CTA has");
-    pl.stages = st;
-    pl.pre_off = static_cast<uint32_t>(stage * st);
-    pl.smem = stage * st + pre + 1024;
+    size_t comb = 0;
+    auto total = [&](int wph, int k) {
+        comb = static_cast<size_t>(wph - 1) * kc * 32 * (NT * (D / 16) * 4 + NT * 4) * sizeof(float);
+        return round_up(stage * wph * k, 128) + 2 * static_cast<size_t>(pl.q_area) + round_up(comb, 16) + pre + 1024;
+    };
+    auto min_per = [](int wph) { return wph == 1 ? 2 : 1; };
+    // Measured on B200: two warps per kv head help when a CTA serves at most two kv heads, one is best otherwise.
+    pl.wph = kc <= 2 ? 2 : 1;
+    if (a.warps_per_kv_head > 0) pl.wph = std::min(a.warps_per_kv_head, std::max(1, kvpd::kMaxConsumerWarps / kc));
+    while (pl.wph > 1 && total(pl.wph, min_per(pl.wph)) > smem_cap) --pl.wph;
+    if (total(pl.wph, min_per(pl.wph)) > smem_cap) {
+        if (total(1, 1) > smem_cap) return fail(KVP_EINVAL, "shape needs more shared memory than a CTA has");
+    }
+    // Stages: a multiple of wph (each stage keeps the same consumers); a ring of about 192 KB for large stages
+    // (three 64 KB stages measured best for 8 kv heads x D=128, one CTA per SM) and about 96 KB for small ones
+    // (two CTAs per SM measured better than a deeper ring); at least two per consumer when one warp serves
+    // each head (when the shared memory allows).
+    const size_t ring = stage >= (48u << 10) ? (192u << 10) : (96u << 10);  // small stages: 2 CTAs per SM
+    int per = a.stages > 0 ? std::max(1, a.stages / pl.wph)
+                           : static_cast<int>(std::max<size_t>(min_per(pl.wph), ring / (stage * pl.wph)));
+    per = std::min(per, kvpd::kMaxStages / pl.wph);
+    while (per > 1 && total(pl.wph, per) > smem_cap) --per;
+    if (total(pl.wph, per) > smem_cap) return fail(KVP_EINVAL, "shape needs more shared memory than a CTA has");
+    pl.smem = total(pl.wph, per);
+    pl.stages = per * pl.wph;
+    pl.q_off = static_cast<uint32_t>(round_up(stage * pl.stages, 128));
+    pl.comb_off = pl.q_off + 2 * pl.q_area;
+    pl.pre_off = static_cast<uint32_t>(pl.comb_off + round_up(comb, 16));
 
     if (pl.streamk) {
         const void* fn = pick_kernel(a.kv_dtype, D, g, true);
-        pl.G = sm_count() * streamk_ctas_per_sm(fn, (kc + 1) * 32, pl.smem);
+        pl.G = sm_count() * streamk_ctas_per_sm(fn, (kc * pl.wph + 1) * 32, pl.smem);
         pl.split_tiles = pl.max_tiles;
         pl.max_splits = 1;
         const size_t rows = (static_cast<size_t>(pl.G) + a.num_seqs) * a.num_heads;
         pl.ws_o_off = round_up(rows * sizeof(float2), 256);
-        pl.ws_pre_off = pl.ws_o_off + round_up(rows * static_cast<size_t>(D) * sizeof(float), 256);
-        pl.ws_bytes = pl.ws_pre_off + round_up((static_cast<size_t>(a.num_seqs) + 1) * 4, 256);
+        pl.ws_cnt_off = pl.ws_o_off + round_up(rows * static_cast<size_t>(D) * sizeof(float), 256);
+        pl.ws_bytes = pl.ws_cnt_off + round_up(static_cast<size_t>(a.num_seqs) * pl.groups * 4, 256);
         *out = pl;
         return KVP_OK;
     }
@@ -957,12 +1185,8 @@ int launch_merge(const kvp_attn_args& a, const AttnPlan& pl, const kvpd::AttnPar
     const long long pairs = static_cast<long long>(a.num_seqs) * a.num_heads;
     if (pairs == 0) return KVP_OK;
     const unsigned blocks = static_cast<unsigned>((pairs + 3) / 4);
-    if (pl.streamk)
-        kvpd::merge_streamk_kernel<D><<<blocks, 128, 0, stream>>>(prm);
-    else if (pl.max_splits > 1)
-        kvpd::merge_splits_kernel<D><<<blocks, 128, 0, stream>>>(prm);
-    else
-        return KVP_OK;
+    if (pl.streamk || pl.max_splits <= 1) return KVP_OK;  // stream-K merges inside the attention kernel
+    kvpd::merge_splits_kernel<D><<<blocks, 128, 0, stream>>>(prm);
     return cuda_status(cudaGetLastError(), "split merge kernel launch");
 }
 
@@ -973,7 +1197,7 @@ int launch_typed(const kvp_attn_args& a, const AttnPlan& pl, const kvpd::AttnPar
     int rc = allow_smem(fn);
     if (rc != KVP_OK) return rc;
     if (a.num_seqs == 0) return KVP_OK;
-    dim3 block(static_cast<unsigned>((pl.kvh_cta + 1) * 32));
+    dim3 block(static_cast<unsigned>((pl.kvh_cta * pl.wph + 1) * 32));
     if (pl.streamk) {
         dim3 grid(static_cast<unsigned>(pl.G), static_cast<unsigned>(pl.groups));
         kvpd::paged_decode_streamk_kernel<D, NT, KV><<<grid, block, pl.smem, stream>>>(km, vm, prm);
@@ -1061,7 +1285,15 @@ extern "C" KVP_API int kvp_paged_attention(const kvp_attn_args* a, void* stream)
         char* ws = static_cast<char*>(a->workspace);
         prm.ws_ml = reinterpret_cast<float2*>(ws);
         prm.ws_o = reinterpret_cast<float*>(ws + pl.ws_o_off);
-        if (pl.streamk) prm.prefix = reinterpret_cast<int32_t*>(ws + pl.ws_pre_off);
+        if (pl.streamk) {
+            prm.counters = reinterpret_cast<int32_t*>(ws + pl.ws_cnt_off);
+            // The counters must start at zero; every completed call leaves them zero again.
+            if (!(a->flags & KVP_ATTN_WORKSPACE_CLEAN)) {
+                const cudaError_t e = cudaMemsetAsync(prm.counters, 0, static_cast<size_t>(a->num_seqs) * pl.groups * 4,
+                                                      static_cast<cudaStream_t>(stream));
+                if (e != cudaSuccess) return cuda_status(e, "workspace counter reset");
+            }
+        }
     }
     prm.status = a->status;
     prm.num_blocks = a->num_blocks > 0 ? a->num_blocks : 0;
@@ -1087,7 +1319,10 @@ extern "C" KVP_API int kvp_paged_attention(const kvp_attn_args* a, void* stream)
     prm.box_tx = pl.box_tx;
     prm.stage_bytes = pl.stage_bytes;
     prm.q_area = pl.q_area;
+    prm.q_off = pl.q_off;
+    prm.comb_off = pl.comb_off;
     prm.pre_off = pl.pre_off;
+    prm.wph = pl.wph;
     prm.oob_row = static_cast<int>(std::min<long long>(rows, 0x7fffffffLL));
     const float scale = a->scale > 0.f ? a->scale : 1.0f / std::sqrt(static_cast<float>(a->head_dim));
     prm.sl2 = scale * 1.4426950408889634f;

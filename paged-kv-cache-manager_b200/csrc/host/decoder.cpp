@@ -240,6 +240,7 @@ int enqueue_device(kvp_decoder* d, int n, const void* q, const void* knew, const
         a.workspace = d->lay.attn_bytes ? d->ws + d->lay.attn : nullptr;
         a.workspace_bytes = d->lay.attn_bytes;
         a.status = d->d_status();
+        a.flags = KVP_ATTN_WORKSPACE_CLEAN;
         rc = kvp_paged_attention(&a, s_comp);
         if (rc != KVP_OK) return rc;
         if (per_layer_events) {
@@ -332,6 +333,8 @@ KVP_API kvp_decoder* kvp_decoder_create(const kvp_decoder_config* c, kvp_mgr* mg
              cudaEventCreateWithFlags(&d->ev_att[static_cast<size_t>(l)], cudaEventDisableTiming) == cudaSuccess;
     }
     ok = ok && cudaMemsetAsync(d->d_status(), 0, sizeof(int32_t), d->s_comp) == cudaSuccess;
+    // The attention workspace's merge counters start at zero and every completed call leaves them zero.
+    if (lay.attn_bytes) ok = ok && cudaMemsetAsync(d->ws + lay.attn, 0, lay.attn_bytes, d->s_comp) == cudaSuccess;
     ok = ok && cudaEventRecord(d->ev_staged, d->s_in) == cudaSuccess;
     ok = ok && cudaStreamSynchronize(d->s_comp) == cudaSuccess;
     if (!ok) {

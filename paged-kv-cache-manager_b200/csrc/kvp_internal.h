@@ -45,12 +45,14 @@ struct AttnPlan {
     uint32_t head_stride = 0, box_slot = 0, stage_half = 0, box_tx = 0;
     int streamk = 0;        // 1: persistent balanced schedule (grid of G CTAs per kv-head group)
     int G = 0;              // stream-K CTAs per group = SMs x resident CTAs per SM
-    uint32_t q_area = 0;    // stream-K: per-stage query area (0: queries read from global memory)
+    int wph = 1;            // consumer warps per kv head
+    uint32_t q_area = 0;    // bytes of one of the two query slots (0: queries read from global memory)
     uint32_t stage_bytes = 0;
-    uint32_t pre_off = 0;   // stream-K: offset of the prefix sums after the stages
+    uint32_t q_off = 0, comb_off = 0;  // offsets of the query slots and of the warp-combine area
+    uint32_t pre_off = 0;   // stream-K: offset of the prefix sums
     size_t smem = 0, ws_bytes = 0;
     size_t ws_o_off = 0;    // byte offset of the partial outputs in the workspace
-    size_t ws_pre_off = 0;  // stream-K: byte offset of the prefix sums in the workspace
+    size_t ws_cnt_off = 0;  // stream-K: byte offset of the per-sequence segment counters in the workspace
 };
 int plan_attention(const kvp_attn_args& a, bool have_workspace, AttnPlan* plan);
 

@@ -298,3 +298,28 @@ def test_balanced_schedule_unaligned_query(kvb, ora, cuda):
     kvb.paged_attention(qv, kt.cuda(), vt.cuda(), torch.from_numpy(T).cuda(), torch.from_numpy(L).cuda(), 16, 4, out=o)
     torch.cuda.synchronize()
     check_close(o.cpu().numpy(), ref, what="unaligned query")
+
+
+def test_balanced_schedule_leaves_workspace_clean(kvb, ora, cuda):
+    """The in-kernel merge counters return to zero after every call, so a workspace zero-filled once can be
+    reused with KVP_ATTN_WORKSPACE_CLEAN indefinitely (three calls in a row, each checked)."""
+    import torch
+    lens = [3000, 17, 1200, 5000, 64]
+    nb = sum((n + 15) // 16 for n in lens) + 2
+    Q, K, V, T, L = _normal_case(21, 5, 32, 8, 128, 16, lens, nb)
+    kt, kf = _round(K, "bf16")
+    vt, vf = _round(V, "bf16")
+    ref = ora.reference_attention(32, 8, 128, 16, Q, kf, vf, T, L)
+    q, k, v = torch.from_numpy(Q).cuda(), kt.cuda(), vt.cuda()
+    t, l = torch.from_numpy(T).cuda(), torch.from_numpy(L).cuda()
+    out = torch.empty(Q.shape, dtype=torch.float32, device="cuda")
+    a = kvb.attention_args(q, k, v, t, l, out, 32, 8, num_blocks=nb)
+    ws = torch.zeros(kvb.workspace_bytes(a), dtype=torch.uint8, device="cuda")
+    a.workspace, a.workspace_bytes, a.flags = ws.data_ptr(), ws.numel(), kvb.KVP_ATTN_WORKSPACE_CLEAN
+    for _ in range(3):
+        out.fill_(float("nan"))
+        assert kvb.lib().kvp_paged_attention(C.byref(a), C.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0
+        torch.cuda.synchronize()
+        check_close(out.cpu().numpy(), ref, what="clean workspace reuse")
+        cnt = ws[-256 * ((5 * 4 + 255) // 256):].view(torch.int32)
+        assert int(cnt.abs().sum().item()) == 0
