@@ -231,19 +231,17 @@ def run_ours(args, cfg, rank, world, dev):
     max_len = int(lens.max()) + steps_total + 1
     max_blocks = (max_len + B - 1) // B
 
-    # Device-resident inputs for the value run: per-step slots and lengths precomputed by the host
-    # manager (the table after all steps serves every step: entries past a sequence are never read).
+    # Device-resident inputs for the value run: per-step lengths precomputed by the host manager (the table
+    # after all steps serves every step: entries past a sequence are never read).  Each step's attention
+    # launch writes the new token of its layer into the slot at position len - 1 (fused append).
     n_value = W + K
-    slots_all = np.empty((n_value, ns), np.int32)
     lens_all = np.empty((n_value, ns), np.int32)
     for s in range(n_value):
-        done, slots, pairs = mgr.append_batch(rids)
+        done, _, pairs = mgr.append_batch(rids)
         assert done == ns and len(pairs) == 0
-        slots_all[s] = slots
         lens_all[s] = [mgr.num_tokens(r) for r in rids]
     tables, _ = mgr.dense_tables(rids, max_blocks, pad=0)
     d_tables = torch.from_numpy(tables).to(dev)
-    d_slots = torch.from_numpy(slots_all).to(dev)
     d_lens = torch.from_numpy(lens_all).to(dev)
     g = torch.Generator(device=dev).manual_seed(99 + rank)
     q = torch.randn((L, ns, nh, D), generator=g, device=dev).to(tdt)
@@ -258,28 +256,24 @@ def run_ours(args, cfg, rank, world, dev):
     ws = torch.zeros(max(kvb.workspace_bytes(a0), 256), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
-    # Launch arguments are built once; a step only repoints the slots / lengths (so the timed loop measures
-    # the kernels, not Python).
+    # Launch arguments are built once; a step only repoints the lengths (so the timed loop measures the
+    # kernels, not Python).
     import ctypes
     L_lib = kvb.lib()
     attn_args = []
     for l in range(L):
         a = kvb.attention_args(q[l], kc[l], vc[l], d_tables, d_lens[0], out[l], nh, kvh, num_blocks=nb,
-                               split_tiles=split, status=status, warps_per_kv_head=args.wph, stages=args.stages)
+                               split_tiles=split, status=status, warps_per_kv_head=args.wph, stages=args.stages,
+                               k_new=knew[l], v_new=vnew[l])
         a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
         a.flags = kvb.KVP_ATTN_WORKSPACE_CLEAN  # zero-filled once; every call leaves the counters zero
         attn_args.append(a)
-    app = kvb.AppendArgs()
-    app.k_new, app.v_new, app.k_cache, app.v_cache = knew.data_ptr(), vnew.data_ptr(), kc.data_ptr(), vc.data_ptr()
-    app.layer_stride, app.kv_dtype, app.num_layers, app.num_seqs = nb * B * kvh * D, kvb._dtype_code(kc), L, ns
-    app.kv_heads, app.head_dim, app.block_size, app.num_blocks, app.status = kvh, D, B, nb, status.data_ptr()
     sptr = ctypes.c_void_p(stream.cuda_stream)
     lens_row = d_lens.stride(0) * 4
-    slots_row = d_slots.stride(0) * 4
+    # launches per layer: one (balanced schedule, or unsplit contexts), two with fixed splits (+ merge)
+    per_layer = 1 if split == 0 or split >= (max_blocks * B + 15) // 16 or split < 0 else 2
 
     def step_device(s, ev=None):
-        app.slots = d_slots.data_ptr() + s * slots_row
-        assert L_lib.kvp_append_scatter(ctypes.byref(app), sptr) == 0
         lp = d_lens.data_ptr() + s * lens_row
         for l in range(L):
             a = attn_args[l]
@@ -316,14 +310,14 @@ def run_ours(args, cfg, rank, world, dev):
         if world > 1:
             dist.all_reduce(vals, op=dist.ReduceOp.MAX)
         ms_total, e2e_ms, attn_avg = [float(x) for x in vals.cpu()]
-        gpu_launches = K * (1 + L * 2)
+        gpu_launches = K * L * per_layer
         return dict(ms_total=ms_total, e2e_ms=e2e_ms, attn_avg_ms=attn_avg, bytes_per_launch=bytes_per_launch,
                     clocks=clk.summary(), ns=ns, nb=nb, split=split, gpu_launches=gpu_launches, h2d=0, d2h=0,
                     lens_mean=float(lens.mean())), lens
 
     # ---------------------------------------------------------------- e2e through the C ABI, host buffers
     # One kvp_decoder_step per decode step: host KVManager appends, metadata upload, new K/V and per-layer
-    # queries copied in from pinned host memory, copy-on-write + scatter + attention for every layer, and
+    # queries copied in from pinned host memory, copy-on-write + fused append/attention for every layer, and
     # each layer's output copied back, with the copies overlapping the attention of other layers.
     h_q = torch.randn((L, ns, nh, D), generator=torch.Generator().manual_seed(5)).to(tdt).pin_memory()
     h_k = torch.randn((L, ns, kvh, D), generator=torch.Generator().manual_seed(6)).to(tdt).pin_memory()
@@ -349,7 +343,7 @@ def run_ours(args, cfg, rank, world, dev):
     # over the K steps is the end-to-end time (the events on the default stream bracket the same interval)
     e2e_ms = max(wall_ms, e0.elapsed_time(e1))
     assert dec.status() == 0
-    h2d = int(h_q.numel() * 2 + h_k.numel() * 2 + h_v.numel() * 2 + (ns * max_blocks + 2 * ns) * 4)
+    h2d = int(h_q.numel() * 2 + h_k.numel() * 2 + h_v.numel() * 2 + (ns * max_blocks + ns) * 4)
 
     # max over ranks (device-timed)
     vals = torch.tensor([ms_total, e2e_ms, float(np.mean(attn_ms))], dtype=torch.float64, device=dev)
@@ -357,7 +351,7 @@ def run_ours(args, cfg, rank, world, dev):
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
     ms_total, e2e_ms, attn_avg = [float(x) for x in vals.cpu()]
     clocks = clk.summary()
-    gpu_launches = K * (1 + L * (2 if split == 0 or split < (max_blocks * B + 15) // 16 else 1))
+    gpu_launches = K * L * per_layer  # the device-timed value region
     res = dict(ms_total=ms_total, e2e_ms=e2e_ms, attn_avg_ms=attn_avg, bytes_per_launch=bytes_per_launch,
                clocks=clocks, ns=ns, nb=nb, split=split, gpu_launches=gpu_launches,
                h2d=h2d, d2h=int(h_out.numel() * 2), lens_mean=float(lens.mean()))
@@ -391,7 +385,7 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     metric = "paged decode-attn achieved HBM TB/s & % peak; decode tok/s at 1/2/4/8 GPUs"
     reduced = " (reduced profiling case)" if (args.requests or args.layers) else ""
-    config = {"workload": f"{args.config}-shaped decode step: append scatter + paged decode attention, all layers"
+    config = {"workload": f"{args.config}-shaped decode step: fused append + paged decode attention, all layers"
                           + reduced,
               "heads": cfg["nh"], "kv_heads": cfg["kvh"], "head_dim": cfg["D"], "layers": cfg["L"],
               "block_size": cfg["B"], "requests_per_gpu": cfg["ns"], "lengths": list(cfg["lens"]),
@@ -452,7 +446,9 @@ def main():
             "hbm_tb_s": round(achieved / 1e3, 3), "pct_of_measured_peak": round(100 * achieved / peak_gbs, 1),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
                          "frac": round(achieved / peak_gbs, 4), "traffic": traffic,
-                         "kernel": "paged_decode_kernel (+ split merge)", "peak_source": peak_src},
+                         "kernel": ("paged_decode_streamk_kernel (fused append, in-kernel merge)" if res["split"] == 0
+                                    else "paged_decode_kernel (fused append; + split merge)"),
+                         "peak_source": peak_src},
             "e2e": {"value": round(ns_total / (e2e_ms_step / 1e3), 1), "unit": "tok/s",
                     "h2d_bytes_per_step": res["h2d"], "d2h_bytes_per_step": res["d2h"]},
             "gpu_launches": res["gpu_launches"], "clocks": res["clocks"],

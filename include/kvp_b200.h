@@ -83,6 +83,14 @@ typedef struct kvp_attn_args {
     int32_t* status; /* optional device word for KVP_STATUS_* bits */
     int32_t warps_per_kv_head; /* tuning, 0: automatic (consumer warps sharing one kv head's tiles) */
     int32_t flags;             /* KVP_ATTN_* bits */
+    /* Fused append (both or neither; 16-byte aligned): [num_seqs][kv_heads][head_dim] in the pool dtype, the
+     * K/V of each sequence's newest token -- position seq_lens[s] - 1, slot table[(len-1)/B]*B + (len-1)%B.
+     * The kernel writes them into the pools (which must then be writable) before it attends over them, so a
+     * decode step needs no separate kvp_append_scatter for this layer.  No other sequence of the call may
+     * read those slots: true after KVManager::append_token (the written block is never shared), not for
+     * several prompt positions of one request in one call. */
+    const void* k_new;
+    const void* v_new;
 } kvp_attn_args;
 
 /* The caller guarantees the workspace's counter words are zero, so the call skips resetting them: true for
@@ -221,10 +229,13 @@ KVP_API int kvp_mgr_dense_tables(kvp_mgr* m, const int64_t* rids, int32_t n, int
 /* ======================================================================== decode-step runtime
  * One call per decode step for one GPU shard: the device form of the reference harness's decode_batch
  * (python/paged_model.py:105-154).  For the given requests, in order: KVManager::append_token (through the
- * caller's kvp_mgr), the copy-on-write copies those appends decided, the append scatter of every layer's new
- * K/V, and paged attention for every layer over the updated cache.  The host-buffer form copies the inputs
- * in and the outputs out on its own streams so that transfers overlap the attention of other layers, and
- * returns once the outputs are in host memory (pinned host buffers make the copies asynchronous).
+ * caller's kvp_mgr), the copy-on-write copies those appends decided, then per layer one paged-attention
+ * launch that writes the layer's new K/V into the appended slot (fused append) and attends over the updated
+ * cache.  The host-buffer form copies each layer's inputs in and its output out on its own streams, so that
+ * transfers overlap the attention of other layers, and returns once the outputs are in host memory (pinned
+ * host buffers make the copies asynchronous).  With `graph` set, the per-layer launches of a step are
+ * captured once into a CUDA graph and replayed while the batch size and buffers stay the same (a step whose
+ * key repeats the previous step's is captured; a stream the caller is capturing is never captured into).
  * Device memory: the caller passes the pools and one workspace of kvp_decoder_workspace_size() bytes; the
  * decoder allocates no device memory (it allocates pinned host staging for tables and slots). */
 typedef struct kvp_decoder_config {
@@ -239,6 +250,7 @@ typedef struct kvp_decoder_config {
     void* v_cache;
     void* workspace; /* device, 256-byte aligned */
     size_t workspace_bytes;
+    int32_t graph;   /* 1: replay each step's per-layer launches as a CUDA graph (see above); 0: plain launches */
 } kvp_decoder_config;
 typedef struct kvp_decoder kvp_decoder;
 KVP_API size_t kvp_decoder_workspace_size(const kvp_decoder_config* c);
@@ -249,8 +261,8 @@ KVP_API void kvp_decoder_destroy(kvp_decoder* d);
  * state then reflects the appends that succeeded; nothing was launched). */
 KVP_API int kvp_decoder_step(kvp_decoder* d, const int64_t* rids, int32_t n, const void* q, const void* k_new,
                              const void* v_new, void* out);
-/* Same with device pointers, asynchronous on `stream` (only the host bookkeeping and the small table / slot
- * upload are done before returning). */
+/* Same with device pointers (k_new / v_new 16-byte aligned), asynchronous on `stream` (only the host
+ * bookkeeping and the small table upload are done before returning). */
 KVP_API int kvp_decoder_step_device(kvp_decoder* d, const int64_t* rids, int32_t n, const void* q,
                                     const void* k_new, const void* v_new, void* out, void* stream);
 /* OR of the KVP_STATUS_* bits the decoder's kernels reported so far (synchronises the decoder's streams). */

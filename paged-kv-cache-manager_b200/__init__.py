@@ -38,7 +38,7 @@ class AttnArgs(C.Structure):
                 ("num_seqs", _i32), ("num_heads", _i32), ("kv_heads", _i32), ("head_dim", _i32),
                 ("block_size", _i32), ("max_blocks", _i32), ("scale", _f32), ("split_tiles", _i32),
                 ("kv_heads_per_cta", _i32), ("stages", _i32), ("workspace", _vp), ("workspace_bytes", _sz),
-                ("status", _vp), ("warps_per_kv_head", _i32), ("flags", _i32)]
+                ("status", _vp), ("warps_per_kv_head", _i32), ("flags", _i32), ("k_new", _vp), ("v_new", _vp)]
 
 
 class AppendArgs(C.Structure):
@@ -65,7 +65,7 @@ class DecoderConfig(C.Structure):
                 ("block_size", _i32), ("kv_dtype", _i32), ("q_dtype", _i32), ("out_dtype", _i32),
                 ("num_blocks", _i64), ("layer_stride", _i64), ("max_seqs", _i32), ("max_blocks_per_seq", _i32),
                 ("split_tiles", _i32), ("k_cache", _vp), ("v_cache", _vp), ("workspace", _vp),
-                ("workspace_bytes", _sz)]
+                ("workspace_bytes", _sz), ("graph", _i32)]
 
 
 # (name, restype, argtypes) of every C-ABI entry point in include/kvp_b200.h.
@@ -349,8 +349,9 @@ def _stream_ptr(stream):
 
 def attention_args(q, k_cache, v_cache, block_tables, seq_lens, out, num_heads, kv_heads, *, num_blocks=None,
                    workspace=None, split_tiles=0, kv_heads_per_cta=0, stages=0, status=None, scale=0.0,
-                   warps_per_kv_head=0) -> AttnArgs:
-    """AttnArgs for one layer; k_cache/v_cache are [num_blocks][B][kv_heads][D] (or views of them)."""
+                   warps_per_kv_head=0, k_new=None, v_new=None) -> AttnArgs:
+    """AttnArgs for one layer; k_cache/v_cache are [num_blocks][B][kv_heads][D] (or views of them).  With
+    k_new/v_new ([num_seqs][kv_heads][D], pool dtype) the kernel first writes each sequence's newest token."""
     nb, B, kvh, D = k_cache.shape[-4:]
     assert kvh == kv_heads
     a = AttnArgs()
@@ -366,6 +367,13 @@ def attention_args(q, k_cache, v_cache, block_tables, seq_lens, out, num_heads, 
     if workspace is not None:
         a.workspace, a.workspace_bytes = _dev(workspace, "workspace"), workspace.numel() * workspace.element_size()
     a.status = _dev(status, "status") if status is not None else None
+    if (k_new is None) != (v_new is None):
+        raise ValueError("k_new and v_new go together")
+    if k_new is not None:
+        for t, name in ((k_new, "k_new"), (v_new, "v_new")):
+            if tuple(t.shape) != (q.shape[0], kv_heads, D) or t.dtype != k_cache.dtype or not t.is_contiguous():
+                raise ValueError(f"{name} must be a contiguous [num_seqs][kv_heads][head_dim] tensor in the pool dtype")
+        a.k_new, a.v_new = _dev(k_new, "k_new"), _dev(v_new, "v_new")
     return a
 
 
@@ -375,15 +383,17 @@ def workspace_bytes(args: AttnArgs) -> int:
 
 def paged_attention(q, k_cache, v_cache, block_tables, seq_lens, num_heads: int, kv_heads: int, *, out=None,
                     out_dtype=None, workspace=None, split_tiles: int = 0, kv_heads_per_cta: int = 0, stages: int = 0,
-                    status=None, stream=None, num_blocks: Optional[int] = None, warps_per_kv_head: int = 0):
+                    status=None, stream=None, num_blocks: Optional[int] = None, warps_per_kv_head: int = 0,
+                    k_new=None, v_new=None):
     """Decode attention through the C ABI (kvp_paged_attention).  Allocates `out` (and a workspace when
-    none is given and the context will be split) with torch if not provided."""
+    none is given and the context will be split) with torch if not provided.  k_new/v_new: fused append of
+    each sequence's newest token (position seq_lens[s] - 1) before attending."""
     import torch
     if out is None:
         out = torch.empty(q.shape, dtype=out_dtype or q.dtype, device=q.device)
     a = attention_args(q, k_cache, v_cache, block_tables, seq_lens, out, num_heads, kv_heads, num_blocks=num_blocks,
                        workspace=workspace, split_tiles=split_tiles, kv_heads_per_cta=kv_heads_per_cta,
-                       stages=stages, status=status, warps_per_kv_head=warps_per_kv_head)
+                       stages=stages, status=status, warps_per_kv_head=warps_per_kv_head, k_new=k_new, v_new=v_new)
     if workspace is None and split_tiles >= 0:
         need = workspace_bytes(a)
         if need:
@@ -453,12 +463,13 @@ def host_slot_bytes(num_layers: int, block_size: int, kv_heads: int, head_dim: i
 
 # ============================================================================ decode-step runtime
 class Decoder:
-    """kvp_decoder: one call per decode step for one GPU shard (appends through `mgr`, copy-on-write, append
-    scatter and attention for every layer).  k_cache / v_cache: [L][num_blocks][B][kv_heads][D] device pools.
-    The workspace is allocated here with torch unless one is passed."""
+    """kvp_decoder: one call per decode step for one GPU shard (appends through `mgr`, copy-on-write, and a
+    fused append + attention launch for every layer).  k_cache / v_cache: [L][num_blocks][B][kv_heads][D]
+    device pools.  The workspace is allocated here with torch unless one is passed.  graph: replay a step's
+    launches as a CUDA graph while the batch size and buffers repeat."""
 
     def __init__(self, mgr: "KVManager", k_cache, v_cache, num_heads: int, max_seqs: int, max_blocks_per_seq: int,
-                 q_dtype=None, out_dtype=None, split_tiles: int = 0, workspace=None):
+                 q_dtype=None, out_dtype=None, split_tiles: int = 0, workspace=None, graph: bool = True):
         import torch
         L, nb, B, kvh, D = k_cache.shape
         c = DecoderConfig()
@@ -469,6 +480,7 @@ class Decoder:
         c.num_blocks, c.layer_stride = nb, nb * B * kvh * D
         c.max_seqs, c.max_blocks_per_seq, c.split_tiles = max_seqs, max_blocks_per_seq, split_tiles
         c.k_cache, c.v_cache = _dev(k_cache, "k_cache"), _dev(v_cache, "v_cache")
+        c.graph = 1 if graph else 0
         self._L = lib()
         need = int(self._L.kvp_decoder_workspace_size(C.byref(c)))
         if need == 0:

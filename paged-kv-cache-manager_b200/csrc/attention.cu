@@ -68,6 +68,13 @@ struct AttnParams {
     uint32_t pre_off;      // stream-K: offset of the prefix sums in dynamic smem
     int oob_row;           // a row coordinate outside the tensor map (zero fill) used for skipped blocks
     float sl2;             // scale * log2(e)
+    // Fused append (null when off): [num_seqs][kvh][D] K/V of each sequence's newest token, written into the
+    // pools at position len - 1 before the tile that holds it is loaded.
+    const void* k_new;
+    const void* v_new;
+    void* k_pool;
+    void* v_pool;
+    int kvh;
 };
 
 // Sequence length in 16-token tiles, or 0 when the length is invalid (len < 1 or more blocks than a
@@ -128,6 +135,35 @@ __device__ __forceinline__ void produce_tile(const AttnParams& p, const CUtensor
             }
         }
     }
+}
+
+// Fused append: the producer warp writes the newest token's K and V rows of the CTA's kv heads (position
+// len - 1, one contiguous kvh_cta * D run per pool) before it issues the copies of the segment holding that
+// position.  Each lane fences its stores against the async proxy and the warp synchronises, so the TMA loads
+// issued afterwards by any lane see the new rows.  An out-of-range block id is skipped here (the tile load
+// reports it and zero-fills).
+template <int D>
+__device__ __forceinline__ void append_new_token(const AttnParams& p, int seq, int len, const int32_t* trow, int kvh0,
+                                                 int lane) {
+    const int pos = len - 1;
+    const int bi = pos / p.B;
+    const int32_t blk = __ldg(trow + bi);
+    if (blk >= 0 && blk < p.num_blocks) {
+        const size_t row = static_cast<size_t>(blk) * p.B + (pos - bi * p.B);
+        const size_t src = (static_cast<size_t>(seq) * p.kvh + kvh0) * D / 8;  // 16-byte chunks
+        const size_t dst = (row * p.kvh + kvh0) * D / 8;
+        const uint4* ks = static_cast<const uint4*>(p.k_new) + src;
+        const uint4* vs = static_cast<const uint4*>(p.v_new) + src;
+        uint4* kd = static_cast<uint4*>(p.k_pool) + dst;
+        uint4* vd = static_cast<uint4*>(p.v_pool) + dst;
+        const int chunks = p.kvh_cta * D / 8;
+        for (int c = lane; c < chunks; c += 32) {
+            kd[c] = __ldg(ks + c);
+            vd[c] = __ldg(vs + c);
+        }
+    }
+    fence_proxy_async_global();
+    __syncwarp();
 }
 
 // Up to 8 consecutive tiles of one sequence at once, lane k producing tile `tile + k` into stage
@@ -594,6 +630,7 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
                     bulk_load(smem_base + p.q_off + static_cast<uint32_t>(slot) * p.q_area, src, q_bytes, qb);
                 }
             }
+            if (p.k_new != nullptr && sg.tile1 == ((len + 15) >> 4)) append_new_token<D>(p, sg.seq, len, trow, kvh0, lane);
             // One run per tile: issue in batches of up to 8 tiles (one per lane); else one tile at a time.
             const int nb_max = p.nruns == 1 ? min(8, S) : 1;
             for (int tile = sg.tile0; tile < sg.tile1;) {
@@ -1252,6 +1289,11 @@ extern "C" KVP_API int kvp_paged_attention(const kvp_attn_args* a, void* stream)
     if (a->num_seqs > 0 && (!a->q || !a->k_cache || !a->v_cache || !a->block_tables || !a->seq_lens || !a->out))
         return fail(KVP_EINVAL, "null buffer");
     if (!aligned16(a->k_cache) || !aligned16(a->v_cache)) return fail(KVP_EINVAL, "K/V pools must be 16-byte aligned");
+    if ((a->k_new == nullptr) != (a->v_new == nullptr)) return fail(KVP_EINVAL, "k_new and v_new go together");
+    if (a->k_new) {
+        if (!aligned16(a->k_new) || !aligned16(a->v_new)) return fail(KVP_EINVAL, "k_new / v_new must be 16-byte aligned");
+        if (a->num_blocks <= 0) return fail(KVP_EINVAL, "the fused append needs num_blocks (it bounds the written slot)");
+    }
     AttnPlan pl;
     int rc = plan_attention(*a, a->workspace != nullptr, &pl);
     if (rc != KVP_OK) return rc;
@@ -1324,6 +1366,11 @@ extern "C" KVP_API int kvp_paged_attention(const kvp_attn_args* a, void* stream)
     prm.pre_off = pl.pre_off;
     prm.wph = pl.wph;
     prm.oob_row = static_cast<int>(std::min<long long>(rows, 0x7fffffffLL));
+    prm.k_new = a->k_new;
+    prm.v_new = a->v_new;
+    prm.k_pool = const_cast<void*>(a->k_cache);
+    prm.v_pool = const_cast<void*>(a->v_cache);
+    prm.kvh = a->kv_heads;
     const float scale = a->scale > 0.f ? a->scale : 1.0f / std::sqrt(static_cast<float>(a->head_dim));
     prm.sl2 = scale * 1.4426950408889634f;
     cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -1,9 +1,10 @@
 // Decode-step runtime: one call per step for one GPU shard (the device form of the reference harness's
 // decode_batch, python/paged_model.py:105-154).
 //
-// Per step: host bookkeeping (KVManager::append_token per request -> write slots and copy-on-write pairs,
-// dense table rows, lengths), one upload of that metadata, then on the compute stream: copy-on-write copies,
-// the append scatter of every layer's new K/V, and paged attention per layer.  With host buffers, a copy-in
+// Per step: host bookkeeping (KVManager::append_token per request -> copy-on-write pairs,
+// dense table rows, lengths), one upload of that metadata, then on the compute stream: copy-on-write copies
+// and one paged-attention launch per layer that first writes the layer's new K/V into the appended slot
+// (fused append) and then attends over the context including it.  With host buffers, a copy-in
 // stream feeds the new K/V and each layer's queries and a copy-out stream drains each layer's output as soon as
 // its attention finishes, so transfers overlap the attention of other layers.
 #include <cuda_runtime.h>
@@ -26,7 +27,7 @@ size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 int elem(int dt) { return dt == KVP_DTYPE_F32 ? 4 : 2; }
 
 struct Layout {
-    size_t meta = 0;        // [tables max_seqs*max_blocks][lens][slots][pairs 2*max_seqs] int32
+    size_t meta = 0;        // [tables max_seqs*max_blocks][lens][pairs 2*max_seqs] int32
     size_t status = 0;      // int32
     size_t attn = 0;        // split partials
     size_t q = 0, k = 0, v = 0, out = 0;  // host-path staging
@@ -39,7 +40,7 @@ Layout layout_of(const kvp_decoder_config& c) {
     const size_t ns = static_cast<size_t>(c.max_seqs);
     size_t o = 0;
     L.meta = o;
-    o = align256(o + sizeof(int32_t) * (ns * static_cast<size_t>(c.max_blocks_per_seq) + 4 * ns));
+    o = align256(o + sizeof(int32_t) * (ns * static_cast<size_t>(c.max_blocks_per_seq) + 3 * ns));
     L.status = o;
     o = align256(o + sizeof(int32_t));
     L.attn = o;
@@ -88,6 +89,17 @@ int check_config(const kvp_decoder_config* c) {
 
 }  // namespace
 
+// What a captured step depends on besides the device-resident metadata: the batch size (it fixes the
+// metadata layout and the kernels' parameters), the per-layer buffers and whether per-layer events are used.
+struct GraphKey {
+    int n = -1;
+    const void *q = nullptr, *k = nullptr, *v = nullptr, *out = nullptr;
+    bool events = false;
+    bool operator==(const GraphKey& o) const {
+        return n == o.n && q == o.q && k == o.k && v == o.v && out == o.out && events == o.events;
+    }
+};
+
 struct kvp_decoder {
     kvp_decoder_config cfg{};
     kvp_mgr* mgr = nullptr;
@@ -101,8 +113,12 @@ struct kvp_decoder {
     std::vector<cudaEvent_t> ev_q, ev_att;
     std::vector<int32_t> pairs;
     int device = 0;
+    GraphKey last_key, exec_key;  // the previous step's key; the key the instantiated graph was captured for
+    cudaGraphExec_t exec = nullptr;
+    bool graph_off = false;       // set when a capture failed: plain launches from then on
 
     ~kvp_decoder() {
+        if (exec) cudaGraphExecDestroy(exec);
         if (h_meta) cudaFreeHost(h_meta);
         for (auto e : ev_q) cudaEventDestroy(e);
         for (auto e : ev_att) cudaEventDestroy(e);
@@ -118,15 +134,14 @@ struct kvp_decoder {
 
 namespace {
 
-// Host bookkeeping of a step: appends, slots, copy-on-write pairs, table rows and lengths into the pinned
-// staging.  Returns KVP_OK or KVP_ENOSPACE (an append found no block).
+// Host bookkeeping of a step: appends, copy-on-write pairs, table rows and lengths into the pinned staging
+// (the fused append derives each written slot from the table row and the length).  Returns KVP_OK or KVP_ENOSPACE (an append found no block).
 int host_step(kvp_decoder* d, const int64_t* rids, int n) {
     kvp::KVManager& m = d->mgr->m;
     const kvp_decoder_config& c = d->cfg;
     const int B = c.block_size, MB = c.max_blocks_per_seq;
     int32_t* tables = d->h_meta;
     int32_t* lens = tables + static_cast<size_t>(n) * MB;
-    int32_t* slots = lens + n;
     d->pairs.clear();
     for (int i = 0; i < n; ++i) {
         const kvp::BlockTable& t = m.table(rids[i]);
@@ -139,11 +154,10 @@ int host_step(kvp_decoder* d, const int64_t* rids, int n) {
         }
         if (static_cast<int>(t.blocks.size()) > MB)
             return kvpi::fail(KVP_EBOUNDS, "request " + std::to_string(rids[i]) + " outgrew max_blocks_per_seq");
-        slots[i] = t.blocks[static_cast<size_t>(pos / B)] * B + pos % B;
         lens[i] = t.tokens;
         std::memcpy(tables + static_cast<size_t>(i) * MB, t.blocks.data(), sizeof(int32_t) * t.blocks.size());
     }
-    std::memcpy(slots + n, d->pairs.data(), sizeof(int32_t) * d->pairs.size());
+    std::memcpy(lens + n, d->pairs.data(), sizeof(int32_t) * d->pairs.size());
     return KVP_OK;
 }
 
@@ -184,39 +198,24 @@ int launch_cow(kvp_decoder* d, const int32_t* d_pairs, cudaStream_t s) {
     return flush(npairs);
 }
 
-int enqueue_device(kvp_decoder* d, int n, const void* q, const void* knew, const void* vnew, void* out,
-                   cudaStream_t s_comp, bool per_layer_events) {
+// The per-layer launches of a step: fused append + attention for every layer, each waiting for its inputs
+// (per-layer events, host path) and marking its output ready.  `ext` marks the event operations as
+// external nodes when the stream is being captured into a graph.
+int enqueue_layers(kvp_decoder* d, int n, const void* q, const void* knew, const void* vnew, void* out,
+                   cudaStream_t s_comp, bool per_layer_events, bool ext) {
     const kvp_decoder_config& c = d->cfg;
     const int32_t* meta = d->d_meta();
     const int32_t* d_tables = meta;
     const int32_t* d_lens = meta + static_cast<size_t>(n) * c.max_blocks_per_seq;
-    const int32_t* d_slots = d_lens + n;
-    const int32_t* d_pairs = d_slots + n;
-    int rc = launch_cow(d, d_pairs, s_comp);
-    if (rc != KVP_OK) return rc;
-    kvp_append_args ap{};
-    ap.k_new = knew;
-    ap.v_new = vnew;
-    ap.k_cache = c.k_cache;
-    ap.v_cache = c.v_cache;
-    ap.layer_stride = d->layer_stride;
-    ap.slots = d_slots;
-    ap.kv_dtype = c.kv_dtype;
-    ap.num_layers = c.num_layers;
-    ap.num_seqs = n;
-    ap.kv_heads = c.kv_heads;
-    ap.head_dim = c.head_dim;
-    ap.block_size = c.block_size;
-    ap.num_blocks = c.num_blocks;
-    ap.status = d->d_status();
-    rc = kvp_append_scatter(&ap, s_comp);
-    if (rc != KVP_OK) return rc;
+    int rc = KVP_OK;
     const int split = c.split_tiles;  // 0: balanced schedule over the step's real context lengths
     const size_t kv_layer_bytes = static_cast<size_t>(d->layer_stride) * 2;
     const size_t q_layer = static_cast<size_t>(n) * c.num_heads * c.head_dim;
+    const size_t kv_layer = static_cast<size_t>(n) * c.kv_heads * c.head_dim * elem(c.kv_dtype);
     for (int l = 0; l < c.num_layers; ++l) {
         if (per_layer_events) {
-            cudaError_t e = cudaStreamWaitEvent(s_comp, d->ev_q[static_cast<size_t>(l)], 0);
+            cudaError_t e = cudaStreamWaitEvent(s_comp, d->ev_q[static_cast<size_t>(l)],
+                                                ext ? cudaEventWaitExternal : cudaEventWaitDefault);
             if (e != cudaSuccess) return kvpi::cuda_status(e, "decoder wait");
         }
         kvp_attn_args a{};
@@ -241,18 +240,75 @@ int enqueue_device(kvp_decoder* d, int n, const void* q, const void* knew, const
         a.workspace_bytes = d->lay.attn_bytes;
         a.status = d->d_status();
         a.flags = KVP_ATTN_WORKSPACE_CLEAN;
+        a.k_new = static_cast<const char*>(knew) + kv_layer * l;  // fused append of this layer's new token
+        a.v_new = static_cast<const char*>(vnew) + kv_layer * l;
         rc = kvp_paged_attention(&a, s_comp);
         if (rc != KVP_OK) return rc;
         if (per_layer_events) {
-            cudaError_t e = cudaEventRecord(d->ev_att[static_cast<size_t>(l)], s_comp);
+            cudaError_t e = cudaEventRecordWithFlags(d->ev_att[static_cast<size_t>(l)], s_comp,
+                                                     ext ? cudaEventRecordExternal : cudaEventRecordDefault);
             if (e != cudaSuccess) return kvpi::cuda_status(e, "decoder record");
         }
     }
     return KVP_OK;
 }
 
+// Captures the per-layer launches into a graph and instantiates it.  Returns false (with the capture ended
+// and the error state cleared) if anything failed; the caller then launches them directly.
+bool capture_layers(kvp_decoder* d, const GraphKey& key, cudaStream_t s) {
+    if (cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    const int rc = enqueue_layers(d, key.n, key.q, key.k, key.v, const_cast<void*>(key.out), s, key.events, true);
+    cudaGraph_t g = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(s, &g);
+    cudaGraphExec_t ex = nullptr;
+    const bool ok = rc == KVP_OK && e == cudaSuccess && g && cudaGraphInstantiate(&ex, g, 0) == cudaSuccess;
+    if (g) cudaGraphDestroy(g);
+    if (!ok) {
+        if (ex) cudaGraphExecDestroy(ex);
+        cudaGetLastError();
+        kvpi::clear_error();
+        return false;
+    }
+    if (d->exec) cudaGraphExecDestroy(d->exec);
+    d->exec = ex;
+    d->exec_key = key;
+    return true;
+}
+
+int enqueue_device(kvp_decoder* d, int n, const void* q, const void* knew, const void* vnew, void* out,
+                   cudaStream_t s_comp, bool per_layer_events) {
+    const kvp_decoder_config& c = d->cfg;
+    const int32_t* d_pairs = d->d_meta() + static_cast<size_t>(n) * c.max_blocks_per_seq + n;
+    int rc = launch_cow(d, d_pairs, s_comp);
+    if (rc != KVP_OK) return rc;
+    if (c.graph && !d->graph_off) {
+        GraphKey key;
+        key.n = n;
+        key.q = q;
+        key.k = knew;
+        key.v = vnew;
+        key.out = out;
+        key.events = per_layer_events;
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        // The legacy default stream cannot be captured; a stream the caller is capturing records our launches.
+        const bool capturable = s_comp != nullptr && cudaStreamIsCapturing(s_comp, &cs) == cudaSuccess &&
+                                cs == cudaStreamCaptureStatusNone;
+        if (capturable) {
+            const bool repeat = key == d->last_key;
+            d->last_key = key;
+            if (!(d->exec && d->exec_key == key) && repeat && !capture_layers(d, key, s_comp)) d->graph_off = true;
+            if (d->exec && d->exec_key == key)
+                return kvpi::cuda_status(cudaGraphLaunch(d->exec, s_comp), "decoder graph launch");
+        }
+    }
+    return enqueue_layers(d, n, q, knew, vnew, out, s_comp, per_layer_events, false);
+}
+
 int upload_meta(kvp_decoder* d, int n, cudaStream_t s) {
-    const size_t ints = static_cast<size_t>(n) * d->cfg.max_blocks_per_seq + 2 * static_cast<size_t>(n) + d->pairs.size();
+    const size_t ints = static_cast<size_t>(n) * d->cfg.max_blocks_per_seq + static_cast<size_t>(n) + d->pairs.size();
     cudaError_t e = cudaMemcpyAsync(d->d_meta(), d->h_meta, ints * sizeof(int32_t), cudaMemcpyHostToDevice, s);
     if (e != cudaSuccess) return kvpi::cuda_status(e, "decoder metadata upload");
     e = cudaEventRecord(d->ev_staged, s);
@@ -359,6 +415,7 @@ KVP_API int kvp_decoder_step_device(kvp_decoder* d, const int64_t* rids, int32_t
         if (!d || (n > 0 && (!rids || !q || !k_new || !v_new || !out))) return kvpi::fail(KVP_EINVAL, "null argument");
         if (n < 0 || n > d->cfg.max_seqs) return kvpi::fail(KVP_EINVAL, "n outside [0, max_seqs]");
         if (n == 0) return KVP_OK;
+        if (!kvpi::aligned16(k_new) || !kvpi::aligned16(v_new)) return kvpi::fail(KVP_EINVAL, "k_new / v_new must be 16-byte aligned");
         int rc = wait_staging(d);
         if (rc != KVP_OK) return rc;
         rc = host_step(d, rids, n);
@@ -383,20 +440,25 @@ KVP_API int kvp_decoder_step(kvp_decoder* d, const int64_t* rids, int32_t n, con
         if (rc != KVP_OK) return rc;
         const size_t q_layer = static_cast<size_t>(n) * c.num_heads * c.head_dim * elem(c.q_dtype);
         const size_t o_layer = static_cast<size_t>(n) * c.num_heads * c.head_dim * elem(c.out_dtype);
-        const size_t kv_all = static_cast<size_t>(c.num_layers) * n * c.kv_heads * c.head_dim * elem(c.kv_dtype);
+        const size_t kv_layer = static_cast<size_t>(n) * c.kv_heads * c.head_dim * elem(c.kv_dtype);
         char* dq = d->ws + d->lay.q;
         char* dk = d->ws + d->lay.k;
         char* dv = d->ws + d->lay.v;
         char* dout = d->ws + d->lay.out;
-        // copy-in stream: metadata, new K/V, then each layer's queries
+        // copy-in stream: metadata, then each layer's queries and new K/V (a layer's launch waits only for
+        // its own inputs)
         rc = upload_meta(d, n, d->s_in);
         if (rc != KVP_OK) return rc;
-        cudaError_t e = cudaMemcpyAsync(dk, k_new, kv_all, cudaMemcpyHostToDevice, d->s_in);
-        if (e == cudaSuccess) e = cudaMemcpyAsync(dv, v_new, kv_all, cudaMemcpyHostToDevice, d->s_in);
-        if (e == cudaSuccess) e = cudaEventRecord(d->ev_meta, d->s_in);
+        cudaError_t e = cudaEventRecord(d->ev_meta, d->s_in);
         for (int l = 0; e == cudaSuccess && l < c.num_layers; ++l) {
             e = cudaMemcpyAsync(dq + q_layer * l, static_cast<const char*>(q) + q_layer * l, q_layer,
                                 cudaMemcpyHostToDevice, d->s_in);
+            if (e == cudaSuccess)
+                e = cudaMemcpyAsync(dk + kv_layer * l, static_cast<const char*>(k_new) + kv_layer * l, kv_layer,
+                                    cudaMemcpyHostToDevice, d->s_in);
+            if (e == cudaSuccess)
+                e = cudaMemcpyAsync(dv + kv_layer * l, static_cast<const char*>(v_new) + kv_layer * l, kv_layer,
+                                    cudaMemcpyHostToDevice, d->s_in);
             if (e == cudaSuccess) e = cudaEventRecord(d->ev_q[static_cast<size_t>(l)], d->s_in);
         }
         if (e != cudaSuccess) return kvpi::cuda_status(e, "decoder input copies");

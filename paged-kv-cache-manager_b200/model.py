@@ -4,7 +4,8 @@ The device form of the reference's Python harness (python/paged_model.py:14-158 
 prathameshpranjale/paged-kv-cache-manager), with the same request API -- prefill / fork / decode /
 decode_batch / free -- and the same block bookkeeping (this library's KVManager).  What moves from torch to
 this library's kernels:
-  * writing each new token's K/V into its slot  -> kvp_append_scatter   (paged_model.py:54-55, 145-146)
+  * writing each new token's K/V into its slot  -> kvp_append_scatter for prompts (paged_model.py:54-55), fused
+                                                   into kvp_paged_attention for decode steps (paged_model.py:145-146)
   * the copy-on-write copy after a fork          -> kvp_cow_copy         (paged_model.py:92-95, 113-117)
   * attention over the context                   -> kvp_paged_attention  (paged_model.py:56-63, 147-151)
 Prefill attention uses the same decode kernel: prompt position p is a one-query sequence of length p + 1
@@ -62,9 +63,12 @@ class PagedEngine:
         return torch.tensor([table[p // B] * B + p % B for p in positions], dtype=torch.int32, device=self.dev)
 
     @torch.no_grad()
-    def _layers(self, h, positions: torch.Tensor, slots: torch.Tensor, tables: torch.Tensor, lens: torch.Tensor):
+    def _layers(self, h, positions: torch.Tensor, slots: Optional[torch.Tensor], tables: torch.Tensor,
+                lens: torch.Tensor):
         """Runs every layer for n query tokens (h: [1, n, H]); token i is at positions[i], writes its K/V to
-        slots[i] and attends over its context: tables[i] / lens[i]."""
+        slots[i] and attends over its context: tables[i] / lens[i].  With slots None (a decode step: every
+        token is the newest of its own request) the attention kernel writes the K/V itself (fused append);
+        otherwise (several prompt positions of one request read each other's slots) a scatter runs first."""
         kvb = _lib()
         mdl = self.m.model
         n = h.shape[1]
@@ -76,10 +80,13 @@ class PagedEngine:
             k = a.k_proj(x).view(1, n, self.kvh, self.hd).transpose(1, 2)
             v = a.v_proj(x).view(1, n, self.kvh, self.hd).transpose(1, 2)
             q, k = self._rope(q, k, cos, sin)
-            kvb.append_scatter(k[0].transpose(0, 1).contiguous()[None], v[0].transpose(0, 1).contiguous()[None],
-                               self.K[li:li + 1], self.V[li:li + 1], slots, status=self.status)
+            kn, vn = k[0].transpose(0, 1).contiguous(), v[0].transpose(0, 1).contiguous()
+            if slots is not None:
+                kvb.append_scatter(kn[None], vn[None], self.K[li:li + 1], self.V[li:li + 1], slots, status=self.status)
+                kn = vn = None
             o = kvb.paged_attention(q[0].transpose(0, 1).contiguous(), self.K[li], self.V[li], tables, lens, self.nh,
-                                    self.kvh, out_dtype=self.dtype, status=self.status, num_blocks=self.num_blocks)
+                                    self.kvh, out_dtype=self.dtype, status=self.status, num_blocks=self.num_blocks,
+                                    k_new=kn, v_new=vn)
             h = h + a.o_proj(o.reshape(1, n, self.nh * self.hd))
             h = h + layer.mlp(layer.post_attention_layernorm(h))
         return mdl.norm(h)
@@ -93,7 +100,7 @@ class PagedEngine:
         return t.to(self.dev)
 
     @torch.no_grad()
-    def _forward(self, rid: int, tokens: Sequence[int], start: int):
+    def _forward(self, rid: int, tokens: Sequence[int], start: int, fused: bool = False):
         """Tokens placed at positions start .. start+n-1 of request rid (the manager already holds them)."""
         n = len(tokens)
         total = start + n
@@ -104,7 +111,8 @@ class PagedEngine:
         tables = self._table_rows([ctx] * n)
         lens = torch.tensor([p + 1 for p in positions], dtype=torch.int32, device=self.dev)
         h = self.m.model.embed_tokens(torch.tensor(tokens, device=self.dev))[None]
-        h = self._layers(h, torch.tensor(positions, device=self.dev), self._slots(table, positions), tables, lens)
+        slots = None if fused else self._slots(table, positions)
+        h = self._layers(h, torch.tensor(positions, device=self.dev), slots, tables, lens)
         return self.m.lm_head(h[:, -1])[0]
 
     def _cow(self, pairs):
@@ -138,20 +146,20 @@ class PagedEngine:
         if done != 1:
             return None
         self._cow(pairs)  # before the new token is written into the copied block
-        return self._forward(rid, [last_token], before)
+        return self._forward(rid, [last_token], before, fused=True)
 
     @torch.no_grad()
     def decode_batch(self, rids: Sequence[int], last_tokens: Sequence[int]):
         """One decode step for several requests in one batched forward: logits [len(rids)][vocab]."""
         before = [self.kv.num_tokens(r) for r in rids]
-        done, slots, pairs = self.kv.append_batch(list(rids))
+        done, _, pairs = self.kv.append_batch(list(rids))
         if done != len(rids):
             raise RuntimeError("out of blocks in decode_batch")
         self._cow(pairs)
         tables = self._table_rows([self.kv.block_table(r)[: (p + self.B) // self.B] for r, p in zip(rids, before)])
         lens = torch.tensor([p + 1 for p in before], dtype=torch.int32, device=self.dev)
         h = self.m.model.embed_tokens(torch.tensor(list(last_tokens), device=self.dev))[None]
-        h = self._layers(h, torch.tensor(before, device=self.dev), torch.from_numpy(slots).to(self.dev), tables, lens)
+        h = self._layers(h, torch.tensor(before, device=self.dev), None, tables, lens)  # fused append
         return self.m.lm_head(h[0])
 
     def free(self, rid: int):

@@ -103,3 +103,28 @@ def test_decoder_config_validation(kvb):
     assert not L.kvp_decoder_create(C.byref(c), m.handle)  # no pools / workspace
     c.split_tiles = -1
     assert L.kvp_decoder_workspace_size(C.byref(c)) < n  # no split-K partials reserved
+
+
+def test_ctypes_struct_layouts_match_the_header(kvb, tmp_path):
+    """Every argument struct the Python binding passes has the header's field order, offsets and size
+    (the header compiled with gcc prints them)."""
+    structs = {"kvp_attn_args": kvb.AttnArgs, "kvp_append_args": kvb.AppendArgs, "kvp_cow_args": kvb.CowArgs,
+               "kvp_swap_args": kvb.SwapArgs, "kvp_decoder_config": kvb.DecoderConfig}
+    lines = ["#include <stdio.h>", "#include <stddef.h>", '#include "kvp_b200.h"', "int main(void) {"]
+    for cname, py in structs.items():
+        lines.append(f'printf("{cname} sizeof %zu\\n", sizeof({cname}));')
+        for field, _ in py._fields_:
+            lines.append(f'printf("{cname} {field} %zu\\n", offsetof({cname}, {field}));')
+    lines += ["return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c99", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    got = {}
+    for ln in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.splitlines():
+        s, f, v = ln.split()
+        got[(s, f)] = int(v)
+    for cname, py in structs.items():
+        assert got[(cname, "sizeof")] == C.sizeof(py), cname
+        for field, _ in py._fields_:
+            assert got[(cname, field)] == getattr(py, field).offset, (cname, field)

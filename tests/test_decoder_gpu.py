@@ -1,6 +1,7 @@
 """The decode-step runtime (kvp_decoder_*) produces exactly what the individual entry points produce when
 driven by hand (append batch -> copy-on-write -> append scatter -> attention per layer), with host buffers
-and with device buffers, and its attention output matches the oracle on the updated cache."""
+and with device buffers, with and without graph replay, and its attention output matches the oracle on the
+updated cache."""
 import numpy as np
 import pytest
 
@@ -32,17 +33,24 @@ def _manual_step(kvb, m, k, v, rids, q, kn, vn, split, max_blocks, nh, kvh):
     return out
 
 
+@pytest.mark.parametrize("graph", [True, False], ids=["graph", "launches"])
+@pytest.mark.parametrize("split", [2, 0], ids=["split2", "balanced"])
 @pytest.mark.parametrize("path", ["host", "device"])
-def test_decoder_matches_manual_path(kvb, cuda, path):
+def test_decoder_matches_manual_path(kvb, cuda, path, split, graph):
+    """Eight steps, the batch size changing once (a graph is captured on the second step of a repeated key and
+    replayed after it, then recaptured for the new size): outputs and pools equal the hand-driven two-launch
+    path (append scatter, then attention) bit for bit."""
     import torch
     nh, kvh, D, L, MB = 8, 2, 64, 4, 40
     k1, v1, m1 = _setup(kvb, 1)
     k2, v2, m2 = k1.clone(), v1.clone(), None
     _, _, m2 = _setup(kvb, 1)
-    dec = kvb.Decoder(m1, k1, v1, nh, max_seqs=8, max_blocks_per_seq=MB, split_tiles=2)
-    rids = [0, 1, 2, 3, 4]
+    dec = kvb.Decoder(m1, k1, v1, nh, max_seqs=8, max_blocks_per_seq=MB, split_tiles=split, graph=graph)
     rng = np.random.default_rng(3)
-    for step in range(6):
+    bufs = {}
+    side = torch.cuda.Stream()
+    for step in range(8):
+        rids = [0, 1, 2, 3, 4] if step < 5 else [0, 2, 4]
         order = [int(x) for x in rng.permutation(rids)]
         n = len(order)
         q = torch.randn((L, n, nh, D)).to(torch.bfloat16)
@@ -52,11 +60,15 @@ def test_decoder_matches_manual_path(kvb, cuda, path):
             out1 = torch.empty((L, n, nh, D), dtype=torch.bfloat16).pin_memory()
             dec.step(order, q.pin_memory(), kn.pin_memory(), vn.pin_memory(), out1)
         else:
-            out1 = torch.empty((L, n, nh, D), dtype=torch.bfloat16, device="cuda")
-            dec.step_device(order, q.cuda(), kn.cuda(), vn.cuda(), out1)
+            if n not in bufs:  # the same device buffers every step of one batch size
+                bufs[n] = [torch.empty(t.shape, dtype=t.dtype, device="cuda") for t in (q, kn, vn, q)]
+            dq, dk, dv, do = bufs[n]
+            dq.copy_(q), dk.copy_(kn), dv.copy_(vn)
+            side.wait_stream(torch.cuda.current_stream())
+            dec.step_device(order, dq, dk, dv, do, stream=side)  # a capturable (non-legacy) stream
             torch.cuda.synchronize()
-            out1 = out1.cpu()
-        out2 = _manual_step(kvb, m2, k2, v2, order, q.cuda(), kn.cuda(), vn.cuda(), 2, MB, nh, kvh)
+            out1 = do.cpu()
+        out2 = _manual_step(kvb, m2, k2, v2, order, q.cuda(), kn.cuda(), vn.cuda(), split, MB, nh, kvh)
         torch.cuda.synchronize()
         assert torch.equal(out1, out2.cpu()), step
         assert torch.equal(k1, k2) and torch.equal(v1, v2), step
