@@ -152,6 +152,32 @@ typedef struct kvp_cow_args {
 } kvp_cow_args;
 KVP_API int kvp_cow_copy(const kvp_cow_args* a, void* stream);
 
+/* Migration between shards: for each (src, dst) pair copies the whole block, every layer, K and V, from one
+ * shard's pools into another's -- on the same GPU, or from a peer GPU over NVLink with plain peer loads into
+ * the destination GPU's own memory.  Launch on the destination pools' device (the current device); peer
+ * access to the source device is enabled on first use (kvp_enable_peer_access).  pairs: device int32
+ * [n_pairs][2] on the destination device; destinations distinct.  The host side of migrating a request is
+ * the reference's swap semantics without the host round trip (src/simulator.cpp:117-133, 193, 231-241):
+ * admit it on the destination KVManager (fresh ids, no sharing), pair the source table with the new table
+ * entry by entry, copy, and free it on the source KVManager once the copy is ordered before any later
+ * source-side write (an event the source stream waits for). */
+typedef struct kvp_migrate_args {
+    const void* src_k_cache;
+    const void* src_v_cache;
+    int64_t src_layer_stride; /* elements; 0: contiguous */
+    int64_t src_num_blocks;
+    void* dst_k_cache;
+    void* dst_v_cache;
+    int64_t dst_layer_stride;
+    int64_t dst_num_blocks;
+    const int32_t* pairs;
+    int32_t n_pairs, kv_dtype, num_layers, kv_heads, head_dim, block_size;
+    int32_t* status;
+} kvp_migrate_args;
+KVP_API int kvp_migrate_blocks(const kvp_migrate_args* a, void* stream);
+/* Lets the current device read peer_device's memory (idempotent; KVP_EINVAL if the pair has no P2P path). */
+KVP_API int kvp_enable_peer_access(int32_t peer_device);
+
 /* Swap between the device pools and a pinned host pool.  A host slot holds one block of every layer:
  * [K: num_layers x block_bytes][V: num_layers x block_bytes], block_bytes = block_size*kv_heads*head_dim*elem.
  * blocks / host_slots are HOST arrays of length n; host_pool is pinned (cudaHostAlloc / registered) memory

@@ -53,6 +53,13 @@ class CowArgs(C.Structure):
                 ("block_size", _i32), ("num_blocks", _i64), ("status", _vp)]
 
 
+class MigrateArgs(C.Structure):
+    _fields_ = [("src_k_cache", _vp), ("src_v_cache", _vp), ("src_layer_stride", _i64), ("src_num_blocks", _i64),
+                ("dst_k_cache", _vp), ("dst_v_cache", _vp), ("dst_layer_stride", _i64), ("dst_num_blocks", _i64),
+                ("pairs", _vp), ("n_pairs", _i32), ("kv_dtype", _i32), ("num_layers", _i32), ("kv_heads", _i32),
+                ("head_dim", _i32), ("block_size", _i32), ("status", _vp)]
+
+
 class SwapArgs(C.Structure):
     _fields_ = [("k_cache", _vp), ("v_cache", _vp), ("layer_stride", _i64), ("kv_dtype", _i32),
                 ("num_layers", _i32), ("kv_heads", _i32), ("head_dim", _i32), ("block_size", _i32),
@@ -77,6 +84,8 @@ _SIGNATURES = [
     ("kvp_paged_attention_noalloc", C.c_int, [C.POINTER(AttnArgs), _vp]),
     ("kvp_append_scatter", C.c_int, [C.POINTER(AppendArgs), _vp]),
     ("kvp_cow_copy", C.c_int, [C.POINTER(CowArgs), _vp]),
+    ("kvp_migrate_blocks", C.c_int, [C.POINTER(MigrateArgs), _vp]),
+    ("kvp_enable_peer_access", C.c_int, [_i32]),
     ("kvp_swap_out", C.c_int, [C.POINTER(SwapArgs), _vp]),
     ("kvp_swap_in", C.c_int, [C.POINTER(SwapArgs), _vp]),
     ("kvp_mgr_create", _vp, [_i32, _i32]),
@@ -340,6 +349,29 @@ def _dev(t, name):
     return t.data_ptr()
 
 
+def _same_device(*named):
+    """All given tensors (None skipped) on one CUDA device; returns it.  Launches go to that device."""
+    dev = None
+    for name, t in named:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError(f"{name} must be a CUDA tensor (the library has no CPU path)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError(f"{name} is on {t.device}, the other operands on {dev}")
+    return dev
+
+
+def _launch(device, fn, args, stream):
+    """Calls a C-ABI launcher with `device` current (the library launches on the current device) on `stream`
+    (default: that device's current stream)."""
+    import torch
+    with torch.cuda.device(device):
+        _check(fn(C.byref(args), _stream_ptr(stream)))
+
+
 def _stream_ptr(stream):
     import torch
     if stream is None:
@@ -389,6 +421,9 @@ def paged_attention(q, k_cache, v_cache, block_tables, seq_lens, num_heads: int,
     none is given and the context will be split) with torch if not provided.  k_new/v_new: fused append of
     each sequence's newest token (position seq_lens[s] - 1) before attending."""
     import torch
+    dev = _same_device(("q", q), ("k_cache", k_cache), ("v_cache", v_cache), ("block_tables", block_tables),
+                       ("seq_lens", seq_lens), ("out", out), ("workspace", workspace), ("status", status),
+                       ("k_new", k_new), ("v_new", v_new))
     if out is None:
         out = torch.empty(q.shape, dtype=out_dtype or q.dtype, device=q.device)
     a = attention_args(q, k_cache, v_cache, block_tables, seq_lens, out, num_heads, kv_heads, num_blocks=num_blocks,
@@ -400,7 +435,7 @@ def paged_attention(q, k_cache, v_cache, block_tables, seq_lens, num_heads: int,
             workspace = torch.zeros(need, dtype=torch.uint8, device=q.device)
             a.workspace, a.workspace_bytes = workspace.data_ptr(), need
             a.flags |= KVP_ATTN_WORKSPACE_CLEAN
-    _check(lib().kvp_paged_attention(C.byref(a), _stream_ptr(stream)))
+    _launch(dev, lib().kvp_paged_attention, a, stream)
     return out
 
 
@@ -414,7 +449,9 @@ def append_scatter(k_new, v_new, k_cache, v_cache, slots, *, status=None, stream
     a.kv_dtype, a.num_layers, a.num_seqs = _dtype_code(k_cache), L, slots.shape[0]
     a.kv_heads, a.head_dim, a.block_size, a.num_blocks = kvh, D, B, nb
     a.status = _dev(status, "status") if status is not None else None
-    _check(lib().kvp_append_scatter(C.byref(a), _stream_ptr(stream)))
+    dev = _same_device(("k_new", k_new), ("v_new", v_new), ("k_cache", k_cache), ("v_cache", v_cache),
+                       ("slots", slots), ("status", status))
+    _launch(dev, lib().kvp_append_scatter, a, stream)
 
 
 def cow_copy(k_cache, v_cache, pairs, *, status=None, stream=None):
@@ -426,7 +463,8 @@ def cow_copy(k_cache, v_cache, pairs, *, status=None, stream=None):
     a.kv_dtype, a.num_layers, a.kv_heads, a.head_dim, a.block_size, a.num_blocks = (
         _dtype_code(k_cache), L, kvh, D, B, nb)
     a.status = _dev(status, "status") if status is not None else None
-    _check(lib().kvp_cow_copy(C.byref(a), _stream_ptr(stream)))
+    dev = _same_device(("k_cache", k_cache), ("v_cache", v_cache), ("pairs", pairs), ("status", status))
+    _launch(dev, lib().kvp_cow_copy, a, stream)
 
 
 def _swap(fn, k_cache, v_cache, blocks, host_slots, host_pool, stream):
@@ -444,7 +482,51 @@ def _swap(fn, k_cache, v_cache, blocks, host_slots, host_pool, stream):
     a.host_pool = host_pool.data_ptr()
     a.host_pool_slots = host_pool.numel() * host_pool.element_size() // host_slot_bytes(L, B, kvh, D,
                                                                                          k_cache.element_size())
-    _check(fn(C.byref(a), _stream_ptr(stream)))
+    _launch(_same_device(("k_cache", k_cache), ("v_cache", v_cache)), fn, a, stream)
+
+
+def migrate_blocks(src_k, src_v, dst_k, dst_v, pairs, *, status=None, stream=None):
+    """Whole-block copies from one shard's pools [L][nb][B][kvh][D] into another's (same or peer GPU), on a
+    stream of the destination device.  pairs: int32 [n][2] (src block, dst block) on the destination device."""
+    L, snb, B, kvh, D = src_k.shape
+    dnb = dst_k.shape[1]
+    if dst_k.shape[0] != L or tuple(dst_k.shape[2:]) != (B, kvh, D) or dst_k.dtype != src_k.dtype:
+        raise ValueError("source and destination pools differ in shape or dtype")
+    a = MigrateArgs()
+    a.src_k_cache, a.src_v_cache = _dev(src_k, "src_k"), _dev(src_v, "src_v")
+    a.dst_k_cache, a.dst_v_cache = _dev(dst_k, "dst_k"), _dev(dst_v, "dst_v")
+    a.src_layer_stride, a.src_num_blocks = snb * B * kvh * D, snb
+    a.dst_layer_stride, a.dst_num_blocks = dnb * B * kvh * D, dnb
+    a.pairs, a.n_pairs = _dev(pairs, "pairs"), pairs.shape[0]
+    a.kv_dtype, a.num_layers, a.kv_heads, a.head_dim, a.block_size = _dtype_code(src_k), L, kvh, D, B
+    a.status = _dev(status, "status") if status is not None else None
+    _same_device(("src_k", src_k), ("src_v", src_v))
+    dev = _same_device(("dst_k", dst_k), ("dst_v", dst_v), ("pairs", pairs), ("status", status))
+    _launch(dev, lib().kvp_migrate_blocks, a, stream)
+
+
+def migrate_request(src_mgr: "KVManager", src_k, src_v, dst_mgr: "KVManager", dst_k, dst_v, rid: int,
+                    dst_rid: Optional[int] = None, *, status=None, stream=None, src_stream=None) -> bool:
+    """Moves request `rid` from one shard to another: admitted on the destination manager with fresh blocks
+    (as `dst_rid`, default the same id), its blocks copied over (kvp_migrate_blocks on `stream`, a stream of
+    the destination device), then freed on the source manager.  The source stream (default: the source
+    device's current stream) waits for the copy, so later source-side writes into the freed blocks cannot
+    overtake it.  Returns False, changing nothing, if the destination has no room."""
+    import numpy as np
+    import torch
+    dst_rid = rid if dst_rid is None else dst_rid
+    tokens = src_mgr.num_tokens(rid)
+    if not dst_mgr.admit(dst_rid, tokens):
+        return False
+    src_tbl, dst_tbl = src_mgr.block_table(rid), dst_mgr.block_table(dst_rid)
+    pairs = torch.from_numpy(np.asarray([src_tbl, dst_tbl], dtype=np.int32).T.copy()).to(dst_k.device)
+    stream = stream or torch.cuda.current_stream(dst_k.device)
+    migrate_blocks(src_k, src_v, dst_k, dst_v, pairs, status=status, stream=stream)
+    ev = torch.cuda.Event()
+    ev.record(stream)
+    (src_stream or torch.cuda.current_stream(src_k.device)).wait_event(ev)
+    src_mgr.free(rid)
+    return True
 
 
 def swap_out(k_cache, v_cache, blocks, host_slots, host_pool, *, stream=None):
@@ -489,7 +571,8 @@ class Decoder:
             workspace = torch.empty(need, dtype=torch.uint8, device=k_cache.device)
         c.workspace, c.workspace_bytes = _dev(workspace, "workspace"), workspace.numel() * workspace.element_size()
         self._ws, self._k, self._v, self._mgr, self.cfg = workspace, k_cache, v_cache, mgr, c
-        h = self._L.kvp_decoder_create(C.byref(c), mgr.handle)
+        with torch.cuda.device(k_cache.device):
+            h = self._L.kvp_decoder_create(C.byref(c), mgr.handle)
         if not h:
             raise KVPError(KVP_EINVAL, last_error())
         self._h = C.c_void_p(h)

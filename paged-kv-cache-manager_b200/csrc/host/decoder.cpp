@@ -318,6 +318,18 @@ int upload_meta(kvp_decoder* d, int n, cudaStream_t s) {
 // The pinned staging may still be read by the previous step's upload.
 int wait_staging(kvp_decoder* d) { return kvpi::cuda_status(cudaEventSynchronize(d->ev_staged), "decoder staging wait"); }
 
+// Makes the decoder's device current for the scope of a call (its streams, events and launches belong to it).
+struct DeviceScope {
+    int prev = -1;
+    explicit DeviceScope(int dev) {
+        if (cudaGetDevice(&prev) == cudaSuccess && prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceScope() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
 template <class F>
 int guarded(F&& f) {
     kvpi::clear_error();
@@ -354,6 +366,17 @@ KVP_API kvp_decoder* kvp_decoder_create(const kvp_decoder_config* c, kvp_mgr* mg
         const long long max_tiles = (static_cast<long long>(c->max_blocks_per_seq) * c->block_size + 15) / 16;
         if ((max_tiles + c->split_tiles - 1) / c->split_tiles > kMaxSplitsCap) {
             kvpi::fail(KVP_EINVAL, "split_tiles gives more than 64 splits per sequence; raise it or pass 0");
+            return nullptr;
+        }
+    }
+    {
+        int cur = -1;
+        cudaPointerAttributes at{};
+        const bool ok_dev = cudaGetDevice(&cur) == cudaSuccess && cudaPointerGetAttributes(&at, c->k_cache) == cudaSuccess &&
+                            at.type == cudaMemoryTypeDevice && at.device == cur;
+        if (!ok_dev) {
+            cudaGetLastError();
+            kvpi::fail(KVP_EINVAL, "the pools must be device memory of the current device");
             return nullptr;
         }
     }
@@ -403,6 +426,7 @@ KVP_API kvp_decoder* kvp_decoder_create(const kvp_decoder_config* c, kvp_mgr* mg
 
 KVP_API void kvp_decoder_destroy(kvp_decoder* d) {
     if (!d) return;
+    DeviceScope scope(d->device);
     cudaStreamSynchronize(d->s_in);
     cudaStreamSynchronize(d->s_comp);
     cudaStreamSynchronize(d->s_out);
@@ -415,6 +439,7 @@ KVP_API int kvp_decoder_step_device(kvp_decoder* d, const int64_t* rids, int32_t
         if (!d || (n > 0 && (!rids || !q || !k_new || !v_new || !out))) return kvpi::fail(KVP_EINVAL, "null argument");
         if (n < 0 || n > d->cfg.max_seqs) return kvpi::fail(KVP_EINVAL, "n outside [0, max_seqs]");
         if (n == 0) return KVP_OK;
+        DeviceScope scope(d->device);
         if (!kvpi::aligned16(k_new) || !kvpi::aligned16(v_new)) return kvpi::fail(KVP_EINVAL, "k_new / v_new must be 16-byte aligned");
         int rc = wait_staging(d);
         if (rc != KVP_OK) return rc;
@@ -433,6 +458,7 @@ KVP_API int kvp_decoder_step(kvp_decoder* d, const int64_t* rids, int32_t n, con
         if (!d || (n > 0 && (!rids || !q || !k_new || !v_new || !out))) return kvpi::fail(KVP_EINVAL, "null argument");
         if (n < 0 || n > d->cfg.max_seqs) return kvpi::fail(KVP_EINVAL, "n outside [0, max_seqs]");
         if (n == 0) return KVP_OK;
+        DeviceScope scope(d->device);
         const kvp_decoder_config& c = d->cfg;
         int rc = wait_staging(d);
         if (rc != KVP_OK) return rc;
@@ -480,6 +506,7 @@ KVP_API int kvp_decoder_step(kvp_decoder* d, const int64_t* rids, int32_t n, con
 
 KVP_API int kvp_decoder_status(kvp_decoder* d) {
     if (!d) return -KVP_EINVAL;
+    DeviceScope scope(d->device);
     cudaStreamSynchronize(d->s_comp);
     int32_t v = 0;
     if (cudaMemcpy(&v, d->d_status(), sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) return -KVP_ECUDA;

@@ -1,6 +1,7 @@
-// Device data plane of the KVManager decisions: append scatter, copy-on-write block copies, swap.
+// Device data plane of the KVManager decisions: append scatter, copy-on-write block copies, swap, and block
+// migration between shards.
 //
-// All three are pure byte movement and HBM-bound (swap: host-link bound).  Copies use 16-byte vectors with
+// All are pure byte movement: HBM-bound (swap: host-link bound; migration from a peer GPU: NVLink-bound).  Copies use 16-byte vectors with
 // several loads in flight per thread; grids are sized in multiples of the SM count.  Results are bit-exact
 // copies, as in the reference's Python data plane (python/paged_model.py:54-55, 92-95, 113-117, 145-146).
 #include <cuda_runtime.h>
@@ -50,21 +51,25 @@ __global__ void __launch_bounds__(256) append_scatter_kernel(const AppendParams 
     }
 }
 
-// ---------------------------------------------------------------- copy-on-write
-// Work item = (pair, layer, K|V): copies block_u 16-byte units.  Each thread moves UNROLL units per round
-// so several loads are in flight before the stores.
-struct CowParams {
-    uint4* k_cache;
-    uint4* v_cache;
+// ---------------------------------------------------------------- whole-block copies
+// Copy-on-write (source and destination pools the same) and migration between two shards' pools (the
+// source possibly on a peer GPU, read with plain loads over NVLink).  Work item = (pair, layer, K|V): copies
+// block_u 16-byte units.  Each thread moves UNROLL units per round so several loads are in flight before
+// the stores (more for peer reads, whose latency is higher).
+struct BlockCopyParams {
+    const uint4* src_k;
+    const uint4* src_v;
+    uint4* dst_k;
+    uint4* dst_v;
     const int32_t* pairs;
     int32_t* status;
-    long long layer_stride_u;
-    long long num_blocks;  // 0: unchecked
+    long long src_layer_u, dst_layer_u;  // 16-byte units between layer pools
+    long long src_blocks, dst_blocks;    // 0: unchecked
     int n_pairs, num_layers, block_u;
 };
 
 template <int UNROLL>
-__global__ void __launch_bounds__(256) cow_copy_kernel(const CowParams p) {
+__global__ void __launch_bounds__(256) block_copy_kernel(const BlockCopyParams p) {
     const long long items = static_cast<long long>(p.n_pairs) * p.num_layers * 2;
     for (long long it = blockIdx.x; it < items; it += gridDim.x) {
         const int kv = static_cast<int>(it & 1);
@@ -72,13 +77,12 @@ __global__ void __launch_bounds__(256) cow_copy_kernel(const CowParams p) {
         const int pair = static_cast<int>(pl / p.num_layers);
         const int layer = static_cast<int>(pl - static_cast<long long>(pair) * p.num_layers);
         const int src = __ldg(p.pairs + 2 * pair), dst = __ldg(p.pairs + 2 * pair + 1);
-        if (p.num_blocks > 0 && (src < 0 || dst < 0 || src >= p.num_blocks || dst >= p.num_blocks)) {
+        if (src < 0 || dst < 0 || (p.src_blocks > 0 && src >= p.src_blocks) || (p.dst_blocks > 0 && dst >= p.dst_blocks)) {
             if (threadIdx.x == 0 && layer == 0 && kv == 0) report(p.status, KVP_STATUS_BAD_BLOCK);
             continue;
         }
-        uint4* base = (kv ? p.v_cache : p.k_cache) + layer * p.layer_stride_u;
-        const uint4* s = base + static_cast<long long>(src) * p.block_u;
-        uint4* d = base + static_cast<long long>(dst) * p.block_u;
+        const uint4* s = (kv ? p.src_v : p.src_k) + layer * p.src_layer_u + static_cast<long long>(src) * p.block_u;
+        uint4* d = (kv ? p.dst_v : p.dst_k) + layer * p.dst_layer_u + static_cast<long long>(dst) * p.block_u;
         for (int u0 = threadIdx.x; u0 < p.block_u; u0 += blockDim.x * UNROLL) {
             uint4 buf[UNROLL];
 #pragma unroll
@@ -165,20 +169,114 @@ extern "C" KVP_API int kvp_cow_copy(const kvp_cow_args* a, void* stream) {
     const long long ls = resolve_layer_stride(a->layer_stride, a->num_blocks, a->block_size, a->kv_heads, a->head_dim);
     if ((ls * 2) % 16 != 0) return fail(KVP_EINVAL, "layer stride must be a multiple of 16 bytes");
     if (a->num_layers > 1 && ls <= 0) return fail(KVP_EINVAL, "layer_stride or num_blocks required for several layers");
-    kvpd::CowParams p;
-    p.k_cache = static_cast<uint4*>(a->k_cache);
-    p.v_cache = static_cast<uint4*>(a->v_cache);
+    kvpd::BlockCopyParams p;
+    p.src_k = static_cast<const uint4*>(a->k_cache);
+    p.src_v = static_cast<const uint4*>(a->v_cache);
+    p.dst_k = static_cast<uint4*>(a->k_cache);
+    p.dst_v = static_cast<uint4*>(a->v_cache);
     p.pairs = a->pairs;
     p.status = a->status;
-    p.layer_stride_u = ls * 2 / 16;
-    p.num_blocks = a->num_blocks;
+    p.src_layer_u = p.dst_layer_u = ls * 2 / 16;
+    p.src_blocks = p.dst_blocks = a->num_blocks;
     p.n_pairs = a->n_pairs;
     p.num_layers = a->num_layers;
     p.block_u = static_cast<int>(block_bytes / 16);
     const long long items = static_cast<long long>(a->n_pairs) * a->num_layers * 2;
     const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(items, static_cast<long long>(sm_count()) * 8)));
-    kvpd::cow_copy_kernel<4><<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+    kvpd::block_copy_kernel<4><<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
     return cuda_status(cudaGetLastError(), "copy-on-write launch");
+}
+
+// ---------------------------------------------------------------- migration between shards
+namespace {
+
+// Device of a device-memory pointer, or -1 (host / unregistered memory).
+int device_of(const void* ptr) {
+    cudaPointerAttributes at{};
+    if (cudaPointerGetAttributes(&at, ptr) != cudaSuccess) {
+        cudaGetLastError();
+        return -1;
+    }
+    return at.type == cudaMemoryTypeDevice ? at.device : -1;
+}
+
+}  // namespace
+
+extern "C" KVP_API int kvp_enable_peer_access(int32_t peer_device) {
+    using namespace kvpi;
+    clear_error();
+    int cur = 0, n = 0;
+    cudaError_t e = cudaGetDevice(&cur);
+    if (e == cudaSuccess) e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) return cuda_status(e, "device query");
+    if (peer_device < 0 || peer_device >= n) return fail(KVP_EINVAL, "peer device out of range");
+    if (peer_device == cur) return KVP_OK;
+    int can = 0;
+    e = cudaDeviceCanAccessPeer(&can, cur, peer_device);
+    if (e != cudaSuccess) return cuda_status(e, "peer access query");
+    if (!can) return fail(KVP_EINVAL, "device " + std::to_string(cur) + " cannot access device " + std::to_string(peer_device));
+    e = cudaDeviceEnablePeerAccess(peer_device, 0);
+    if (e == cudaErrorPeerAccessAlreadyEnabled) {
+        cudaGetLastError();
+        return KVP_OK;
+    }
+    return cuda_status(e, "enable peer access");
+}
+
+extern "C" KVP_API int kvp_migrate_blocks(const kvp_migrate_args* a, void* stream) {
+    using namespace kvpi;
+    clear_error();
+    if (!a) return fail(KVP_EINVAL, "null arguments");
+    if (!(a->kv_dtype == KVP_DTYPE_F16 || a->kv_dtype == KVP_DTYPE_BF16))
+        return fail(KVP_EINVAL, "pool dtype must be fp16 or bf16");
+    if (a->n_pairs < 0 || a->num_layers < 0 || a->kv_heads < 1 || a->head_dim < 1 || a->block_size < 1 ||
+        a->src_num_blocks < 0 || a->dst_num_blocks < 0)
+        return fail(KVP_EINVAL, "bad shape");
+    const long long block_bytes = static_cast<long long>(a->block_size) * a->kv_heads * a->head_dim * 2;
+    if (block_bytes % 16 != 0) return fail(KVP_EINVAL, "block bytes must be a multiple of 16");
+    if (a->n_pairs == 0 || a->num_layers == 0) return KVP_OK;
+    if (!a->src_k_cache || !a->src_v_cache || !a->dst_k_cache || !a->dst_v_cache || !a->pairs)
+        return fail(KVP_EINVAL, "null buffer");
+    if (!aligned16(a->src_k_cache) || !aligned16(a->src_v_cache) || !aligned16(a->dst_k_cache) || !aligned16(a->dst_v_cache))
+        return fail(KVP_EINVAL, "pools must be 16-byte aligned");
+    const long long sls = resolve_layer_stride(a->src_layer_stride, a->src_num_blocks, a->block_size, a->kv_heads, a->head_dim);
+    const long long dls = resolve_layer_stride(a->dst_layer_stride, a->dst_num_blocks, a->block_size, a->kv_heads, a->head_dim);
+    if ((sls * 2) % 16 != 0 || (dls * 2) % 16 != 0) return fail(KVP_EINVAL, "layer strides must be multiples of 16 bytes");
+    if (a->num_layers > 1 && (sls <= 0 || dls <= 0))
+        return fail(KVP_EINVAL, "layer strides or pool sizes required for several layers");
+    int cur = 0;
+    cudaError_t e = cudaGetDevice(&cur);
+    if (e != cudaSuccess) return cuda_status(e, "device query");
+    const int sdev = device_of(a->src_k_cache), ddev = device_of(a->dst_k_cache);
+    if (sdev < 0 || ddev < 0 || device_of(a->src_v_cache) != sdev || device_of(a->dst_v_cache) != ddev)
+        return fail(KVP_EINVAL, "pools must be device memory (K and V of one shard on one device)");
+    if (ddev != cur) return fail(KVP_EINVAL, "launch on the destination pools' device");
+    if (sdev != cur) {
+        const int rc = kvp_enable_peer_access(sdev);
+        if (rc != KVP_OK) return rc;
+    }
+    kvpd::BlockCopyParams p;
+    p.src_k = static_cast<const uint4*>(a->src_k_cache);
+    p.src_v = static_cast<const uint4*>(a->src_v_cache);
+    p.dst_k = static_cast<uint4*>(a->dst_k_cache);
+    p.dst_v = static_cast<uint4*>(a->dst_v_cache);
+    p.pairs = a->pairs;
+    p.status = a->status;
+    p.src_layer_u = sls * 2 / 16;
+    p.dst_layer_u = dls * 2 / 16;
+    p.src_blocks = a->src_num_blocks;
+    p.dst_blocks = a->dst_num_blocks;
+    p.n_pairs = a->n_pairs;
+    p.num_layers = a->num_layers;
+    p.block_u = static_cast<int>(block_bytes / 16);
+    const long long items = static_cast<long long>(a->n_pairs) * a->num_layers * 2;
+    const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(items, static_cast<long long>(sm_count()) * 8)));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (sdev != cur)
+        kvpd::block_copy_kernel<8><<<grid, 256, 0, s>>>(p);
+    else
+        kvpd::block_copy_kernel<4><<<grid, 256, 0, s>>>(p);
+    return cuda_status(cudaGetLastError(), "migration launch");
 }
 
 // ---------------------------------------------------------------- swap (host link)

@@ -109,7 +109,8 @@ def test_ctypes_struct_layouts_match_the_header(kvb, tmp_path):
     """Every argument struct the Python binding passes has the header's field order, offsets and size
     (the header compiled with gcc prints them)."""
     structs = {"kvp_attn_args": kvb.AttnArgs, "kvp_append_args": kvb.AppendArgs, "kvp_cow_args": kvb.CowArgs,
-               "kvp_swap_args": kvb.SwapArgs, "kvp_decoder_config": kvb.DecoderConfig}
+               "kvp_swap_args": kvb.SwapArgs, "kvp_decoder_config": kvb.DecoderConfig,
+               "kvp_migrate_args": kvb.MigrateArgs}
     lines = ["#include <stdio.h>", "#include <stddef.h>", '#include "kvp_b200.h"', "int main(void) {"]
     for cname, py in structs.items():
         lines.append(f'printf("{cname} sizeof %zu\\n", sizeof({cname}));')
