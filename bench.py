@@ -1,8 +1,8 @@
 """Decode-step benchmark of the paged KV-cache data plane on B200.
 
 A step = one decode step of every request of this GPU's shard: the host KVManager appends one token per
-request (slots, copy-on-write pairs, new table entries), the append-scatter kernel writes every layer's new
-K/V into its slot, and paged decode attention runs for every layer.  Default workload: the Llama-3-8B-shaped
+request (slots, copy-on-write pairs, new table entries), and one paged decode attention launch per layer
+writes the layer's new K/V into its slot (fused append) and attends over every context.  Default workload: the Llama-3-8B-shaped
 request-sharded config (32 query / 8 kv heads, head_dim 128, 32 layers, block 16, bf16, 256 requests per
 GPU, context lengths log-normal with median 4096 clipped to 32768, a pool of about 150 GB per GPU).
 Inputs are synthetic, seeded N(0,1).
@@ -15,6 +15,8 @@ Inputs are synthetic, seeded N(0,1).
   cpu_baseline : the reference's own CPU paged_attention_cpu (oracle/_ref) on a bounded sample, all host cores
 
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config llama3-8b|...]
+       python bench.py --op migrate|cow   (block movers: one process; migrate reads GPU 1's pool into GPU 0's
+                                           over NVLink when two GPUs are visible)
 Multi-GPU: launched under torch.distributed.run, one process per GPU, requests sharded with no collective
 on the data path (weak scaling); timings are the max over ranks.
 """
@@ -358,6 +360,84 @@ def run_ours(args, cfg, rank, world, dev):
     return res, lens
 
 
+def run_block_mover(args, cfg):
+    """Whole-block movers of the data plane, device timed: `migrate` copies blocks from a second GPU's pool into
+    this GPU's pool (kvp_migrate_blocks, peer loads over NVLink; two pools on one GPU when only one is
+    visible), `cow` copies blocks within one pool (kvp_cow_copy).  A step moves `blocks` random (src, dst)
+    pairs of config blocks (every layer, K and V)."""
+    import torch
+    kvb = importlib.import_module("paged-kv-cache-manager_b200")
+    L, B, kvh, D = cfg["L"], cfg["B"], cfg["kvh"], cfg["D"]
+    tdt = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float16
+    nblk = 2048
+    nb = 2 * nblk
+    two = args.op == "migrate" and torch.cuda.device_count() >= 2
+    dst_dev = torch.device("cuda", 0)
+    src_dev = torch.device("cuda", 1) if two else dst_dev
+
+    def pool(dev):
+        t = torch.empty((L, nb, B, kvh, D), dtype=tdt, device=dev)
+        t.view(torch.int16).random_(-30000, 30000)
+        return t
+
+    dk, dv = pool(dst_dev), pool(dst_dev)
+    sk, sv = (pool(src_dev), pool(src_dev)) if args.op == "migrate" else (dk, dv)
+    rng = np.random.default_rng(0)
+    steps_total = args.warmup + args.steps
+    pairs = []
+    for _ in range(steps_total):
+        src = rng.permutation(nb)[:nblk]
+        dst = rng.permutation(nb)[:nblk] if args.op == "migrate" else np.setdiff1d(np.arange(nb), src)
+        pairs.append(torch.from_numpy(np.stack([src, rng.permutation(dst)], 1).astype(np.int32)).to(dst_dev))
+    st = torch.zeros(1, dtype=torch.int32, device=dst_dev)
+    stream = torch.cuda.current_stream(dst_dev)
+
+    def one(i):
+        if args.op == "migrate":
+            kvb.migrate_blocks(sk, sv, dk, dv, pairs[i], status=st, stream=stream)
+        else:
+            kvb.cow_copy(dk, dv, pairs[i], status=st, stream=stream)
+
+    for i in range(args.warmup):
+        one(i)
+    torch.cuda.synchronize(dst_dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        e0.record(stream)
+        for i in range(args.steps):
+            one(args.warmup + i)
+        e1.record(stream)
+        torch.cuda.synchronize(dst_dev)
+    assert int(st.item()) == 0
+    # bit-exact spot check of the last step
+    p = pairs[-1][:64].long()
+    assert torch.equal(dk[:, p[:, 1].to(dst_dev)].view(torch.int16).cpu(), sk[:, p[:, 0].to(src_dev)].view(torch.int16).cpu())
+    ms = e0.elapsed_time(e1) / args.steps
+    moved = nblk * block_bytes_all_layers(cfg)  # bytes copied per step
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    if two:
+        bound, peak, unit, algo = "nvlink", 770.0, "GB/s", moved  # measured peer-copy bandwidth per direction
+        peak_src = "measured peer copy per direction"
+    else:
+        bound, peak, unit, algo = "hbm", float(peaks.get("hbm_gbs", 6650.0)), "GB/s", 2 * moved  # read + write
+        peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+    achieved = algo / (ms / 1e3) / 1e9
+    line = {"metric": f"block {args.op} bandwidth", "value": round(moved / (ms / 1e3) / 1e9, 1), "unit": "GB/s",
+            "n_gpus": 2 if two else 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "op": args.op, "dtype": cfg["dtype"], "data": "synthetic random bits",
+            "config": {"workload": f"{args.config}-shaped blocks ({block_bytes_all_layers(cfg)} bytes, every layer, "
+                                   f"K and V), {nblk} random pairs per step",
+                       "src": str(src_dev), "dst": str(dst_dev)},
+            "roofline": {"bound": bound, "achieved": round(achieved, 1), "peak": peak, "unit": unit,
+                         "frac": round(achieved / peak, 4), "peak_source": peak_src},
+            "gpu_launches": args.steps, "clocks": clk.summary()}
+    print(json.dumps(line))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -373,6 +453,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--requests", type=int, default=0, help="profiling: requests per GPU (pool sized to need)")
     ap.add_argument("--layers", type=int, default=0, help="profiling: number of layers (pool sized to need)")
+    ap.add_argument("--op", default="decode", choices=["decode", "migrate", "cow"],
+                    help="decode step (default) or a whole-block mover measured alone")
     args = ap.parse_args()
     assert args.warmup >= 3, "at least 3 warm-up steps"
     cfg = dict(CONFIGS[args.config])
@@ -411,6 +493,9 @@ def main():
         print(json.dumps(line))
         return
 
+    if args.op != "decode":
+        run_block_mover(args, cfg)
+        return
     import torch
     import torch.distributed as dist
     if world > 1:
