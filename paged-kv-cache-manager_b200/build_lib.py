@@ -53,6 +53,11 @@ def _compile(src, verbose):
     r = subprocess.run(cmd, capture_output=True, text=True)
     if verbose or r.returncode:
         sys.stderr.write(" ".join(cmd) + "\n" + r.stdout + r.stderr)
+    else:
+        # register spills are a performance bug worth seeing in every build
+        for line in r.stderr.splitlines():
+            if "spill" in line:
+                sys.stderr.write(f"{os.path.basename(src)}: {line.strip()}\n")
     if r.returncode:
         raise RuntimeError(f"compilation failed: {src}")
     return obj

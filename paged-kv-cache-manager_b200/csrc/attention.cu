@@ -590,6 +590,20 @@ __device__ __forceinline__ void init_barriers(const AttnParams& p, uint64_t* ful
 template <int D>
 __device__ __forceinline__ void merge_rows(const AttnParams& p, size_t row0, size_t stride, int n, size_t out_off,
                                            int lane);
+template <int D, int IT, int U>
+__device__ __forceinline__ void merge_group(const AttnParams& p, int seq, int c0, int nseg, int hq0, int heads,
+                                            int tid, int nthreads);
+
+// Merge batch shape per kernel instantiation (items per thread x partials per load round), the widest that
+// keeps the kernel free of register spills; 0 = one warp per head (merge_rows) for the instantiations whose
+// main loop already needs nearly every register (more than 8 query heads per kv head at head_dim >= 96, and
+// head_dim 256).
+template <int D, int NT>
+struct MergeShape {
+    static constexpr bool per_warp = (NT == 2 && D >= 96) || D >= 256;
+    static constexpr int IT = 2;
+    static constexpr int U = (D <= 64 && NT == 1) ? 4 : 2;
+};
 
 template <int D, int NT, class KV, class Segs>
 __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap* km, const CUtensorMap* vm, Segs segs,
@@ -726,11 +740,17 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
             named_barrier(kMaxConsumerWarps + 1, NC * 32);
             if (*last_flag) {
                 __threadfence();
-                // every consumer warp merges some of the group's query heads
-                for (int jj = warp; jj < p.kvh_cta * p.g; jj += NC) {
-                    const int hq = kvh0 * p.g + jj;
-                    merge_rows<D>(p, static_cast<size_t>(sg.c0 + sg.seq) * p.nh + hq, static_cast<size_t>(p.nh),
-                                  sg.nseg, (static_cast<size_t>(sg.seq) * p.nh + hq) * D, lane);
+                using MS = MergeShape<D, NT>;
+                if constexpr (MS::per_warp) {
+                    for (int jj = warp; jj < p.kvh_cta * p.g; jj += NC) {
+                        const int hq = kvh0 * p.g + jj;
+                        merge_rows<D>(p, static_cast<size_t>(sg.c0 + sg.seq) * p.nh + hq, static_cast<size_t>(p.nh),
+                                      sg.nseg, (static_cast<size_t>(sg.seq) * p.nh + hq) * D, lane);
+                    }
+                } else {
+                    // all consumer threads merge the group's query heads, a 4-float column each
+                    merge_group<D, MS::IT, MS::U>(p, sg.seq, sg.c0, sg.nseg, kvh0 * p.g, p.kvh_cta * p.g, threadIdx.x,
+                                                  NC * 32);
                 }
             }
             named_barrier(kMaxConsumerWarps + 1, NC * 32);  // the flag is rewritten by the next segment
@@ -848,12 +868,17 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
     const long long T = P[ns];
     if (c == 0) {
         // Sequences with an invalid length own no tile: report them and write zeros for this group's heads.
-        const int heads = p.kvh_cta * p.g;
-        for (int s = 0; s < ns; ++s) {
-            if (P[s + 1] != P[s]) continue;
-            if (threadIdx.x == 0 && grp == 0) report(p.status, KVP_STATUS_BAD_LEN);
-            for (int i = threadIdx.x; i < heads * D; i += blockDim.x)
-                store_any(p.out, (static_cast<size_t>(s) * p.nh + grp * heads + i / D) * D + i % D, p.out_dtype, 0.f);
+        // The scan is spread over the threads; the (rare) zero writes only run when it found one.
+        bool bad = false;
+        for (int s = threadIdx.x; s < ns; s += blockDim.x) bad |= P[s + 1] == P[s];
+        if (__syncthreads_or(bad)) {
+            const int heads = p.kvh_cta * p.g;
+            for (int s = 0; s < ns; ++s) {
+                if (P[s + 1] != P[s]) continue;
+                if (threadIdx.x == 0 && grp == 0) report(p.status, KVP_STATUS_BAD_LEN);
+                for (int i = threadIdx.x; i < heads * D; i += blockDim.x)
+                    store_any(p.out, (static_cast<size_t>(s) * p.nh + grp * heads + i / D) * D + i % D, p.out_dtype, 0.f);
+            }
         }
     }
     // With fewer tiles than CTAs only the first T CTAs work, so every working CTA owns >= 1 tile.
@@ -920,6 +945,79 @@ __device__ __forceinline__ void merge_rows(const AttnParams& p, size_t row0, siz
     for (int q = 0; q < PER; ++q) {
         const int d = q * 32 + lane;
         if (d < D) store_any(p.out, out_off + d, p.out_dtype, acc[q] * invL);
+    }
+}
+
+// Stream-K merge of one sequence's partials (CTAs c0 .. c0 + nseg - 1, rows (c + seq) * nh + head) for `heads`
+// query heads from hq0, by nthreads threads: item = (head, 4-float column of the output).  Every partial's
+// (m, l) and column are loaded U partials at a time, for IT items of a thread at once, before they are
+// combined (a running max with rescaling), so a merge costs about one L2 round trip per U partials and IT items
+// instead of a dependent chain per head.  Partials
+// written by other CTAs of the same launch are read through L2 (ld.global.cg).
+template <int D, int IT, int U>
+__device__ __forceinline__ void merge_group(const AttnParams& p, int seq, int c0, int nseg, int hq0, int heads,
+                                            int tid, int nthreads) {
+    constexpr int C4 = D / 4;
+    const int items = heads * C4;
+    for (int base = tid; base < items; base += nthreads * IT) {
+        float M[IT], Lsum[IT];
+        float4 acc[IT];
+        size_t row0[IT];
+        int col[IT];
+        bool on[IT];
+#pragma unroll
+        for (int t = 0; t < IT; ++t) {
+            const int item = base + t * nthreads;
+            on[t] = item < items;
+            const int h = on[t] ? item / C4 : 0;
+            col[t] = on[t] ? item - h * C4 : 0;
+            row0[t] = static_cast<size_t>(c0 + seq) * p.nh + hq0 + h;
+            M[t] = -INFINITY;
+            Lsum[t] = 0.f;
+            acc[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        for (int k0 = 0; k0 < nseg; k0 += U) {
+            float2 ml[IT][U];
+            float4 o[IT][U];
+#pragma unroll
+            for (int t = 0; t < IT; ++t) {
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    if (on[t] && k0 + u < nseg) {
+                        const size_t row = row0[t] + static_cast<size_t>(k0 + u) * p.nh;
+                        ml[t][u] = __ldcg(&p.ws_ml[row]);
+                        o[t][u] = __ldcg(reinterpret_cast<const float4*>(p.ws_o + row * D) + col[t]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < IT; ++t) {
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    if (on[t] && k0 + u < nseg) {
+                        const float Mn = fmaxf(M[t], ml[t][u].x);
+                        const float a = M[t] == -INFINITY ? 0.f : fast_exp2(M[t] - Mn);
+                        const float b = fast_exp2(ml[t][u].x - Mn);
+                        Lsum[t] = Lsum[t] * a + ml[t][u].y * b;
+                        acc[t].x = acc[t].x * a + o[t][u].x * b;
+                        acc[t].y = acc[t].y * a + o[t][u].y * b;
+                        acc[t].z = acc[t].z * a + o[t][u].z * b;
+                        acc[t].w = acc[t].w * a + o[t][u].w * b;
+                        M[t] = Mn;
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < IT; ++t) {
+            if (!on[t]) continue;
+            const float inv = 1.f / Lsum[t];
+            const size_t out = (row0[t] - static_cast<size_t>(c0) * p.nh) * D + static_cast<size_t>(col[t]) * 4;
+            store_any(p.out, out + 0, p.out_dtype, acc[t].x * inv);
+            store_any(p.out, out + 1, p.out_dtype, acc[t].y * inv);
+            store_any(p.out, out + 2, p.out_dtype, acc[t].z * inv);
+            store_any(p.out, out + 3, p.out_dtype, acc[t].w * inv);
+        }
     }
 }
 
