@@ -288,38 +288,57 @@ struct Consumer {
         }
     }
 
-    // Same from the query area of a stage: [kvh_cta * g heads][D] in the query dtype.
-    __device__ __forceinline__ void load_q_smem(const AttnParams& p, uint32_t qsm, int warp, int lane) {
+    // Same from the query area of a stage: [kvh_cta * g heads][D] in the query dtype (a generic pointer into
+    // shared memory; every load is issued before the conversions).
+    __device__ __forceinline__ void load_q_smem(const AttnParams& p, const uint8_t* qs, int warp, int lane) {
         const int gid = lane >> 2, c4 = lane & 3;
-        const uint32_t esz = p.q_dtype == KVP_DTYPE_F32 ? 4u : 2u;
+        if (p.q_dtype == KVP_DTYPE_F32) {
+            float2 v[NT][KS][2];
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            const int j = nt * 8 + gid;
-            const bool live = j < p.g;
-            const uint32_t row = qsm + static_cast<uint32_t>((warp * p.g + (live ? j : 0)) * D) * esz;
+            for (int nt = 0; nt < NT; ++nt) {
+                const int j = nt * 8 + gid;
+                const float* row = reinterpret_cast<const float*>(qs) + (warp * p.g + (j < p.g ? j : 0)) * D;
 #pragma unroll
-            for (int ks = 0; ks < KS; ++ks)
+                for (int ks = 0; ks < KS; ++ks)
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const uint32_t a = row + static_cast<uint32_t>(ks * 16 + 2 * c4 + h * 8) * esz;
-                    float x0 = 0.f, x1 = 0.f;
-                    if (live) {
-                        if (p.q_dtype == KVP_DTYPE_F32) {
-                            asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(x0), "=f"(x1) : "r"(a));
-                        } else {
-                            uint32_t v;
-                            asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
-                            if (p.q_dtype == KVP_DTYPE_F16) {
-                                x0 = F16Traits<__half>::unpack_lo(v);
-                                x1 = F16Traits<__half>::unpack_hi(v);
-                            } else {
-                                x0 = F16Traits<__nv_bfloat16>::unpack_lo(v);
-                                x1 = F16Traits<__nv_bfloat16>::unpack_hi(v);
-                            }
-                        }
+                    for (int h = 0; h < 2; ++h)
+                        v[nt][ks][h] = *reinterpret_cast<const float2*>(row + ks * 16 + 2 * c4 + h * 8);
+            }
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                const bool live = nt * 8 + gid < p.g;
+#pragma unroll
+                for (int ks = 0; ks < KS; ++ks)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+                        set_q(nt, ks, h, live ? v[nt][ks][h].x : 0.f, live ? v[nt][ks][h].y : 0.f);
+            }
+        } else {
+            uint32_t v[NT][KS][2];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                const int j = nt * 8 + gid;
+                const uint16_t* row = reinterpret_cast<const uint16_t*>(qs) + (warp * p.g + (j < p.g ? j : 0)) * D;
+#pragma unroll
+                for (int ks = 0; ks < KS; ++ks)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+                        v[nt][ks][h] = *reinterpret_cast<const uint32_t*>(row + ks * 16 + 2 * c4 + h * 8);
+            }
+            const bool f16 = p.q_dtype == KVP_DTYPE_F16;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                const bool live = nt * 8 + gid < p.g;
+#pragma unroll
+                for (int ks = 0; ks < KS; ++ks)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const uint32_t x = v[nt][ks][h];
+                        float x0 = f16 ? F16Traits<__half>::unpack_lo(x) : F16Traits<__nv_bfloat16>::unpack_lo(x);
+                        float x1 = f16 ? F16Traits<__half>::unpack_hi(x) : F16Traits<__nv_bfloat16>::unpack_hi(x);
+                        set_q(nt, ks, h, live ? x0 : 0.f, live ? x1 : 0.f);
                     }
-                    set_q(nt, ks, h, x0, x1);
-                }
+            }
         }
     }
 
@@ -517,6 +536,7 @@ __device__ __forceinline__ void named_barrier(int id, int threads) {
 // as the partial row `part_row`.
 struct Segment {
     int seq, tile0, tile1;
+    int len;  // the sequence's context length
     bool single;
     size_t part_row;
     int c0, nseg;  // stream-K: first CTA holding part of the sequence and how many do (0: merged elsewhere)
@@ -534,18 +554,32 @@ struct SplitSegments {
     }
 };
 
+// floor(a * b / c) for 0 <= a * b < 2^53 and c > 0: a double-precision quotient (the product is exact in a
+// double) corrected by one integer step, instead of a 64-bit integer division routine.
+__device__ __forceinline__ long long muldiv_floor(long long a, long long b, long long c) {
+    const long long n = a * b;
+    long long q = static_cast<long long>(static_cast<double>(n) / static_cast<double>(c));
+    if (q * c > n) --q;
+    else if ((q + 1) * c <= n) ++q;
+    return q;
+}
+
 // CTA c of Ge owns tiles [c*T/Ge, (c+1)*T/Ge) of the concatenation of all sequences' tiles (T in total).
-__device__ __forceinline__ long long cta_begin(long long c, long long T, int G) { return c * T / G; }
+__device__ __forceinline__ long long cta_begin(long long c, long long T, int G) { return muldiv_floor(c, T, G); }
+// The owner of tile t: the c with c*T < (t+1)*G <= (c+1)*T, i.e. floor(((t+1)*G - 1) / T).  The quotient is
+// below 2^16, so a single-precision estimate is off by at most one and one integer step corrects it.
 __device__ __forceinline__ int cta_of_tile(long long t, long long T, int G) {
-    long long c = t * G / T;
-    while (c + 1 < G && cta_begin(c + 1, T, G) <= t) ++c;
-    while (c > 0 && cta_begin(c, T, G) > t) --c;
+    const long long n = (t + 1) * G - 1;
+    long long c = static_cast<long long>(static_cast<float>(n) / static_cast<float>(T));
+    if (c * T > n) --c;
+    else if ((c + 1) * T <= n) ++c;
     return static_cast<int>(c);
 }
 
 // Stream-K: the CTA's tile range [t, end) of the concatenated sequences, cut at sequence boundaries.
 struct StreamSegments {
     const int32_t* P;  // tile prefix sums in shared memory
+    const uint8_t* R;  // tokens in each sequence's last tile, in shared memory
     long long t, end, T;
     int s, cta, nh, Ge;
     __device__ __forceinline__ bool next(Segment& sg) {
@@ -553,6 +587,7 @@ struct StreamSegments {
         while (P[s + 1] <= t) ++s;
         const long long e = min(end, static_cast<long long>(P[s + 1]));
         sg.seq = s;
+        sg.len = (P[s + 1] - P[s] - 1) * 16 + R[s];
         sg.tile0 = static_cast<int>(t - P[s]);
         sg.tile1 = static_cast<int>(e - P[s]);
         sg.single = (t == P[s]) && (e == P[s + 1]);
@@ -608,7 +643,7 @@ struct MergeShape {
 template <int D, int NT, class KV, class Segs>
 __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap* km, const CUtensorMap* vm, Segs segs,
                                          uint8_t* dyn, uint32_t smem_base, uint64_t* full_bar, uint64_t* empty_bar,
-                                         uint64_t* qfull, uint64_t* qempty, int grp, int* last_flag) {
+                                         uint64_t* qfull, uint64_t* qempty, int grp, int* pend) {
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int NC = p.kvh_cta * p.wph;
@@ -626,7 +661,7 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
         bool ok = true;
         int i = 0, j = 0;
         while (segs.next(sg)) {
-            const int len = __ldg(p.lens + sg.seq);
+            const int len = sg.len;
             const int32_t* trow = p.tables + static_cast<size_t>(sg.seq) * p.max_blocks;
             int cache_lo = -(1 << 30);
             int32_t cached = 0;
@@ -685,15 +720,19 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
     constexpr int NREG = Consumer<D, NT, KV>::NREG;
     bool ok = true;
     int i = 0, j = 0;
+    // Split segments of this CTA: at most two (only the first and the last segment of a CTA's range can be
+    // parts of a longer sequence); pend[k] flags a merge, pend[2 + 3k ..] holds (seq, c0, nseg); old0 / old1
+    // hold a writer warp's counter values from before its adds.
+    int np = 0, old0 = -1, old1 = -1;
     while (segs.next(sg)) {
-        const int len = __ldg(p.lens + sg.seq);
+        const int len = sg.len;
         if (p.q_area != 0) {
             const int slot = j & 1;
             if (ok && !mbar_wait(smem_u32(&qfull[slot]), static_cast<uint32_t>((j >> 1) & 1))) {
                 if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
                 ok = false;
             }
-            if (ok) cs.load_q_smem(p, smem_base + p.q_off + static_cast<uint32_t>(slot) * p.q_area, head, lane);
+            if (ok) cs.load_q_smem(p, dyn + p.q_off + static_cast<size_t>(slot) * p.q_area, head, lane);
             __syncwarp();
             if (ok && lane == 0) mbar_arrive(smem_u32(&qempty[slot]));
         } else {
@@ -723,39 +762,57 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
             named_barrier(1 + head, p.wph * 32);  // the area is rewritten by the next segment
         }
         if (sub == 0 && ok) cs.finish(p, lane, sg.seq, kvh_global, sg.single, sg.part_row);
-        // Stream-K, sequence split across CTAs: the last CTA to finish its part merges the partials of every
-        // head of its group (the counter is reset so the workspace stays clean for the next call).
+        // Stream-K, sequence split across CTAs: each head's writer warp counts its partial rows as done with
+        // one releasing add (the warp barrier orders its lanes' rows before it); a sequence is complete when
+        // every writer warp of every CTA holding part of it has added (nseg * kvh_cta).  The add's old value
+        // is only examined after the CTA's last segment, so no warp waits for its round trip or for another
+        // warp here.
         if (!sg.single && sg.nseg > 0) {
-            if (sub == 0) __threadfence();  // this warp's partial rows, device-wide
-            named_barrier(kMaxConsumerWarps + 1, NC * 32);
+            if (sub == 0) {
+                __syncwarp();
+                if (lane == 0 && ok) {
+                    const int old = atom_add_acq_rel_gpu(p.counters + static_cast<size_t>(sg.seq) * p.groups + grp, 1);
+                    if (np == 0) old0 = old; else old1 = old;
+                }
+            }
             if (warp == 0 && lane == 0) {
-                int last = 0;
-                if (ok) {
-                    int* cnt = p.counters + static_cast<size_t>(sg.seq) * p.groups + grp;
-                    last = atomicAdd(cnt, 1) == sg.nseg - 1;
-                    if (last) atomicExch(cnt, 0);
-                }
-                *last_flag = last;
+                pend[2 + 3 * np] = sg.seq;
+                pend[3 + 3 * np] = sg.c0;
+                pend[4 + 3 * np] = sg.nseg;
             }
-            named_barrier(kMaxConsumerWarps + 1, NC * 32);
-            if (*last_flag) {
-                __threadfence();
-                using MS = MergeShape<D, NT>;
-                if constexpr (MS::per_warp) {
-                    for (int jj = warp; jj < p.kvh_cta * p.g; jj += NC) {
-                        const int hq = kvh0 * p.g + jj;
-                        merge_rows<D>(p, static_cast<size_t>(sg.c0 + sg.seq) * p.nh + hq, static_cast<size_t>(p.nh),
-                                      sg.nseg, (static_cast<size_t>(sg.seq) * p.nh + hq) * D, lane);
-                    }
-                } else {
-                    // all consumer threads merge the group's query heads, a 4-float column each
-                    merge_group<D, MS::IT, MS::U>(p, sg.seq, sg.c0, sg.nseg, kvh0 * p.g, p.kvh_cta * p.g, threadIdx.x,
-                                                  NC * 32);
-                }
-            }
-            named_barrier(kMaxConsumerWarps + 1, NC * 32);  // the flag is rewritten by the next segment
+            ++np;
         }
         ++j;
+    }
+    // The writer warp whose add completed a sequence's count resets the counter and flags the merge; the CTA
+    // then merges (that acquiring add made the other parts' rows visible; the barrier extends it to every
+    // merging thread).
+    if (np > 0) {
+        named_barrier(kMaxConsumerWarps + 1, NC * 32);  // pend coordinates written
+        if (sub == 0 && lane == 0 && ok) {
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                if (k >= np || (k ? old1 : old0) != pend[4 + 3 * k] * p.kvh_cta - 1) continue;
+                atomicExch(p.counters + static_cast<size_t>(pend[2 + 3 * k]) * p.groups + grp, 0);
+                pend[k] = 1;
+            }
+        }
+        named_barrier(kMaxConsumerWarps + 1, NC * 32);  // merge flags written
+        for (int k = 0; k < np; ++k) {
+            if (!pend[k]) continue;
+            const int seq = pend[2 + 3 * k], c0 = pend[3 + 3 * k], nseg = pend[4 + 3 * k];
+            using MS = MergeShape<D, NT>;
+            if constexpr (MS::per_warp) {
+                for (int jj = warp; jj < p.kvh_cta * p.g; jj += NC) {
+                    const int hq = kvh0 * p.g + jj;
+                    merge_rows<D>(p, static_cast<size_t>(c0 + seq) * p.nh + hq, static_cast<size_t>(p.nh), nseg,
+                                  (static_cast<size_t>(seq) * p.nh + hq) * D, lane);
+                }
+            } else {
+                // all consumer threads merge the group's query heads, a 4-float column each
+                merge_group<D, MS::IT, MS::U>(p, seq, c0, nseg, kvh0 * p.g, p.kvh_cta * p.g, threadIdx.x, NC * 32);
+            }
+        }
     }
 }
 
@@ -792,6 +849,7 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
     init_barriers(p, full_bar, empty_bar, qfull, qempty);
     SplitSegments segs;
     segs.seg.seq = seq;
+    segs.seg.len = len;
     segs.seg.tile0 = split * p.split_tiles;
     segs.seg.tile1 = min(ntiles, segs.seg.tile0 + p.split_tiles);
     segs.seg.single = nsplit == 1;
@@ -805,8 +863,9 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
 
 // ---------------------------------------------------------------- stream-K schedule
 
-// Tile prefix sums P[0..ns] of all sequences into shared memory (invalid lengths count 0 tiles).
-__device__ __forceinline__ void build_prefix(const AttnParams& p, int32_t* P, int32_t* warp_tot) {
+// Tile prefix sums P[0..ns] of all sequences into shared memory (invalid lengths count 0 tiles), and R[s] =
+// the tokens in sequence s's last tile, so segment starts need no global load of the length.
+__device__ __forceinline__ void build_prefix(const AttnParams& p, int32_t* P, uint8_t* R, int32_t* warp_tot) {
     const int ns = p.num_seqs, nthr = blockDim.x, tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31, nwarps = (nthr + 31) >> 5;
     const int per = (ns + nthr - 1) / nthr;
@@ -833,8 +892,10 @@ __device__ __forceinline__ void build_prefix(const AttnParams& p, int32_t* P, in
     __syncthreads();
     int run = (warp > 0 ? warp_tot[warp - 1] : 0) + (x - local);
     for (int i = b; i < e; ++i) {
+        const int len = __ldg(p.lens + i);
         P[i] = run;
-        run += tiles_of_len(p, __ldg(p.lens + i));
+        run += tiles_of_len(p, len);
+        R[i] = static_cast<uint8_t>(((len - 1) & 15) + 1);
     }
     if (tid == nthr - 1) P[ns] = warp_tot[nwarps - 1];
     __syncthreads();
@@ -863,7 +924,8 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
     const int c = blockIdx.x, grp = blockIdx.y;
     const uint32_t base_off = ((smem_u32(dyn_smem) + 1023u) & ~1023u) - smem_u32(dyn_smem);
     int32_t* P = reinterpret_cast<int32_t*>(dyn_smem + base_off + p.pre_off);
-    build_prefix(p, P, warp_tot);
+    uint8_t* R = reinterpret_cast<uint8_t*>(P + p.num_seqs + 1);
+    build_prefix(p, P, R, warp_tot);
     const int ns = p.num_seqs;
     const long long T = P[ns];
     if (c == 0) {
@@ -886,6 +948,7 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
     if (c >= Ge) return;
     StreamSegments segs;
     segs.P = P;
+    segs.R = R;
     segs.T = T;
     segs.Ge = Ge;
     segs.t = cta_begin(c, T, Ge);
@@ -893,10 +956,11 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
     segs.s = seq_of_tile(P, ns, segs.t);
     segs.cta = c;
     segs.nh = p.nh;
-    init_barriers(p, full_bar, empty_bar, qfull, qempty);
-    __shared__ int last_flag;
+    __shared__ int pend[8];  // merge flags and coordinates of the CTA's split segments
+    if (threadIdx.x < 2) pend[threadIdx.x] = 0;
+    init_barriers(p, full_bar, empty_bar, qfull, qempty);  // (its barrier also publishes pend)
     cta_body<D, NT, KV>(p, &kmap, &vmap, segs, dyn_smem + base_off, smem_u32(dyn_smem) + base_off, full_bar,
-                        empty_bar, qfull, qempty, grp, &last_flag);
+                        empty_bar, qfull, qempty, grp, pend);
 }
 
 // ---------------------------------------------------------------- merges
@@ -1255,7 +1319,7 @@ int plan_attention(const kvp_attn_args& a, bool have_workspace, AttnPlan* out) {
     pl.stage_bytes = 2u * pl.stage_half;
     const size_t stage = pl.stage_bytes;
     const int NT = g <= 8 ? 1 : 2;
-    const size_t pre = pl.streamk ? round_up((static_cast<size_t>(a.num_seqs) + 1) * 4, 128) : 0;
+    const size_t pre = pl.streamk ? round_up((static_cast<size_t>(a.num_seqs) + 1) * 4 + a.num_seqs, 128) : 0;
     const size_t smem_cap = kDynSmemCap;
     size_t comb = 0;
     auto total = [&](int wph, int k) {

@@ -83,6 +83,15 @@ __device__ __forceinline__ void fence_barrier_init() {
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+// Device-scope fetch-and-add with acquire-release semantics: releases the writes ordered before it (other
+// threads' writes included when a CTA barrier orders them before it) and acquires those released by the
+// earlier adders.
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* addr, int v) {
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
+    return old;
+}
+
 // Orders this thread's generic-proxy global stores before later async-proxy (TMA) reads of them.
 __device__ __forceinline__ void fence_proxy_async_global() {
     asm volatile("fence.proxy.async.global;" ::: "memory");
