@@ -97,6 +97,11 @@ typedef struct kvp_attn_args {
  * workspace memory that was zero-filled once and has since only been used by completed calls (each call
  * leaves the counters zero).  Without it every balanced-schedule call first clears them on the stream. */
 #define KVP_ATTN_WORKSPACE_CLEAN 1
+/* Early start (programmatic dependent launch; balanced schedule only): the kernel may begin while the previous
+ * kernel on the stream is still running.  Its prologue (tile prefix sums, barrier setup) reads seq_lens --
+ * which that previous kernel therefore must not write -- and everything else waits for it to complete, so
+ * back-to-back launches (one per layer) hide each other's start-up. */
+#define KVP_ATTN_EARLY_START 2
 
 /* Bytes of workspace kvp_paged_attention needs for these arguments (0 when no context is split).  With
  * split_tiles == 0 and a workspace the balanced persistent schedule is used: the step's tiles are divided

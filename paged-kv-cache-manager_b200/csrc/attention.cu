@@ -706,6 +706,7 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
             }
             ++j;
         }
+        griddep_launch_dependents();
         return;
     }
     if (warp > NC) return;
@@ -784,6 +785,7 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
         }
         ++j;
     }
+    griddep_launch_dependents();  // the next kernel may start its prologue during the merges
     // The writer warp whose add completed a sequence's count resets the counter and flags the merge; the CTA
     // then merges (that acquiring add made the other parts' rows visible; the barrier extends it to every
     // merging thread).
@@ -928,6 +930,25 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
     build_prefix(p, P, R, warp_tot);
     const int ns = p.num_seqs;
     const long long T = P[ns];
+    // With fewer tiles than CTAs only the first T CTAs work, so every working CTA owns >= 1 tile.
+    const int Ge = static_cast<int>(min(static_cast<long long>(p.G), T));
+    StreamSegments segs;
+    segs.P = P;
+    segs.R = R;
+    segs.T = T;
+    segs.Ge = Ge;
+    segs.t = Ge > 0 ? cta_begin(c, T, Ge) : 0;
+    segs.end = Ge > 0 ? cta_begin(c + 1, T, Ge) : 0;
+    segs.s = seq_of_tile(P, ns, segs.t);
+    segs.cta = c;
+    segs.nh = p.nh;
+    __shared__ int pend[8];  // merge flags and coordinates of the CTA's split segments
+    if (threadIdx.x < 2) pend[threadIdx.x] = 0;
+    init_barriers(p, full_bar, empty_bar, qfull, qempty);  // (its barrier also publishes pend)
+    // Everything above reads only seq_lens and shared memory; with an early start (programmatic dependent
+    // launch) it overlaps the previous kernel's tail.  What follows may read what that kernel wrote or write
+    // what it reads, so it waits for it.
+    griddep_wait();
     if (c == 0) {
         // Sequences with an invalid length own no tile: report them and write zeros for this group's heads.
         // The scan is spread over the threads; the (rare) zero writes only run when it found one.
@@ -943,22 +964,7 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
             }
         }
     }
-    // With fewer tiles than CTAs only the first T CTAs work, so every working CTA owns >= 1 tile.
-    const int Ge = static_cast<int>(min(static_cast<long long>(p.G), T));
     if (c >= Ge) return;
-    StreamSegments segs;
-    segs.P = P;
-    segs.R = R;
-    segs.T = T;
-    segs.Ge = Ge;
-    segs.t = cta_begin(c, T, Ge);
-    segs.end = cta_begin(c + 1, T, Ge);
-    segs.s = seq_of_tile(P, ns, segs.t);
-    segs.cta = c;
-    segs.nh = p.nh;
-    __shared__ int pend[8];  // merge flags and coordinates of the CTA's split segments
-    if (threadIdx.x < 2) pend[threadIdx.x] = 0;
-    init_barriers(p, full_bar, empty_bar, qfull, qempty);  // (its barrier also publishes pend)
     cta_body<D, NT, KV>(p, &kmap, &vmap, segs, dyn_smem + base_off, smem_u32(dyn_smem) + base_off, full_bar,
                         empty_bar, qfull, qempty, grp, pend);
 }
@@ -1399,7 +1405,22 @@ int launch_typed(const kvp_attn_args& a, const AttnPlan& pl, const kvpd::AttnPar
     dim3 block(static_cast<unsigned>((pl.kvh_cta * pl.wph + 1) * 32));
     if (pl.streamk) {
         dim3 grid(static_cast<unsigned>(pl.G), static_cast<unsigned>(pl.groups));
-        kvpd::paged_decode_streamk_kernel<D, NT, KV><<<grid, block, pl.smem, stream>>>(km, vm, prm);
+        if (a.flags & KVP_ATTN_EARLY_START) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = grid;
+            cfg.blockDim = block;
+            cfg.dynamicSmemBytes = pl.smem;
+            cfg.stream = stream;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[0].val.programmaticStreamSerializationAllowed = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            cudaError_t e = cudaLaunchKernelEx(&cfg, kvpd::paged_decode_streamk_kernel<D, NT, KV>, km, vm, prm);
+            if (e != cudaSuccess) return cuda_status(e, "attention kernel launch");
+        } else {
+            kvpd::paged_decode_streamk_kernel<D, NT, KV><<<grid, block, pl.smem, stream>>>(km, vm, prm);
+        }
     } else {
         dim3 grid(static_cast<unsigned>(a.num_seqs * pl.groups), static_cast<unsigned>(pl.max_splits));
         kvpd::paged_decode_kernel<D, NT, KV><<<grid, block, pl.smem, stream>>>(km, vm, prm);

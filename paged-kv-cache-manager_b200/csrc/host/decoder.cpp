@@ -239,7 +239,9 @@ int enqueue_layers(kvp_decoder* d, int n, const void* q, const void* knew, const
         a.workspace = d->lay.attn_bytes ? d->ws + d->lay.attn : nullptr;
         a.workspace_bytes = d->lay.attn_bytes;
         a.status = d->d_status();
-        a.flags = KVP_ATTN_WORKSPACE_CLEAN;
+        // lengths are uploaded before the step's first launch and no kernel writes them: each layer's launch
+        // may start during the previous one
+        a.flags = KVP_ATTN_WORKSPACE_CLEAN | KVP_ATTN_EARLY_START;
         a.k_new = static_cast<const char*>(knew) + kv_layer * l;  // fused append of this layer's new token
         a.v_new = static_cast<const char*>(vnew) + kv_layer * l;
         rc = kvp_paged_attention(&a, s_comp);

@@ -92,6 +92,13 @@ __device__ __forceinline__ int atom_add_acq_rel_gpu(int* addr, int v) {
     return old;
 }
 
+// Programmatic dependent launch.  griddep_wait: blocks until the previous kernel on the stream has completed
+// and its memory is visible (returns at once when the kernel was launched without the programmatic
+// serialization attribute).  griddep_launch_dependents: lets the next kernel on the stream start its own
+// prologue once every CTA of this grid has called it or exited (its griddep_wait still waits for this grid).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 // Orders this thread's generic-proxy global stores before later async-proxy (TMA) reads of them.
 __device__ __forceinline__ void fence_proxy_async_global() {
     asm volatile("fence.proxy.async.global;" ::: "memory");

@@ -323,3 +323,43 @@ def test_balanced_schedule_leaves_workspace_clean(kvb, ora, cuda):
         check_close(out.cpu().numpy(), ref, what="clean workspace reuse")
         cnt = ws[-256 * ((5 * 4 + 255) // 256):].view(torch.int32)
         assert int(cnt.abs().sum().item()) == 0
+
+
+@pytest.mark.parametrize("shape", [(14, 2, 64), (32, 8, 128)], ids=["qwen", "llama"])
+def test_early_start_back_to_back_bit_exact(kvb, cuda, shape):
+    """Eight layers launched back to back on one stream with early start (each kernel's prologue overlapping
+    the previous kernel's tail) and the fused append give outputs and pools bit-identical to plain launches."""
+    import torch
+    nh, kvh, D = shape
+    L, B, ns = 8, 16, 48
+    rng = np.random.default_rng(5)
+    lens = rng.integers(1, 900, size=ns)
+    nblk = [(int(x) + B - 1) // B for x in lens]
+    nb = sum(nblk) + 4
+    perm = rng.permutation(nb)
+    T = np.zeros((ns, max(nblk)), np.int32)
+    o = 0
+    for i, n in enumerate(nblk):
+        T[i, :n] = perm[o:o + n]
+        o += n
+    g = torch.Generator(device="cuda").manual_seed(3)
+    K = torch.randn((L, nb, B, kvh, D), generator=g, device="cuda").to(torch.bfloat16)
+    V = torch.randn_like(K)
+    q = torch.randn((L, ns, nh, D), generator=g, device="cuda").to(torch.bfloat16)
+    kn = torch.randn((L, ns, kvh, D), generator=g, device="cuda").to(torch.bfloat16)
+    vn = torch.randn_like(kn)
+    t = torch.from_numpy(T).cuda()
+    ln = torch.from_numpy(lens.astype(np.int32)).cuda()
+    res = []
+    for early in (False, True):
+        k2, v2 = K.clone(), V.clone()
+        out = torch.empty_like(q)
+        st = torch.zeros(1, dtype=torch.int32, device="cuda")
+        for layer in range(L):
+            kvb.paged_attention(q[layer], k2[layer], v2[layer], t, ln, nh, kvh, out=out[layer], status=st,
+                                k_new=kn[layer], v_new=vn[layer], early_start=early)
+        torch.cuda.synchronize()
+        assert int(st.item()) == 0
+        res.append((out, k2, v2))
+    for a, b in zip(*res):
+        assert torch.equal(a, b)

@@ -129,3 +129,14 @@ def test_ctypes_struct_layouts_match_the_header(kvb, tmp_path):
         assert got[(cname, "sizeof")] == C.sizeof(py), cname
         for field, _ in py._fields_:
             assert got[(cname, field)] == getattr(py, field).offset, (cname, field)
+
+
+def test_header_constants_match_the_binding(kvb):
+    """Every integer #define of include/kvp_b200.h that the Python binding mirrors has the same value, and the
+    status, status-bit and attention-flag constants are all mirrored."""
+    src = open(os.path.join(ROOT, "include", "kvp_b200.h")).read()
+    defs = {m.group(1): int(m.group(2)) for m in re.finditer(r"#define\s+(KVP_\w+)\s+(\d+)\b", src)}
+    assert len(defs) >= 11
+    for name, value in defs.items():
+        if name.startswith(("KVP_STATUS_", "KVP_ATTN_", "KVP_E")) or name == "KVP_OK":
+            assert getattr(kvb, name) == value, name
