@@ -7,11 +7,13 @@ request-sharded config (32 query / 8 kv heads, head_dim 128, 32 layers, block 16
 GPU, context lengths log-normal with median 4096 clipped to 32768, a pool of about 150 GB per GPU).
 Inputs are synthetic, seeded N(0,1).
 
-  value : decode tokens/s over all GPUs with every input already resident in HBM (device timed)
+  value : decode tokens/s over all GPUs with every input already resident in HBM (device timed; each step's
+          per-layer launches replayed from a CUDA graph, or launched from Python with --eager)
   e2e   : the same step through the C ABI with host buffers: per-layer queries and new K/V copied from pinned
           host memory, the host KVManager step, and the attention output copied back, inside the timed region
   roofline : the attention kernel's algorithmic bytes (unique K/V bytes of the contexts) per launch / its
-          average CUDA-event duration, against the measured HBM copy peak
+          average duration (CUDA events around each launch with --eager; otherwise the replayed steps' CUDA-event
+          time over their launches, gaps between launches included), against the measured HBM copy peak
   cpu_baseline : the reference's own CPU paged_attention_cpu (oracle/_ref) on a bounded sample, all host cores
 
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config llama3-8b|...]
@@ -291,19 +293,42 @@ def run_ours(args, cfg, rank, world, dev):
     for s in range(W):
         step_device(s)
     torch.cuda.synchronize(dev)
+    # A step's per-layer launches are replayed from a CUDA graph (one per step: its lengths row is baked into
+    # the launches), so launch-bound small steps are not timed at the host's launch rate.
+    graphs = []
+    if not args.eager:
+        cap = torch.cuda.Stream(dev)
+        for s in range(W + K):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap, capture_error_mode="thread_local"):
+                lp = d_lens.data_ptr() + s * lens_row
+                csp = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+                for l in range(L):
+                    a = attn_args[l]
+                    a.seq_lens = lp
+                    assert L_lib.kvp_paged_attention(ctypes.byref(a), csp) == 0
+            graphs.append(g)
+        for s in range(W):
+            graphs[s].replay()
+        torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
-           for _ in range(K)]
+           for _ in range(K)] if args.eager else None
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(torch.cuda.current_device() if dev.index is None else dev.index) as clk:
         t_start.record(stream)
         for s in range(K):
-            step_device(W + s, evs[s])
+            if args.eager:
+                step_device(W + s, evs[s])
+            else:
+                graphs[W + s].replay()
         t_end.record(stream)
         torch.cuda.synchronize(dev)
     ms_total = t_start.elapsed_time(t_end)
-    attn_ms = [e0.elapsed_time(e1) for row in evs for (e0, e1) in row]
+    # per launch: CUDA events around each launch (eager), or the replayed step time over its launches
+    attn_ms = ([e0.elapsed_time(e1) for row in evs for (e0, e1) in row] if args.eager else [ms_total / (K * L)])
+    del graphs
     assert int(status.item()) == 0, f"device status {int(status.item())}"
     # algorithmic bytes per attention launch: unique K/V bytes of every context, averaged over the steps
     elem = 2
@@ -452,6 +477,7 @@ def main():
     ap.add_argument("--wph", type=int, default=0, help="tuning: consumer warps per kv head (0: automatic)")
     ap.add_argument("--stages", type=int, default=0, help="tuning: pipeline stages (0: automatic)")
     ap.add_argument("--no-e2e", action="store_true", help="tuning runs: skip the end-to-end leg")
+    ap.add_argument("--eager", action="store_true", help="launch every layer from Python instead of a CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--requests", type=int, default=0, help="profiling: requests per GPU (pool sized to need)")
     ap.add_argument("--layers", type=int, default=0, help="profiling: number of layers (pool sized to need)")
@@ -474,6 +500,8 @@ def main():
               "heads": cfg["nh"], "kv_heads": cfg["kvh"], "head_dim": cfg["D"], "layers": cfg["L"],
               "block_size": cfg["B"], "requests_per_gpu": cfg["ns"], "lengths": list(cfg["lens"]),
               "kv_dtype": cfg["dtype"], "l2": "inputs larger than L2 (every step reads the whole context)",
+              "launch": "per-layer launches from Python" if args.eager else
+                        "CUDA graph per step (one launch per layer, early start)",
               "parallelism": f"request-sharded x{args.gpus}, no collective"}
 
     if args.impl == "reference":
