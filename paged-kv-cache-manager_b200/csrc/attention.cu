@@ -67,6 +67,7 @@ struct AttnParams {
     uint32_t comb_off;     // offset of the warp-combine area in dynamic smem
     uint32_t pre_off;      // stream-K: offset of the prefix sums in dynamic smem
     int oob_row;           // a row coordinate outside the tensor map (zero fill) used for skipped blocks
+    int Bshift;            // log2(block_size) when it is a power of two, else -1
     float sl2;             // scale * log2(e)
     // Fused append (null when off): [num_seqs][kvh][D] K/V of each sequence's newest token, written into the
     // pools at position len - 1 before the tile that holds it is loaded.
@@ -76,6 +77,10 @@ struct AttnParams {
     void* v_pool;
     int kvh;
 };
+
+// Block index of a token position: a shift for power-of-two block sizes (no integer division in the
+// per-tile paths).
+__device__ __forceinline__ int blk_of(const AttnParams& p, int tok) { return p.Bshift >= 0 ? tok >> p.Bshift : tok / p.B; }
 
 // Sequence length in 16-token tiles, or 0 when the length is invalid (len < 1 or more blocks than a
 // table row holds).
@@ -107,7 +112,7 @@ __device__ __forceinline__ void produce_tile(const AttnParams& p, const CUtensor
     if (lane == 0) mbar_arrive_expect_tx(fb, static_cast<uint32_t>(nr) * G_::NCH * 2u * p.box_tx + extra_tx);
     for (int j = 0; j < nr; ++j) {
         const int tok = tb + j * p.R;
-        const int bi = tok / p.B;
+        const int bi = blk_of(p, tok);
         if (bi < cache_lo || bi >= cache_lo + 32) {
             cache_lo = bi;
             cached = (bi + lane < p.max_blocks) ? __ldg(trow + bi + lane) : 0;
@@ -146,7 +151,7 @@ template <int D>
 __device__ __forceinline__ void append_new_token(const AttnParams& p, int seq, int len, const int32_t* trow, int kvh0,
                                                  int lane) {
     const int pos = len - 1;
-    const int bi = pos / p.B;
+    const int bi = blk_of(p, pos);
     const int32_t blk = __ldg(trow + bi);
     if (blk >= 0 && blk < p.num_blocks) {
         const size_t row = static_cast<size_t>(blk) * p.B + (pos - bi * p.B);
@@ -168,24 +173,25 @@ __device__ __forceinline__ void append_new_token(const AttnParams& p, int seq, i
 
 // Up to 8 consecutive tiles of one sequence at once, lane k producing tile `tile + k` into stage
 // (i + k) % S: each lane waits for its own stage, arms its own barrier and issues its own copies, so the
-// per-tile issue cost is paid in parallel.  Only for one run per tile (block_size a multiple of 16).
-// Returns false (after reporting) if a wait gave up.
+// per-tile issue cost is paid in parallel.  Only for one run per tile (block_size a multiple of 16).  The
+// tile counter i is passed as (st0, r0) = (i % S, i / S); nb <= S.  Returns false (after reporting) if a wait
+// gave up.
 template <int D>
 __device__ __forceinline__ bool produce_batch(const AttnParams& p, const CUtensorMap* km, const CUtensorMap* vm,
-                                              uint32_t smem_base, uint64_t* full_bar, uint64_t* empty_bar, int i,
-                                              int tile, int nb, int len, const int32_t* trow, int kvh0, int lane,
-                                              int& cache_lo, int32_t& cached) {
+                                              uint32_t smem_base, uint64_t* full_bar, uint64_t* empty_bar, int st0,
+                                              int r0, int tile, int nb, int len, const int32_t* trow, int kvh0,
+                                              int lane, int& cache_lo, int32_t& cached) {
     using G_ = Geo<D>;
     const int S = p.stages;
-    const int bi_first = tile * 16 / p.B;
-    const int bi_last = (min((tile + nb) * 16, len) - 1) / p.B;
+    const int bi_first = blk_of(p, tile * 16);
+    const int bi_last = blk_of(p, min((tile + nb) * 16, len) - 1);
     if (bi_first < cache_lo || bi_last >= cache_lo + 32) {
         cache_lo = bi_first;
         cached = (bi_first + lane < p.max_blocks) ? __ldg(trow + bi_first + lane) : 0;
     }
     const bool act = lane < nb;
     const int tok = (tile + (act ? lane : 0)) * 16;
-    const int bi = tok / p.B;
+    const int bi = blk_of(p, tok);
     const int32_t blk = __shfl_sync(0xffffffffu, cached, bi - cache_lo);
     bool ok = true;
     if (act) {
@@ -194,9 +200,12 @@ __device__ __forceinline__ bool produce_batch(const AttnParams& p, const CUtenso
             report(p.status, KVP_STATUS_BAD_BLOCK);
             row = p.oob_row;
         }
-        const int ii = i + lane;
-        const int st = ii % S;
-        if (ii >= S && !mbar_wait(smem_u32(&empty_bar[st]), static_cast<uint32_t>((ii / S - 1) & 1))) {
+        int st = st0 + lane, r = r0;
+        if (st >= S) {
+            st -= S;
+            ++r;
+        }
+        if (r >= 1 && !mbar_wait(smem_u32(&empty_bar[st]), static_cast<uint32_t>((r - 1) & 1))) {
             report(p.status, KVP_STATUS_TIMEOUT);
             ok = false;
         }
@@ -659,7 +668,7 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
             prefetch_tensormap(vm);
         }
         bool ok = true;
-        int i = 0, j = 0;
+        int pst = 0, pr = 0, j = 0;  // stage and round (i % S, i / S) of the running tile counter i
         while (segs.next(sg)) {
             const int len = sg.len;
             const int32_t* trow = p.tables + static_cast<size_t>(sg.seq) * p.max_blocks;
@@ -686,11 +695,11 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
                 const int nb = min(nb_max, sg.tile1 - tile);
                 if (ok) {
                     if (nb_max > 1) {
-                        ok = produce_batch<D>(p, km, vm, smem_base, full_bar, empty_bar, i, tile, nb, len, trow, kvh0,
-                                              lane, cache_lo, cached);
+                        ok = produce_batch<D>(p, km, vm, smem_base, full_bar, empty_bar, pst, pr, tile, nb, len, trow,
+                                              kvh0, lane, cache_lo, cached);
                     } else {
-                        const int st = i % S;
-                        if (i >= S && !mbar_wait(smem_u32(&empty_bar[st]), static_cast<uint32_t>((i / S - 1) & 1))) {
+                        const int st = pst;
+                        if (pr >= 1 && !mbar_wait(smem_u32(&empty_bar[st]), static_cast<uint32_t>((pr - 1) & 1))) {
                             if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
                             ok = false;
                         } else {
@@ -702,7 +711,11 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
                     __syncwarp();
                 }
                 tile += nb;
-                i += nb;
+                pst += nb;
+                if (pst >= S) {
+                    pst -= S;
+                    ++pr;
+                }
             }
             ++j;
         }
@@ -720,7 +733,8 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
     float* comb = reinterpret_cast<float*>(dyn + p.comb_off);
     constexpr int NREG = Consumer<D, NT, KV>::NREG;
     bool ok = true;
-    int i = 0, j = 0;
+    int j = 0;
+    int cst = 0, cph = 0, turn = 0;  // stage, its phase and the sub-warp whose turn it is, for the next tile
     // Split segments of this CTA: at most two (only the first and the last segment of a CTA's range can be
     // parts of a longer sequence); pend[k] flags a merge, pend[2 + 3k ..] holds (seq, c0, nseg); old0 / old1
     // hold a writer warp's counter values from before its adds.
@@ -740,10 +754,16 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
             cs.load_q_global(p, sg.seq, kvh_global, lane);
         }
         cs.reset();
-        for (int tile = sg.tile0; tile < sg.tile1; ++tile, ++i) {
-            if (!ok || (i % p.wph) != sub) continue;
-            const int st = i % S;
-            if (!mbar_wait(smem_u32(&full_bar[st]), static_cast<uint32_t>((i / S) & 1))) {
+        for (int tile = sg.tile0; tile < sg.tile1; ++tile) {
+            const int st = cst, ph = cph;
+            const bool mine = turn == sub;
+            if (++cst == S) {
+                cst = 0;
+                cph ^= 1;
+            }
+            if (++turn == p.wph) turn = 0;
+            if (!ok || !mine) continue;
+            if (!mbar_wait(smem_u32(&full_bar[st]), static_cast<uint32_t>(ph))) {
                 if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
                 ok = false;
                 continue;
@@ -1549,6 +1569,10 @@ extern "C" KVP_API int kvp_paged_attention(const kvp_attn_args* a, void* stream)
     prm.pre_off = pl.pre_off;
     prm.wph = pl.wph;
     prm.oob_row = static_cast<int>(std::min<long long>(rows, 0x7fffffffLL));
+    prm.Bshift = -1;
+    if ((a->block_size & (a->block_size - 1)) == 0)
+        for (int b = 0; (1 << b) <= a->block_size; ++b)
+            if ((1 << b) == a->block_size) prm.Bshift = b;
     prm.k_new = a->k_new;
     prm.v_new = a->v_new;
     prm.k_pool = const_cast<void*>(a->k_cache);
