@@ -6,7 +6,9 @@
 // and one paged-attention launch per layer that first writes the layer's new K/V into the appended slot
 // (fused append) and then attends over the context including it.  With host buffers, a copy-in
 // stream feeds the new K/V and each layer's queries and a copy-out stream drains each layer's output as soon as
-// its attention finishes, so transfers overlap the attention of other layers.
+// its attention finishes, so transfers overlap the attention of other layers.  Once a step's key (batch size
+// and buffers) repeats, that whole body -- copies and launches on the three streams -- is replayed from one
+// CUDA graph, so a step costs the host a handful of runtime calls.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -90,14 +92,11 @@ int check_config(const kvp_decoder_config* c) {
 }  // namespace
 
 // What a captured step depends on besides the device-resident metadata: the batch size (it fixes the
-// metadata layout and the kernels' parameters), the per-layer buffers and whether per-layer events are used.
+// metadata layout and the kernels' parameters) and the per-layer buffers (device or host).
 struct GraphKey {
     int n = -1;
     const void *q = nullptr, *k = nullptr, *v = nullptr, *out = nullptr;
-    bool events = false;
-    bool operator==(const GraphKey& o) const {
-        return n == o.n && q == o.q && k == o.k && v == o.v && out == o.out && events == o.events;
-    }
+    bool operator==(const GraphKey& o) const { return n == o.n && q == o.q && k == o.k && v == o.v && out == o.out; }
 };
 
 struct kvp_decoder {
@@ -109,20 +108,24 @@ struct kvp_decoder {
     size_t meta_bytes = 0;
     int64_t layer_stride = 0;   // elements
     cudaStream_t s_in = nullptr, s_comp = nullptr, s_out = nullptr;
-    cudaEvent_t ev_meta = nullptr, ev_staged = nullptr, ev_done = nullptr;
+    cudaEvent_t ev_staged = nullptr;  // after the latest metadata upload (the pinned staging is reusable)
+    cudaEvent_t ev_fork = nullptr, ev_join_in = nullptr, ev_join_out = nullptr;
     std::vector<cudaEvent_t> ev_q, ev_att;
     std::vector<int32_t> pairs;
     int device = 0;
     GraphKey last_key, exec_key;  // the previous step's key; the key the instantiated graph was captured for
     cudaGraphExec_t exec = nullptr;
+    GraphKey last_full, full_key;  // the same for the whole host-buffer step (copies included)
+    cudaGraphExec_t exec_full = nullptr;
     bool graph_off = false;       // set when a capture failed: plain launches from then on
 
     ~kvp_decoder() {
         if (exec) cudaGraphExecDestroy(exec);
+        if (exec_full) cudaGraphExecDestroy(exec_full);
         if (h_meta) cudaFreeHost(h_meta);
         for (auto e : ev_q) cudaEventDestroy(e);
         for (auto e : ev_att) cudaEventDestroy(e);
-        for (auto e : {ev_meta, ev_staged, ev_done})
+        for (auto e : {ev_staged, ev_fork, ev_join_in, ev_join_out})
             if (e) cudaEventDestroy(e);
         for (auto s : {s_in, s_comp, s_out})
             if (s) cudaStreamDestroy(s);
@@ -201,23 +204,19 @@ int launch_cow(kvp_decoder* d, const int32_t* d_pairs, cudaStream_t s) {
 // The per-layer launches of a step: fused append + attention for every layer, each waiting for its inputs
 // (per-layer events, host path) and marking its output ready.  `ext` marks the event operations as
 // external nodes when the stream is being captured into a graph.
-int enqueue_layers(kvp_decoder* d, int n, const void* q, const void* knew, const void* vnew, void* out,
-                   cudaStream_t s_comp, bool per_layer_events, bool ext) {
+// Layer l's attention launch (fused append of its new token) on stream s; q / knew / vnew / out are the
+// device arrays of all layers.
+int launch_layer(kvp_decoder* d, int n, int l, const void* q, const void* knew, const void* vnew, void* out,
+                 cudaStream_t s_comp) {
     const kvp_decoder_config& c = d->cfg;
     const int32_t* meta = d->d_meta();
     const int32_t* d_tables = meta;
     const int32_t* d_lens = meta + static_cast<size_t>(n) * c.max_blocks_per_seq;
-    int rc = KVP_OK;
     const int split = c.split_tiles;  // 0: balanced schedule over the step's real context lengths
     const size_t kv_layer_bytes = static_cast<size_t>(d->layer_stride) * 2;
     const size_t q_layer = static_cast<size_t>(n) * c.num_heads * c.head_dim;
     const size_t kv_layer = static_cast<size_t>(n) * c.kv_heads * c.head_dim * elem(c.kv_dtype);
-    for (int l = 0; l < c.num_layers; ++l) {
-        if (per_layer_events) {
-            cudaError_t e = cudaStreamWaitEvent(s_comp, d->ev_q[static_cast<size_t>(l)],
-                                                ext ? cudaEventWaitExternal : cudaEventWaitDefault);
-            if (e != cudaSuccess) return kvpi::cuda_status(e, "decoder wait");
-        }
+    {
         kvp_attn_args a{};
         a.q = static_cast<const char*>(q) + q_layer * elem(c.q_dtype) * l;
         a.q_dtype = c.q_dtype;
@@ -244,25 +243,61 @@ int enqueue_layers(kvp_decoder* d, int n, const void* q, const void* knew, const
         a.flags = KVP_ATTN_WORKSPACE_CLEAN | KVP_ATTN_EARLY_START;
         a.k_new = static_cast<const char*>(knew) + kv_layer * l;  // fused append of this layer's new token
         a.v_new = static_cast<const char*>(vnew) + kv_layer * l;
-        rc = kvp_paged_attention(&a, s_comp);
+        return kvp_paged_attention(&a, s_comp);
+    }
+}
+
+// Every layer's launch, in order on stream s (device buffers).
+int enqueue_layers(kvp_decoder* d, int n, const void* q, const void* knew, const void* vnew, void* out,
+                   cudaStream_t s) {
+    for (int l = 0; l < d->cfg.num_layers; ++l) {
+        const int rc = launch_layer(d, n, l, q, knew, vnew, out, s);
         if (rc != KVP_OK) return rc;
-        if (per_layer_events) {
-            cudaError_t e = cudaEventRecordWithFlags(d->ev_att[static_cast<size_t>(l)], s_comp,
-                                                     ext ? cudaEventRecordExternal : cudaEventRecordDefault);
-            if (e != cudaSuccess) return kvpi::cuda_status(e, "decoder record");
-        }
     }
     return KVP_OK;
 }
 
-// Captures the per-layer launches into a graph and instantiates it.  Returns false (with the capture ended
-// and the error state cleared) if anything failed; the caller then launches them directly.
-bool capture_layers(kvp_decoder* d, const GraphKey& key, cudaStream_t s) {
-    if (cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
-        cudaGetLastError();
-        return false;
+// The host-buffer step's device work after the metadata upload and the copy-on-write copies, forked from and
+// joined back into the compute stream: per layer, its query and new K/V copies on the copy-in stream, its
+// attention launch on the compute stream once they have landed, and its output copy on the copy-out stream
+// once the launch is done, so transfers overlap the attention of other layers.  The same calls are captured
+// into one graph when a step's key repeats.
+int enqueue_host_body(kvp_decoder* d, int n, const char* hq, const char* hk, const char* hv, char* hout) {
+    const kvp_decoder_config& c = d->cfg;
+    const size_t q_layer = static_cast<size_t>(n) * c.num_heads * c.head_dim * elem(c.q_dtype);
+    const size_t o_layer = static_cast<size_t>(n) * c.num_heads * c.head_dim * elem(c.out_dtype);
+    const size_t kv_layer = static_cast<size_t>(n) * c.kv_heads * c.head_dim * elem(c.kv_dtype);
+    char* dq = d->ws + d->lay.q;
+    char* dk = d->ws + d->lay.k;
+    char* dv = d->ws + d->lay.v;
+    char* dout = d->ws + d->lay.out;
+    cudaError_t e = cudaEventRecord(d->ev_fork, d->s_comp);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(d->s_in, d->ev_fork, 0);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(d->s_out, d->ev_fork, 0);
+    for (int l = 0; e == cudaSuccess && l < c.num_layers; ++l) {
+        const size_t L = static_cast<size_t>(l);
+        e = cudaMemcpyAsync(dq + q_layer * L, hq + q_layer * L, q_layer, cudaMemcpyHostToDevice, d->s_in);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(dk + kv_layer * L, hk + kv_layer * L, kv_layer, cudaMemcpyHostToDevice, d->s_in);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(dv + kv_layer * L, hv + kv_layer * L, kv_layer, cudaMemcpyHostToDevice, d->s_in);
+        if (e == cudaSuccess) e = cudaEventRecord(d->ev_q[L], d->s_in);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(d->s_comp, d->ev_q[L], 0);
+        if (e != cudaSuccess) break;
+        const int rc = launch_layer(d, n, l, dq, dk, dv, dout, d->s_comp);
+        if (rc != KVP_OK) return rc;
+        e = cudaEventRecord(d->ev_att[L], d->s_comp);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(d->s_out, d->ev_att[L], 0);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(hout + o_layer * L, dout + o_layer * L, o_layer, cudaMemcpyDeviceToHost, d->s_out);
     }
-    const int rc = enqueue_layers(d, key.n, key.q, key.k, key.v, const_cast<void*>(key.out), s, key.events, true);
+    if (e == cudaSuccess) e = cudaEventRecord(d->ev_join_in, d->s_in);
+    if (e == cudaSuccess) e = cudaEventRecord(d->ev_join_out, d->s_out);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(d->s_comp, d->ev_join_in, 0);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(d->s_comp, d->ev_join_out, 0);
+    return kvpi::cuda_status(e, "decoder step copies");
+}
+
+// Ends a capture on s and instantiates its graph into *out (replacing any previous one).  Returns false, with
+// the error state cleared, if the capture or the instantiation failed.
+bool finish_capture(cudaStream_t s, int rc, cudaGraphExec_t* out) {
     cudaGraph_t g = nullptr;
     const cudaError_t e = cudaStreamEndCapture(s, &g);
     cudaGraphExec_t ex = nullptr;
@@ -274,14 +309,41 @@ bool capture_layers(kvp_decoder* d, const GraphKey& key, cudaStream_t s) {
         kvpi::clear_error();
         return false;
     }
-    if (d->exec) cudaGraphExecDestroy(d->exec);
-    d->exec = ex;
+    if (*out) cudaGraphExecDestroy(*out);
+    *out = ex;
+    return true;
+}
+
+// Captures the per-layer launches (device buffers) into a graph and instantiates it.  Returns false if
+// anything failed; the caller then launches them directly.
+bool capture_layers(kvp_decoder* d, const GraphKey& key, cudaStream_t s) {
+    if (cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    const int rc = enqueue_layers(d, key.n, key.q, key.k, key.v, const_cast<void*>(key.out), s);
+    if (!finish_capture(s, rc, &d->exec)) return false;
     d->exec_key = key;
     return true;
 }
 
+// The same for the whole host-buffer step body (copies included), captured from the compute stream.
+bool capture_host_body(kvp_decoder* d, const GraphKey& key) {
+    if (cudaStreamBeginCapture(d->s_comp, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    const int rc = enqueue_host_body(d, key.n, static_cast<const char*>(key.q), static_cast<const char*>(key.k),
+                                     static_cast<const char*>(key.v), static_cast<char*>(const_cast<void*>(key.out)));
+    if (!finish_capture(d->s_comp, rc, &d->exec_full)) return false;
+    d->full_key = key;
+    return true;
+}
+
+// Device-buffer step after the metadata upload: copy-on-write copies, then the layer launches (replayed from
+// a graph once the key repeats, unless the caller is capturing the stream itself).
 int enqueue_device(kvp_decoder* d, int n, const void* q, const void* knew, const void* vnew, void* out,
-                   cudaStream_t s_comp, bool per_layer_events) {
+                   cudaStream_t s_comp) {
     const kvp_decoder_config& c = d->cfg;
     const int32_t* d_pairs = d->d_meta() + static_cast<size_t>(n) * c.max_blocks_per_seq + n;
     int rc = launch_cow(d, d_pairs, s_comp);
@@ -293,7 +355,6 @@ int enqueue_device(kvp_decoder* d, int n, const void* q, const void* knew, const
         key.k = knew;
         key.v = vnew;
         key.out = out;
-        key.events = per_layer_events;
         cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
         // The legacy default stream cannot be captured; a stream the caller is capturing records our launches.
         const bool capturable = s_comp != nullptr && cudaStreamIsCapturing(s_comp, &cs) == cudaSuccess &&
@@ -306,7 +367,7 @@ int enqueue_device(kvp_decoder* d, int n, const void* q, const void* knew, const
                 return kvpi::cuda_status(cudaGraphLaunch(d->exec, s_comp), "decoder graph launch");
         }
     }
-    return enqueue_layers(d, n, q, knew, vnew, out, s_comp, per_layer_events, false);
+    return enqueue_layers(d, n, q, knew, vnew, out, s_comp);
 }
 
 int upload_meta(kvp_decoder* d, int n, cudaStream_t s) {
@@ -404,9 +465,10 @@ KVP_API kvp_decoder* kvp_decoder_create(const kvp_decoder_config* c, kvp_mgr* mg
     ok = ok && cudaStreamCreateWithFlags(&d->s_in, cudaStreamNonBlocking) == cudaSuccess;
     ok = ok && cudaStreamCreateWithFlags(&d->s_comp, cudaStreamNonBlocking) == cudaSuccess;
     ok = ok && cudaStreamCreateWithFlags(&d->s_out, cudaStreamNonBlocking) == cudaSuccess;
-    ok = ok && cudaEventCreateWithFlags(&d->ev_meta, cudaEventDisableTiming) == cudaSuccess;
     ok = ok && cudaEventCreateWithFlags(&d->ev_staged, cudaEventDisableTiming) == cudaSuccess;
-    ok = ok && cudaEventCreateWithFlags(&d->ev_done, cudaEventDisableTiming) == cudaSuccess;
+    ok = ok && cudaEventCreateWithFlags(&d->ev_fork, cudaEventDisableTiming) == cudaSuccess;
+    ok = ok && cudaEventCreateWithFlags(&d->ev_join_in, cudaEventDisableTiming) == cudaSuccess;
+    ok = ok && cudaEventCreateWithFlags(&d->ev_join_out, cudaEventDisableTiming) == cudaSuccess;
     d->ev_q.resize(static_cast<size_t>(c->num_layers));
     d->ev_att.resize(static_cast<size_t>(c->num_layers));
     for (int l = 0; ok && l < c->num_layers; ++l) {
@@ -450,7 +512,7 @@ KVP_API int kvp_decoder_step_device(kvp_decoder* d, const int64_t* rids, int32_t
         cudaStream_t s = static_cast<cudaStream_t>(stream);
         rc = upload_meta(d, n, s);
         if (rc != KVP_OK) return rc;
-        return enqueue_device(d, n, q, k_new, v_new, out, s, false);
+        return enqueue_device(d, n, q, k_new, v_new, out, s);
     });
 }
 
@@ -466,43 +528,35 @@ KVP_API int kvp_decoder_step(kvp_decoder* d, const int64_t* rids, int32_t n, con
         if (rc != KVP_OK) return rc;
         rc = host_step(d, rids, n);
         if (rc != KVP_OK) return rc;
-        const size_t q_layer = static_cast<size_t>(n) * c.num_heads * c.head_dim * elem(c.q_dtype);
-        const size_t o_layer = static_cast<size_t>(n) * c.num_heads * c.head_dim * elem(c.out_dtype);
-        const size_t kv_layer = static_cast<size_t>(n) * c.kv_heads * c.head_dim * elem(c.kv_dtype);
-        char* dq = d->ws + d->lay.q;
-        char* dk = d->ws + d->lay.k;
-        char* dv = d->ws + d->lay.v;
-        char* dout = d->ws + d->lay.out;
-        // copy-in stream: metadata, then each layer's queries and new K/V (a layer's launch waits only for
-        // its own inputs)
-        rc = upload_meta(d, n, d->s_in);
+        // compute stream: metadata, copy-on-write copies, then the step body (copies in, launches, copies out)
+        rc = upload_meta(d, n, d->s_comp);
         if (rc != KVP_OK) return rc;
-        cudaError_t e = cudaEventRecord(d->ev_meta, d->s_in);
-        for (int l = 0; e == cudaSuccess && l < c.num_layers; ++l) {
-            e = cudaMemcpyAsync(dq + q_layer * l, static_cast<const char*>(q) + q_layer * l, q_layer,
-                                cudaMemcpyHostToDevice, d->s_in);
-            if (e == cudaSuccess)
-                e = cudaMemcpyAsync(dk + kv_layer * l, static_cast<const char*>(k_new) + kv_layer * l, kv_layer,
-                                    cudaMemcpyHostToDevice, d->s_in);
-            if (e == cudaSuccess)
-                e = cudaMemcpyAsync(dv + kv_layer * l, static_cast<const char*>(v_new) + kv_layer * l, kv_layer,
-                                    cudaMemcpyHostToDevice, d->s_in);
-            if (e == cudaSuccess) e = cudaEventRecord(d->ev_q[static_cast<size_t>(l)], d->s_in);
-        }
-        if (e != cudaSuccess) return kvpi::cuda_status(e, "decoder input copies");
-        e = cudaStreamWaitEvent(d->s_comp, d->ev_meta, 0);
-        if (e != cudaSuccess) return kvpi::cuda_status(e, "decoder wait");
-        rc = enqueue_device(d, n, dq, dk, dv, dout, d->s_comp, true);
+        const int32_t* d_pairs = d->d_meta() + static_cast<size_t>(n) * c.max_blocks_per_seq + n;
+        rc = launch_cow(d, d_pairs, d->s_comp);
         if (rc != KVP_OK) return rc;
-        // copy-out stream: each layer's output as soon as its attention is done
-        for (int l = 0; e == cudaSuccess && l < c.num_layers; ++l) {
-            e = cudaStreamWaitEvent(d->s_out, d->ev_att[static_cast<size_t>(l)], 0);
-            if (e == cudaSuccess)
-                e = cudaMemcpyAsync(static_cast<char*>(out) + o_layer * l, dout + o_layer * l, o_layer,
-                                    cudaMemcpyDeviceToHost, d->s_out);
+        bool launched = false;
+        if (c.graph && !d->graph_off) {
+            GraphKey key;
+            key.n = n;
+            key.q = q;
+            key.k = k_new;
+            key.v = v_new;
+            key.out = out;
+            const bool repeat = key == d->last_full;
+            d->last_full = key;
+            if (!(d->exec_full && d->full_key == key) && repeat && !capture_host_body(d, key)) d->graph_off = true;
+            if (d->exec_full && d->full_key == key) {
+                const cudaError_t e = cudaGraphLaunch(d->exec_full, d->s_comp);
+                if (e != cudaSuccess) return kvpi::cuda_status(e, "decoder graph launch");
+                launched = true;
+            }
         }
-        if (e == cudaSuccess) e = cudaStreamSynchronize(d->s_out);
-        return kvpi::cuda_status(e, "decoder output copies");
+        if (!launched) {
+            rc = enqueue_host_body(d, n, static_cast<const char*>(q), static_cast<const char*>(k_new),
+                                   static_cast<const char*>(v_new), static_cast<char*>(out));
+            if (rc != KVP_OK) return rc;
+        }
+        return kvpi::cuda_status(cudaStreamSynchronize(d->s_comp), "decoder step");  // outputs are in host memory
     });
 }
 
