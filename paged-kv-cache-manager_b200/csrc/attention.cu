@@ -1,28 +1,6 @@
-// Paged decode attention for sm_100a: flash-decoding over 16-token tiles of the context.
-//
-// Two schedules share the same tile pipeline:
-//   * stream-K (default): a persistent grid of as many CTAs as fit on the GPU; the step's tiles (all
-//     sequences, concatenated) are divided evenly between CTAs regardless of sequence boundaries, so every
-//     CTA streams the same number of bytes with one pipeline ramp per launch.  A CTA's range is cut into
-//     segments at sequence boundaries; a segment that covers a whole sequence is normalised and written
-//     directly, the others leave (m, l, unnormalised O) partials that merge_streamk combines.
-//   * fixed splits: one CTA per (sequence, kv-head group, split of split_tiles tiles); split_tiles large
-//     enough means one CTA per sequence and no workspace at all (the reference's signature).
-//
-// Tile pipeline (per CTA): a producer warp reads block ids from the sequence's table row (32 entries per
-// coalesced load) and issues TMA tiled loads of the K and V rows of every kv head of the CTA's group into a
-// ring of shared-memory stages (128B/64B swizzled; completion counted on an mbarrier); at the start of a
-// stream-K segment it also bulk-copies the sequence's queries into the stage.  One consumer warp per kv head
-// computes, per tile,
-//     S^T[16 tokens x 8 heads] = K_tile[16 x D] . Q^T[D x 8]      (mma.sync m16n8k16, fp32 accumulate)
-// so the GQA group of query heads (up to 8 per n-tile) shares every K/V byte; an online softmax in the
-// log2 domain with warp-shuffle reductions; then
-//     O^T[D x 8] += V_tile^T[D x 16] . P^T[16 x 8]
-// with P^T obtained from the S^T accumulator by movmatrix.  P (and an fp32 query) are split into a 16-bit
-// high part plus a 16-bit residual, so the result keeps close to fp32 accuracy.
-//
-// Numerics follow the reference's paged_attention_cpu (src/paged_attention.cpp:68-114): per-partition
-// running (m, l, acc) with rescaling by exp(m_old - m_new), partitions merged by exp(m_p - M).
+// Paged decode attention: host side -- launch planning, tensor maps, workspace, the C ABI entry point.  The
+// kernels live in attention_kernels.cuh and are compiled by attention_inst_*.cu (one translation unit per
+// K/V dtype x query residual).
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
@@ -31,1101 +9,10 @@
 #include <cmath>
 #include <cstring>
 #include <mutex>
-#include <type_traits>
 #include <utility>
 #include <vector>
 
-#include "kvp_device.cuh"
-#include "kvp_internal.h"
-
-namespace kvpd {
-
-constexpr int kMaxStages = 16;
-constexpr int kMaxConsumerWarps = 8;
-constexpr int kMaxKvhPerCta = 8;
-constexpr int kMaxStreamSeqs = 8192;  // stream-K keeps the tile prefix sums of all sequences in smem
-
-struct AttnParams {
-    const void* q;
-    const int32_t* tables;
-    const int32_t* lens;
-    void* out;
-    float2* ws_ml;   // partial (m in log2 units, l) rows of nh heads
-    float* ws_o;     // partial unnormalised outputs, D per row
-    int32_t* counters;  // stream-K: [num_seqs][groups] finished-segment counters (zero between calls)
-    int32_t* status;
-    long long num_blocks;  // 0: unchecked
-    int q_dtype, out_dtype;
-    int num_seqs, nh, g, max_blocks, B, R, nruns;
-    int kvh_cta, groups, stages, split_tiles, max_splits, per_head;
-    int G;                 // stream-K CTAs per kv-head group
-    int wph;               // consumer warps per kv head (they take turns over the stages)
-    uint32_t head_stride, box_slot, stage_half, box_tx;
-    uint32_t stage_bytes;  // stride between stages (2 * stage_half)
-    uint32_t q_area;       // bytes of one query slot (0: queries read from global memory)
-    uint32_t q_off;        // offset of the two query slots in dynamic smem
-    uint32_t comb_off;     // offset of the warp-combine area in dynamic smem
-    uint32_t pre_off;      // stream-K: offset of the prefix sums in dynamic smem
-    int oob_row;           // a row coordinate outside the tensor map (zero fill) used for skipped blocks
-    int Bshift;            // log2(block_size) when it is a power of two, else -1
-    float sl2;             // scale * log2(e)
-    // Fused append (null when off): [num_seqs][kvh][D] K/V of each sequence's newest token, written into the
-    // pools at position len - 1 before the tile that holds it is loaded.
-    const void* k_new;
-    const void* v_new;
-    void* k_pool;
-    void* v_pool;
-    int kvh;
-};
-
-// Block index of a token position: a shift for power-of-two block sizes (no integer division in the
-// per-tile paths).
-__device__ __forceinline__ int blk_of(const AttnParams& p, int tok) { return p.Bshift >= 0 ? tok >> p.Bshift : tok / p.B; }
-
-// Sequence length in 16-token tiles, or 0 when the length is invalid (len < 1 or more blocks than a
-// table row holds).
-__device__ __forceinline__ int tiles_of_len(const AttnParams& p, int len) {
-    const long long nblk = (static_cast<long long>(len) + p.B - 1) / p.B;
-    if (len < 1 || nblk > p.max_blocks) return 0;
-    return (len + 15) >> 4;
-}
-
-template <int D>
-struct Geo {
-    static constexpr int W = (D % 64 == 0) ? 64 : 32;  // elements per smem row
-    static constexpr int ROWB = W * 2;                  // bytes per smem row
-    static constexpr int NCH = D / W;
-    static constexpr int KS = D / 16;                   // k-steps of the score MMA / m-tiles of the PV MMA
-    static constexpr uint32_t SWM = (ROWB == 128) ? 7u : 3u;
-};
-
-// ---------------------------------------------------------------- producer: one tile into one stage
-// All 32 lanes call this (the table cache is a warp-wide register array); lane 0 issues the copies.
-// Returns the transaction bytes the tile adds to the stage's barrier.
-template <int D>
-__device__ __forceinline__ void produce_tile(const AttnParams& p, const CUtensorMap* km, const CUtensorMap* vm,
-                                             uint32_t kst, uint32_t vst, uint32_t fb, int tb, int len,
-                                             const int32_t* trow, int kvh0, int lane, int& cache_lo,
-                                             int32_t& cached, uint32_t extra_tx) {
-    using G_ = Geo<D>;
-    const int nr = min(p.nruns, (len - tb + p.R - 1) / p.R);
-    if (lane == 0) mbar_arrive_expect_tx(fb, static_cast<uint32_t>(nr) * G_::NCH * 2u * p.box_tx + extra_tx);
-    for (int j = 0; j < nr; ++j) {
-        const int tok = tb + j * p.R;
-        const int bi = blk_of(p, tok);
-        if (bi < cache_lo || bi >= cache_lo + 32) {
-            cache_lo = bi;
-            cached = (bi + lane < p.max_blocks) ? __ldg(trow + bi + lane) : 0;
-        }
-        const int32_t blk = __shfl_sync(0xffffffffu, cached, bi - cache_lo);
-        int row = blk * p.B + (tok - bi * p.B);
-        if (p.num_blocks > 0 && (blk < 0 || blk >= p.num_blocks)) {
-            if (lane == 0) report(p.status, KVP_STATUS_BAD_BLOCK);
-            row = p.oob_row;
-        }
-        if (lane == 0) {
-#pragma unroll
-            for (int c = 0; c < G_::NCH; ++c) {
-                const uint32_t off = static_cast<uint32_t>(j * G_::NCH + c) * p.box_slot;
-                if (!p.per_head) {
-                    tma_load_3d(kst + off, km, fb, c * G_::W, row, kvh0);
-                    tma_load_3d(vst + off, vm, fb, c * G_::W, row, kvh0);
-                } else {
-                    for (int w = 0; w < p.kvh_cta; ++w) {
-                        const uint32_t ho = off + static_cast<uint32_t>(w) * p.head_stride;
-                        tma_load_3d(kst + ho, km, fb, c * G_::W, kvh0 + w, row);
-                        tma_load_3d(vst + ho, vm, fb, c * G_::W, kvh0 + w, row);
-                    }
-                }
-            }
-        }
-    }
-}
-
-// Fused append: the producer warp writes the newest token's K and V rows of the CTA's kv heads (position
-// len - 1, one contiguous kvh_cta * D run per pool) before it issues the copies of the segment holding that
-// position.  Each lane fences its stores against the async proxy and the warp synchronises, so the TMA loads
-// issued afterwards by any lane see the new rows.  An out-of-range block id is skipped here (the tile load
-// reports it and zero-fills).
-template <int D>
-__device__ __forceinline__ void append_new_token(const AttnParams& p, int seq, int len, const int32_t* trow, int kvh0,
-                                                 int lane) {
-    const int pos = len - 1;
-    const int bi = blk_of(p, pos);
-    const int32_t blk = __ldg(trow + bi);
-    if (blk >= 0 && blk < p.num_blocks) {
-        const size_t row = static_cast<size_t>(blk) * p.B + (pos - bi * p.B);
-        const size_t src = (static_cast<size_t>(seq) * p.kvh + kvh0) * D / 8;  // 16-byte chunks
-        const size_t dst = (row * p.kvh + kvh0) * D / 8;
-        const uint4* ks = static_cast<const uint4*>(p.k_new) + src;
-        const uint4* vs = static_cast<const uint4*>(p.v_new) + src;
-        uint4* kd = static_cast<uint4*>(p.k_pool) + dst;
-        uint4* vd = static_cast<uint4*>(p.v_pool) + dst;
-        const int chunks = p.kvh_cta * D / 8;
-        for (int c = lane; c < chunks; c += 32) {
-            kd[c] = __ldg(ks + c);
-            vd[c] = __ldg(vs + c);
-        }
-    }
-    fence_proxy_async_global();
-    __syncwarp();
-}
-
-// Up to 8 consecutive tiles of one sequence at once, lane k producing tile `tile + k` into stage
-// (i + k) % S: each lane waits for its own stage, arms its own barrier and issues its own copies, so the
-// per-tile issue cost is paid in parallel.  Only for one run per tile (block_size a multiple of 16).  The
-// tile counter i is passed as (st0, r0) = (i % S, i / S); nb <= S.  Returns false (after reporting) if a wait
-// gave up.
-template <int D>
-__device__ __forceinline__ bool produce_batch(const AttnParams& p, const CUtensorMap* km, const CUtensorMap* vm,
-                                              uint32_t smem_base, uint64_t* full_bar, uint64_t* empty_bar, int st0,
-                                              int r0, int tile, int nb, int len, const int32_t* trow, int kvh0,
-                                              int lane, int& cache_lo, int32_t& cached) {
-    using G_ = Geo<D>;
-    const int S = p.stages;
-    const int bi_first = blk_of(p, tile * 16);
-    const int bi_last = blk_of(p, min((tile + nb) * 16, len) - 1);
-    if (bi_first < cache_lo || bi_last >= cache_lo + 32) {
-        cache_lo = bi_first;
-        cached = (bi_first + lane < p.max_blocks) ? __ldg(trow + bi_first + lane) : 0;
-    }
-    const bool act = lane < nb;
-    const int tok = (tile + (act ? lane : 0)) * 16;
-    const int bi = blk_of(p, tok);
-    const int32_t blk = __shfl_sync(0xffffffffu, cached, bi - cache_lo);
-    bool ok = true;
-    if (act) {
-        int row = blk * p.B + (tok - bi * p.B);
-        if (p.num_blocks > 0 && (blk < 0 || blk >= p.num_blocks)) {
-            report(p.status, KVP_STATUS_BAD_BLOCK);
-            row = p.oob_row;
-        }
-        int st = st0 + lane, r = r0;
-        if (st >= S) {
-            st -= S;
-            ++r;
-        }
-        if (r >= 1 && !mbar_wait(smem_u32(&empty_bar[st]), static_cast<uint32_t>((r - 1) & 1))) {
-            report(p.status, KVP_STATUS_TIMEOUT);
-            ok = false;
-        }
-        if (ok) {
-            const uint32_t fb = smem_u32(&full_bar[st]);
-            const uint32_t kst = smem_base + static_cast<uint32_t>(st) * p.stage_bytes;
-            const uint32_t vst = kst + p.stage_half;
-            mbar_arrive_expect_tx(fb, static_cast<uint32_t>(G_::NCH) * 2u * p.box_tx);
-#pragma unroll
-            for (int c = 0; c < G_::NCH; ++c) {
-                const uint32_t off = static_cast<uint32_t>(c) * p.box_slot;
-                if (!p.per_head) {
-                    tma_load_3d(kst + off, km, fb, c * G_::W, row, kvh0);
-                    tma_load_3d(vst + off, vm, fb, c * G_::W, row, kvh0);
-                } else {
-                    for (int w = 0; w < p.kvh_cta; ++w) {
-                        const uint32_t ho = off + static_cast<uint32_t>(w) * p.head_stride;
-                        tma_load_3d(kst + ho, km, fb, c * G_::W, kvh0 + w, row);
-                        tma_load_3d(vst + ho, vm, fb, c * G_::W, kvh0 + w, row);
-                    }
-                }
-            }
-        }
-    }
-    return __all_sync(0xffffffffu, ok);
-}
-
-// ---------------------------------------------------------------- consumer: one warp, one kv head
-template <int D, int NT, class KV>
-struct Consumer {
-    using G_ = Geo<D>;
-    using Tr = F16Traits<KV>;
-    static constexpr int KS = G_::KS;
-    uint32_t k_row_off, v_row_off, k_x, v_x;
-    int k_doff, v_doff;
-    uint32_t qhi[NT][KS][2], qlo[NT][KS][2];
-    float o[NT][KS][4];
-    float m_run[NT][2], l_run[NT][2];
-
-    // Per-lane shared-memory geometry.  For ldmatrix matrix index jm = lane >> 3 and row rr = lane & 7:
-    //   score operand (K, non-transposed): token (jm & 1) * 8 + rr, dim offset (jm >> 1) * 8
-    //   PV operand    (V, transposed):     token (jm >> 1) * 8 + rr, dim offset (jm & 1) * 8
-    __device__ __forceinline__ void init_geometry(const AttnParams& p, int warp, int lane) {
-        const int jm = lane >> 3, rr = lane & 7;
-        const int tk = (jm & 1) * 8 + rr;
-        const int tv = (jm >> 1) * 8 + rr;
-        const uint32_t hoff = static_cast<uint32_t>(warp) * p.head_stride;
-        k_row_off = static_cast<uint32_t>(tk / p.R) * G_::NCH * p.box_slot + hoff + static_cast<uint32_t>(tk % p.R) * G_::ROWB;
-        v_row_off = static_cast<uint32_t>(tv / p.R) * G_::NCH * p.box_slot + hoff + static_cast<uint32_t>(tv % p.R) * G_::ROWB;
-        k_x = (k_row_off >> 7) & G_::SWM;  // swizzle phase of this row (box slots are 1024-byte aligned)
-        v_x = (v_row_off >> 7) & G_::SWM;
-        k_doff = (jm >> 1) * 8;
-        v_doff = (jm & 1) * 8;
-    }
-
-    __device__ __forceinline__ void reset() {
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            m_run[nt][0] = m_run[nt][1] = -INFINITY;
-            l_run[nt][0] = l_run[nt][1] = 0.f;
-#pragma unroll
-            for (int ks = 0; ks < KS; ++ks) o[nt][ks][0] = o[nt][ks][1] = o[nt][ks][2] = o[nt][ks][3] = 0.f;
-        }
-    }
-
-    __device__ __forceinline__ void set_q(int nt, int ks, int h, float x0, float x1) {
-        const uint32_t hi = Tr::pack(x0, x1);
-        qhi[nt][ks][h] = hi;
-        qlo[nt][ks][h] = Tr::pack(x0 - Tr::unpack_lo(hi), x1 - Tr::unpack_hi(hi));
-    }
-
-    // Query fragments (B operand of the score MMA): head nt*8+gid, dims ks*16 + 2*c4 (+1, +8, +9), read from
-    // global memory.
-    __device__ __forceinline__ void load_q_global(const AttnParams& p, int seq, int kvh_global, int lane) {
-        const int gid = lane >> 2, c4 = lane & 3;
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            const int j = nt * 8 + gid;
-            const bool live = j < p.g;
-            const size_t qbase = (static_cast<size_t>(seq) * p.nh + kvh_global * p.g + (live ? j : 0)) * D;
-#pragma unroll
-            for (int ks = 0; ks < KS; ++ks)
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int d = ks * 16 + 2 * c4 + h * 8;
-                    set_q(nt, ks, h, live ? load_any(p.q, qbase + d, p.q_dtype) : 0.f,
-                          live ? load_any(p.q, qbase + d + 1, p.q_dtype) : 0.f);
-                }
-        }
-    }
-
-    // Same from the query area of a stage: [kvh_cta * g heads][D] in the query dtype (a generic pointer into
-    // shared memory; every load is issued before the conversions).
-    __device__ __forceinline__ void load_q_smem(const AttnParams& p, const uint8_t* qs, int warp, int lane) {
-        const int gid = lane >> 2, c4 = lane & 3;
-        if (p.q_dtype == KVP_DTYPE_F32) {
-            float2 v[NT][KS][2];
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                const int j = nt * 8 + gid;
-                const float* row = reinterpret_cast<const float*>(qs) + (warp * p.g + (j < p.g ? j : 0)) * D;
-#pragma unroll
-                for (int ks = 0; ks < KS; ++ks)
-#pragma unroll
-                    for (int h = 0; h < 2; ++h)
-                        v[nt][ks][h] = *reinterpret_cast<const float2*>(row + ks * 16 + 2 * c4 + h * 8);
-            }
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                const bool live = nt * 8 + gid < p.g;
-#pragma unroll
-                for (int ks = 0; ks < KS; ++ks)
-#pragma unroll
-                    for (int h = 0; h < 2; ++h)
-                        set_q(nt, ks, h, live ? v[nt][ks][h].x : 0.f, live ? v[nt][ks][h].y : 0.f);
-            }
-        } else {
-            uint32_t v[NT][KS][2];
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                const int j = nt * 8 + gid;
-                const uint16_t* row = reinterpret_cast<const uint16_t*>(qs) + (warp * p.g + (j < p.g ? j : 0)) * D;
-#pragma unroll
-                for (int ks = 0; ks < KS; ++ks)
-#pragma unroll
-                    for (int h = 0; h < 2; ++h)
-                        v[nt][ks][h] = *reinterpret_cast<const uint32_t*>(row + ks * 16 + 2 * c4 + h * 8);
-            }
-            const bool f16 = p.q_dtype == KVP_DTYPE_F16;
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                const bool live = nt * 8 + gid < p.g;
-#pragma unroll
-                for (int ks = 0; ks < KS; ++ks)
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const uint32_t x = v[nt][ks][h];
-                        float x0 = f16 ? F16Traits<__half>::unpack_lo(x) : F16Traits<__nv_bfloat16>::unpack_lo(x);
-                        float x1 = f16 ? F16Traits<__half>::unpack_hi(x) : F16Traits<__nv_bfloat16>::unpack_hi(x);
-                        set_q(nt, ks, h, live ? x0 : 0.f, live ? x1 : 0.f);
-                    }
-            }
-        }
-    }
-
-    // One 16-token tile: `valid` rows hold context tokens.
-    __device__ __forceinline__ void tile(const AttnParams& p, uint32_t kst, uint32_t vst, int valid, int warp,
-                                         int lane, bool use_qlo) {
-        const int gid = lane >> 2;
-        float sacc[NT][4];
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
-        // ---- scores S^T = K . Q^T
-#pragma unroll
-        for (int ks = 0; ks < KS; ++ks) {
-            const int d = ks * 16 + k_doff;
-            const uint32_t addr = kst + k_row_off + static_cast<uint32_t>(d / G_::W) * p.box_slot +
-                                  ((static_cast<uint32_t>((d % G_::W) >> 3) ^ k_x) << 4);
-            uint32_t a[4];
-            ldsm_x4(addr, a);
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                mma16816<KV>(sacc[nt], a, qhi[nt][ks][0], qhi[nt][ks][1]);
-                if (use_qlo) mma16816<KV>(sacc[nt], a, qlo[nt][ks][0], qlo[nt][ks][1]);
-            }
-        }
-        // ---- online softmax (log2 domain); rows gid / gid+8 are tokens, columns 2*c4, 2*c4+1 heads
-        uint32_t pb_hi[NT][2], pb_lo[NT][2];
-        const bool row0_ok = gid < valid, row1_ok = gid + 8 < valid;
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            float sv[4];
-            sv[0] = row0_ok ? sacc[nt][0] * p.sl2 : -INFINITY;
-            sv[1] = row0_ok ? sacc[nt][1] * p.sl2 : -INFINITY;
-            sv[2] = row1_ok ? sacc[nt][2] * p.sl2 : -INFINITY;
-            sv[3] = row1_ok ? sacc[nt][3] * p.sl2 : -INFINITY;
-            float mx0 = fmaxf(sv[0], sv[2]), mx1 = fmaxf(sv[1], sv[3]);
-#pragma unroll
-            for (int off = 4; off < 32; off <<= 1) {
-                mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
-                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
-            }
-            const float mn0 = fmaxf(m_run[nt][0], mx0), mn1 = fmaxf(m_run[nt][1], mx1);
-            const float corr0 = fast_exp2(m_run[nt][0] - mn0), corr1 = fast_exp2(m_run[nt][1] - mn1);
-            m_run[nt][0] = mn0;
-            m_run[nt][1] = mn1;
-            const float p0 = fast_exp2(sv[0] - mn0), p1 = fast_exp2(sv[1] - mn1);
-            const float p2 = fast_exp2(sv[2] - mn0), p3 = fast_exp2(sv[3] - mn1);
-            l_run[nt][0] = l_run[nt][0] * corr0 + (p0 + p2);
-            l_run[nt][1] = l_run[nt][1] * corr1 + (p1 + p3);
-#pragma unroll
-            for (int ks = 0; ks < KS; ++ks) {
-                o[nt][ks][0] *= corr0;
-                o[nt][ks][1] *= corr1;
-                o[nt][ks][2] *= corr0;
-                o[nt][ks][3] *= corr1;
-            }
-            const uint32_t h01 = Tr::pack(p0, p1), h23 = Tr::pack(p2, p3);
-            const uint32_t l01 = Tr::pack(p0 - Tr::unpack_lo(h01), p1 - Tr::unpack_hi(h01));
-            const uint32_t l23 = Tr::pack(p2 - Tr::unpack_lo(h23), p3 - Tr::unpack_hi(h23));
-            pb_hi[nt][0] = movmatrix_trans(h01);
-            pb_hi[nt][1] = movmatrix_trans(h23);
-            pb_lo[nt][0] = movmatrix_trans(l01);
-            pb_lo[nt][1] = movmatrix_trans(l23);
-        }
-        // ---- rows past the end of the context: zero this head's V rows so stale bytes cannot turn
-        // 0 * garbage into NaN in the PV product.
-        if (valid < 16) {
-            constexpr int UPR = G_::NCH * (G_::W / 8);  // 16-byte units per token row of one head
-            const int units = (16 - valid) * UPR;
-            for (int u = lane; u < units; u += 32) {
-                const int t = valid + u / UPR;
-                const int rem = u % UPR;
-                const int c = rem / (G_::W / 8), cu = rem % (G_::W / 8);
-                const uint32_t ro = static_cast<uint32_t>(t / p.R) * G_::NCH * p.box_slot +
-                                    static_cast<uint32_t>(c) * p.box_slot + static_cast<uint32_t>(warp) * p.head_stride +
-                                    static_cast<uint32_t>(t % p.R) * G_::ROWB;
-                const uint32_t a = vst + ro + ((static_cast<uint32_t>(cu) ^ ((ro >> 7) & G_::SWM)) << 4);
-                asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0u) : "memory");
-            }
-            __syncwarp();
-        }
-        // ---- O^T += V^T . P^T
-#pragma unroll
-        for (int mt = 0; mt < KS; ++mt) {
-            const int d = mt * 16 + v_doff;
-            const uint32_t addr = vst + v_row_off + static_cast<uint32_t>(d / G_::W) * p.box_slot +
-                                  ((static_cast<uint32_t>((d % G_::W) >> 3) ^ v_x) << 4);
-            uint32_t a[4];
-            ldsm_x4_trans(addr, a);
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                mma16816<KV>(o[nt][mt], a, pb_hi[nt][0], pb_hi[nt][1]);
-                mma16816<KV>(o[nt][mt], a, pb_lo[nt][0], pb_lo[nt][1]);
-            }
-        }
-        if (valid < 16) fence_proxy_async_smem();  // generic writes above precede the next TMA into this stage
-    }
-
-    // Lane-wise state exchange between the warps of one kv head: NREG floats per lane.
-    static constexpr int NREG = NT * KS * 4 + NT * 4;
-    __device__ __forceinline__ void store_state(float* area, int lane) const {
-        int r = 0;
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-#pragma unroll
-            for (int ks = 0; ks < KS; ++ks)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) area[(r++) * 32 + lane] = o[nt][ks][e];
-            area[(r++) * 32 + lane] = m_run[nt][0];
-            area[(r++) * 32 + lane] = m_run[nt][1];
-            area[(r++) * 32 + lane] = l_run[nt][0];
-            area[(r++) * 32 + lane] = l_run[nt][1];
-        }
-    }
-    // Folds another warp's state (same lane layout) into this one: per head column, rescale both sides to
-    // the larger running max.  A warp that saw no tile has m = -inf and contributes nothing.
-    __device__ __forceinline__ void merge_state(const float* area, int lane) {
-        int r = 0;
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            const int rm = r + KS * 4;
-            float a[2], b[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                const float m2 = area[(rm + e) * 32 + lane];
-                const float l2 = area[(rm + 2 + e) * 32 + lane];
-                const float M = fmaxf(m_run[nt][e], m2);
-                a[e] = M == -INFINITY ? 0.f : fast_exp2(m_run[nt][e] - M);
-                b[e] = M == -INFINITY ? 0.f : fast_exp2(m2 - M);
-                l_run[nt][e] = l_run[nt][e] * a[e] + l2 * b[e];
-                m_run[nt][e] = M;
-            }
-#pragma unroll
-            for (int ks = 0; ks < KS; ++ks)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float v = area[(r++) * 32 + lane];
-                    o[nt][ks][e] = o[nt][ks][e] * a[e & 1] + v * b[e & 1];
-                }
-            r += 4;
-        }
-    }
-
-    // Segment epilogue: the final normalised output (`single`) or a partial row `part_row` (nh heads).
-    __device__ __forceinline__ void finish(const AttnParams& p, int lane, int seq, int kvh_global, bool single,
-                                           size_t part_row) {
-        const int gid = lane >> 2, c4 = lane & 3;
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                float l = l_run[nt][e];
-#pragma unroll
-                for (int off = 4; off < 32; off <<= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-                l_run[nt][e] = l;
-            }
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                const int j = nt * 8 + 2 * c4 + e;
-                if (j >= p.g) continue;
-                const int hq = kvh_global * p.g + j;
-                if (single) {
-                    const float inv = 1.f / l_run[nt][e];
-                    const size_t ob = (static_cast<size_t>(seq) * p.nh + hq) * D;
-#pragma unroll
-                    for (int mt = 0; mt < KS; ++mt) {
-                        store_any(p.out, ob + mt * 16 + gid, p.out_dtype, o[nt][mt][e] * inv);
-                        store_any(p.out, ob + mt * 16 + gid + 8, p.out_dtype, o[nt][mt][2 + e] * inv);
-                    }
-                } else {
-                    float* wo = p.ws_o + (part_row + hq) * D;
-#pragma unroll
-                    for (int mt = 0; mt < KS; ++mt) {
-                        wo[mt * 16 + gid] = o[nt][mt][e];
-                        wo[mt * 16 + gid + 8] = o[nt][mt][2 + e];
-                    }
-                    if (gid == 0) p.ws_ml[part_row + hq] = make_float2(m_run[nt][e], l_run[nt][e]);
-                }
-            }
-    }
-};
-
-template <class KV>
-__device__ __forceinline__ bool q_needs_residual(const AttnParams& p) {
-    const int kv_dt = std::is_same<KV, __half>::value ? KVP_DTYPE_F16 : KVP_DTYPE_BF16;
-    return p.q_dtype != kv_dt;
-}
-
-__device__ __forceinline__ void named_barrier(int id, int threads) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
-// One attention segment: tiles [tile0, tile1) of sequence `seq`, written as the final output (`single`) or
-// as the partial row `part_row`.
-struct Segment {
-    int seq, tile0, tile1;
-    int len;  // the sequence's context length
-    bool single;
-    size_t part_row;
-    int c0, nseg;  // stream-K: first CTA holding part of the sequence and how many do (0: merged elsewhere)
-};
-
-// Fixed splits: the CTA's one segment.
-struct SplitSegments {
-    Segment seg;
-    bool done;
-    __device__ __forceinline__ bool next(Segment& s) {
-        if (done) return false;
-        s = seg;
-        done = true;
-        return true;
-    }
-};
-
-// floor(a * b / c) for 0 <= a * b < 2^53 and c > 0: a double-precision quotient (the product is exact in a
-// double) corrected by one integer step, instead of a 64-bit integer division routine.
-__device__ __forceinline__ long long muldiv_floor(long long a, long long b, long long c) {
-    const long long n = a * b;
-    long long q = static_cast<long long>(static_cast<double>(n) / static_cast<double>(c));
-    if (q * c > n) --q;
-    else if ((q + 1) * c <= n) ++q;
-    return q;
-}
-
-// CTA c of Ge owns tiles [c*T/Ge, (c+1)*T/Ge) of the concatenation of all sequences' tiles (T in total).
-__device__ __forceinline__ long long cta_begin(long long c, long long T, int G) { return muldiv_floor(c, T, G); }
-// The owner of tile t: the c with c*T < (t+1)*G <= (c+1)*T, i.e. floor(((t+1)*G - 1) / T).  The quotient is
-// below 2^16, so a single-precision estimate is off by at most one and one integer step corrects it.
-__device__ __forceinline__ int cta_of_tile(long long t, long long T, int G) {
-    const long long n = (t + 1) * G - 1;
-    long long c = static_cast<long long>(static_cast<float>(n) / static_cast<float>(T));
-    if (c * T > n) --c;
-    else if ((c + 1) * T <= n) ++c;
-    return static_cast<int>(c);
-}
-
-// Stream-K: the CTA's tile range [t, end) of the concatenated sequences, cut at sequence boundaries.
-struct StreamSegments {
-    const int32_t* P;  // tile prefix sums in shared memory
-    const uint8_t* R;  // tokens in each sequence's last tile, in shared memory
-    long long t, end, T;
-    int s, cta, nh, Ge;
-    __device__ __forceinline__ bool next(Segment& sg) {
-        if (t >= end) return false;
-        while (P[s + 1] <= t) ++s;
-        const long long e = min(end, static_cast<long long>(P[s + 1]));
-        sg.seq = s;
-        sg.len = (P[s + 1] - P[s] - 1) * 16 + R[s];
-        sg.tile0 = static_cast<int>(t - P[s]);
-        sg.tile1 = static_cast<int>(e - P[s]);
-        sg.single = (t == P[s]) && (e == P[s + 1]);
-        sg.part_row = static_cast<size_t>(cta + s) * nh;
-        sg.c0 = sg.single ? cta : cta_of_tile(P[s], T, Ge);
-        sg.nseg = sg.single ? 1 : cta_of_tile(P[s + 1] - 1, T, Ge) - sg.c0 + 1;
-        t = e;
-        return true;
-    }
-};
-
-__device__ __forceinline__ void init_barriers(const AttnParams& p, uint64_t* full_bar, uint64_t* empty_bar,
-                                              uint64_t* qfull, uint64_t* qempty) {
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < p.stages; ++s) {
-            mbar_init(smem_u32(&full_bar[s]), 1);
-            mbar_init(smem_u32(&empty_bar[s]), static_cast<uint32_t>(p.kvh_cta));
-        }
-        for (int s = 0; s < 2; ++s) {
-            mbar_init(smem_u32(&qfull[s]), 1);
-            mbar_init(smem_u32(&qempty[s]), static_cast<uint32_t>(p.kvh_cta * p.wph));
-        }
-        fence_barrier_init();
-    }
-    __syncthreads();
-}
-
-// The work of one CTA over its segments.  Warp kvh_cta * wph is the producer; consumer warp w serves kv head
-// w % kvh_cta and takes the tiles whose stage index is congruent to w / kvh_cta modulo wph (the stage count
-// is a multiple of wph, so each stage always has the same kvh_cta consumers).  At the end of a segment the
-// wph warps of a head combine their (m, l, O) lane by lane through shared memory.
-//
-// Every wait is bounded: a warp that gives up reports KVP_STATUS_TIMEOUT and then runs through the rest of
-// its control flow without waiting (so the named barriers of its partner warps are still reached).
-template <int D>
-__device__ __forceinline__ void merge_rows(const AttnParams& p, size_t row0, size_t stride, int n, size_t out_off,
-                                           int lane);
-template <int D, int IT, int U>
-__device__ __forceinline__ void merge_group(const AttnParams& p, int seq, int c0, int nseg, int hq0, int heads,
-                                            int tid, int nthreads);
-
-// Merge batch shape per kernel instantiation (items per thread x partials per load round), the widest that
-// keeps the kernel free of register spills; 0 = one warp per head (merge_rows) for the instantiations whose
-// main loop already needs nearly every register (more than 8 query heads per kv head at head_dim >= 96, and
-// head_dim 256).
-template <int D, int NT>
-struct MergeShape {
-    static constexpr bool per_warp = (NT == 2 && D >= 96) || D >= 256;
-    static constexpr int IT = 2;
-    static constexpr int U = (D <= 64 && NT == 1) ? 4 : 2;
-};
-
-template <int D, int NT, class KV, class Segs>
-__device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap* km, const CUtensorMap* vm, Segs segs,
-                                         uint8_t* dyn, uint32_t smem_base, uint64_t* full_bar, uint64_t* empty_bar,
-                                         uint64_t* qfull, uint64_t* qempty, int grp, int* pend) {
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    const int NC = p.kvh_cta * p.wph;
-    const int S = p.stages;
-    const uint32_t qelem = p.q_dtype == KVP_DTYPE_F32 ? 4u : 2u;
-    const uint32_t q_bytes = static_cast<uint32_t>(p.kvh_cta * p.g * D) * qelem;
-    const int kvh0 = grp * p.kvh_cta;
-    Segment sg;
-    if (warp == NC) {
-        // ------------------------------------------------------------ producer warp
-        if (lane == 0) {
-            prefetch_tensormap(km);
-            prefetch_tensormap(vm);
-        }
-        bool ok = true;
-        int pst = 0, pr = 0, j = 0;  // stage and round (i % S, i / S) of the running tile counter i
-        while (segs.next(sg)) {
-            const int len = sg.len;
-            const int32_t* trow = p.tables + static_cast<size_t>(sg.seq) * p.max_blocks;
-            int cache_lo = -(1 << 30);
-            int32_t cached = 0;
-            if (p.q_area != 0) {
-                const int slot = j & 1;
-                if (ok && j >= 2 && !mbar_wait(smem_u32(&qempty[slot]), static_cast<uint32_t>(((j >> 1) - 1) & 1))) {
-                    if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
-                    ok = false;
-                }
-                if (ok && lane == 0) {
-                    const uint32_t qb = smem_u32(&qfull[slot]);
-                    mbar_arrive_expect_tx(qb, q_bytes);
-                    const char* src = static_cast<const char*>(p.q) +
-                                      (static_cast<size_t>(sg.seq) * p.nh + static_cast<size_t>(kvh0) * p.g) * D * qelem;
-                    bulk_load(smem_base + p.q_off + static_cast<uint32_t>(slot) * p.q_area, src, q_bytes, qb);
-                }
-            }
-            if (p.k_new != nullptr && sg.tile1 == ((len + 15) >> 4)) append_new_token<D>(p, sg.seq, len, trow, kvh0, lane);
-            // One run per tile: issue in batches of up to 8 tiles (one per lane); else one tile at a time.
-            const int nb_max = p.nruns == 1 ? min(8, S) : 1;
-            for (int tile = sg.tile0; tile < sg.tile1;) {
-                const int nb = min(nb_max, sg.tile1 - tile);
-                if (ok) {
-                    if (nb_max > 1) {
-                        ok = produce_batch<D>(p, km, vm, smem_base, full_bar, empty_bar, pst, pr, tile, nb, len, trow,
-                                              kvh0, lane, cache_lo, cached);
-                    } else {
-                        const int st = pst;
-                        if (pr >= 1 && !mbar_wait(smem_u32(&empty_bar[st]), static_cast<uint32_t>((pr - 1) & 1))) {
-                            if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
-                            ok = false;
-                        } else {
-                            const uint32_t kst = smem_base + static_cast<uint32_t>(st) * p.stage_bytes;
-                            produce_tile<D>(p, km, vm, kst, kst + p.stage_half, smem_u32(&full_bar[st]), tile * 16, len,
-                                            trow, kvh0, lane, cache_lo, cached, 0u);
-                        }
-                    }
-                    __syncwarp();
-                }
-                tile += nb;
-                pst += nb;
-                if (pst >= S) {
-                    pst -= S;
-                    ++pr;
-                }
-            }
-            ++j;
-        }
-        griddep_launch_dependents();
-        return;
-    }
-    if (warp > NC) return;
-
-    // ---------------------------------------------------------------- consumer warps
-    const int head = warp % p.kvh_cta, sub = warp / p.kvh_cta;
-    const int kvh_global = kvh0 + head;
-    Consumer<D, NT, KV> cs;
-    cs.init_geometry(p, head, lane);
-    const bool use_qlo = q_needs_residual<KV>(p);
-    float* comb = reinterpret_cast<float*>(dyn + p.comb_off);
-    constexpr int NREG = Consumer<D, NT, KV>::NREG;
-    bool ok = true;
-    int j = 0;
-    int cst = 0, cph = 0, turn = 0;  // stage, its phase and the sub-warp whose turn it is, for the next tile
-    // Split segments of this CTA: at most two (only the first and the last segment of a CTA's range can be
-    // parts of a longer sequence); pend[k] flags a merge, pend[2 + 3k ..] holds (seq, c0, nseg); old0 / old1
-    // hold a writer warp's counter values from before its adds.
-    int np = 0, old0 = -1, old1 = -1;
-    while (segs.next(sg)) {
-        const int len = sg.len;
-        if (p.q_area != 0) {
-            const int slot = j & 1;
-            if (ok && !mbar_wait(smem_u32(&qfull[slot]), static_cast<uint32_t>((j >> 1) & 1))) {
-                if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
-                ok = false;
-            }
-            if (ok) cs.load_q_smem(p, dyn + p.q_off + static_cast<size_t>(slot) * p.q_area, head, lane);
-            __syncwarp();
-            if (ok && lane == 0) mbar_arrive(smem_u32(&qempty[slot]));
-        } else {
-            cs.load_q_global(p, sg.seq, kvh_global, lane);
-        }
-        cs.reset();
-        for (int tile = sg.tile0; tile < sg.tile1; ++tile) {
-            const int st = cst, ph = cph;
-            const bool mine = turn == sub;
-            if (++cst == S) {
-                cst = 0;
-                cph ^= 1;
-            }
-            if (++turn == p.wph) turn = 0;
-            if (!ok || !mine) continue;
-            if (!mbar_wait(smem_u32(&full_bar[st]), static_cast<uint32_t>(ph))) {
-                if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
-                ok = false;
-                continue;
-            }
-            const uint32_t kst = smem_base + static_cast<uint32_t>(st) * p.stage_bytes;
-            cs.tile(p, kst, kst + p.stage_half, min(16, len - tile * 16), head, lane, use_qlo);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&empty_bar[st]));
-        }
-        if (p.wph > 1) {
-            float* area = comb + static_cast<size_t>(head) * NREG * 32;
-            const size_t stride = static_cast<size_t>(p.kvh_cta) * NREG * 32;
-            if (sub > 0) cs.store_state(area + (sub - 1) * stride, lane);
-            named_barrier(1 + head, p.wph * 32);
-            if (sub == 0)
-                for (int k = 1; k < p.wph; ++k) cs.merge_state(area + (k - 1) * stride, lane);
-            named_barrier(1 + head, p.wph * 32);  // the area is rewritten by the next segment
-        }
-        if (sub == 0 && ok) cs.finish(p, lane, sg.seq, kvh_global, sg.single, sg.part_row);
-        // Stream-K, sequence split across CTAs: each head's writer warp counts its partial rows as done with
-        // one releasing add (the warp barrier orders its lanes' rows before it); a sequence is complete when
-        // every writer warp of every CTA holding part of it has added (nseg * kvh_cta).  The add's old value
-        // is only examined after the CTA's last segment, so no warp waits for its round trip or for another
-        // warp here.
-        if (!sg.single && sg.nseg > 0) {
-            if (sub == 0) {
-                __syncwarp();
-                if (lane == 0 && ok) {
-                    const int old = atom_add_acq_rel_gpu(p.counters + static_cast<size_t>(sg.seq) * p.groups + grp, 1);
-                    if (np == 0) old0 = old; else old1 = old;
-                }
-            }
-            if (warp == 0 && lane == 0) {
-                pend[2 + 3 * np] = sg.seq;
-                pend[3 + 3 * np] = sg.c0;
-                pend[4 + 3 * np] = sg.nseg;
-            }
-            ++np;
-        }
-        ++j;
-    }
-    griddep_launch_dependents();  // the next kernel may start its prologue during the merges
-    // The writer warp whose add completed a sequence's count resets the counter and flags the merge; the CTA
-    // then merges (that acquiring add made the other parts' rows visible; the barrier extends it to every
-    // merging thread).
-    if (np > 0) {
-        named_barrier(kMaxConsumerWarps + 1, NC * 32);  // pend coordinates written
-        if (sub == 0 && lane == 0 && ok) {
-#pragma unroll
-            for (int k = 0; k < 2; ++k) {
-                if (k >= np || (k ? old1 : old0) != pend[4 + 3 * k] * p.kvh_cta - 1) continue;
-                atomicExch(p.counters + static_cast<size_t>(pend[2 + 3 * k]) * p.groups + grp, 0);
-                pend[k] = 1;
-            }
-        }
-        named_barrier(kMaxConsumerWarps + 1, NC * 32);  // merge flags written
-        for (int k = 0; k < np; ++k) {
-            if (!pend[k]) continue;
-            const int seq = pend[2 + 3 * k], c0 = pend[3 + 3 * k], nseg = pend[4 + 3 * k];
-            using MS = MergeShape<D, NT>;
-            if constexpr (MS::per_warp) {
-                for (int jj = warp; jj < p.kvh_cta * p.g; jj += NC) {
-                    const int hq = kvh0 * p.g + jj;
-                    merge_rows<D>(p, static_cast<size_t>(c0 + seq) * p.nh + hq, static_cast<size_t>(p.nh), nseg,
-                                  (static_cast<size_t>(seq) * p.nh + hq) * D, lane);
-                }
-            } else {
-                // all consumer threads merge the group's query heads, a 4-float column each
-                merge_group<D, MS::IT, MS::U>(p, seq, c0, nseg, kvh0 * p.g, p.kvh_cta * p.g, threadIdx.x, NC * 32);
-            }
-        }
-    }
-}
-
-// ---------------------------------------------------------------- fixed-split schedule
-template <int D, int NT, class KV>
-__global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
-    paged_decode_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
-                        const AttnParams p) {
-    __shared__ __align__(8) uint64_t full_bar[kMaxStages];
-    __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
-    __shared__ __align__(8) uint64_t qfull[2], qempty[2];
-    extern __shared__ uint8_t dyn_smem[];
-
-    const int seq = blockIdx.x / p.groups;
-    const int grp = blockIdx.x - seq * p.groups;
-    const int split = blockIdx.y;
-    const int len = p.lens[seq];
-    const int ntiles = tiles_of_len(p, len);
-    const int nsplit = (ntiles + p.split_tiles - 1) / p.split_tiles;
-    if (ntiles == 0) {
-        // Invalid length: report once and write zeros so the output is deterministic.
-        if (split == 0) {
-            if (threadIdx.x == 0) report(p.status, KVP_STATUS_BAD_LEN);
-            const int heads = p.kvh_cta * p.g;
-            for (int i = threadIdx.x; i < heads * D; i += blockDim.x) {
-                const int hq = grp * heads + i / D;
-                store_any(p.out, (static_cast<size_t>(seq) * p.nh + hq) * D + i % D, p.out_dtype, 0.f);
-            }
-        }
-        return;
-    }
-    if (split >= nsplit) return;
-    const uint32_t base_off = ((smem_u32(dyn_smem) + 1023u) & ~1023u) - smem_u32(dyn_smem);
-    init_barriers(p, full_bar, empty_bar, qfull, qempty);
-    SplitSegments segs;
-    segs.seg.seq = seq;
-    segs.seg.len = len;
-    segs.seg.tile0 = split * p.split_tiles;
-    segs.seg.tile1 = min(ntiles, segs.seg.tile0 + p.split_tiles);
-    segs.seg.single = nsplit == 1;
-    segs.seg.part_row = (static_cast<size_t>(seq) * p.max_splits + split) * p.nh;
-    segs.seg.c0 = 0;
-    segs.seg.nseg = 0;
-    segs.done = false;
-    cta_body<D, NT, KV>(p, &kmap, &vmap, segs, dyn_smem + base_off, smem_u32(dyn_smem) + base_off, full_bar,
-                        empty_bar, qfull, qempty, grp, nullptr);
-}
-
-// ---------------------------------------------------------------- stream-K schedule
-
-// Tile prefix sums P[0..ns] of all sequences into shared memory (invalid lengths count 0 tiles), and R[s] =
-// the tokens in sequence s's last tile, so segment starts need no global load of the length.
-__device__ __forceinline__ void build_prefix(const AttnParams& p, int32_t* P, uint8_t* R, int32_t* warp_tot) {
-    const int ns = p.num_seqs, nthr = blockDim.x, tid = threadIdx.x;
-    const int warp = tid >> 5, lane = tid & 31, nwarps = (nthr + 31) >> 5;
-    const int per = (ns + nthr - 1) / nthr;
-    const int b = min(tid * per, ns), e = min(b + per, ns);
-    int local = 0;
-    for (int i = b; i < e; ++i) local += tiles_of_len(p, __ldg(p.lens + i));
-    int x = local;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, x, off);
-        if (lane >= off) x += y;
-    }
-    if (lane == 31) warp_tot[warp] = x;
-    __syncthreads();
-    if (warp == 0) {
-        int v = lane < nwarps ? warp_tot[lane] : 0;
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, v, off);
-            if (lane >= off) v += y;
-        }
-        if (lane < nwarps) warp_tot[lane] = v;
-    }
-    __syncthreads();
-    int run = (warp > 0 ? warp_tot[warp - 1] : 0) + (x - local);
-    for (int i = b; i < e; ++i) {
-        const int len = __ldg(p.lens + i);
-        P[i] = run;
-        run += tiles_of_len(p, len);
-        R[i] = static_cast<uint8_t>(((len - 1) & 15) + 1);
-    }
-    if (tid == nthr - 1) P[ns] = warp_tot[nwarps - 1];
-    __syncthreads();
-}
-
-// First sequence whose tile range ends after tile t (P[s+1] > t).
-__device__ __forceinline__ int seq_of_tile(const int32_t* P, int ns, long long t) {
-    int lo = 0, hi = ns - 1;
-    while (lo < hi) {
-        const int mid = (lo + hi) >> 1;
-        if (P[mid + 1] > t) hi = mid; else lo = mid + 1;
-    }
-    return lo;
-}
-
-template <int D, int NT, class KV>
-__global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
-    paged_decode_streamk_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
-                                const AttnParams p) {
-    __shared__ __align__(8) uint64_t full_bar[kMaxStages];
-    __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
-    __shared__ __align__(8) uint64_t qfull[2], qempty[2];
-    __shared__ int32_t warp_tot[32];
-    extern __shared__ uint8_t dyn_smem[];
-
-    const int c = blockIdx.x, grp = blockIdx.y;
-    const uint32_t base_off = ((smem_u32(dyn_smem) + 1023u) & ~1023u) - smem_u32(dyn_smem);
-    int32_t* P = reinterpret_cast<int32_t*>(dyn_smem + base_off + p.pre_off);
-    uint8_t* R = reinterpret_cast<uint8_t*>(P + p.num_seqs + 1);
-    build_prefix(p, P, R, warp_tot);
-    const int ns = p.num_seqs;
-    const long long T = P[ns];
-    // With fewer tiles than CTAs only the first T CTAs work, so every working CTA owns >= 1 tile.
-    const int Ge = static_cast<int>(min(static_cast<long long>(p.G), T));
-    StreamSegments segs;
-    segs.P = P;
-    segs.R = R;
-    segs.T = T;
-    segs.Ge = Ge;
-    segs.t = Ge > 0 ? cta_begin(c, T, Ge) : 0;
-    segs.end = Ge > 0 ? cta_begin(c + 1, T, Ge) : 0;
-    segs.s = seq_of_tile(P, ns, segs.t);
-    segs.cta = c;
-    segs.nh = p.nh;
-    __shared__ int pend[8];  // merge flags and coordinates of the CTA's split segments
-    if (threadIdx.x < 2) pend[threadIdx.x] = 0;
-    init_barriers(p, full_bar, empty_bar, qfull, qempty);  // (its barrier also publishes pend)
-    // Everything above reads only seq_lens and shared memory; with an early start (programmatic dependent
-    // launch) it overlaps the previous kernel's tail.  What follows may read what that kernel wrote or write
-    // what it reads, so it waits for it.
-    griddep_wait();
-    if (c == 0) {
-        // Sequences with an invalid length own no tile: report them and write zeros for this group's heads.
-        // The scan is spread over the threads; the (rare) zero writes only run when it found one.
-        bool bad = false;
-        for (int s = threadIdx.x; s < ns; s += blockDim.x) bad |= P[s + 1] == P[s];
-        if (__syncthreads_or(bad)) {
-            const int heads = p.kvh_cta * p.g;
-            for (int s = 0; s < ns; ++s) {
-                if (P[s + 1] != P[s]) continue;
-                if (threadIdx.x == 0 && grp == 0) report(p.status, KVP_STATUS_BAD_LEN);
-                for (int i = threadIdx.x; i < heads * D; i += blockDim.x)
-                    store_any(p.out, (static_cast<size_t>(s) * p.nh + grp * heads + i / D) * D + i % D, p.out_dtype, 0.f);
-            }
-        }
-    }
-    if (c >= Ge) return;
-    cta_body<D, NT, KV>(p, &kmap, &vmap, segs, dyn_smem + base_off, smem_u32(dyn_smem) + base_off, full_bar,
-                        empty_bar, qfull, qempty, grp, pend);
-}
-
-// ---------------------------------------------------------------- merges
-// Combines `n` partial rows of one (sequence, head) -- rows row0 + k * stride -- into the output: one warp.
-// Lane k holds partial k's (m, l) (one L2 round trip), the weights stay in registers and the output loop's
-// loads are independent of each other.  Partials written by other CTAs of the same launch are read through
-// L2 (ld.global.cg).
-template <int D>
-__device__ __forceinline__ void merge_rows(const AttnParams& p, size_t row0, size_t stride, int n, size_t out_off,
-                                           int lane) {
-    constexpr int PER = (D + 31) / 32;
-    float acc[PER];
-#pragma unroll
-    for (int q = 0; q < PER; ++q) acc[q] = 0.f;
-    float M = -INFINITY, L = 0.f;
-    for (int k0 = 0; k0 < n; k0 += 32) {
-        const int kk = k0 + lane;
-        const float2 ml = kk < n ? __ldcg(&p.ws_ml[row0 + kk * stride]) : make_float2(-INFINITY, 0.f);
-        float Mc = ml.x;
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) Mc = fmaxf(Mc, __shfl_xor_sync(0xffffffffu, Mc, off));
-        const float Mn = fmaxf(M, Mc);
-        const float rescale = M == -INFINITY ? 0.f : fast_exp2(M - Mn);
-        const float w = kk < n ? fast_exp2(ml.x - Mn) : 0.f;
-        float Lc = ml.y * w;
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) Lc += __shfl_xor_sync(0xffffffffu, Lc, off);
-        L = L * rescale + Lc;
-#pragma unroll
-        for (int q = 0; q < PER; ++q) acc[q] *= rescale;
-        M = Mn;
-        const int cnt = min(32, n - k0);
-#pragma unroll 4
-        for (int k = 0; k < cnt; ++k) {
-            const float wk = __shfl_sync(0xffffffffu, w, k);
-            const float* src = p.ws_o + (row0 + static_cast<size_t>(k0 + k) * stride) * D;
-#pragma unroll
-            for (int q = 0; q < PER; ++q) {
-                const int d = q * 32 + lane;
-                if (d < D) acc[q] += __ldcg(src + d) * wk;
-            }
-        }
-    }
-    const float invL = 1.f / L;
-#pragma unroll
-    for (int q = 0; q < PER; ++q) {
-        const int d = q * 32 + lane;
-        if (d < D) store_any(p.out, out_off + d, p.out_dtype, acc[q] * invL);
-    }
-}
-
-// Stream-K merge of one sequence's partials (CTAs c0 .. c0 + nseg - 1, rows (c + seq) * nh + head) for `heads`
-// query heads from hq0, by nthreads threads: item = (head, 4-float column of the output).  Every partial's
-// (m, l) and column are loaded U partials at a time, for IT items of a thread at once, before they are
-// combined (a running max with rescaling), so a merge costs about one L2 round trip per U partials and IT items
-// instead of a dependent chain per head.  Partials
-// written by other CTAs of the same launch are read through L2 (ld.global.cg).
-template <int D, int IT, int U>
-__device__ __forceinline__ void merge_group(const AttnParams& p, int seq, int c0, int nseg, int hq0, int heads,
-                                            int tid, int nthreads) {
-    constexpr int C4 = D / 4;
-    const int items = heads * C4;
-    for (int base = tid; base < items; base += nthreads * IT) {
-        float M[IT], Lsum[IT];
-        float4 acc[IT];
-        size_t row0[IT];
-        int col[IT];
-        bool on[IT];
-#pragma unroll
-        for (int t = 0; t < IT; ++t) {
-            const int item = base + t * nthreads;
-            on[t] = item < items;
-            const int h = on[t] ? item / C4 : 0;
-            col[t] = on[t] ? item - h * C4 : 0;
-            row0[t] = static_cast<size_t>(c0 + seq) * p.nh + hq0 + h;
-            M[t] = -INFINITY;
-            Lsum[t] = 0.f;
-            acc[t] = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-        for (int k0 = 0; k0 < nseg; k0 += U) {
-            float2 ml[IT][U];
-            float4 o[IT][U];
-#pragma unroll
-            for (int t = 0; t < IT; ++t) {
-#pragma unroll
-                for (int u = 0; u < U; ++u) {
-                    if (on[t] && k0 + u < nseg) {
-                        const size_t row = row0[t] + static_cast<size_t>(k0 + u) * p.nh;
-                        ml[t][u] = __ldcg(&p.ws_ml[row]);
-                        o[t][u] = __ldcg(reinterpret_cast<const float4*>(p.ws_o + row * D) + col[t]);
-                    }
-                }
-            }
-#pragma unroll
-            for (int t = 0; t < IT; ++t) {
-#pragma unroll
-                for (int u = 0; u < U; ++u) {
-                    if (on[t] && k0 + u < nseg) {
-                        const float Mn = fmaxf(M[t], ml[t][u].x);
-                        const float a = M[t] == -INFINITY ? 0.f : fast_exp2(M[t] - Mn);
-                        const float b = fast_exp2(ml[t][u].x - Mn);
-                        Lsum[t] = Lsum[t] * a + ml[t][u].y * b;
-                        acc[t].x = acc[t].x * a + o[t][u].x * b;
-                        acc[t].y = acc[t].y * a + o[t][u].y * b;
-                        acc[t].z = acc[t].z * a + o[t][u].z * b;
-                        acc[t].w = acc[t].w * a + o[t][u].w * b;
-                        M[t] = Mn;
-                    }
-                }
-            }
-        }
-#pragma unroll
-        for (int t = 0; t < IT; ++t) {
-            if (!on[t]) continue;
-            const float inv = 1.f / Lsum[t];
-            const size_t out = (row0[t] - static_cast<size_t>(c0) * p.nh) * D + static_cast<size_t>(col[t]) * 4;
-            store_any(p.out, out + 0, p.out_dtype, acc[t].x * inv);
-            store_any(p.out, out + 1, p.out_dtype, acc[t].y * inv);
-            store_any(p.out, out + 2, p.out_dtype, acc[t].z * inv);
-            store_any(p.out, out + 3, p.out_dtype, acc[t].w * inv);
-        }
-    }
-}
-
-// Fixed-split schedule: one warp per (sequence, head) whose context was split.
-template <int D>
-__global__ void __launch_bounds__(128) merge_splits_kernel(const AttnParams p) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const long long idx = static_cast<long long>(blockIdx.x) * 4 + warp;
-    if (idx >= static_cast<long long>(p.num_seqs) * p.nh) return;
-    const int seq = static_cast<int>(idx / p.nh), hq = static_cast<int>(idx % p.nh);
-    const int ntiles = tiles_of_len(p, p.lens[seq]);
-    const int nsplit = (ntiles + p.split_tiles - 1) / p.split_tiles;
-    if (nsplit <= 1) return;
-    merge_rows<D>(p, static_cast<size_t>(seq) * p.max_splits * p.nh + hq, static_cast<size_t>(p.nh), nsplit,
-                  (static_cast<size_t>(seq) * p.nh + hq) * D, lane);
-}
-
-}  // namespace kvpd
+#include "attention_common.h"
 
 // ============================================================================ host side
 namespace kvpi {
@@ -1219,36 +106,7 @@ int pool_map_mode() {
     return mode;
 }
 
-// ---- kernel instantiations by (kv dtype, head_dim, n-tiles)
-template <int D, int NT, class KV>
-struct Kernels {
-    static const void* decode() { return reinterpret_cast<const void*>(&kvpd::paged_decode_kernel<D, NT, KV>); }
-    static const void* streamk() { return reinterpret_cast<const void*>(&kvpd::paged_decode_streamk_kernel<D, NT, KV>); }
-};
-
-template <class KV, int D>
-const void* pick_d(int NT, bool streamk) {
-    if (NT == 1) return streamk ? Kernels<D, 1, KV>::streamk() : Kernels<D, 1, KV>::decode();
-    if constexpr (D <= 128) return streamk ? Kernels<D, 2, KV>::streamk() : Kernels<D, 2, KV>::decode();
-    return nullptr;
-}
-
-template <class KV>
-const void* pick_kv(int D, int NT, bool streamk) {
-    switch (D) {
-        case 32: return pick_d<KV, 32>(NT, streamk);
-        case 64: return pick_d<KV, 64>(NT, streamk);
-        case 96: return pick_d<KV, 96>(NT, streamk);
-        case 128: return pick_d<KV, 128>(NT, streamk);
-        case 256: return pick_d<KV, 256>(NT, streamk);
-        default: return nullptr;
-    }
-}
-
-const void* pick_kernel(int kv_dtype, int D, int g, bool streamk) {
-    const int NT = g <= 8 ? 1 : 2;
-    return kv_dtype == KVP_DTYPE_F16 ? pick_kv<__half>(D, NT, streamk) : pick_kv<__nv_bfloat16>(D, NT, streamk);
-}
+}  // namespace
 
 // Opts a kernel into the whole dynamic shared-memory budget, once per device.
 int allow_smem(const void* fn) {
@@ -1264,6 +122,8 @@ int allow_smem(const void* fn) {
     done.emplace_back(fn, dev);
     return KVP_OK;
 }
+
+namespace {
 
 // Resident CTAs per SM of the stream-K kernel for this launch shape (occupancy API; shared-memory estimate
 // when no device is present, e.g. for a workspace query on a build machine).
@@ -1294,6 +154,15 @@ int streamk_ctas_per_sm(const void* fn, int threads, size_t smem) {
     std::lock_guard<std::mutex> lock(mu);
     cache.push_back(Key{fn, threads, smem, dev, n});
     return n;
+}
+
+// The kernel of a (kv dtype, query dtype, head_dim, group size, schedule) combination.  The query's low-half
+// residual MMA is compiled in only when the query dtype differs from the K/V dtype.
+const void* pick_kernel(int kv_dtype, int q_dtype, int D, int g, bool streamk) {
+    const int NT = g <= 8 ? 1 : 2;
+    const bool qres = q_dtype != kv_dtype;
+    if (kv_dtype == KVP_DTYPE_F16) return qres ? kvpd::kernel_f16_qres(D, NT, streamk) : kvpd::kernel_f16(D, NT, streamk);
+    return qres ? kvpd::kernel_bf16_qres(D, NT, streamk) : kvpd::kernel_bf16(D, NT, streamk);
 }
 
 }  // namespace
@@ -1377,7 +246,7 @@ int plan_attention(const kvp_attn_args& a, bool have_workspace, AttnPlan* out) {
     pl.pre_off = static_cast<uint32_t>(pl.comb_off + round_up(comb, 16));
 
     if (pl.streamk) {
-        const void* fn = pick_kernel(a.kv_dtype, D, g, true);
+        const void* fn = pick_kernel(a.kv_dtype, a.q_dtype, D, g, true);
         pl.G = sm_count() * streamk_ctas_per_sm(fn, (kc * pl.wph + 1) * 32, pl.smem);
         pl.split_tiles = pl.max_tiles;
         pl.max_splits = 1;
@@ -1402,76 +271,6 @@ int plan_attention(const kvp_attn_args& a, bool have_workspace, AttnPlan* out) {
     *out = pl;
     return KVP_OK;
 }
-
-namespace {
-
-template <int D>
-int launch_merge(const kvp_attn_args& a, const AttnPlan& pl, const kvpd::AttnParams& prm, cudaStream_t stream) {
-    const long long pairs = static_cast<long long>(a.num_seqs) * a.num_heads;
-    if (pairs == 0) return KVP_OK;
-    const unsigned blocks = static_cast<unsigned>((pairs + 3) / 4);
-    if (pl.streamk || pl.max_splits <= 1) return KVP_OK;  // stream-K merges inside the attention kernel
-    kvpd::merge_splits_kernel<D><<<blocks, 128, 0, stream>>>(prm);
-    return cuda_status(cudaGetLastError(), "split merge kernel launch");
-}
-
-template <int D, int NT, class KV>
-int launch_typed(const kvp_attn_args& a, const AttnPlan& pl, const kvpd::AttnParams& prm, const CUtensorMap& km,
-                 const CUtensorMap& vm, cudaStream_t stream) {
-    const void* fn = pl.streamk ? Kernels<D, NT, KV>::streamk() : Kernels<D, NT, KV>::decode();
-    int rc = allow_smem(fn);
-    if (rc != KVP_OK) return rc;
-    if (a.num_seqs == 0) return KVP_OK;
-    dim3 block(static_cast<unsigned>((pl.kvh_cta * pl.wph + 1) * 32));
-    if (pl.streamk) {
-        dim3 grid(static_cast<unsigned>(pl.G), static_cast<unsigned>(pl.groups));
-        if (a.flags & KVP_ATTN_EARLY_START) {
-            cudaLaunchConfig_t cfg = {};
-            cfg.gridDim = grid;
-            cfg.blockDim = block;
-            cfg.dynamicSmemBytes = pl.smem;
-            cfg.stream = stream;
-            cudaLaunchAttribute attr[1];
-            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-            attr[0].val.programmaticStreamSerializationAllowed = 1;
-            cfg.attrs = attr;
-            cfg.numAttrs = 1;
-            cudaError_t e = cudaLaunchKernelEx(&cfg, kvpd::paged_decode_streamk_kernel<D, NT, KV>, km, vm, prm);
-            if (e != cudaSuccess) return cuda_status(e, "attention kernel launch");
-        } else {
-            kvpd::paged_decode_streamk_kernel<D, NT, KV><<<grid, block, pl.smem, stream>>>(km, vm, prm);
-        }
-    } else {
-        dim3 grid(static_cast<unsigned>(a.num_seqs * pl.groups), static_cast<unsigned>(pl.max_splits));
-        kvpd::paged_decode_kernel<D, NT, KV><<<grid, block, pl.smem, stream>>>(km, vm, prm);
-    }
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_status(e, "attention kernel launch");
-    return launch_merge<D>(a, pl, prm, stream);
-}
-
-template <int D, class KV>
-int launch_nt(const kvp_attn_args& a, const AttnPlan& pl, const kvpd::AttnParams& prm, const CUtensorMap& km,
-              const CUtensorMap& vm, cudaStream_t s) {
-    if (prm.g <= 8) return launch_typed<D, 1, KV>(a, pl, prm, km, vm, s);
-    if constexpr (D <= 128) return launch_typed<D, 2, KV>(a, pl, prm, km, vm, s);
-    return fail(KVP_EINVAL, "head_dim 256 supports at most 8 query heads per kv head");
-}
-
-template <class KV>
-int launch_d(const kvp_attn_args& a, const AttnPlan& pl, const kvpd::AttnParams& prm, const CUtensorMap& km,
-             const CUtensorMap& vm, cudaStream_t s) {
-    switch (a.head_dim) {
-        case 32: return launch_nt<32, KV>(a, pl, prm, km, vm, s);
-        case 64: return launch_nt<64, KV>(a, pl, prm, km, vm, s);
-        case 96: return launch_nt<96, KV>(a, pl, prm, km, vm, s);
-        case 128: return launch_nt<128, KV>(a, pl, prm, km, vm, s);
-        case 256: return launch_nt<256, KV>(a, pl, prm, km, vm, s);
-        default: return fail(KVP_EINVAL, "unsupported head_dim");
-    }
-}
-
-}  // namespace
 
 }  // namespace kvpi
 
@@ -1581,6 +380,8 @@ extern "C" KVP_API int kvp_paged_attention(const kvp_attn_args* a, void* stream)
     const float scale = a->scale > 0.f ? a->scale : 1.0f / std::sqrt(static_cast<float>(a->head_dim));
     prm.sl2 = scale * 1.4426950408889634f;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (a->kv_dtype == KVP_DTYPE_F16) return launch_d<__half>(*a, pl, prm, km, vm, s);
-    return launch_d<__nv_bfloat16>(*a, pl, prm, km, vm, s);
+    const bool qres = a->q_dtype != a->kv_dtype;
+    if (a->kv_dtype == KVP_DTYPE_F16)
+        return qres ? kvpd::launch_f16_qres(*a, pl, prm, km, vm, s) : kvpd::launch_f16(*a, pl, prm, km, vm, s);
+    return qres ? kvpd::launch_bf16_qres(*a, pl, prm, km, vm, s) : kvpd::launch_bf16(*a, pl, prm, km, vm, s);
 }
