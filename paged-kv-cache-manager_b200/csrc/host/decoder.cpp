@@ -138,7 +138,8 @@ struct kvp_decoder {
 namespace {
 
 // Host bookkeeping of a step: appends, copy-on-write pairs, table rows and lengths into the pinned staging
-// (the fused append derives each written slot from the table row and the length).  Returns KVP_OK or KVP_ENOSPACE (an append found no block).
+// (the fused append derives each written slot from the table row and the length).  Returns KVP_OK or
+// KVP_ENOSPACE (an append found no block).
 int host_step(kvp_decoder* d, const int64_t* rids, int n) {
     kvp::KVManager& m = d->mgr->m;
     const kvp_decoder_config& c = d->cfg;
@@ -201,50 +202,43 @@ int launch_cow(kvp_decoder* d, const int32_t* d_pairs, cudaStream_t s) {
     return flush(npairs);
 }
 
-// The per-layer launches of a step: fused append + attention for every layer, each waiting for its inputs
-// (per-layer events, host path) and marking its output ready.  `ext` marks the event operations as
-// external nodes when the stream is being captured into a graph.
 // Layer l's attention launch (fused append of its new token) on stream s; q / knew / vnew / out are the
 // device arrays of all layers.
 int launch_layer(kvp_decoder* d, int n, int l, const void* q, const void* knew, const void* vnew, void* out,
-                 cudaStream_t s_comp) {
+                 cudaStream_t s) {
     const kvp_decoder_config& c = d->cfg;
     const int32_t* meta = d->d_meta();
-    const int32_t* d_tables = meta;
-    const int32_t* d_lens = meta + static_cast<size_t>(n) * c.max_blocks_per_seq;
-    const int split = c.split_tiles;  // 0: balanced schedule over the step's real context lengths
+    const size_t L = static_cast<size_t>(l);
     const size_t kv_layer_bytes = static_cast<size_t>(d->layer_stride) * 2;
     const size_t q_layer = static_cast<size_t>(n) * c.num_heads * c.head_dim;
     const size_t kv_layer = static_cast<size_t>(n) * c.kv_heads * c.head_dim * elem(c.kv_dtype);
-    {
-        kvp_attn_args a{};
-        a.q = static_cast<const char*>(q) + q_layer * elem(c.q_dtype) * l;
-        a.q_dtype = c.q_dtype;
-        a.k_cache = static_cast<const char*>(c.k_cache) + kv_layer_bytes * l;
-        a.v_cache = static_cast<const char*>(c.v_cache) + kv_layer_bytes * l;
-        a.kv_dtype = c.kv_dtype;
-        a.num_blocks = c.num_blocks;
-        a.block_tables = d_tables;
-        a.seq_lens = d_lens;
-        a.out = static_cast<char*>(out) + q_layer * elem(c.out_dtype) * l;
-        a.out_dtype = c.out_dtype;
-        a.num_seqs = n;
-        a.num_heads = c.num_heads;
-        a.kv_heads = c.kv_heads;
-        a.head_dim = c.head_dim;
-        a.block_size = c.block_size;
-        a.max_blocks = c.max_blocks_per_seq;
-        a.split_tiles = split;
-        a.workspace = d->lay.attn_bytes ? d->ws + d->lay.attn : nullptr;
-        a.workspace_bytes = d->lay.attn_bytes;
-        a.status = d->d_status();
-        // lengths are uploaded before the step's first launch and no kernel writes them: each layer's launch
-        // may start during the previous one
-        a.flags = KVP_ATTN_WORKSPACE_CLEAN | KVP_ATTN_EARLY_START;
-        a.k_new = static_cast<const char*>(knew) + kv_layer * l;  // fused append of this layer's new token
-        a.v_new = static_cast<const char*>(vnew) + kv_layer * l;
-        return kvp_paged_attention(&a, s_comp);
-    }
+    kvp_attn_args a{};
+    a.q = static_cast<const char*>(q) + q_layer * elem(c.q_dtype) * L;
+    a.q_dtype = c.q_dtype;
+    a.k_cache = static_cast<const char*>(c.k_cache) + kv_layer_bytes * L;
+    a.v_cache = static_cast<const char*>(c.v_cache) + kv_layer_bytes * L;
+    a.kv_dtype = c.kv_dtype;
+    a.num_blocks = c.num_blocks;
+    a.block_tables = meta;                                              // [n][max_blocks_per_seq]
+    a.seq_lens = meta + static_cast<size_t>(n) * c.max_blocks_per_seq;  // [n]
+    a.out = static_cast<char*>(out) + q_layer * elem(c.out_dtype) * L;
+    a.out_dtype = c.out_dtype;
+    a.num_seqs = n;
+    a.num_heads = c.num_heads;
+    a.kv_heads = c.kv_heads;
+    a.head_dim = c.head_dim;
+    a.block_size = c.block_size;
+    a.max_blocks = c.max_blocks_per_seq;
+    a.split_tiles = c.split_tiles;  // 0: balanced schedule over the step's real context lengths
+    a.workspace = d->lay.attn_bytes ? d->ws + d->lay.attn : nullptr;
+    a.workspace_bytes = d->lay.attn_bytes;
+    a.status = d->d_status();
+    // lengths are uploaded before the step's first launch and no kernel writes them: each layer's launch may
+    // start during the previous one
+    a.flags = KVP_ATTN_WORKSPACE_CLEAN | KVP_ATTN_EARLY_START;
+    a.k_new = static_cast<const char*>(knew) + kv_layer * L;  // fused append of this layer's new token
+    a.v_new = static_cast<const char*>(vnew) + kv_layer * L;
+    return kvp_paged_attention(&a, s);
 }
 
 // Every layer's launch, in order on stream s (device buffers).
