@@ -251,11 +251,19 @@ int enqueue_layers(kvp_decoder* d, int n, const void* q, const void* knew, const
     return KVP_OK;
 }
 
+// Layers per host copy: enough consecutive layers that each query copy moves at least ~512 KB (small copies
+// pay a fixed cost each on the copy engines), while later groups still overlap earlier layers' attention.
+int layers_per_copy(const kvp_decoder_config& c, int n) {
+    const size_t q_layer = static_cast<size_t>(n) * c.num_heads * c.head_dim * elem(c.q_dtype);
+    const size_t want = size_t(512) << 10;
+    return static_cast<int>(std::min<size_t>(static_cast<size_t>(c.num_layers), std::max<size_t>(1, (want + q_layer - 1) / q_layer)));
+}
+
 // The host-buffer step's device work after the metadata upload and the copy-on-write copies, forked from and
-// joined back into the compute stream: per layer, its query and new K/V copies on the copy-in stream, its
-// attention launch on the compute stream once they have landed, and its output copy on the copy-out stream
-// once the launch is done, so transfers overlap the attention of other layers.  The same calls are captured
-// into one graph when a step's key repeats.
+// joined back into the compute stream: per group of layers, their queries and new K/V copied in on the
+// copy-in stream, each layer's attention launch on the compute stream once its group has landed, and the
+// group's outputs copied out on the copy-out stream once its last launch is done, so transfers overlap the
+// attention of other layers.  The same calls are captured into one graph when a step's key repeats.
 int enqueue_host_body(kvp_decoder* d, int n, const char* hq, const char* hk, const char* hv, char* hout) {
     const kvp_decoder_config& c = d->cfg;
     const size_t q_layer = static_cast<size_t>(n) * c.num_heads * c.head_dim * elem(c.q_dtype);
@@ -265,22 +273,28 @@ int enqueue_host_body(kvp_decoder* d, int n, const char* hq, const char* hk, con
     char* dk = d->ws + d->lay.k;
     char* dv = d->ws + d->lay.v;
     char* dout = d->ws + d->lay.out;
+    const int per = layers_per_copy(c, n);
     cudaError_t e = cudaEventRecord(d->ev_fork, d->s_comp);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(d->s_in, d->ev_fork, 0);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(d->s_out, d->ev_fork, 0);
-    for (int l = 0; e == cudaSuccess && l < c.num_layers; ++l) {
-        const size_t L = static_cast<size_t>(l);
-        e = cudaMemcpyAsync(dq + q_layer * L, hq + q_layer * L, q_layer, cudaMemcpyHostToDevice, d->s_in);
-        if (e == cudaSuccess) e = cudaMemcpyAsync(dk + kv_layer * L, hk + kv_layer * L, kv_layer, cudaMemcpyHostToDevice, d->s_in);
-        if (e == cudaSuccess) e = cudaMemcpyAsync(dv + kv_layer * L, hv + kv_layer * L, kv_layer, cudaMemcpyHostToDevice, d->s_in);
-        if (e == cudaSuccess) e = cudaEventRecord(d->ev_q[L], d->s_in);
-        if (e == cudaSuccess) e = cudaStreamWaitEvent(d->s_comp, d->ev_q[L], 0);
-        if (e != cudaSuccess) break;
-        const int rc = launch_layer(d, n, l, dq, dk, dv, dout, d->s_comp);
-        if (rc != KVP_OK) return rc;
-        e = cudaEventRecord(d->ev_att[L], d->s_comp);
-        if (e == cudaSuccess) e = cudaStreamWaitEvent(d->s_out, d->ev_att[L], 0);
-        if (e == cudaSuccess) e = cudaMemcpyAsync(hout + o_layer * L, dout + o_layer * L, o_layer, cudaMemcpyDeviceToHost, d->s_out);
+    for (int l0 = 0; e == cudaSuccess && l0 < c.num_layers; l0 += per) {
+        const size_t G = static_cast<size_t>(std::min(per, c.num_layers - l0)), L0 = static_cast<size_t>(l0);
+        const size_t ev = L0 / static_cast<size_t>(per);  // one event pair per group
+        e = cudaMemcpyAsync(dq + q_layer * L0, hq + q_layer * L0, q_layer * G, cudaMemcpyHostToDevice, d->s_in);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(dk + kv_layer * L0, hk + kv_layer * L0, kv_layer * G, cudaMemcpyHostToDevice, d->s_in);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(dv + kv_layer * L0, hv + kv_layer * L0, kv_layer * G, cudaMemcpyHostToDevice, d->s_in);
+        if (e == cudaSuccess) e = cudaEventRecord(d->ev_q[ev], d->s_in);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(d->s_comp, d->ev_q[ev], 0);
+        for (size_t l = L0; e == cudaSuccess && l < L0 + G; ++l) {
+            const int rc = launch_layer(d, n, static_cast<int>(l), dq, dk, dv, dout, d->s_comp);
+            if (rc != KVP_OK) return rc;
+        }
+        if (e == cudaSuccess) e = cudaEventRecord(d->ev_att[ev], d->s_comp);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(d->s_out, d->ev_att[ev], 0);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(hout + o_layer * L0, dout + o_layer * L0, o_layer * G, cudaMemcpyDeviceToHost, d->s_out);
     }
     if (e == cudaSuccess) e = cudaEventRecord(d->ev_join_in, d->s_in);
     if (e == cudaSuccess) e = cudaEventRecord(d->ev_join_out, d->s_out);
