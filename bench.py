@@ -270,9 +270,10 @@ def run_ours(args, cfg, rank, world, dev):
                                split_tiles=split, status=status, warps_per_kv_head=args.wph, stages=args.stages,
                                k_new=knew[l], v_new=vnew[l])
         a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
-        # zero-filled once, every call leaves the counters zero; lengths are never written by a kernel, so each
-        # layer's launch may start during the previous one
-        a.flags = kvb.KVP_ATTN_WORKSPACE_CLEAN | kvb.KVP_ATTN_EARLY_START
+        # zero-filled once, every call leaves the counters zero; lengths and tables are never written by a kernel
+        # and a layer's kernel writes only its own pool, so each layer's launch may start and load K/V during
+        # the previous one
+        a.flags = kvb.KVP_ATTN_WORKSPACE_CLEAN | kvb.KVP_ATTN_EARLY_LOAD
         attn_args.append(a)
     sptr = ctypes.c_void_p(stream.cuda_stream)
     lens_row = d_lens.stride(0) * 4

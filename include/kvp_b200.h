@@ -102,6 +102,10 @@ typedef struct kvp_attn_args {
  * which that previous kernel therefore must not write -- and everything else waits for it to complete, so
  * back-to-back launches (one per layer) hide each other's start-up. */
 #define KVP_ATTN_EARLY_START 2
+/* Early load (implies early start): additionally the previous kernel on the stream writes neither block_tables
+ * nor this call's K/V pools, so each CTA may load its first K/V tiles before waiting for it.  True between the
+ * per-layer launches of a decode step (a layer's kernel writes only its own layer's pool). */
+#define KVP_ATTN_EARLY_LOAD 4
 
 /* Bytes of workspace kvp_paged_attention needs for these arguments (0 when no context is split).  With
  * split_tiles == 0 and a workspace the balanced persistent schedule is used: the step's tiles are divided

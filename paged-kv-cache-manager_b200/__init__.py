@@ -24,6 +24,7 @@ KVP_OK, KVP_EINVAL, KVP_ECUDA, KVP_EBOUNDS, KVP_ENOSPACE, KVP_ESTATE = 0, 1, 2, 
 KVP_STATUS_BAD_BLOCK, KVP_STATUS_BAD_LEN, KVP_STATUS_TIMEOUT = 1, 2, 4
 KVP_ATTN_WORKSPACE_CLEAN = 1
 KVP_ATTN_EARLY_START = 2
+KVP_ATTN_EARLY_LOAD = 4
 F32, F16, BF16 = 0, 1, 2
 NO_REQUEST = -1
 STATS_FIELDS = ("requests", "used_tokens", "allocated_blocks", "allocated_slots", "internal_waste",
@@ -417,11 +418,12 @@ def workspace_bytes(args: AttnArgs) -> int:
 def paged_attention(q, k_cache, v_cache, block_tables, seq_lens, num_heads: int, kv_heads: int, *, out=None,
                     out_dtype=None, workspace=None, split_tiles: int = 0, kv_heads_per_cta: int = 0, stages: int = 0,
                     status=None, stream=None, num_blocks: Optional[int] = None, warps_per_kv_head: int = 0,
-                    k_new=None, v_new=None, early_start: bool = False):
+                    k_new=None, v_new=None, early_start: bool = False, early_load: bool = False):
     """Decode attention through the C ABI (kvp_paged_attention).  Allocates `out` (and a workspace when
     none is given and the context will be split) with torch if not provided.  k_new/v_new: fused append of
     each sequence's newest token (position seq_lens[s] - 1) before attending.  early_start: the kernel may start
-    while the previous kernel on the stream still runs (it must not write seq_lens)."""
+    while the previous kernel on the stream still runs (it must not write seq_lens); early_load: it may also
+    load K/V before that kernel ends (which must not write block_tables or these pools either)."""
     import torch
     dev = _same_device(("q", q), ("k_cache", k_cache), ("v_cache", v_cache), ("block_tables", block_tables),
                        ("seq_lens", seq_lens), ("out", out), ("workspace", workspace), ("status", status),
@@ -439,6 +441,8 @@ def paged_attention(q, k_cache, v_cache, block_tables, seq_lens, num_heads: int,
             a.flags |= KVP_ATTN_WORKSPACE_CLEAN
     if early_start:
         a.flags |= KVP_ATTN_EARLY_START
+    if early_load:
+        a.flags |= KVP_ATTN_EARLY_LOAD
     _launch(dev, lib().kvp_paged_attention, a, stream)
     return out
 

@@ -377,6 +377,7 @@ extern "C" KVP_API int kvp_paged_attention(const kvp_attn_args* a, void* stream)
     prm.k_pool = const_cast<void*>(a->k_cache);
     prm.v_pool = const_cast<void*>(a->v_cache);
     prm.kvh = a->kv_heads;
+    prm.early_load = (a->flags & KVP_ATTN_EARLY_LOAD) ? 1 : 0;
     const float scale = a->scale > 0.f ? a->scale : 1.0f / std::sqrt(static_cast<float>(a->head_dim));
     prm.sl2 = scale * 1.4426950408889634f;
     cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -51,6 +51,7 @@ struct AttnParams {
     void* k_pool;
     void* v_pool;
     int kvh;
+    int early_load;  // the producer may load the first K/V tiles before waiting for the previous kernel
 };
 
 // Per-variant entry points: K/V dtype x whether the query needs a low-half residual MMA (its dtype differs

@@ -604,7 +604,7 @@ struct MergeShape {
 template <int D, int NT, class KV, bool QLO, class Segs>
 __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap* km, const CUtensorMap* vm, Segs segs,
                                          uint8_t* dyn, uint32_t smem_base, uint64_t* full_bar, uint64_t* empty_bar,
-                                         uint64_t* qfull, uint64_t* qempty, int grp, int* pend) {
+                                         uint64_t* qfull, uint64_t* qempty, int grp, int* pend, bool waited) {
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int NC = p.kvh_cta * p.wph;
@@ -626,6 +626,47 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
             const int32_t* trow = p.tables + static_cast<size_t>(sg.seq) * p.max_blocks;
             int cache_lo = -(1 << 30);
             int32_t cached = 0;
+            // One run per tile: issue in batches of up to 8 tiles (one per lane); else one tile at a time.
+            const int nb_max = p.nruns == 1 ? min(8, S) : 1;
+            auto produce_range = [&](int from, int to) {
+                for (int tile = from; tile < to;) {
+                    const int nb = min(nb_max, to - tile);
+                    if (ok) {
+                        if (nb_max > 1) {
+                            ok = produce_batch<D>(p, km, vm, smem_base, full_bar, empty_bar, pst, pr, tile, nb, len, trow,
+                                                  kvh0, lane, cache_lo, cached);
+                        } else {
+                            const int st = pst;
+                            if (pr >= 1 && !mbar_wait(smem_u32(&empty_bar[st]), static_cast<uint32_t>((pr - 1) & 1))) {
+                                if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
+                                ok = false;
+                            } else {
+                                const uint32_t kst = smem_base + static_cast<uint32_t>(st) * p.stage_bytes;
+                                produce_tile<D>(p, km, vm, kst, kst + p.stage_half, smem_u32(&full_bar[st]), tile * 16,
+                                                len, trow, kvh0, lane, cache_lo, cached, 0u);
+                            }
+                        }
+                        __syncwarp();
+                    }
+                    tile += nb;
+                    pst += nb;
+                    if (pst >= S) {
+                        pst -= S;
+                        ++pr;
+                    }
+                }
+            };
+            const bool appends = p.k_new != nullptr && sg.tile1 == ((len + 15) >> 4);
+            int first = sg.tile0;
+            if (!waited) {
+                // Early load: the first tiles of the CTA's range -- one ring at most, so no stage has to be freed
+                // by the consumers, and short of the tile the fused append writes into -- before waiting for the
+                // previous kernel; queries, the append and every write come after the wait.
+                first = min(sg.tile1 - (appends ? 1 : 0), sg.tile0 + S);
+                produce_range(sg.tile0, first);
+                griddep_wait();
+                waited = true;
+            }
             if (p.q_area != 0) {
                 const int slot = j & 1;
                 if (ok && j >= 2 && !mbar_wait(smem_u32(&qempty[slot]), static_cast<uint32_t>(((j >> 1) - 1) & 1))) {
@@ -640,35 +681,8 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
                     bulk_load(smem_base + p.q_off + static_cast<uint32_t>(slot) * p.q_area, src, q_bytes, qb);
                 }
             }
-            if (p.k_new != nullptr && sg.tile1 == ((len + 15) >> 4)) append_new_token<D>(p, sg.seq, len, trow, kvh0, lane);
-            // One run per tile: issue in batches of up to 8 tiles (one per lane); else one tile at a time.
-            const int nb_max = p.nruns == 1 ? min(8, S) : 1;
-            for (int tile = sg.tile0; tile < sg.tile1;) {
-                const int nb = min(nb_max, sg.tile1 - tile);
-                if (ok) {
-                    if (nb_max > 1) {
-                        ok = produce_batch<D>(p, km, vm, smem_base, full_bar, empty_bar, pst, pr, tile, nb, len, trow,
-                                              kvh0, lane, cache_lo, cached);
-                    } else {
-                        const int st = pst;
-                        if (pr >= 1 && !mbar_wait(smem_u32(&empty_bar[st]), static_cast<uint32_t>((pr - 1) & 1))) {
-                            if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
-                            ok = false;
-                        } else {
-                            const uint32_t kst = smem_base + static_cast<uint32_t>(st) * p.stage_bytes;
-                            produce_tile<D>(p, km, vm, kst, kst + p.stage_half, smem_u32(&full_bar[st]), tile * 16, len,
-                                            trow, kvh0, lane, cache_lo, cached, 0u);
-                        }
-                    }
-                    __syncwarp();
-                }
-                tile += nb;
-                pst += nb;
-                if (pst >= S) {
-                    pst -= S;
-                    ++pr;
-                }
-            }
+            if (appends) append_new_token<D>(p, sg.seq, len, trow, kvh0, lane);
+            produce_range(first, sg.tile1);
             ++j;
         }
         griddep_launch_dependents();
@@ -831,7 +845,7 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
     segs.seg.nseg = 0;
     segs.done = false;
     cta_body<D, NT, KV, QLO>(p, &kmap, &vmap, segs, dyn_smem + base_off, smem_u32(dyn_smem) + base_off, full_bar,
-                        empty_bar, qfull, qempty, grp, nullptr);
+                        empty_bar, qfull, qempty, grp, nullptr, true);
 }
 
 // ---------------------------------------------------------------- stream-K schedule
@@ -918,8 +932,10 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
     init_barriers(p, full_bar, empty_bar, qfull, qempty);  // (its barrier also publishes pend)
     // Everything above reads only seq_lens and shared memory; with an early start (programmatic dependent
     // launch) it overlaps the previous kernel's tail.  What follows may read what that kernel wrote or write
-    // what it reads, so it waits for it.
-    griddep_wait();
+    // what it reads, so it waits for it -- with an early load, the producer warps first issue their CTA's
+    // first tile loads (CTA 0, which may write zero rows below, waits here).
+    const bool waited = !p.early_load || c == 0;
+    if (waited) griddep_wait();
     if (c == 0) {
         // Sequences with an invalid length own no tile: report them and write zeros for this group's heads.
         // The scan is spread over the threads; the (rare) zero writes only run when it found one.
@@ -937,7 +953,7 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
     }
     if (c >= Ge) return;
     cta_body<D, NT, KV, QLO>(p, &kmap, &vmap, segs, dyn_smem + base_off, smem_u32(dyn_smem) + base_off, full_bar,
-                        empty_bar, qfull, qempty, grp, pend);
+                        empty_bar, qfull, qempty, grp, pend, waited);
 }
 
 // ---------------------------------------------------------------- merges
@@ -1123,7 +1139,7 @@ int launch_typed(const kvp_attn_args& a, const kvpi::AttnPlan& pl, const AttnPar
     dim3 block(static_cast<unsigned>((pl.kvh_cta * pl.wph + 1) * 32));
     if (pl.streamk) {
         dim3 grid(static_cast<unsigned>(pl.G), static_cast<unsigned>(pl.groups));
-        if (a.flags & KVP_ATTN_EARLY_START) {
+        if (a.flags & (KVP_ATTN_EARLY_START | KVP_ATTN_EARLY_LOAD)) {
             cudaLaunchConfig_t cfg = {};
             cfg.gridDim = grid;
             cfg.blockDim = block;

@@ -233,9 +233,10 @@ int launch_layer(kvp_decoder* d, int n, int l, const void* q, const void* knew, 
     a.workspace = d->lay.attn_bytes ? d->ws + d->lay.attn : nullptr;
     a.workspace_bytes = d->lay.attn_bytes;
     a.status = d->d_status();
-    // lengths are uploaded before the step's first launch and no kernel writes them: each layer's launch may
-    // start during the previous one
-    a.flags = KVP_ATTN_WORKSPACE_CLEAN | KVP_ATTN_EARLY_START;
+    // lengths and tables are uploaded before the step's first launch and no kernel writes them: each layer's
+    // launch may start during the previous one, and from the second layer on (the previous kernel then writes
+    // only its own layer's pool) also load K/V before it ends
+    a.flags = KVP_ATTN_WORKSPACE_CLEAN | (l > 0 ? KVP_ATTN_EARLY_LOAD : KVP_ATTN_EARLY_START);
     a.k_new = static_cast<const char*>(knew) + kv_layer * L;  // fused append of this layer's new token
     a.v_new = static_cast<const char*>(vnew) + kv_layer * L;
     return kvp_paged_attention(&a, s);

@@ -328,7 +328,8 @@ def test_balanced_schedule_leaves_workspace_clean(kvb, ora, cuda):
 @pytest.mark.parametrize("shape", [(14, 2, 64), (32, 8, 128)], ids=["qwen", "llama"])
 def test_early_start_back_to_back_bit_exact(kvb, cuda, shape):
     """Eight layers launched back to back on one stream with early start (each kernel's prologue overlapping
-    the previous kernel's tail) and the fused append give outputs and pools bit-identical to plain launches."""
+    the previous kernel's tail) and early load (its first K/V tiles loaded before the previous kernel ends), with
+    the fused append, give outputs and pools bit-identical to plain launches."""
     import torch
     nh, kvh, D = shape
     L, B, ns = 8, 16, 48
@@ -351,15 +352,17 @@ def test_early_start_back_to_back_bit_exact(kvb, cuda, shape):
     t = torch.from_numpy(T).cuda()
     ln = torch.from_numpy(lens.astype(np.int32)).cuda()
     res = []
-    for early in (False, True):
+    for mode in ("plain", "early_start", "early_load"):
         k2, v2 = K.clone(), V.clone()
         out = torch.empty_like(q)
         st = torch.zeros(1, dtype=torch.int32, device="cuda")
         for layer in range(L):
             kvb.paged_attention(q[layer], k2[layer], v2[layer], t, ln, nh, kvh, out=out[layer], status=st,
-                                k_new=kn[layer], v_new=vn[layer], early_start=early)
+                                k_new=kn[layer], v_new=vn[layer], early_start=mode == "early_start",
+                                early_load=mode == "early_load" and layer > 0)
         torch.cuda.synchronize()
         assert int(st.item()) == 0
         res.append((out, k2, v2))
-    for a, b in zip(*res):
-        assert torch.equal(a, b)
+    for other in res[1:]:
+        for a, b in zip(res[0], other):
+            assert torch.equal(a, b)
