@@ -17,8 +17,9 @@ Inputs are synthetic, seeded N(0,1).
   cpu_baseline : the reference's own CPU paged_attention_cpu (oracle/_ref) on a bounded sample, all host cores
 
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config llama3-8b|...]
-       python bench.py --op migrate|cow   (block movers: one process; migrate reads GPU 1's pool into GPU 0's
-                                           over NVLink when two GPUs are visible)
+       python bench.py --op migrate|cow|swap   (block movers: one process; migrate reads GPU 1's pool into
+                                                GPU 0's over NVLink when two GPUs are visible; swap moves blocks
+                                                to a pinned host pool and back)
 Multi-GPU: launched under torch.distributed.run, one process per GPU, requests sharded with no collective
 on the data path (weak scaling); timings are the max over ranks.
 """
@@ -388,6 +389,62 @@ def run_ours(args, cfg, rank, world, dev):
     return res, lens
 
 
+def run_swap(args, cfg):
+    """Swap (preemption) traffic, device timed: a step swaps 512 random config blocks (every layer, K and V) out
+    to a pinned host pool (kvp_swap_out) and back into fresh block ids (kvp_swap_in), on a side stream as the
+    decode runtime issues them.  Reports GB/s per direction against the host link."""
+    import torch
+    kvb = importlib.import_module("paged-kv-cache-manager_b200")
+    L, B, kvh, D = cfg["L"], cfg["B"], cfg["kvh"], cfg["D"]
+    tdt = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float16
+    nblk, nb = 512, 2048
+    dev = torch.device("cuda", 0)
+    k = torch.empty((L, nb, B, kvh, D), dtype=tdt, device=dev)
+    v = torch.empty_like(k)
+    k.view(torch.int16).random_(-30000, 30000)
+    v.view(torch.int16).random_(-30000, 30000)
+    slot = kvb.host_slot_bytes(L, B, kvh, D)
+    pool = torch.empty(slot * nblk, dtype=torch.uint8).pin_memory()
+    rng = np.random.default_rng(0)
+    side = torch.cuda.Stream(dev)
+    steps = args.warmup + args.steps
+    outs = [rng.permutation(nb)[:nblk].tolist() for _ in range(steps)]
+    ins = [rng.permutation(nb)[:nblk].tolist() for _ in range(steps)]
+    slots = list(range(nblk))
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    t_out = t_in = 0.0
+    with ClockSampler(0) as clk:
+        for i in range(steps):
+            ev[0].record(side)
+            kvb.swap_out(k, v, outs[i], slots, pool, stream=side)
+            ev[1].record(side)
+            kvb.swap_in(k, v, ins[i], slots, pool, stream=side)
+            ev[2].record(side)
+            side.synchronize()
+            if i >= args.warmup:
+                t_out += ev[0].elapsed_time(ev[1])
+                t_in += ev[1].elapsed_time(ev[2])
+    # bit-exact round trip of the last step: each block swapped in equals its host slot's K and V
+    bb = B * kvh * D * 2
+    for j in range(8):
+        hk = pool[j * slot:j * slot + L * bb].view(torch.int16).view(L, B, kvh, D)
+        hv = pool[j * slot + L * bb:(j + 1) * slot].view(torch.int16).view(L, B, kvh, D)
+        assert torch.equal(k[:, ins[-1][j]].view(torch.int16).cpu(), hk)
+        assert torch.equal(v[:, ins[-1][j]].view(torch.int16).cpu(), hv)
+    moved = nblk * block_bytes_all_layers(cfg)
+    g_out = moved / (t_out / args.steps / 1e3) / 1e9
+    g_in = moved / (t_in / args.steps / 1e3) / 1e9
+    line = {"metric": "block swap bandwidth (out, in)", "value": round(min(g_out, g_in), 1), "unit": "GB/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "op": "swap",
+            "out_gbs": round(g_out, 1), "in_gbs": round(g_in, 1),
+            "ms_per_step": round((t_out + t_in) / args.steps, 3), "dtype": cfg["dtype"], "data": "synthetic random bits",
+            "config": {"workload": f"{args.config}-shaped blocks ({block_bytes_all_layers(cfg)} bytes, every layer, K "
+                                   f"and V), {nblk} random blocks out and {nblk} back in per step, pinned host pool",
+                       "copies": "one cudaMemcpy2DAsync per (block, K|V), layers strided"},
+            "gpu_launches": 0, "clocks": clk.summary()}
+    print(json.dumps(line))
+
+
 def run_block_mover(args, cfg):
     """Whole-block movers of the data plane, device timed: `migrate` copies blocks from a second GPU's pool into
     this GPU's pool (kvp_migrate_blocks, peer loads over NVLink; two pools on one GPU when only one is
@@ -482,7 +539,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--requests", type=int, default=0, help="profiling: requests per GPU (pool sized to need)")
     ap.add_argument("--layers", type=int, default=0, help="profiling: number of layers (pool sized to need)")
-    ap.add_argument("--op", default="decode", choices=["decode", "migrate", "cow"],
+    ap.add_argument("--op", default="decode", choices=["decode", "migrate", "cow", "swap"],
                     help="decode step (default) or a whole-block mover measured alone")
     args = ap.parse_args()
     assert args.warmup >= 3, "at least 3 warm-up steps"
@@ -524,6 +581,9 @@ def main():
         print(json.dumps(line))
         return
 
+    if args.op == "swap":
+        run_swap(args, cfg)
+        return
     if args.op != "decode":
         run_block_mover(args, cfg)
         return
