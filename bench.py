@@ -591,7 +591,8 @@ def main():
     import torch.distributed as dist
     if world > 1:
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     res, lens = run_ours(args, cfg, rank, world, dev)
