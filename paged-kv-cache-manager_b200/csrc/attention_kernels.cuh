@@ -5,21 +5,25 @@
 //     sequences, concatenated) are divided evenly between CTAs regardless of sequence boundaries, so every
 //     CTA streams the same number of bytes with one pipeline ramp per launch.  A CTA's range is cut into
 //     segments at sequence boundaries; a segment that covers a whole sequence is normalised and written
-//     directly, the others leave (m, l, unnormalised O) partials that merge_streamk combines.
-//   * fixed splits: one CTA per (sequence, kv-head group, split of split_tiles tiles); split_tiles large
-//     enough means one CTA per sequence and no workspace at all (the reference's signature).
+//     directly, the others leave (m, l, unnormalised O) partials, counted per sequence, and the CTA whose
+//     count completes a sequence merges it in the same kernel.  With an early start (programmatic dependent
+//     launch) the prologue -- and with an early load the first ring of K/V loads -- overlaps the previous
+//     kernel on the stream.
+//   * fixed splits: one CTA per (sequence, kv-head group, split of split_tiles tiles), partials merged by
+//     merge_splits_kernel; split_tiles large enough means one CTA per sequence and no workspace at all (the
+//     reference's signature).
 //
 // Tile pipeline (per CTA): a producer warp reads block ids from the sequence's table row (32 entries per
 // coalesced load) and issues TMA tiled loads of the K and V rows of every kv head of the CTA's group into a
 // ring of shared-memory stages (128B/64B swizzled; completion counted on an mbarrier); at the start of a
-// stream-K segment it also bulk-copies the sequence's queries into the stage.  One consumer warp per kv head
-// computes, per tile,
+// segment it also bulk-copies the sequence's queries into a query slot and, with the fused append, first
+// writes the sequence's newest K/V row.  One or two consumer warps per kv head compute, per tile,
 //     S^T[16 tokens x 8 heads] = K_tile[16 x D] . Q^T[D x 8]      (mma.sync m16n8k16, fp32 accumulate)
 // so the GQA group of query heads (up to 8 per n-tile) shares every K/V byte; an online softmax in the
 // log2 domain with warp-shuffle reductions; then
 //     O^T[D x 8] += V_tile^T[D x 16] . P^T[16 x 8]
-// with P^T obtained from the S^T accumulator by movmatrix.  P (and an fp32 query) are split into a 16-bit
-// high part plus a 16-bit residual, so the result keeps close to fp32 accuracy.
+// with P^T obtained from the S^T accumulator by movmatrix.  P (and a query in another dtype, QLO) are split
+// into a 16-bit high part plus a 16-bit residual, so the result keeps close to fp32 accuracy.
 //
 // Numerics follow the reference's paged_attention_cpu (src/paged_attention.cpp:68-114): per-partition
 // running (m, l, acc) with rescaling by exp(m_old - m_new), partitions merged by exp(m_p - M).
