@@ -4,8 +4,11 @@
 // fp16 q / k_cache / v_cache / out, fp32 math; layouts as in kvpage/paged_attention.h.  head_dim must be
 // one of 32, 64, 96, 128, 256; num_heads % kv_heads == 0; `warps` must be 1..8 (validated as the reference
 // does; the B200 kernel chooses its own warp layout).  Returns cudaErrorInvalidValue for invalid
-// arguments, otherwise the launch status.  Asynchronous on `stream`; no allocation.  Without a pool size
-// the kernel cannot bounds-check table entries, exactly like the reference kernel.
+// arguments, otherwise the launch status.  Asynchronous on `stream`; no allocation: long contexts are split
+// across CTAs (balanced schedule) with the partials in the library's fixed no-allocation scratch
+// (kvp_paged_attention_noalloc), and calls on one device are ordered through an event so that calls on
+// different streams never overlap on it.  Without a pool size the kernel cannot bounds-check table entries,
+// exactly like the reference kernel.
 #pragma once
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>

@@ -8,6 +8,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <mutex>
 #include <stdexcept>
 #include <string>
 
@@ -47,6 +48,23 @@ void paged_attention(const AttnShape& s, int num_seqs, int max_blocks, const voi
 
 }  // namespace kvp
 
+namespace {
+
+// The drop-in entry point keeps its split partials in the library's no-allocation scratch, which all such
+// calls on a device share.  The reference's entry point lets callers use any streams concurrently, so calls
+// are ordered through one event per device: each call's stream waits for the previous call's launch (a wait
+// on the same stream costs nothing).  Streams being captured skip the ordering; the graph's order applies.
+struct DropInOrder {
+    std::mutex mu;
+    cudaEvent_t ev[64] = {};
+};
+DropInOrder& drop_in_order() {
+    static DropInOrder o;
+    return o;
+}
+
+}  // namespace
+
 cudaError_t launch_paged_attention(const __half* q, const __half* k_cache, const __half* v_cache,
                                    const int* block_tables, const int* seq_lens, __half* out, int num_seqs,
                                    int num_heads, int kv_heads, int head_dim, int block_size, int max_blocks,
@@ -73,8 +91,25 @@ cudaError_t launch_paged_attention(const __half* q, const __half* k_cache, const
     a.head_dim = head_dim;
     a.block_size = block_size;
     a.max_blocks = max_blocks;
-    a.split_tiles = -1;  // no workspace in this signature: one CTA per (sequence, kv-head group)
-    const int rc = kvp_paged_attention(&a, stream);
+    a.split_tiles = 0;  // balanced schedule, partials in the library's scratch (this signature has no workspace)
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    DropInOrder& o = drop_in_order();
+    std::lock_guard<std::mutex> lock(o.mu);
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    const bool ordered = cudaStreamIsCapturing(stream, &cs) == cudaSuccess && cs == cudaStreamCaptureStatusNone;
+    if (ordered) {
+        if (!o.ev[dev]) e = cudaEventCreateWithFlags(&o.ev[dev], cudaEventDisableTiming);
+        else e = cudaStreamWaitEvent(stream, o.ev[dev], 0);
+        if (e != cudaSuccess) return e;
+    }
+    const int rc = kvp_paged_attention_noalloc(&a, stream);
+    if (rc == KVP_OK && ordered) {
+        e = cudaEventRecord(o.ev[dev], stream);
+        if (e != cudaSuccess) return e;
+    }
     if (rc == KVP_OK) return cudaSuccess;
     if (rc == KVP_ECUDA) {
         const cudaError_t e = cudaGetLastError();

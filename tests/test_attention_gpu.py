@@ -366,3 +366,18 @@ def test_early_start_back_to_back_bit_exact(kvb, cuda, shape):
     for other in res[1:]:
         for a, b in zip(res[0], other):
             assert torch.equal(a, b)
+
+
+def test_reference_cuda_test_binary_on_drop_in(cuda):
+    """The reference's own GPU test (cuda/test_paged_attention.cu: its case list -- block sizes 1..32, shared
+    prefixes, Llama/Qwen head shapes, head_dim 32..256 -- checked against its own CPU reference_attention),
+    built by oracle/Makefile with this library's launch_paged_attention in place of the reference kernel."""
+    import os
+    import subprocess
+    exe = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle", "_ref", "ref_cuda_test")
+    if not os.path.exists(exe):
+        pytest.skip("oracle/_ref/ref_cuda_test not built (needs the reference sources at build time)")
+    r = subprocess.run([exe, "--no-bench"], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+    assert "ALL PASSED" in r.stdout
+    assert r.stdout.count("| PASS |") >= 45
