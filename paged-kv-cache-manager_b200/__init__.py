@@ -30,6 +30,17 @@ NO_REQUEST = -1
 STATS_FIELDS = ("requests", "used_tokens", "allocated_blocks", "allocated_slots", "internal_waste",
                 "logical_blocks", "blocks_saved", "cow_copies", "cached_blocks", "cache_evictions")
 
+class KVStats(dict):
+    """KVManager statistics (kvpage::KVStats): a dict of STATS_FIELDS that also reads as attributes
+    (`stats().cow_copies`), as the reference's Python binding exposes them (python/kvpage_py.cpp:14-20)."""
+
+    def __getattr__(self, name):
+        try:
+            return self[name]
+        except KeyError:
+            raise AttributeError(name) from None
+
+
 _i32, _i64, _vp, _f32, _sz = C.c_int32, C.c_int64, C.c_void_p, C.c_float, C.c_size_t
 _pi32, _pi64 = C.POINTER(C.c_int32), C.POINTER(C.c_int64)
 
@@ -260,21 +271,21 @@ class KVManager:
     def can_admit(self, prompt: int) -> bool:
         return _bool(self._L.kvp_mgr_can_admit(self._h, prompt))
 
-    def blocks_needed_to_admit(self, parent: int, shared: int, prompt: int) -> int:
-        v = self._L.kvp_mgr_blocks_needed_to_admit(self._h, parent, shared, prompt)
+    def blocks_needed_to_admit(self, parent: int, shared_tokens: int, prompt_tokens: int) -> int:
+        v = self._L.kvp_mgr_blocks_needed_to_admit(self._h, parent, shared_tokens, prompt_tokens)
         if v < 0 and last_error():
             _bool(v)
         return v
 
-    def stats(self) -> dict:
+    def stats(self) -> KVStats:
         buf = (C.c_int64 * 10)()
         self._L.kvp_mgr_stats(self._h, buf)
-        return dict(zip(STATS_FIELDS, list(buf)))
+        return KVStats(zip(STATS_FIELDS, list(buf)))
 
-    def recompute_stats(self) -> dict:
+    def recompute_stats(self) -> KVStats:
         buf = (C.c_int64 * 10)()
         self._L.kvp_mgr_recompute_stats(self._h, buf)
-        return dict(zip(STATS_FIELDS, list(buf)))
+        return KVStats(zip(STATS_FIELDS, list(buf)))
 
     def validate(self) -> str:
         buf = C.create_string_buffer(1024)
