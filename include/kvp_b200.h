@@ -91,6 +91,9 @@ typedef struct kvp_attn_args {
      * several prompt positions of one request in one call. */
     const void* k_new;
     const void* v_new;
+    /* tuning (balanced schedule), 0: automatic: a sequence's start cost, in 16-token tiles, charged to the CTA
+     * that starts it when the step's tiles are divided between CTAs; < 0: none */
+    int32_t seq_start_tiles;
 } kvp_attn_args;
 
 /* The caller guarantees the workspace's counter words are zero, so the call skips resetting them: true for

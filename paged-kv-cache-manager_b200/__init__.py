@@ -51,7 +51,8 @@ class AttnArgs(C.Structure):
                 ("num_seqs", _i32), ("num_heads", _i32), ("kv_heads", _i32), ("head_dim", _i32),
                 ("block_size", _i32), ("max_blocks", _i32), ("scale", _f32), ("split_tiles", _i32),
                 ("kv_heads_per_cta", _i32), ("stages", _i32), ("workspace", _vp), ("workspace_bytes", _sz),
-                ("status", _vp), ("warps_per_kv_head", _i32), ("flags", _i32), ("k_new", _vp), ("v_new", _vp)]
+                ("status", _vp), ("warps_per_kv_head", _i32), ("flags", _i32), ("k_new", _vp), ("v_new", _vp),
+                ("seq_start_tiles", _i32)]
 
 
 class AppendArgs(C.Structure):
@@ -394,7 +395,7 @@ def _stream_ptr(stream):
 
 def attention_args(q, k_cache, v_cache, block_tables, seq_lens, out, num_heads, kv_heads, *, num_blocks=None,
                    workspace=None, split_tiles=0, kv_heads_per_cta=0, stages=0, status=None, scale=0.0,
-                   warps_per_kv_head=0, k_new=None, v_new=None) -> AttnArgs:
+                   warps_per_kv_head=0, k_new=None, v_new=None, seq_start_tiles=0) -> AttnArgs:
     """AttnArgs for one layer; k_cache/v_cache are [num_blocks][B][kv_heads][D] (or views of them).  With
     k_new/v_new ([num_seqs][kv_heads][D], pool dtype) the kernel first writes each sequence's newest token."""
     nb, B, kvh, D = k_cache.shape[-4:]
@@ -409,6 +410,7 @@ def attention_args(q, k_cache, v_cache, block_tables, seq_lens, out, num_heads, 
     a.block_size, a.max_blocks = B, block_tables.shape[1]
     a.scale, a.split_tiles, a.kv_heads_per_cta, a.stages = scale, split_tiles, kv_heads_per_cta, stages
     a.warps_per_kv_head = warps_per_kv_head
+    a.seq_start_tiles = seq_start_tiles
     if workspace is not None:
         a.workspace, a.workspace_bytes = _dev(workspace, "workspace"), workspace.numel() * workspace.element_size()
     a.status = _dev(status, "status") if status is not None else None
@@ -429,7 +431,8 @@ def workspace_bytes(args: AttnArgs) -> int:
 def paged_attention(q, k_cache, v_cache, block_tables, seq_lens, num_heads: int, kv_heads: int, *, out=None,
                     out_dtype=None, workspace=None, split_tiles: int = 0, kv_heads_per_cta: int = 0, stages: int = 0,
                     status=None, stream=None, num_blocks: Optional[int] = None, warps_per_kv_head: int = 0,
-                    k_new=None, v_new=None, early_start: bool = False, early_load: bool = False):
+                    k_new=None, v_new=None, early_start: bool = False, early_load: bool = False,
+                    seq_start_tiles: int = 0):
     """Decode attention through the C ABI (kvp_paged_attention).  Allocates `out` (and a workspace when
     none is given and the context will be split) with torch if not provided.  k_new/v_new: fused append of
     each sequence's newest token (position seq_lens[s] - 1) before attending.  early_start: the kernel may start
@@ -443,7 +446,8 @@ def paged_attention(q, k_cache, v_cache, block_tables, seq_lens, num_heads: int,
         out = torch.empty(q.shape, dtype=out_dtype or q.dtype, device=q.device)
     a = attention_args(q, k_cache, v_cache, block_tables, seq_lens, out, num_heads, kv_heads, num_blocks=num_blocks,
                        workspace=workspace, split_tiles=split_tiles, kv_heads_per_cta=kv_heads_per_cta,
-                       stages=stages, status=status, warps_per_kv_head=warps_per_kv_head, k_new=k_new, v_new=v_new)
+                       stages=stages, status=status, warps_per_kv_head=warps_per_kv_head, k_new=k_new, v_new=v_new,
+                       seq_start_tiles=seq_start_tiles)
     if workspace is None and split_tiles >= 0:
         need = workspace_bytes(a)
         if need:

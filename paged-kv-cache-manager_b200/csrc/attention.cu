@@ -248,6 +248,32 @@ int plan_attention(const kvp_attn_args& a, bool have_workspace, AttnPlan* out) {
     if (pl.streamk) {
         const void* fn = pick_kernel(a.kv_dtype, a.q_dtype, D, g, true);
         pl.G = sm_count() * streamk_ctas_per_sm(fn, (kc * pl.wph + 1) * 32, pl.smem);
+        // The partition of a step depends on the grid once a step has more units than CTAs.  Block sizes that
+        // are not multiples of 16 pad their stages (more shared memory, fewer resident CTAs), so they take the
+        // grid of the 16-token layout: the same contexts give the same partition -- and bit-identical results
+        // -- in every block size.  CTAs beyond residency simply start later (no CTA waits on another).
+        if (pl.R != 16) {
+            kvp_attn_args b = a;
+            b.block_size = 16;
+            b.max_blocks = pl.max_tiles;
+            AttnPlan p16;
+            if (plan_attention(b, have_workspace, &p16) == KVP_OK && p16.streamk) pl.G = p16.G;
+        }
+        // A sequence switch (query load, state reset, segment epilogue, and with two warps per kv head their
+        // state combine) costs a CTA about 3.8 us, 5.3 us with two warps per head (the optima of start-cost
+        // sweeps on B200 for the Qwen2.5-0.5B, TinyLlama and Llama-3-8B shapes); charge it in tiles: a tile's
+        // time at the full bandwidth shared by the CTAs of one SM.  Only quantities independent of the block
+        // size enter (the tile's K/V bytes, one CTA per SM for 48 KB tiles or more, else two), so every block
+        // size and placement of the same contexts gets the same partition -- and bit-identical results.
+        if (a.seq_start_tiles > 0) {
+            pl.seq_units = std::min(a.seq_start_tiles, 1024);
+        } else if (a.seq_start_tiles == 0) {
+            const double tile_bytes = 16.0 * kc * D * 2 * 2;
+            const double ctas = static_cast<double>(sm_count()) * (tile_bytes >= (48 << 10) ? 1 : 2);
+            const double switch_us = pl.wph > 1 ? 5.3 : 3.8;
+            const double tile_us = tile_bytes * ctas / 6.4e6;
+            pl.seq_units = static_cast<int>(std::min(32.0, std::max(0.0, std::round(switch_us / tile_us))));
+        }
         pl.split_tiles = pl.max_tiles;
         pl.max_splits = 1;
         const size_t rows = (static_cast<size_t>(pl.G) + a.num_seqs) * a.num_heads;
@@ -378,6 +404,7 @@ extern "C" KVP_API int kvp_paged_attention(const kvp_attn_args* a, void* stream)
     prm.v_pool = const_cast<void*>(a->v_cache);
     prm.kvh = a->kv_heads;
     prm.early_load = (a->flags & KVP_ATTN_EARLY_LOAD) ? 1 : 0;
+    prm.seq_units = pl.seq_units;
     const float scale = a->scale > 0.f ? a->scale : 1.0f / std::sqrt(static_cast<float>(a->head_dim));
     prm.sl2 = scale * 1.4426950408889634f;
     cudaStream_t s = static_cast<cudaStream_t>(stream);

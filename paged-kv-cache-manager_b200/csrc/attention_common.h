@@ -52,6 +52,7 @@ struct AttnParams {
     void* v_pool;
     int kvh;
     int early_load;  // the producer may load the first K/V tiles before waiting for the previous kernel
+    int seq_units;   // stream-K: start-cost units charged ahead of each sequence's tiles
 };
 
 // Per-variant entry points: K/V dtype x whether the query needs a low-half residual MMA (its dtype differs

@@ -542,25 +542,34 @@ __device__ __forceinline__ int cta_of_tile(long long t, long long T, int G) {
 }
 
 // Stream-K: the CTA's tile range [t, end) of the concatenated sequences, cut at sequence boundaries.
+// The concatenated space is counted in units: each valid sequence spans X start-cost units (the time a CTA
+// spends switching to a new sequence, in tiles) followed by its tiles, so the balanced split charges that
+// cost to the CTA that starts the sequence.  A CTA whose range holds only a sequence's start-cost units does
+// no work for it; the CTAs holding its tiles are c0 .. c0 + nseg - 1.
 struct StreamSegments {
-    const int32_t* P;  // tile prefix sums in shared memory
+    const int32_t* P;  // unit prefix sums in shared memory
     const uint8_t* R;  // tokens in each sequence's last tile, in shared memory
     long long t, end, T;
-    int s, cta, nh, Ge;
+    int s, cta, nh, Ge, X;
     __device__ __forceinline__ bool next(Segment& sg) {
-        if (t >= end) return false;
-        while (P[s + 1] <= t) ++s;
-        const long long e = min(end, static_cast<long long>(P[s + 1]));
-        sg.seq = s;
-        sg.len = (P[s + 1] - P[s] - 1) * 16 + R[s];
-        sg.tile0 = static_cast<int>(t - P[s]);
-        sg.tile1 = static_cast<int>(e - P[s]);
-        sg.single = (t == P[s]) && (e == P[s + 1]);
-        sg.part_row = static_cast<size_t>(cta + s) * nh;
-        sg.c0 = sg.single ? cta : cta_of_tile(P[s], T, Ge);
-        sg.nseg = sg.single ? 1 : cta_of_tile(P[s + 1] - 1, T, Ge) - sg.c0 + 1;
-        t = e;
-        return true;
+        while (t < end) {
+            while (P[s + 1] <= t) ++s;
+            const long long e = min(end, static_cast<long long>(P[s + 1]));
+            const long long first = static_cast<long long>(P[s]) + X;  // the sequence's first tile, in units
+            const long long a = max(t, first);
+            t = e;
+            if (a >= e) continue;  // only start-cost units of this sequence here
+            sg.seq = s;
+            sg.len = (P[s + 1] - P[s] - X - 1) * 16 + R[s];
+            sg.tile0 = static_cast<int>(a - first);
+            sg.tile1 = static_cast<int>(e - first);
+            sg.single = (a == first) && (e == P[s + 1]);
+            sg.part_row = static_cast<size_t>(cta + s) * nh;
+            sg.c0 = sg.single ? cta : cta_of_tile(first, T, Ge);
+            sg.nseg = sg.single ? 1 : cta_of_tile(P[s + 1] - 1, T, Ge) - sg.c0 + 1;
+            return true;
+        }
+        return false;
     }
 };
 
@@ -854,7 +863,8 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
 
 // ---------------------------------------------------------------- stream-K schedule
 
-// Tile prefix sums P[0..ns] of all sequences into shared memory (invalid lengths count 0 tiles), and R[s] =
+// Unit prefix sums P[0..ns] of all sequences into shared memory (a valid sequence counts seq_units start-cost
+// units plus its tiles, an invalid length counts nothing), and R[s] =
 // the tokens in sequence s's last tile, so segment starts need no global load of the length.
 __device__ __forceinline__ void build_prefix(const AttnParams& p, int32_t* P, uint8_t* R, int32_t* warp_tot) {
     const int ns = p.num_seqs, nthr = blockDim.x, tid = threadIdx.x;
@@ -862,7 +872,10 @@ __device__ __forceinline__ void build_prefix(const AttnParams& p, int32_t* P, ui
     const int per = (ns + nthr - 1) / nthr;
     const int b = min(tid * per, ns), e = min(b + per, ns);
     int local = 0;
-    for (int i = b; i < e; ++i) local += tiles_of_len(p, __ldg(p.lens + i));
+    for (int i = b; i < e; ++i) {
+        const int n = tiles_of_len(p, __ldg(p.lens + i));
+        local += n ? n + p.seq_units : 0;
+    }
     int x = local;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
@@ -885,7 +898,8 @@ __device__ __forceinline__ void build_prefix(const AttnParams& p, int32_t* P, ui
     for (int i = b; i < e; ++i) {
         const int len = __ldg(p.lens + i);
         P[i] = run;
-        run += tiles_of_len(p, len);
+        const int n = tiles_of_len(p, len);
+        run += n ? n + p.seq_units : 0;
         R[i] = static_cast<uint8_t>(((len - 1) & 15) + 1);
     }
     if (tid == nthr - 1) P[ns] = warp_tot[nwarps - 1];
@@ -926,6 +940,7 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
     segs.R = R;
     segs.T = T;
     segs.Ge = Ge;
+    segs.X = p.seq_units;
     segs.t = Ge > 0 ? cta_begin(c, T, Ge) : 0;
     segs.end = Ge > 0 ? cta_begin(c + 1, T, Ge) : 0;
     segs.s = seq_of_tile(P, ns, segs.t);

@@ -39,7 +39,7 @@ def check_close(got, ref, out_dtype="f32", what=""):
 
 
 def run_attention(kvb, ora, Q, K, V, T, L, nh, kvh, *, kv="bf16", q="f32", out="f32", split_tiles=0,
-                  kvh_cta=0, stages=0, num_blocks=None, ref=None):
+                  kvh_cta=0, stages=0, num_blocks=None, ref=None, seq_start_tiles=0):
     import torch
     dev = torch.device("cuda:0")
     kt, kf = _round(K, kv)
@@ -51,7 +51,8 @@ def run_attention(kvb, ora, Q, K, V, T, L, nh, kvh, *, kv="bf16", q="f32", out="
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     kvb.paged_attention(qt.to(dev), kt.to(dev), vt.to(dev), torch.from_numpy(T).to(dev),
                         torch.from_numpy(np.asarray(L, np.int32)).to(dev), nh, kvh, out=o, split_tiles=split_tiles,
-                        kv_heads_per_cta=kvh_cta, stages=stages, status=status, num_blocks=num_blocks)
+                        kv_heads_per_cta=kvh_cta, stages=stages, status=status, num_blocks=num_blocks,
+                        seq_start_tiles=seq_start_tiles)
     torch.cuda.synchronize()
     assert int(status.item()) == 0, f"device status {int(status.item())}"
     return o.float().cpu().numpy(), ref
@@ -269,18 +270,21 @@ def test_empty_batch_is_a_no_op(kvb, cuda):
     torch.cuda.synchronize()
 
 
+@pytest.mark.parametrize("start", [0, -1, 40], ids=["start-auto", "start-none", "start-40"])
 @pytest.mark.parametrize("lens", [
     [1, 2, 3, 1, 16],                       # fewer tiles than persistent CTAs
     [32768] + [17] * 100,                    # one very long context among many short ones
     [5000] * 3 + [1] * 300 + [700] * 50,     # many sequences, mixed
 ])
-def test_balanced_schedule_edge_cases(kvb, ora, cuda, lens):
-    """The persistent balanced schedule (automatic split): CTA ranges cut through sequences anywhere,
-    sequences entirely inside one CTA are written directly, the rest merged."""
+def test_balanced_schedule_edge_cases(kvb, ora, cuda, lens, start):
+    """The persistent balanced schedule (automatic split): CTA ranges cut through sequences anywhere (in
+    units that charge each sequence's start cost -- automatic, none, or a large 40 tiles, so that some CTAs
+    hold only start-cost units), sequences entirely inside one CTA are written directly, the rest merged."""
     nb = sum((n + 15) // 16 for n in lens) + 3
     Q, K, V, T, L = _normal_case(len(lens), len(lens), 32, 8, 128, 16, lens, nb)
-    got, ref = run_attention(kvb, ora, Q, K, V, T, L, 32, 8, kv="bf16", q="bf16", split_tiles=0)
-    check_close(got, ref, what=f"balanced schedule {len(lens)} sequences")
+    got, ref = run_attention(kvb, ora, Q, K, V, T, L, 32, 8, kv="bf16", q="bf16", split_tiles=0,
+                             seq_start_tiles=start)
+    check_close(got, ref, what=f"balanced schedule {len(lens)} sequences, start cost {start}")
 
 
 def test_balanced_schedule_unaligned_query(kvb, ora, cuda):
