@@ -1,0 +1,169 @@
+"""The reference's own scheduler simulation driving the device data plane.
+
+tests/golden/sim_traces.npz holds decision streams recorded from the reference's run_paged
+(src/simulator.cpp:80-289) over the reference's own KVManager (tests/golden/simtrace/make_sim_traces.py), with
+the reference's metrics, in three scenarios: FCFS with swap preemption, a persistent prefix cache and two
+samples per request (fork + copy-on-write); shortest-prompt-first with recompute preemption and shared
+prefixes; priority classes with displacement, a swap pool too small for every victim, and block size 8.
+
+CPU: this package's KVManager re-makes every decision with the recorded result, matches every end-of-step
+statistics marker, and the replay's totals (tokens, prefill tokens, cache hits, copy-on-write copies, swapped
+blocks) equal the reference's metrics.
+
+GPU: DataPlane replays the same streams with real K/V (synthetic rows that respect prefix groups and fork
+lineage): prefill writes, copy-on-write copies, swap-out / swap-in through a pinned pool, and per-layer paged
+attention with the new token fused in (or scattered first).  Every 20 steps each live request's context,
+gathered from the pools through its table, equals its logical rows bit for bit; sampled attention batches
+match the fp64 oracle over the logical contexts (2e-3 abs + 2e-3 rel)."""
+import importlib
+import json
+import os
+
+import numpy as np
+import pytest
+
+from conftest import PKG
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "sim_traces.npz")
+NAMES = json.loads(bytes(np.load(GOLDEN)["names"]).decode())
+L, KVH, D, NH = 2, 2, 64, 8
+
+
+def _load(name):
+    z = np.load(GOLDEN)
+    return {k: z[f"{name}_{k}"] for k in ("requests", "config", "metrics", "trace")}
+
+
+def _dp(kvb):
+    return importlib.import_module(PKG + ".dataplane")
+
+
+def _metrics(sc):
+    keys = ("steps", "generated", "preemptions", "recomputed", "cow", "swap_out", "swap_in", "hits", "evictions",
+            "prefill", "completed")
+    return dict(zip(keys, (int(x) for x in sc["metrics"])))
+
+
+def _max_swapped_blocks(dp, trace, B):
+    """Host slots the replay needs: the peak of blocks sitting in the swap pool."""
+    used = peak = 0
+    held = {}
+    for row in trace:
+        if row[0] == dp.TRACE_FREE and row[6] == dp.FREE_SWAPPED:
+            held[int(row[1])] = -(-int(row[2]) // B)
+            used += held[int(row[1])]
+            peak = max(peak, used)
+        elif row[0] == dp.TRACE_ADMIT_PREFIX and row[6] == 1:
+            used -= held.pop(int(row[1]))
+    return peak
+
+
+def test_fixture_covers_the_paths():
+    for name in NAMES:
+        m = _metrics(_load(name))
+        assert m["completed"] > 30 and m["preemptions"] > 5
+    by = {n: _metrics(_load(n)) for n in NAMES}
+    assert any(m["swap_out"] > 0 for m in by.values()) and any(m["recomputed"] > 0 for m in by.values())
+    assert any(m["cow"] > 0 for m in by.values()) and any(m["hits"] > 0 for m in by.values())
+    assert any(m["evictions"] > 0 for m in by.values())
+
+
+@pytest.mark.parametrize("name", NAMES)
+def test_decisions_match_reference_simulation(kvb, name):
+    dp = _dp(kvb)
+    sc = _load(name)
+    nb, B = (int(x) for x in sc["config"][:2])
+    mgr = kvb.KVManager(nb, B)
+    n = dp.replay_decisions(mgr, sc["trace"])
+    m = _metrics(sc)
+    assert (n.steps, n.tokens_generated, n.cow_copies) == (m["steps"], m["generated"], m["cow"])
+    assert (n.swap_out_blocks, n.swap_in_blocks) == (m["swap_out"], m["swap_in"])
+    assert (n.prefill_tokens, n.cache_hits) == (m["prefill"], m["hits"])
+    assert mgr.validate() == "" and mgr.free_blocks() == nb
+
+
+def test_a_wrong_decision_is_reported(kvb):
+    dp = _dp(kvb)
+    sc = _load(NAMES[0])
+    nb, B = (int(x) for x in sc["config"][:2])
+    t = sc["trace"].copy()
+    i = int(np.nonzero((t[:, 0] == dp.TRACE_APPEND) & (t[:, 5] == 1))[0][5])
+    t[i, 5] = 0  # plant a wrong recorded result
+    with pytest.raises(dp.TraceMismatch):
+        dp.replay_decisions(kvb.KVManager(nb, B), t)
+
+
+def _oracle_check(ora, content, rids, q, out, B):
+    ctx = [content(r, np.arange(int(n), dtype=np.int64)) for r, n in rids]
+    nblk = [-(-int(n) // B) for _, n in rids]
+    tables = np.zeros((len(rids), max(nblk)), np.int32)
+    lens = np.asarray([int(n) for _, n in rids], np.int32)
+    b0 = 0
+    for i, nbk in enumerate(nblk):
+        tables[i, :nbk] = np.arange(b0, b0 + nbk)
+        b0 += nbk
+    for layer in range(L):
+        K = np.zeros((b0 * B, KVH, D), np.float32)
+        V = np.zeros_like(K)
+        for i, (k, v) in enumerate(ctx):
+            s = int(tables[i, 0]) * B
+            K[s:s + lens[i]] = k[layer].float().cpu().numpy()
+            V[s:s + lens[i]] = v[layer].float().cpu().numpy()
+        ref = ora.reference_attention(NH, KVH, D, B, q[layer].float().cpu().numpy(), K.reshape(b0, B, KVH, D),
+                                      V.reshape(b0, B, KVH, D), tables, lens)
+        got = out[layer].float().cpu().numpy()
+        assert (np.abs(got - ref) <= 2e-3 + 2e-3 * np.abs(ref)).all(), (layer, np.abs(got - ref).max())
+
+
+def _contexts_check(plane, content):
+    import torch
+    torch.cuda.synchronize()
+    for r in sorted(plane.live):
+        n = plane.mgr.num_tokens(r)
+        idx = torch.tensor(plane.mgr.block_table(r), dtype=torch.long, device=plane.dev)
+        gk = plane.k[:, idx].reshape(L, -1, KVH, D)[:, :n]
+        gv = plane.v[:, idx].reshape(L, -1, KVH, D)[:, :n]
+        ek, ev = content(r, np.arange(n, dtype=np.int64))
+        assert torch.equal(gk.view(torch.int16), ek.view(torch.int16)), f"K of request {r}"
+        assert torch.equal(gv.view(torch.int16), ev.view(torch.int16)), f"V of request {r}"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "scatter"])
+@pytest.mark.parametrize("name", NAMES)
+def test_replay_on_device(kvb, ora, cuda, name, fused):
+    import torch
+    dp = _dp(kvb)
+    sc = _load(name)
+    nb, B = (int(x) for x in sc["config"][:2])
+    content = dp.SyntheticContent(sc["requests"], layers=L, kv_heads=KVH, head_dim=D, num_heads=NH, device=cuda,
+                                  seed=5)
+    batches = {"n": 0, "checked": 0}
+
+    def on_attention(rids, q, out, tables, lens):
+        batches["n"] += 1
+        if batches["n"] % 9 == 1:
+            _oracle_check(ora, content, list(zip(rids, lens)), q, out, B)
+            batches["checked"] += 1
+
+    plane = dp.DataPlane(nb, B, layers=L, num_heads=NH, kv_heads=KVH, head_dim=D, source=content,
+                         queries=content.queries, device=cuda, swap_slots=_max_swapped_blocks(dp, sc["trace"], B),
+                         fused_append=fused, on_attention=on_attention)
+    steps_checked = []
+
+    def on_step(i):
+        if i % 20 == 0:
+            _contexts_check(plane, content)
+            steps_checked.append(i)
+
+    n = plane.run(sc["trace"], on_step=on_step)
+    assert plane.status_word() == 0
+    _contexts_check(plane, content)
+    m = _metrics(sc)
+    assert (n.steps, n.tokens_generated, n.cow_copies) == (m["steps"], m["generated"], m["cow"])
+    assert (n.swap_out_blocks, n.swap_in_blocks) == (m["swap_out"], m["swap_in"])
+    assert (n.prefill_tokens, n.cache_hits) == (m["prefill"], m["hits"])
+    assert n.attention_rows == m["generated"]
+    assert plane.mgr.free_blocks() == nb and not plane.live
+    assert batches["checked"] >= 5 and len(steps_checked) >= 8
+    torch.cuda.synchronize()
