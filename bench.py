@@ -445,6 +445,113 @@ def run_swap(args, cfg):
     print(json.dumps(line))
 
 
+class _BankContent:
+    """The data-plane benchmark's K/V source: each row is a row of a seeded random bank (4096 rows of every
+    layer's K and V), picked by a hash of the row's origin and position -- the prefix and fork sharing of
+    dataplane.SyntheticContent at the cost of one gather (content does not matter for timing)."""
+
+    def __init__(self, requests, cfg, dev, tdt, max_rows):
+        import torch
+        dp = importlib.import_module("paged-kv-cache-manager_b200.dataplane")
+        L, kvh, D, nh = cfg["L"], cfg["kvh"], cfg["D"], cfg["nh"]
+        self.origins = dp.SyntheticContent(requests, layers=1, kv_heads=1, head_dim=1, num_heads=1,
+                                           device=dev).origins
+        g = torch.Generator(device=dev).manual_seed(11)
+        self.bank = torch.randn((2, L, 4096, kvh, D), generator=g, device=dev).to(tdt)
+        self.qbank = torch.randn((L, max_rows, nh, D), generator=g, device=dev).to(tdt)
+        self.dev = dev
+
+    def __call__(self, rids, positions):
+        import torch
+        key = (self.origins(rids, positions) * 1000003 + np.asarray(positions) * 7919) % 4096
+        idx = torch.from_numpy(key).pin_memory().to(self.dev, non_blocking=True)
+        return self.bank[0].index_select(1, idx), self.bank[1].index_select(1, idx)
+
+    def queries(self, rids):
+        return self.qbank[:, :len(rids)]
+
+
+def run_sim(args, cfg):
+    """Scheduler-driven data plane: the reference simulator's recorded decision stream at serving scale
+    (tests/golden/sim_traces.npz, `serving_fcfs_swap`: 256 requests, long-tail prompts up to 3072 tokens, shared
+    prefixes + prefix cache, FCFS, swap preemption, 3072 blocks of 16 tokens) replayed by dataplane.DataPlane at
+    this config's head shape: prefill writes, copy-on-write, swap-out / swap-in through a pinned pool, and
+    per-layer fused append + attention of every generating request, all decisions re-made by the KVManager.
+    One warm-up replay, then `--sim-replays` timed replays, each on fresh pools; wall time includes the host."""
+    import time
+    import torch
+    dp = importlib.import_module("paged-kv-cache-manager_b200.dataplane")
+    z = np.load(os.path.join(ROOT, "tests", "golden", "sim_traces.npz"))
+    name = "serving_fcfs_swap"
+    trace, req, conf, met = (z[f"{name}_{k}"] for k in ("trace", "requests", "config", "metrics"))
+    nb, B = int(conf[0]), int(conf[1])
+    L, kvh, D, nh = cfg["L"], cfg["kvh"], cfg["D"], cfg["nh"]
+    tdt = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float16
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    held, used, peak = {}, 0, 0
+    for row in trace:
+        if row[0] == dp.TRACE_FREE and row[6] == dp.FREE_SWAPPED:
+            held[int(row[1])] = -(-int(row[2]) // B)
+            used += held[int(row[1])]
+            peak = max(peak, used)
+        elif row[0] == dp.TRACE_ADMIT_PREFIX and row[6] == 1:
+            used -= held.pop(int(row[1]))
+    content = _BankContent(req, cfg, dev, tdt, max_rows=512)
+    tok_bytes = L * kvh * D * 2 * (2 if tdt != torch.float32 else 4)
+
+    def replay():
+        plane = dp.DataPlane(nb, B, layers=L, num_heads=nh, kv_heads=kvh, head_dim=D, source=content,
+                             queries=content.queries, dtype=tdt, device=dev, swap_slots=peak)
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        n = plane.run(trace)
+        st = plane.status_word()  # synchronises
+        wall = time.perf_counter() - t0
+        assert st == 0, st
+        secs, attn_bytes = plane.attention_time()
+        return n, wall, secs, attn_bytes
+
+    replay()
+    runs = []
+    with ClockSampler(0) as clk:
+        for _ in range(args.sim_replays):
+            runs.append(replay())
+    n = runs[-1][0]
+    assert (n.steps, n.tokens_generated, n.swap_out_blocks, n.prefill_tokens) == \
+        (int(met[0]), int(met[1]), int(met[5]), int(met[9]))
+    wall = float(np.mean([r[1] for r in runs]))
+    attn_s = float(np.mean([r[2] for r in runs]))
+    attn_bytes = runs[-1][3]
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    peak_hbm = float(peaks.get("hbm_gbs", 6650.0))
+    achieved = attn_bytes / attn_s / 1e9
+    blk = B * tok_bytes
+    line = {"metric": "scheduler-driven decode replay throughput", "value": round(n.tokens_generated / wall, 1),
+            "unit": "tok/s", "n_gpus": 1, "steps": args.sim_replays, "warmup": 1,
+            "ms_per_step": round(1e3 * wall, 2), "higher_is_better": True, "op": "sim", "dtype": cfg["dtype"],
+            "data": "reference simulator decision stream; synthetic K/V rows",
+            "config": {"workload": f"{args.config}-shaped heads, {L} layers; {name}: {len(trace)} decisions, "
+                                   f"{n.steps} scheduler steps, {nb} blocks x {B} tokens",
+                       "step": "one replay of the whole decision stream (host decisions included)"},
+            "scheduler_steps_per_s": round(n.steps / wall, 1),
+            "attention": {"launches": n.attention_launches, "seconds": round(attn_s, 4),
+                          "algorithmic_bytes": attn_bytes, "share_of_wall": round(attn_s / wall, 3)},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_hbm, "unit": "GB/s",
+                         "frac": round(achieved / peak_hbm, 4), "traffic": None,
+                         "kernel": "paged_decode_streamk_kernel inside the replay (event time per batch)",
+                         "peak_source": "measured" if "hbm_gbs" in peaks else "fallback"},
+            "data_plane_bytes": {"prefill": n.prefill_tokens * tok_bytes, "appended": n.tokens_generated * tok_bytes,
+                                 "cow_copied": n.cow_copies * blk, "swap_out": n.swap_out_blocks * blk,
+                                 "swap_in": n.swap_in_blocks * blk},
+            "counters": n.as_dict(), "gpu_launches": n.attention_launches, "clocks": clk.summary()}
+    print(json.dumps(line))
+
+
 def run_block_mover(args, cfg):
     """Whole-block movers of the data plane, device timed: `migrate` copies blocks from a second GPU's pool into
     this GPU's pool (kvp_migrate_blocks, peer loads over NVLink; two pools on one GPU when only one is
@@ -539,8 +646,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--requests", type=int, default=0, help="profiling: requests per GPU (pool sized to need)")
     ap.add_argument("--layers", type=int, default=0, help="profiling: number of layers (pool sized to need)")
-    ap.add_argument("--op", default="decode", choices=["decode", "migrate", "cow", "swap"],
-                    help="decode step (default) or a whole-block mover measured alone")
+    ap.add_argument("--op", default="decode", choices=["decode", "migrate", "cow", "swap", "sim"],
+                    help="decode step (default), a whole-block mover measured alone, or the scheduler-driven "
+                         "data plane (sim)")
+    ap.add_argument("--sim-replays", type=int, default=2, help="sim: timed replays of the decision stream")
     args = ap.parse_args()
     assert args.warmup >= 3, "at least 3 warm-up steps"
     cfg = dict(CONFIGS[args.config])
@@ -583,6 +692,9 @@ def main():
 
     if args.op == "swap":
         run_swap(args, cfg)
+        return
+    if args.op == "sim":
+        run_sim(args, cfg)
         return
     if args.op != "decode":
         run_block_mover(args, cfg)

@@ -97,8 +97,10 @@ typedef struct kvp_attn_args {
 } kvp_attn_args;
 
 /* The caller guarantees the workspace's counter words are zero, so the call skips resetting them: true for
- * workspace memory that was zero-filled once and has since only been used by completed calls (each call
- * leaves the counters zero).  Without it every balanced-schedule call first clears them on the stream. */
+ * workspace memory that was zero-filled once and has since only been used by completed calls with the same
+ * num_heads, kv_heads, head_dim and kv_heads_per_cta (each call leaves the counters zero; they sit at the
+ * start of the workspace in a region whose size does not depend on num_seqs, so the batch size may change
+ * from call to call).  Without it every balanced-schedule call first clears them on the stream. */
 #define KVP_ATTN_WORKSPACE_CLEAN 1
 /* Early start (programmatic dependent launch; balanced schedule only): the kernel may begin while the previous
  * kernel on the stream is still running.  Its prologue (tile prefix sums, barrier setup) reads seq_lens --

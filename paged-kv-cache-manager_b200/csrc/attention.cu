@@ -276,10 +276,14 @@ int plan_attention(const kvp_attn_args& a, bool have_workspace, AttnPlan* out) {
         }
         pl.split_tiles = pl.max_tiles;
         pl.max_splits = 1;
+        // The merge counters come first, in a region sized for the most sequences a call may have, so their
+        // place does not depend on num_seqs: a workspace left clean by one call is clean for the next call of
+        // the same head shape whatever its batch size (the partials behind them need no initial value).
         const size_t rows = (static_cast<size_t>(pl.G) + a.num_seqs) * a.num_heads;
-        pl.ws_o_off = round_up(rows * sizeof(float2), 256);
-        pl.ws_cnt_off = pl.ws_o_off + round_up(rows * static_cast<size_t>(D) * sizeof(float), 256);
-        pl.ws_bytes = pl.ws_cnt_off + round_up(static_cast<size_t>(a.num_seqs) * pl.groups * 4, 256);
+        pl.ws_cnt_off = 0;
+        pl.ws_ml_off = round_up(static_cast<size_t>(kvpd::kMaxStreamSeqs) * pl.groups * 4, 256);
+        pl.ws_o_off = pl.ws_ml_off + round_up(rows * sizeof(float2), 256);
+        pl.ws_bytes = pl.ws_o_off + round_up(rows * static_cast<size_t>(D) * sizeof(float), 256);
         *out = pl;
         return KVP_OK;
     }
@@ -353,7 +357,7 @@ extern "C" KVP_API int kvp_paged_attention(const kvp_attn_args* a, void* stream)
     prm.out = a->out;
     if (pl.ws_bytes > 0) {
         char* ws = static_cast<char*>(a->workspace);
-        prm.ws_ml = reinterpret_cast<float2*>(ws);
+        prm.ws_ml = reinterpret_cast<float2*>(ws + pl.ws_ml_off);
         prm.ws_o = reinterpret_cast<float*>(ws + pl.ws_o_off);
         if (pl.streamk) {
             prm.counters = reinterpret_cast<int32_t*>(ws + pl.ws_cnt_off);

@@ -52,8 +52,9 @@ struct AttnPlan {
     uint32_t pre_off = 0;   // stream-K: offset of the prefix sums
     int seq_units = 0;      // stream-K: start-cost units charged ahead of each sequence's tiles
     size_t smem = 0, ws_bytes = 0;
+    size_t ws_ml_off = 0;   // byte offset of the partial (m, l) pairs in the workspace
     size_t ws_o_off = 0;    // byte offset of the partial outputs in the workspace
-    size_t ws_cnt_off = 0;  // stream-K: byte offset of the per-sequence segment counters in the workspace
+    size_t ws_cnt_off = 0;  // stream-K: byte offset of the per-sequence segment counters (a fixed-size region)
 };
 int plan_attention(const kvp_attn_args& a, bool have_workspace, AttnPlan* plan);
 

@@ -141,15 +141,17 @@ class DataPlane:
     """One shard: K/V pools [layers][num_blocks][block_size][kv_heads][head_dim] on `device`, a pinned host
     swap pool of `swap_slots` block slots (all layers, K and V), this package's KVManager, one stream.
 
-    `source(rid, positions) -> (k, v)` supplies the K/V rows of a request's token positions, [layers][n]
-    [kv_heads][head_dim] device tensors in the pool dtype (what a model's prefill / decode step would produce);
-    `queries(rids) -> q` the step's queries [layers][n][num_heads][head_dim].  `on_attention(rids, q, out,
-    tables, lens)` (optional) sees every attention batch after its launches."""
+    `source(rids, positions) -> (k, v)` supplies K/V rows -- row i is position positions[i] of request rids[i]
+    -- as [layers][n][kv_heads][head_dim] device tensors in the pool dtype (what a model's prefill / decode
+    step would produce); `queries(rids) -> q` the queries of an attention batch, [layers][n][num_heads]
+    [head_dim].  `on_attention(rids, q, out, tables, lens)` (optional) sees every attention batch after its
+    launches.  The host never waits for the device: metadata goes up through pinned staging copies, and
+    every launch, copy and allocation is ordered on the shard's stream."""
 
     def __init__(self, num_blocks: int, block_size: int, *, layers: int, num_heads: int, kv_heads: int,
                  head_dim: int, source: Callable, queries: Callable, dtype=None, device="cuda",
                  swap_slots: int = 0, fused_append: bool = True, on_attention: Optional[Callable] = None,
-                 out_dtype=None):
+                 out_dtype=None, early_start: bool = True):
         import torch
         kvb = _lib()
         self.kvb = kvb
@@ -169,19 +171,22 @@ class DataPlane:
         self.swapped = {}          # rid -> (host slots, tokens)
         self.status = torch.zeros(1, dtype=torch.int32, device=self.dev)
         self.stream = torch.cuda.Stream(self.dev)
+        self.workspace = torch.zeros(0, dtype=torch.uint8, device=self.dev)
         self.source, self.queries, self.on_attention = source, queries, on_attention
-        self.fused = fused_append
+        self.fused, self.early = fused_append, early_start
         self.out_dtype = out_dtype or torch.float32
         self.pending = {}          # rid -> position of the token it appended this step (attention not run yet)
         self.pending_cow = []      # (old, new) block pairs not yet copied
         self.pending_tokens = []   # (rid, slot, pos): non-fused token rows not yet scattered
-        self.live = set()          # requests holding blocks
+        self.tokens = {}           # rid -> tokens, for every request holding blocks
         self.n = DecisionCounters()
+        self.events = []           # (start, end, algorithmic bytes) of each attention batch
 
     # ------------------------------------------------------------------ device traffic
     def _to_dev(self, a):
+        """Host array -> device through a pinned staging copy, asynchronous on the current stream."""
         import torch
-        return torch.from_numpy(np.ascontiguousarray(a)).to(self.dev)
+        return torch.from_numpy(np.ascontiguousarray(a)).pin_memory().to(self.dev, non_blocking=True)
 
     def _write_rows(self, rid: int, positions: np.ndarray):
         """K/V rows of `positions` of rid into their slots through its table."""
@@ -189,7 +194,7 @@ class DataPlane:
             return
         tbl = np.asarray(self.mgr.block_table(rid), dtype=np.int64)
         slots = (tbl[positions // self.B] * self.B + positions % self.B).astype(np.int32)
-        k, v = self.source(rid, positions)
+        k, v = self.source(np.full(len(positions), rid, dtype=np.int64), positions)
         self.kvb.append_scatter(k, v, self.k, self.v, self._to_dev(slots), status=self.status,
                                 stream=self.stream)
 
@@ -199,11 +204,10 @@ class DataPlane:
                               status=self.status, stream=self.stream)
             self.pending_cow = []
         if self.pending_tokens:
-            import torch
-            ks, vs = zip(*(self.source(r, np.asarray([p], dtype=np.int64)) for r, _, p in self.pending_tokens))
-            slots = np.asarray([s for _, s, _ in self.pending_tokens], dtype=np.int32)
-            self.kvb.append_scatter(torch.cat(ks, dim=1), torch.cat(vs, dim=1), self.k, self.v,
-                                    self._to_dev(slots), status=self.status, stream=self.stream)
+            r, slots, pos = (np.asarray(x, dtype=np.int64) for x in zip(*self.pending_tokens))
+            k, v = self.source(r, pos)
+            self.kvb.append_scatter(k, v, self.k, self.v, self._to_dev(slots.astype(np.int32)),
+                                    status=self.status, stream=self.stream)
             self.pending_tokens = []
 
     def _flush_attention(self):
@@ -211,20 +215,48 @@ class DataPlane:
         if not self.pending:
             return
         import torch
+        kvb = self.kvb
         rids = list(self.pending)
-        mb = max(len(self.mgr.block_table(r)) for r in rids)
-        tables, lens = self.mgr.dense_tables(rids, mb)
+        tables, lens = self.mgr.dense_tables(rids, max(self.pending.values()) // self.B + 1)
         t, ln = self._to_dev(tables), self._to_dev(lens)
         q = self.queries(rids)
         out = torch.empty((self.L, len(rids), self.nh, self.D), dtype=self.out_dtype, device=self.dev)
         kn = vn = None
         if self.fused:
-            ks, vs = zip(*(self.source(r, np.asarray([self.pending[r]], dtype=np.int64)) for r in rids))
-            kn, vn = torch.cat(ks, dim=1), torch.cat(vs, dim=1)
+            r = np.asarray(rids, dtype=np.int64)
+            kn, vn = self.source(r, np.asarray([self.pending[x] for x in rids], dtype=np.int64))
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        a = kvb.attention_args(q[0], self.k[0], self.v[0], t, ln, out[0], self.nh, self.kvh, status=self.status,
+                               k_new=None if kn is None else kn[0], v_new=None if vn is None else vn[0])
+        need = kvb.workspace_bytes(a)  # the same for every layer of the batch
+        if need > self.workspace.numel():
+            self.workspace = torch.zeros(need + need // 4, dtype=torch.uint8, device=self.dev)
+        if need:
+            a.workspace, a.workspace_bytes = self.workspace.data_ptr(), self.workspace.numel()
+            a.flags |= kvb.KVP_ATTN_WORKSPACE_CLEAN  # counters return to zero after every launch
+        fn = kvb.lib().kvp_paged_attention
+        # per-layer byte strides (each layer's slice is contiguous, which attention_args checked for layer 0)
+        layer_k, layer_q, layer_o = (t.stride(0) * t.element_size() for t in (self.k, q, out))
+        layer_n = 0 if kn is None else kn.stride(0) * kn.element_size()
+        if kn is not None and vn.stride(0) != kn.stride(0):
+            raise ValueError("k_new and v_new rows must share a layout")
+        ev0.record(self.stream)
         for layer in range(self.L):
-            self.kvb.paged_attention(q[layer], self.k[layer], self.v[layer], t, ln, self.nh, self.kvh,
-                                     out=out[layer], status=self.status, stream=self.stream,
-                                     k_new=None if kn is None else kn[layer], v_new=None if vn is None else vn[layer])
+            if layer:  # the same arguments, moved to the next layer's buffers
+                a.q += layer_q
+                a.k_cache += layer_k
+                a.v_cache += layer_k
+                a.out += layer_o
+                if kn is not None:
+                    a.k_new += layer_n
+                    a.v_new += layer_n
+                if self.early:  # the previous kernel is layer-1's: it writes neither these pools nor the
+                    a.flags |= kvb.KVP_ATTN_EARLY_LOAD  # tables and lengths
+            kvb._launch(self.dev, fn, a, self.stream)
+        ev1.record(self.stream)
+        ctx_tokens = int(lens.sum())
+        self.events.append((ev0, ev1, ctx_tokens * self.L * self.kvh * self.D * 2 * self.k.element_size()))
         self.n.attention_launches += self.L
         self.n.attention_rows += len(rids)
         self.pending = {}
@@ -239,11 +271,38 @@ class DataPlane:
         with torch.cuda.stream(self.stream):
             self._apply(row)
 
+    def _appends(self, rows):
+        """A run of consecutive append decisions: one batched manager call (which stops at the first failure,
+        changing nothing for it, as the recorded run does)."""
+        rids = [int(x) for x in rows[:, 1]]
+        want = rows[:, 5]
+        fail = np.nonzero(want == 0)[0]
+        upto = int(fail[0]) + 1 if len(fail) else len(rids)
+        done, slots, pairs = self.mgr.append_batch(rids[:upto])
+        _expect(done, upto - (1 if len(fail) else 0), rows[min(done, len(rows) - 1)], "append_token run")
+        if upto < len(rids):
+            raise TraceMismatch("append decisions recorded after a failed append in the same run")
+        if not done:
+            return
+        if len(pairs):
+            self.pending_cow.extend(map(tuple, pairs.tolist()))
+            self.n.cow_copies += len(pairs)
+        for i in range(done):
+            r = rids[i]
+            pos = self.tokens[r]
+            self.tokens[r] = pos + 1
+            if not self.fused:
+                self.pending_tokens.append((r, int(slots[i]), pos))
+            self.pending[r] = pos
+        self.n.tokens_generated += done
+
     def _apply(self, row):
         op, res, flag = int(row[0]), int(row[5]), int(row[6])
         mgr = self.mgr
-        if op != TRACE_APPEND:
-            self._flush_copies()
+        if op == TRACE_APPEND:
+            self._appends(np.asarray(row).reshape(1, -1))
+            return
+        self._flush_copies()
         if op == TRACE_STEP:
             self._flush_attention()
             _check_step(mgr, row)
@@ -255,10 +314,10 @@ class DataPlane:
             _expect(int(fn(r, int(row[2]), int(row[3]), prompt)), res, row, "admission")
             if not res:
                 return
-            self.live.add(r)
+            self.tokens[r] = prompt
             if flag == 1:  # swap-in: fresh blocks, no sharing
                 slots, tokens = self.swapped.pop(r)
-                _expect(mgr.num_tokens(r), tokens, row, "swapped-in tokens")
+                _expect(prompt, tokens, row, "swapped-in tokens")
                 blocks = mgr.block_table(r)
                 self.kvb.swap_in(self.k, self.v, blocks, slots, self.pool, stream=self.stream)
                 self.free_slots.extend(reversed(slots))
@@ -276,24 +335,10 @@ class DataPlane:
                 self._flush_attention()
             _expect(int(mgr.fork(int(row[1]), int(row[2]))), res, row, "fork")
             if res:
-                self.live.add(int(row[1]))
-        elif op == TRACE_APPEND:
-            r = int(row[1])
-            pos = mgr.num_tokens(r)
-            done, slots, pairs = mgr.append_batch([r])
-            _expect(done, res, row, "append_token")
-            if not done:
-                return
-            self.n.tokens_generated += 1
-            if len(pairs):
-                self.pending_cow.extend(map(tuple, pairs.tolist()))
-                self.n.cow_copies += len(pairs)
-            if not self.fused:
-                self.pending_tokens.append((r, int(slots[0]), pos))
-            self.pending[r] = pos
+                self.tokens[int(row[1])] = self.tokens[int(row[2])]
         elif op == TRACE_FREE:
             r = int(row[1])
-            _expect(mgr.num_tokens(r), int(row[2]), row, "tokens at free")
+            _expect(self.tokens.get(r), int(row[2]), row, "tokens at free")
             if r in self.pending:  # it generated this step: attend before its blocks can be reused
                 self._flush_attention()
             if flag == FREE_SWAPPED:
@@ -305,22 +350,43 @@ class DataPlane:
                 self.swapped[r] = (slots, int(row[2]))
                 self.n.swap_out_blocks += len(blocks)
             mgr.free(r)
-            self.live.discard(r)
+            del self.tokens[r]
         elif op == TRACE_CLEAR_CACHE:
             mgr.clear_cache()
         else:
             raise ValueError(f"unknown trace op {op}")
 
     def run(self, trace, *, on_step: Optional[Callable] = None) -> DecisionCounters:
-        """Replays a decision stream; `on_step(step_index)` runs after each end-of-step marker."""
+        """Replays a decision stream; `on_step(step_index)` runs after each end-of-step marker.  Runs of
+        consecutive appends go to the manager as one batch."""
         import torch
+        t = np.asarray(trace)
+        op = t[:, 0]
+        # boundaries of runs of consecutive APPEND rows
+        is_app = op == TRACE_APPEND
         with torch.cuda.stream(self.stream):
-            for row in np.asarray(trace):
-                self._apply(row)
-                if on_step is not None and int(row[0]) == TRACE_STEP:
+            i, n = 0, len(t)
+            while i < n:
+                if is_app[i]:
+                    j = i
+                    while j < n and is_app[j] and (j == i or t[j - 1, 5] == 1):
+                        j += 1
+                    self._appends(t[i:j])
+                    i = j
+                    continue
+                self._apply(t[i])
+                if on_step is not None and op[i] == TRACE_STEP:
                     on_step(self.n.steps - 1)
+                i += 1
             self._flush_attention()
         return self.n
+
+    def attention_time(self):
+        """(seconds, algorithmic bytes) summed over the attention batches so far (synchronises)."""
+        import torch
+        torch.cuda.synchronize(self.dev)
+        secs = sum(a.elapsed_time(b) for a, b, _ in self.events) / 1e3
+        return secs, sum(x for _, _, x in self.events)
 
     def status_word(self) -> int:
         import torch
@@ -345,23 +411,26 @@ class SyntheticContent:
         self.dtype = dtype or torch.bfloat16
         self.dev = torch.device(device)
         req = np.asarray(requests, dtype=np.int64).reshape(-1, 8)
-        self.info = {int(r[0]): (int(r[2]), int(r[4]), int(r[5]), int(r[6])) for r in req}
+        self.index = {int(r[0]): i for i, r in enumerate(req)}
+        self.prompt, self.group, self.plen = req[:, 2], req[:, 4], req[:, 5]
+        self.leader = np.asarray([self.index.get(int(f), -1) if f != NO_REQUEST else -1 for f in req[:, 6]])
+        self.ids = req[:, 0]
         self.seed = seed
         self.gen = torch.Generator(device=self.dev).manual_seed(seed)
         e = layers * kv_heads * head_dim
         self.elem = torch.arange(2 * e, dtype=torch.int64, device=self.dev)
 
-    def origins(self, rid: int, positions: np.ndarray) -> np.ndarray:
-        """Origin key of each position (a request id, or 2^40 + group for prefix-group positions)."""
-        prompt, group, plen, leader = self.info[rid]
-        out = np.full(len(positions), rid, dtype=np.int64)
-        if group >= 0:
-            out[positions < plen] = (1 << 40) + group
-        if leader != NO_REQUEST:
-            lp = self.info[leader][0]
-            below = positions < lp
-            if below.any():
-                out[below] = self.origins(leader, positions[below])
+    def origins(self, rids, positions) -> np.ndarray:
+        """Origin key of each row (a request id, or 2^40 + group for prefix-group positions)."""
+        rids = np.asarray(rids, dtype=np.int64)
+        positions = np.asarray(positions, dtype=np.int64)
+        ix = np.fromiter((self.index[int(r)] for r in rids), dtype=np.int64, count=len(rids))
+        lead = self.leader[ix]
+        forked = (lead >= 0) & (positions < self.prompt[np.maximum(lead, 0)])
+        ix = np.where(forked, lead, ix)  # below the fork point a sample is its leader
+        out = self.ids[ix].copy()
+        grp = (self.group[ix] >= 0) & (positions < self.plen[ix])
+        out[grp] = (1 << 40) + self.group[ix][grp]
         return out
 
     def _hash(self, x):
@@ -369,14 +438,14 @@ class SyntheticContent:
             x = (x * 48271) % self.P
         return x
 
-    def __call__(self, rid: int, positions: np.ndarray):
+    def __call__(self, rids, positions):
         import torch
         positions = np.asarray(positions, dtype=np.int64)
-        keys = (self.origins(rid, positions) % self.P) * 1000003 + positions + self.seed * 7919
-        row = self._hash(torch.from_numpy(keys % self.P).to(self.dev))
+        keys = (self.origins(rids, positions) % self.P) * 1000003 + positions + self.seed * 7919
+        row = self._hash(torch.from_numpy(keys % self.P).pin_memory().to(self.dev, non_blocking=True))
         x = self._hash((row[:, None] * 65599 + self.elem[None, :] + 1) % self.P)
         vals = ((x >> 7) % 2048).to(torch.float32) / 1024.0 - 1.0
-        n, e = len(positions), self.L * self.kvh * self.D
+        n = len(positions)
         kv = vals.view(n, 2, self.L, self.kvh, self.D).permute(1, 2, 0, 3, 4).to(self.dtype).contiguous()
         return kv[0], kv[1]
 

@@ -87,6 +87,26 @@ std::vector<Scenario> scenarios() {
         s.c.prefix_cache = true;
         out.push_back(s);
     }
+    {  // serving scale (the data-plane benchmark's stream): long-tail prompts, shared prefixes, FCFS, swap
+        Scenario s{"serving_fcfs_swap", {}, {}};
+        s.w.seed = 21;
+        s.w.num_requests = 256;
+        s.w.mean_interarrival = 0.25;
+        s.w.prompt_dist = Dist::LongTail;
+        s.w.prompt_min = 256;
+        s.w.prompt_max = 3072;
+        s.w.output_min = 32;
+        s.w.output_max = 160;
+        s.w.shared_prefix_fraction = 0.3;
+        s.w.prefix_len = 512;
+        s.w.num_prefix_groups = 4;
+        s.w.max_seq_len = 3300;
+        s.c.num_blocks = 3072;
+        s.c.block_size = 16;
+        s.c.preempt_mode = PreemptMode::Swap;
+        s.c.prefix_cache = true;
+        out.push_back(s);
+    }
     return out;
 }
 

@@ -325,8 +325,48 @@ def test_balanced_schedule_leaves_workspace_clean(kvb, ora, cuda):
         assert kvb.lib().kvp_paged_attention(C.byref(a), C.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0
         torch.cuda.synchronize()
         check_close(out.cpu().numpy(), ref, what="clean workspace reuse")
-        cnt = ws[-256 * ((5 * 4 + 255) // 256):].view(torch.int32)
+        cnt = ws[:8192 * 4].view(torch.int32)  # the counter region: 8192 sequences x 1 kv-head group
         assert int(cnt.abs().sum().item()) == 0
+
+
+def test_clean_workspace_reuse_across_batch_sizes(kvb, ora, cuda):
+    """One workspace, zero-filled once and passed with KVP_ATTN_WORKSPACE_CLEAN, serves calls whose batch size
+    changes from call to call (the merge counters sit in a region whose place does not depend on num_seqs):
+    long contexts split every sequence across CTAs, so the partials of one call cover the places a
+    num_seqs-dependent layout would give the next call's counters.  Each call equals, bit for bit, the same
+    call on a fresh workspace, and matches the oracle."""
+    import torch
+    rng = np.random.default_rng(17)
+    nh, kvh, D, B = 8, 2, 64, 16
+    sizes = [12, 3, 20, 7, 1, 16, 5]
+    nmax = max(sizes)
+    lens_all = rng.integers(800, 4000, size=nmax)
+    nb = int(sum((n + 15) // 16 for n in lens_all)) + 4
+    Q, K, V, T, L = _normal_case(23, nmax, nh, kvh, D, B, [int(x) for x in lens_all], nb)
+    kt, kf = _round(K, "bf16")
+    vt, vf = _round(V, "bf16")
+    k, v = kt.cuda(), vt.cuda()
+    q_all, t_all, l_all = torch.from_numpy(Q).cuda(), torch.from_numpy(T).cuda(), torch.from_numpy(L).cuda()
+    out = torch.empty((nmax, nh, D), dtype=torch.float32, device="cuda")
+    a = kvb.attention_args(q_all, k, v, t_all, l_all, out, nh, kvh, num_blocks=nb)
+    ws = torch.zeros(kvb.workspace_bytes(a), dtype=torch.uint8, device="cuda")
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for i, n in enumerate(sizes):
+        sel = rng.permutation(nmax)[:n]
+        q, t, l = q_all[sel].contiguous(), t_all[sel].contiguous(), l_all[sel].contiguous()
+        o1 = torch.full((n, nh, D), float("nan"), dtype=torch.float32, device="cuda")
+        o2 = torch.full_like(o1, float("nan"))
+        a = kvb.attention_args(q, k, v, t, l, o1, nh, kvh, num_blocks=nb)
+        assert kvb.workspace_bytes(a) <= ws.numel()
+        a.workspace, a.workspace_bytes, a.flags = ws.data_ptr(), ws.numel(), kvb.KVP_ATTN_WORKSPACE_CLEAN
+        assert kvb.lib().kvp_paged_attention(C.byref(a), stream) == 0
+        kvb.paged_attention(q, k, v, t, l, nh, kvh, out=o2, num_blocks=nb)  # fresh zeroed workspace
+        torch.cuda.synchronize()
+        assert torch.equal(o1, o2), (i, n)
+        if i % 3 == 0:
+            ref = ora.reference_attention(nh, kvh, D, B, Q[sel], kf, vf, T[sel], L[sel])
+            check_close(o1.cpu().numpy(), ref, what=f"batch of {n}")
+    assert int(ws[:8192 * 4].view(torch.int32).abs().sum().item()) == 0
 
 
 @pytest.mark.parametrize("shape", [(14, 2, 64), (32, 8, 128)], ids=["qwen", "llama"])
