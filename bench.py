@@ -20,6 +20,9 @@ Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|referenc
        python bench.py --op migrate|cow|swap   (block movers: one process; migrate reads GPU 1's pool into
                                                 GPU 0's over NVLink when two GPUs are visible; swap moves blocks
                                                 to a pinned host pool and back)
+       python bench.py --op sim                (the reference scheduler's recorded serving stream replayed by
+                                                the data plane: prefill, append, copy-on-write, swap, attention)
+       python bench.py --op latency            (config 1's per-call latency, the drop-in entry point included)
 Multi-GPU: launched under torch.distributed.run, one process per GPU, requests sharded with no collective
 on the data path (weak scaling); timings are the max over ranks.
 """
@@ -160,6 +163,67 @@ def cpu_baseline(cfg, lens, target_s=12.0, kind_pref="reference"):
             "gb_s": round(gbs, 3),
             "sample": f"{ns} sequences x 1 layer ({int(sl.sum())} tokens, lengths drawn from the workload), "
                       f"{reps} timed calls over {el:.1f}s, scaled to {len(lens)} requests x {cfg['L']} layers"}
+
+
+def reference_gpu_kernel(cfg, lens, nseq=32):
+    """The reference's own GPU kernel (cuda/paged_attention.cu, built from its source into oracle/_ref; fp16
+    only) timed on one layer of a bounded sample of this workload -- `nseq` requests drawn from the same
+    lengths, random block tables over a pool of exactly their blocks -- with CUDA events, at 4 and 8 warps
+    (the better is reported).  Reported beside the CPU baseline as extra context; None without a GPU or the
+    built kernel."""
+    try:
+        import torch
+        import oracle
+    except Exception:
+        return None
+    if not torch.cuda.is_available() or not oracle.have_ref_gpu():
+        return None
+    nh, kvh, D, B = cfg["nh"], cfg["kvh"], cfg["D"], cfg["B"]
+    rng = np.random.default_rng(78)
+    sl = rng.choice(lens, size=nseq, replace=True).astype(np.int32)
+    nblk = (sl + B - 1) // B
+    pool = int(nblk.sum())
+    perm = rng.permutation(pool).astype(np.int32)
+    T = np.zeros((nseq, int(nblk.max())), np.int32)
+    o = 0
+    for i in range(nseq):
+        T[i, :nblk[i]] = perm[o:o + nblk[i]]
+        o += int(nblk[i])
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(5)
+    k = torch.randn((pool, B, kvh, D), generator=g, device=dev).half()
+    v = torch.randn((pool, B, kvh, D), generator=g, device=dev).half()
+    q = torch.randn((nseq, nh, D), generator=g, device=dev).half()
+    out = torch.empty_like(q)
+    t, ln = torch.from_numpy(T).to(dev), torch.from_numpy(sl).to(dev)
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    best = None
+    for warps in (4, 8):
+        def call():
+            rc = oracle.ref_gpu_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), t.data_ptr(), ln.data_ptr(),
+                                          out.data_ptr(), nseq, nh, kvh, D, B, T.shape[1], warps, stream.cuda_stream)
+            assert rc == 0, rc
+        call()
+        torch.cuda.synchronize(dev)
+        reps = 5
+        e0.record(stream)
+        for _ in range(reps):
+            call()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / reps
+        if best is None or ms < best[0]:
+            best = (ms, warps)
+    ms, warps = best
+    sample_bytes = float(sl.sum()) * kvh * D * 2 * 2
+    gbs = sample_bytes / (ms / 1e3) / 1e9
+    step_bytes = float(lens.sum()) * kvh * D * 2 * 2 * cfg["L"]
+    return {"value": round(len(lens) / (step_bytes / (gbs * 1e9)), 2), "unit": "tok/s", "gb_s": round(gbs, 1),
+            "ms_per_layer_sample": round(ms, 3), "warps": warps, "dtype": "f16",
+            "sample": f"{nseq} requests x 1 layer ({int(sl.sum())} tokens, lengths drawn from the workload), fp16 "
+                      f"(the kernel's only type; same bytes as bf16), scaled to {len(lens)} requests x {cfg['L']} "
+                      f"layers by its GB/s"}
 
 
 # ----------------------------------------------------------------------------- GPU workload
@@ -552,6 +616,139 @@ def run_sim(args, cfg):
     print(json.dumps(line))
 
 
+def _drop_in_fn(kvb):
+    """The drop-in launch_paged_attention (C++ symbol) from the library, bound with ctypes."""
+    import ctypes as C
+    import subprocess
+    out = subprocess.run(["nm", "-D", "--defined-only", kvb.LIB_PATH], capture_output=True, text=True).stdout
+    name = [ln.split()[-1] for ln in out.splitlines() if "launch_paged_attention" in ln][0]
+    f = getattr(kvb.lib(), name)
+    f.restype = C.c_int
+    f.argtypes = [C.c_void_p] * 6 + [C.c_int] * 7 + [C.c_void_p]
+    return f
+
+
+def run_latency(args):
+    """Config 1, the reference's correctness case, timed for latency: 8 sequences, 8/8 heads, head_dim 64, block
+    16, lengths U{1..512} (seeded), fp32 queries, fp16 K/V in a 1024-block pool (each request's blocks a random
+    permutation of pool ids), fp32 output, one layer -- about 4 MB per call, L2-resident and launch-bound.
+    Times kvp_paged_attention (per call back to back on a stream, replayed from a CUDA graph, and one call
+    alone between events) and the drop-in launch_paged_attention (fp16 in and out, the reference's signature),
+    with the reference's paged_attention_cpu on the same input beside it."""
+    import ctypes as C
+    import time
+    import torch
+    import oracle
+    kvb = importlib.import_module("paged-kv-cache-manager_b200")
+    nh, kvh, D, B, ns, nb = 8, 8, 64, 16, 8, 1024
+    rng = np.random.default_rng(1)
+    lens = rng.integers(1, 513, size=ns).astype(np.int32)
+    nblk = (lens + B - 1) // B
+    mb = int(nblk.max())
+    perm = rng.permutation(nb).astype(np.int32)
+    T = np.zeros((ns, mb), np.int32)
+    o = 0
+    for i in range(ns):
+        T[i, :nblk[i]] = perm[o:o + nblk[i]]
+        o += int(nblk[i])
+    Q = rng.standard_normal((ns, nh, D), dtype=np.float32)
+    K = rng.standard_normal((nb, B, kvh, D), dtype=np.float32).astype(np.float16)
+    V = rng.standard_normal((nb, B, kvh, D), dtype=np.float32).astype(np.float16)
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    q, k, v = torch.from_numpy(Q).to(dev), torch.from_numpy(K).to(dev), torch.from_numpy(V).to(dev)
+    t, ln = torch.from_numpy(T).to(dev), torch.from_numpy(lens).to(dev)
+    out = torch.empty((ns, nh, D), dtype=torch.float32, device=dev)
+    a = kvb.attention_args(q, k, v, t, ln, out, nh, kvh, num_blocks=nb)
+    ws = torch.zeros(max(kvb.workspace_bytes(a), 256), dtype=torch.uint8, device=dev)
+    a.workspace, a.workspace_bytes, a.flags = ws.data_ptr(), ws.numel(), kvb.KVP_ATTN_WORKSPACE_CLEAN
+    fn = kvb.lib().kvp_paged_attention
+    stream = torch.cuda.Stream(dev)
+    sp = C.c_void_p(stream.cuda_stream)
+
+    def launch():
+        rc = fn(C.byref(a), sp)
+        assert rc == 0, kvb.last_error()
+
+    n_b2b = 200
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+
+    def back_to_back(body):
+        vals = []
+        for _ in range(args.steps):
+            ev[0].record(stream)
+            body()
+            ev[1].record(stream)
+            stream.synchronize()
+            vals.append(ev[0].elapsed_time(ev[1]) * 1e3 / n_b2b)
+        return float(np.median(vals))
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup * 20):
+            launch()
+        stream.synchronize()
+        with ClockSampler(0) as clk:
+            us_stream = back_to_back(lambda: [launch() for _ in range(n_b2b)])
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for _ in range(n_b2b):
+                    launch()
+            g.replay()
+            stream.synchronize()
+            us_graph = back_to_back(g.replay)
+            single = []
+            for _ in range(max(args.steps, 20)):
+                stream.synchronize()
+                ev[0].record(stream)
+                launch()
+                ev[1].record(stream)
+                stream.synchronize()
+                single.append(ev[0].elapsed_time(ev[1]) * 1e3)
+            us_single = float(np.median(single))
+            # the drop-in entry point: fp16 queries and output, the reference's signature
+            f = _drop_in_fn(kvb)
+            qh = q.half()
+            oh = torch.empty((ns, nh, D), dtype=torch.float16, device=dev)
+
+            def drop_in():
+                rc = f(qh.data_ptr(), k.data_ptr(), v.data_ptr(), t.data_ptr(), ln.data_ptr(), oh.data_ptr(), ns, nh,
+                       kvh, D, B, mb, 4, stream.cuda_stream)
+                assert rc == 0
+            for _ in range(20):
+                drop_in()
+            us_drop_in = back_to_back(lambda: [drop_in() for _ in range(n_b2b)])
+        del g
+    # the reference's CPU function on the same input (fp32 copies of the fp16 K/V), 1 thread and all cores
+    impl = "ref" if oracle.have_ref() else "c"
+    cores = os.cpu_count() or 1
+    Kf, Vf = K.astype(np.float32), V.astype(np.float32)
+    cpu = {}
+    for nthreads in (1, cores):
+        oracle.paged_attention_cpu(nh, kvh, D, B, Q, Kf, Vf, T, lens, partitions=1, nthreads=nthreads, impl=impl)
+        reps, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 2.0:
+            oracle.paged_attention_cpu(nh, kvh, D, B, Q, Kf, Vf, T, lens, partitions=1, nthreads=nthreads, impl=impl)
+            reps += 1
+        cpu[nthreads] = (time.perf_counter() - t0) / reps * 1e6
+    algo = float(lens.sum()) * kvh * D * 2 * 2
+    line = {"metric": "paged decode-attn latency (config 1)", "value": round(us_stream, 2), "unit": "us",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(us_stream / 1e3, 5),
+            "higher_is_better": False, "op": "latency", "dtype": "f16", "data": "synthetic N(0,1), seeded",
+            "config": {"workload": "config 1: 8 sequences, 8/8 heads, head_dim 64, block 16, lengths U{1..512}, "
+                                   "fp32 q / fp16 K,V / fp32 out, 1024-block pool, one layer",
+                       "context_tokens": int(lens.sum()), "kv_bytes": int(algo),
+                       "l2": "L2-resident (about 4 MB per call): a latency, not a bandwidth, figure"},
+            "us_per_call": {"stream_back_to_back": round(us_stream, 2), "cuda_graph": round(us_graph, 2),
+                            "single_call_between_events": round(us_single, 2),
+                            "drop_in_launch_paged_attention_back_to_back": round(us_drop_in, 2)},
+            "cpu_baseline": {"value": round(cpu[cores], 1), "unit": "us", "cores": cores,
+                             "one_thread_us": round(cpu[1], 1),
+                             "kind": "reference" if impl == "ref" else "port",
+                             "sample": "the same 8 sequences, paged_attention_cpu (partitions 1), timed over 2 s"},
+            "gpu_launches": n_b2b * args.steps, "clocks": clk.summary()}
+    print(json.dumps(line))
+
+
 def run_block_mover(args, cfg):
     """Whole-block movers of the data plane, device timed: `migrate` copies blocks from a second GPU's pool into
     this GPU's pool (kvp_migrate_blocks, peer loads over NVLink; two pools on one GPU when only one is
@@ -646,9 +843,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--requests", type=int, default=0, help="profiling: requests per GPU (pool sized to need)")
     ap.add_argument("--layers", type=int, default=0, help="profiling: number of layers (pool sized to need)")
-    ap.add_argument("--op", default="decode", choices=["decode", "migrate", "cow", "swap", "sim"],
-                    help="decode step (default), a whole-block mover measured alone, or the scheduler-driven "
-                         "data plane (sim)")
+    ap.add_argument("--op", default="decode", choices=["decode", "migrate", "cow", "swap", "sim", "latency"],
+                    help="decode step (default), a whole-block mover measured alone, the scheduler-driven "
+                         "data plane (sim), or config 1's per-call latency (latency)")
     ap.add_argument("--sim-replays", type=int, default=2, help="sim: timed replays of the decision stream")
     args = ap.parse_args()
     assert args.warmup >= 3, "at least 3 warm-up steps"
@@ -682,11 +879,14 @@ def main():
         v = float(np.mean([x["value"] for x in vals]))
         cb = dict(vals[-1])
         cb["value"] = v
+        ref_gpu = reference_gpu_kernel(cfg, lens)
         line = {"metric": metric, "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": 1000.0 * cfg["ns"] / v, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1)",
                 "config": config, "impl": "reference", "cpu_baseline": cb,
                 "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        if ref_gpu is not None:
+            line["reference_gpu_kernel"] = ref_gpu
         print(json.dumps(line))
         return
 
@@ -695,6 +895,9 @@ def main():
         return
     if args.op == "sim":
         run_sim(args, cfg)
+        return
+    if args.op == "latency":
+        run_latency(args)
         return
     if args.op != "decode":
         run_block_mover(args, cfg)

@@ -7,6 +7,8 @@ CPU-baseline leg (and its reference arm) load this package; the product never do
     (src/paged_attention.cpp:25-114 of prathameshpranjale/paged-kv-cache-manager).
   * ref(): oracle/_ref/libkvpage_ref.so, the reference's own C++ sources compiled here (oracle/Makefile)
     with a C shim (ref_shim.cpp): the real KVManager and the real attention functions.
+  * ref_gpu_attention(): oracle/_ref/libref_gpu_attention.so, the reference's own GPU kernel
+    (cuda/paged_attention.cu) compiled here for sm_100a -- the implementation the drop-in replaces.
   * RefKVManager: the reference KVManager with the same Python interface as the product's KVManager.
   * DataPlane: a numpy model of the bytes the reference's Python harness moves
     (python/paged_model.py:54-55 scatter, :92-95 / :113-117 copy-on-write) plus swap as a host copy.
@@ -22,6 +24,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 C_LIB = os.path.join(HERE, "_build", "libkvp_oracle.so")
 REF_LIB = os.path.join(HERE, "_ref", "libkvpage_ref.so")
+REF_GPU_LIB = os.path.join(HERE, "_ref", "libref_gpu_attention.so")
 
 _pf, _pi32 = C.POINTER(C.c_float), C.POINTER(C.c_int32)
 _ATTN = [C.c_int] * 6 + [_pf, _pf, _pf, _pi32, _pi32, _pf]
@@ -99,6 +102,29 @@ def ref() -> C.CDLL:
             f.restype, f.argtypes = res, args
         _r = L
     return _r
+
+
+_g = None
+
+
+def have_ref_gpu() -> bool:
+    return os.path.exists(REF_GPU_LIB)
+
+
+def ref_gpu_attention(q, k_cache, v_cache, block_tables, seq_lens, out, num_seqs, num_heads, kv_heads, head_dim,
+                      block_size, max_blocks, warps, stream=None) -> int:
+    """The reference's launch_paged_attention (cuda/paged_attention.cuh:16-19) on device pointers (fp16 q, K/V
+    and out; int32 tables and lengths); returns its cudaError_t."""
+    global _g
+    if _g is None:
+        if not have_ref_gpu():
+            raise RuntimeError(f"{REF_GPU_LIB} missing: run `make -C oracle ref` where the reference sources exist")
+        L = C.CDLL(REF_GPU_LIB)
+        L.ref_gpu_launch_paged_attention.restype = C.c_int
+        L.ref_gpu_launch_paged_attention.argtypes = [C.c_void_p] * 6 + [C.c_int] * 7 + [C.c_void_p]
+        _g = L
+    return _g.ref_gpu_launch_paged_attention(q, k_cache, v_cache, block_tables, seq_lens, out, num_seqs, num_heads,
+                                             kv_heads, head_dim, block_size, max_blocks, warps, stream)
 
 
 # ----------------------------------------------------------------------------- attention

@@ -120,6 +120,38 @@ def test_drop_in_launch_paged_attention(kvb, ora, cuda):
                  len(lens), nh, kvh, 48, B, T.shape[1], 4, None) == 1
 
 
+def test_matches_the_reference_gpu_kernel(kvb, ora, cuda):
+    """The reference's own GPU kernel (cuda/paged_attention.cu, compiled here from its source into oracle/_ref)
+    and this library's drop-in, on the same fp16 inputs: the reference's GPU case list plus long contexts at
+    the Qwen2.5-0.5B and Llama-3-8B head shapes.  Both are within the fp16 bar of the fp64 reference, hence
+    within twice that bar of each other."""
+    import torch
+    if not ora.have_ref_gpu():
+        pytest.skip("the reference's GPU kernel was not built (needs the reference sources)")
+    f = _legacy_fn(kvb)
+    cases = cuda_test_cases() + [(14, 2, 64, 16, [512, 1999, 4096, 3000], False),
+                                 (32, 8, 128, 16, [4096, 777, 8192], False)]
+    for i, (nh, kvh, hd, B, lens, share) in enumerate(cases):
+        Q, K, V, T, L = attention_inputs(300 + i, nh, kvh, hd, B, lens, share, kvb.KVManager)
+        kt, kf = _round(K, "f16")
+        vt, vf = _round(V, "f16")
+        qt, qf = _round(Q, "f16")
+        ref = ora.reference_attention(nh, kvh, hd, B, qf, kf, vf, T, L)
+        q, k, v = qt.cuda(), kt.cuda(), vt.cuda()
+        t, ln = torch.from_numpy(T).cuda(), torch.from_numpy(L).cuda()
+        theirs = torch.full(Q.shape, float("nan"), dtype=torch.float16, device="cuda")
+        ours = torch.full_like(theirs, float("nan"))
+        args = (q.data_ptr(), k.data_ptr(), v.data_ptr(), t.data_ptr(), ln.data_ptr())
+        shape = (len(lens), nh, kvh, hd, B, T.shape[1], 4)
+        assert ora.ref_gpu_attention(*args, theirs.data_ptr(), *shape, None) == 0
+        assert f(*args, ours.data_ptr(), *shape, None) == 0
+        torch.cuda.synchronize()
+        a, b = theirs.float().cpu().numpy(), ours.float().cpu().numpy()
+        check_close(a, ref, out_dtype="f16", what=f"reference kernel, case {i}")
+        check_close(b, ref, out_dtype="f16", what=f"drop-in, case {i}")
+        assert (np.abs(a - b) <= 2 * (ATOL + (RTOL + 2.0 ** -11) * np.abs(ref))).all(), i
+
+
 def _normal_case(seed, ns, nh, kvh, hd, B, lens, pool_blocks):
     """Workload-style inputs: N(0,1) K/V/Q, each request's blocks a random permutation of pool ids."""
     rng = np.random.default_rng(seed)
