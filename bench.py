@@ -15,6 +15,8 @@ Inputs are synthetic, seeded N(0,1).
           average duration (CUDA events around each launch with --eager; otherwise the replayed steps' CUDA-event
           time over their launches, gaps between launches included), against the measured HBM copy peak
   cpu_baseline : the reference's own CPU paged_attention_cpu (oracle/_ref) on a bounded sample, all host cores
+  --impl reference : that CPU baseline as its own line, plus (reference_gpu_kernel) the reference's own GPU
+          kernel built from its source, timed on one layer of a 32-request sample of the same workload
 
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config llama3-8b|...]
        python bench.py --op migrate|cow|swap   (block movers: one process; migrate reads GPU 1's pool into
