@@ -698,7 +698,6 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
             produce_range(first, sg.tile1);
             ++j;
         }
-        griddep_launch_dependents();
         return;
     }
     if (warp > NC) return;
@@ -783,7 +782,6 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
         }
         ++j;
     }
-    griddep_launch_dependents();  // the next kernel may start its prologue during the merges
     // The writer warp whose add completed a sequence's count resets the counter and flags the merge; the CTA
     // then merges (that acquiring add made the other parts' rows visible; the barrier extends it to every
     // merging thread).
@@ -926,6 +924,10 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
     __shared__ int32_t warp_tot[32];
     extern __shared__ uint8_t dyn_smem[];
 
+    // Let the next kernel on the stream (a programmatic dependent launch) be scheduled now: its CTAs then take
+    // each SM slot this grid frees, and run their prologue and early loads during this grid's tail.  Its
+    // griddepcontrol.wait still waits for this whole grid to complete; the trigger only moves its scheduling.
+    griddep_launch_dependents();
     const int c = blockIdx.x, grp = blockIdx.y;
     const uint32_t base_off = ((smem_u32(dyn_smem) + 1023u) & ~1023u) - smem_u32(dyn_smem);
     int32_t* P = reinterpret_cast<int32_t*>(dyn_smem + base_off + p.pre_off);
