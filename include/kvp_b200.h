@@ -126,8 +126,9 @@ KVP_API int kvp_paged_attention(const kvp_attn_args* a, void* stream);
  * library (held by every GPU that loads it, until exit); it calls no allocator.  The array's device address
  * is looked up on the first call made on each device, so make that first call before any stream capture.
  * With split_tiles == 0 the splits are coarsened until the partials fit; an explicit split_tiles whose
- * partials exceed the array returns KVP_ENOSPACE.  All calls share the array: calls that overlap on the GPU
- * race and must be serialised by the caller. */
+ * partials exceed the array returns KVP_ENOSPACE.  KVP_ATTN_WORKSPACE_CLEAN is ignored: every call clears the
+ * merge counters it uses.  All calls share the array: calls that overlap on the GPU race and must be
+ * serialised by the caller. */
 #define KVP_NOALLOC_SCRATCH_BYTES (32u << 20)
 KVP_API int kvp_paged_attention_noalloc(const kvp_attn_args* a, void* stream);
 

@@ -11,9 +11,10 @@
 // The array is KVP_NOALLOC_SCRATCH_BYTES (32 MiB) of device memory that every GPU which loads the library
 // holds until the process exits.  Its device address is looked up once per device, on the first call made
 // with that device current, so that first call should come before any stream capture.  All calls share the
-// array and it keeps whatever the last call left there: nothing in it needs to start at zero (every split
-// writes its partials before the merge reads them), but two calls that overlap on the GPU -- on different
-// streams, or from different threads -- race on it and must be serialised by the caller.
+// array and it keeps whatever the last call left there: the only words that must start at zero, the merge
+// counters of the balanced schedule, are cleared on the stream by every call (every split writes its partials
+// before the merge reads them), and two calls that overlap on the GPU -- on different streams, or from
+// different threads -- race on it and must be serialised by the caller.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -63,6 +64,9 @@ extern "C" KVP_API int kvp_paged_attention_noalloc(const kvp_attn_args* a, void*
     kvp_attn_args b = *a;
     b.workspace = scratch;
     b.workspace_bytes = kScratchBytes;
+    // The shared array may hold another call's partials where this call keeps its merge counters (a call with
+    // fixed splits puts partials there), so the counters are always cleared on the stream, never assumed clean.
+    b.flags &= ~KVP_ATTN_WORKSPACE_CLEAN;
     size_t need = kvp_attention_workspace_size(&b);
     if (need > kScratchBytes) {
         if (a->split_tiles != 0)

@@ -85,3 +85,21 @@ def test_no_alloc_automatic_split_fits_and_oversize_is_rejected(kvb, cuda):
     rc = kvb.lib().kvp_paged_attention_noalloc(C.byref(a), C.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert rc == kvb.KVP_ENOSPACE
     assert "no-allocation scratch" in kvb.last_error()
+
+
+def test_no_alloc_balanced_call_after_fixed_splits(kvb, cuda):
+    # A call with fixed splits leaves partials where the next balanced call keeps its merge counters; the
+    # balanced call must still merge correctly, even when its caller claims a clean workspace (the flag is
+    # ignored here: every call clears its counters).
+    import torch
+    args = _inputs(4, [3000, 1200, 4096, 77, 2500])
+    want = _with_workspace(kvb, *args, 0)
+    _no_alloc(kvb, *args, 2)  # fills the start of the shared array with partials
+    q, k, v, t, l, nh, kvh = args
+    out = torch.full(q.shape, float("nan"), dtype=torch.float32, device=q.device)
+    a = kvb.attention_args(q, k, v, t, l, out, nh, kvh)
+    a.flags = kvb.KVP_ATTN_WORKSPACE_CLEAN
+    rc = kvb.lib().kvp_paged_attention_noalloc(C.byref(a), C.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0, kvb.last_error()
+    torch.cuda.synchronize()
+    _close(out, want)
