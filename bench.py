@@ -24,7 +24,8 @@ Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|referenc
                                                 to a pinned host pool and back)
        python bench.py --op sim                (the reference scheduler's recorded serving stream replayed by
                                                 the data plane: prefill, append, copy-on-write, swap, attention)
-       python bench.py --op latency            (config 1's per-call latency, the drop-in entry point included)
+       python bench.py --op latency            (per-call latency of the small 8-sequence case, the drop-in
+                                                entry point included)
 Multi-GPU: launched under torch.distributed.run, one process per GPU, requests sharded with no collective
 on the data path (weak scaling); timings are the max over ranks.
 """
@@ -631,7 +632,7 @@ def _drop_in_fn(kvb):
 
 
 def run_latency(args):
-    """Config 1, the reference's correctness case, timed for latency: 8 sequences, 8/8 heads, head_dim 64, block
+    """The small 8-sequence correctness case, timed for latency: 8 sequences, 8/8 heads, head_dim 64, block
     16, lengths U{1..512} (seeded), fp32 queries, fp16 K/V in a 1024-block pool (each request's blocks a random
     permutation of pool ids), fp32 output, one layer -- about 4 MB per call, L2-resident and launch-bound.
     Times kvp_paged_attention (per call back to back on a stream, replayed from a CUDA graph, and one call
@@ -733,10 +734,10 @@ def run_latency(args):
             reps += 1
         cpu[nthreads] = (time.perf_counter() - t0) / reps * 1e6
     algo = float(lens.sum()) * kvh * D * 2 * 2
-    line = {"metric": "paged decode-attn latency (config 1)", "value": round(us_stream, 2), "unit": "us",
+    line = {"metric": "paged decode-attn latency (8 sequences, 8/8 heads, D 64)", "value": round(us_stream, 2), "unit": "us",
             "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(us_stream / 1e3, 5),
             "higher_is_better": False, "op": "latency", "dtype": "f16", "data": "synthetic N(0,1), seeded",
-            "config": {"workload": "config 1: 8 sequences, 8/8 heads, head_dim 64, block 16, lengths U{1..512}, "
+            "config": {"workload": "small correctness case: 8 sequences, 8/8 heads, head_dim 64, block 16, lengths U{1..512}, "
                                    "fp32 q / fp16 K,V / fp32 out, 1024-block pool, one layer",
                        "context_tokens": int(lens.sum()), "kv_bytes": int(algo),
                        "l2": "L2-resident (about 4 MB per call): a latency, not a bandwidth, figure"},
@@ -847,7 +848,7 @@ def main():
     ap.add_argument("--layers", type=int, default=0, help="profiling: number of layers (pool sized to need)")
     ap.add_argument("--op", default="decode", choices=["decode", "migrate", "cow", "swap", "sim", "latency"],
                     help="decode step (default), a whole-block mover measured alone, the scheduler-driven "
-                         "data plane (sim), or config 1's per-call latency (latency)")
+                         "data plane (sim), or the small 8-sequence case's per-call latency (latency)")
     ap.add_argument("--sim-replays", type=int, default=2, help="sim: timed replays of the decision stream")
     args = ap.parse_args()
     assert args.warmup >= 3, "at least 3 warm-up steps"

@@ -169,15 +169,15 @@ def _normal_case(seed, ns, nh, kvh, hd, B, lens, pool_blocks):
     return Q, K, V, T, np.asarray(lens, np.int32)
 
 
-def test_config1_full_size(kvb, ora, cuda):
-    """Config 1 at its full size: 8 sequences, 8/8 heads, D=64, B=16, lengths U{1..512}, fp32 Q, fp16 K/V,
-    1024-block pool, random block permutation."""
+def test_eight_sequence_case_full_size(kvb, ora, cuda):
+    """The small correctness case at its full size: 8 sequences, 8/8 heads, D=64, B=16, lengths U{1..512},
+    fp32 Q, fp16 K/V, 1024-block pool, random block permutation."""
     rng = np.random.default_rng(2024)
     lens = rng.integers(1, 513, size=8).tolist()
     Q, K, V, T, L = _normal_case(1, 8, 8, 8, 64, 16, lens, 1024)
     for split in (-1, 0, 2):
         got, ref = run_attention(kvb, ora, Q, K, V, T, L, 8, 8, kv="f16", q="f32", split_tiles=split)
-        check_close(got, ref, what=f"cfg1 split={split}")
+        check_close(got, ref, what=f"8-sequence case split={split}")
 
 
 @pytest.mark.parametrize("shape", [
@@ -224,7 +224,7 @@ def test_gqa_16_heads_per_kv_head(kvb, ora, cuda):
 
 
 def test_layout_invariance_bit_exact(kvb, ora, cuda):
-    """Config 2 at full size (64 sequences, lengths U{512..4096}, 14/2 heads, D=64, fp16, 64k-block pool):
+    """The Qwen2.5-0.5B-shaped workload at full size (64 sequences, lengths U{512..4096}, 14/2 heads, D=64, fp16, 64k-block pool):
     relabelling the physical blocks (a different permutation, pool bytes moved accordingly) gives a
     bit-identical output -- the property of the reference's model_check.py:304-330 -- and a sample of
     sequences matches the oracle."""
@@ -263,7 +263,7 @@ def test_layout_invariance_bit_exact(kvb, ora, cuda):
     bt = torch.from_numpy(blocks).to(dev)
     ref = ora.reference_attention(nh, kvh, hd, B, Q[idx].float().cpu().numpy(), K[bt].float().cpu().numpy(),
                                   V[bt].float().cpu().numpy(), Ts, lens[idx].astype(np.int32))
-    check_close(o1[idx].cpu().numpy(), ref, what="cfg2 sample")
+    check_close(o1[idx].cpu().numpy(), ref, what="Qwen-shaped sample")
 
 
 def test_bad_inputs_report_status_without_fault(kvb, ora, cuda):

@@ -125,11 +125,11 @@ def test_swap_round_trip_bit_exact(kvb, cuda):
         np.testing.assert_array_equal(kb[:, b_new], ks)
 
 
-def test_kv_op_mix_config5_shape(kvb, cuda):
-    """Config 5's op mix at reduced scale: a shared 2048-token prefix admitted with admit_with_prefix, each
+def test_kv_op_mix_shared_prefix_samples(kvb, cuda):
+    """The KV-op mix workload at reduced scale: a shared 2048-token prefix admitted with admit_with_prefix, each
     request forked into 8 samples (the original + 7 forks), appends whose first one copies the shared partial
     block, and every 4 steps 10% of the requests swapped out and back in (re-admitted with fresh ids).
-    8 kv heads, D=128, bf16, B=16 as in config 5; 8 layers instead of 32 to keep the host model small.
+    8 kv heads, D=128, bf16, B=16 as in that workload; 8 layers instead of 32 to keep the host model small.
     KVManager state and pool bytes are compared bit-exact after every step."""
     import torch
     L, B, kvh, D = 8, 16, 8, 128
@@ -178,7 +178,7 @@ def test_kv_op_mix_config5_shape(kvb, cuda):
 
 def test_cow_copy_full_block_property_large(kvb, cuda):
     """Size-independent property at a large size: 4096 copy-on-write pairs of 2 MiB blocks (32 layers x K/V,
-    config 5's block size, 17 GB of pools) leave every destination bit-equal to its source and the sources
+    the KV-op mix workload's block size, 17 GB of pools) leave every destination bit-equal to its source and the sources
     untouched."""
     import torch
     L, B, kvh, D = 32, 16, 8, 128
