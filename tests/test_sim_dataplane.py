@@ -170,3 +170,64 @@ def test_replay_on_device(kvb, ora, cuda, name, fused):
     assert plane.mgr.free_blocks() == nb and not plane.tokens
     assert batches["checked"] >= 5 and len(steps_checked) >= 8
     torch.cuda.synchronize()
+
+
+@pytest.mark.gpu
+def test_replay_llama_heads_with_strided_queries(kvb, ora, cuda):
+    """The first 40 scheduler steps of the serving-scale stream at the Llama-3-8B head shape (32/8 heads,
+    head_dim 128, 4 layers, bf16), with the queries of each batch a strided view of a larger bank (each layer's
+    rows contiguous, the layers 512 rows apart), as the data-plane benchmark passes them: contexts bit-exact
+    every 10 steps, and three rows of every fifth attention batch against the fp64 oracle on layers 0 and 3."""
+    import torch
+    dp = _dp(kvb)
+    sc = _load("serving_fcfs_swap")
+    nb, B = (int(x) for x in sc["config"][:2])
+    t = sc["trace"]
+    cut = int(np.nonzero(t[:, 0] == dp.TRACE_STEP)[0][39]) + 1
+    trace = t[:cut]
+    Lq, nh, kvh, Dq = 4, 32, 8, 128
+    content = dp.SyntheticContent(sc["requests"], layers=Lq, kv_heads=kvh, head_dim=Dq, num_heads=nh, device=cuda,
+                                  seed=9)
+    bank = torch.randn((Lq, 512, nh, Dq), device=cuda).to(torch.bfloat16)
+    seen = {"n": 0, "checked": 0}
+
+    def queries(rids):
+        return bank[:, :len(rids)]
+
+    def on_attention(rids, q, out, tables, lens):
+        seen["n"] += 1
+        if seen["n"] % 5 != 1:
+            return
+        n = len(rids)
+        for i in sorted({0, n // 2, n - 1}):
+            ln = int(lens[i])
+            k, v = content(np.full(ln, rids[i], dtype=np.int64), np.arange(ln, dtype=np.int64))
+            nbk = -(-ln // B)
+            for layer in (0, Lq - 1):
+                K = np.zeros((nbk * B, kvh, Dq), np.float32)
+                V = np.zeros_like(K)
+                K[:ln] = k[layer].float().cpu().numpy()
+                V[:ln] = v[layer].float().cpu().numpy()
+                ref = ora.reference_attention(nh, kvh, Dq, B, q[layer, i:i + 1].float().cpu().numpy(),
+                                              K.reshape(nbk, B, kvh, Dq), V.reshape(nbk, B, kvh, Dq),
+                                              np.arange(nbk, dtype=np.int32)[None], np.asarray([ln], np.int32))
+                got = out[layer, i:i + 1].float().cpu().numpy()
+                assert (np.abs(got - ref) <= 2e-3 + 2e-3 * np.abs(ref)).all(), (layer, i, np.abs(got - ref).max())
+        seen["checked"] += 1
+
+    plane = dp.DataPlane(nb, B, layers=Lq, num_heads=nh, kv_heads=kvh, head_dim=Dq, source=content, queries=queries,
+                         device=cuda, swap_slots=max(1, _max_swapped_blocks(dp, trace, B)), on_attention=on_attention)
+
+    def contexts(i):
+        if i % 10 == 0:
+            torch.cuda.synchronize()
+            for r in sorted(plane.tokens):
+                n = plane.mgr.num_tokens(r)
+                idx = torch.tensor(plane.mgr.block_table(r), dtype=torch.long, device=plane.dev)
+                gk = plane.k[:, idx].reshape(Lq, -1, kvh, Dq)[:, :n]
+                ek, _ = content(np.full(n, r, dtype=np.int64), np.arange(n, dtype=np.int64))
+                assert torch.equal(gk.view(torch.int16), ek.view(torch.int16)), f"K of request {r}"
+
+    n = plane.run(trace, on_step=contexts)
+    assert plane.status_word() == 0
+    assert n.steps == 40 and n.tokens_generated > 200 and seen["checked"] >= 6
