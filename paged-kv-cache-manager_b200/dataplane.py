@@ -139,14 +139,19 @@ def replay_decisions(mgr, trace) -> DecisionCounters:
 
 class DataPlane:
     """One shard: K/V pools [layers][num_blocks][block_size][kv_heads][head_dim] on `device`, a pinned host
-    swap pool of `swap_slots` block slots (all layers, K and V), this package's KVManager, one stream.
+    swap pool of `swap_slots` block slots (all layers, K and V), this package's KVManager, a compute stream and
+    a swap stream.
 
     `source(rids, positions) -> (k, v)` supplies K/V rows -- row i is position positions[i] of request rids[i]
     -- as [layers][n][kv_heads][head_dim] device tensors in the pool dtype (what a model's prefill / decode
     step would produce); `queries(rids) -> q` the queries of an attention batch, [layers][n][num_heads]
     [head_dim].  `on_attention(rids, q, out, tables, lens)` (optional) sees every attention batch after its
     launches.  The host never waits for the device: metadata goes up through pinned staging copies, and
-    every launch, copy and allocation is ordered on the shard's stream."""
+    every launch, copy and allocation is ordered on the shard's compute stream -- except the swaps, which run
+    on the swap stream: a swap-out starts after everything queued before it and the compute stream waits for
+    it before its next write (the freed blocks may be handed out again at once); a swap-in (into fresh
+    blocks) overlaps all work that does not touch its request, and the compute stream waits for it only
+    before attending that request, sharing its blocks (fork, prefix, prefix cache) or freeing it."""
 
     def __init__(self, num_blocks: int, block_size: int, *, layers: int, num_heads: int, kv_heads: int,
                  head_dim: int, source: Callable, queries: Callable, dtype=None, device="cuda",
@@ -171,6 +176,9 @@ class DataPlane:
         self.swapped = {}          # rid -> (host slots, tokens)
         self.status = torch.zeros(1, dtype=torch.int32, device=self.dev)
         self.stream = torch.cuda.Stream(self.dev)
+        self.side = torch.cuda.Stream(self.dev)  # swaps
+        self.swapins = {}          # rid -> event after its swap-in (not yet waited for by the compute stream)
+        self.swapout_ev = None     # event after the latest swap-out (not yet waited for)
         self.workspace = torch.zeros(0, dtype=torch.uint8, device=self.dev)
         self.source, self.queries, self.on_attention = source, queries, on_attention
         self.fused, self.early = fused_append, early_start
@@ -188,10 +196,29 @@ class DataPlane:
         import torch
         return torch.from_numpy(np.ascontiguousarray(a)).pin_memory().to(self.dev, non_blocking=True)
 
+    def _wait_swapouts(self):
+        """Before a compute-stream write: blocks freed by a swap-out may have been handed out again."""
+        if self.swapout_ev is not None:
+            self.stream.wait_event(self.swapout_ev)
+            self.swapout_ev = None
+
+    def _wait_swapin(self, rid: int):
+        ev = self.swapins.pop(rid, None)
+        if ev is not None:
+            self.stream.wait_event(ev)
+
+    def _side_after_compute(self):
+        """The swap stream starts after everything queued on the compute stream so far."""
+        import torch
+        ev = torch.cuda.Event()
+        ev.record(self.stream)
+        self.side.wait_event(ev)
+
     def _write_rows(self, rid: int, positions: np.ndarray):
         """K/V rows of `positions` of rid into their slots through its table."""
         if len(positions) == 0:
             return
+        self._wait_swapouts()
         tbl = np.asarray(self.mgr.block_table(rid), dtype=np.int64)
         slots = (tbl[positions // self.B] * self.B + positions % self.B).astype(np.int32)
         k, v = self.source(np.full(len(positions), rid, dtype=np.int64), positions)
@@ -199,6 +226,8 @@ class DataPlane:
                                 stream=self.stream)
 
     def _flush_copies(self):
+        if self.pending_cow or self.pending_tokens:
+            self._wait_swapouts()
         if self.pending_cow:
             self.kvb.cow_copy(self.k, self.v, self._to_dev(np.asarray(self.pending_cow, dtype=np.int32)),
                               status=self.status, stream=self.stream)
@@ -217,6 +246,9 @@ class DataPlane:
         import torch
         kvb = self.kvb
         rids = list(self.pending)
+        self._wait_swapouts()  # the fused append writes
+        for r in rids:
+            self._wait_swapin(r)
         tables, lens = self.mgr.dense_tables(rids, max(self.pending.values()) // self.B + 1)
         t, ln = self._to_dev(tables), self._to_dev(lens)
         q = self.queries(rids)
@@ -309,6 +341,8 @@ class DataPlane:
             self.n.steps += 1
         elif op in (TRACE_ADMIT_PREFIX, TRACE_ADMIT_CACHED):
             r, prompt = int(row[1]), int(row[4])
+            if op == TRACE_ADMIT_PREFIX and int(row[2]) != NO_REQUEST:
+                self._wait_swapin(int(row[2]))  # its blocks are about to be shared
             shared = _admission_shared_tokens(mgr, row)
             fn = mgr.admit_with_prefix if op == TRACE_ADMIT_PREFIX else mgr.admit_with_cached_prefix
             _expect(int(fn(r, int(row[2]), int(row[3]), prompt)), res, row, "admission")
@@ -316,10 +350,15 @@ class DataPlane:
                 return
             self.tokens[r] = prompt
             if flag == 1:  # swap-in: fresh blocks, no sharing
+                import torch
                 slots, tokens = self.swapped.pop(r)
                 _expect(prompt, tokens, row, "swapped-in tokens")
                 blocks = mgr.block_table(r)
-                self.kvb.swap_in(self.k, self.v, blocks, slots, self.pool, stream=self.stream)
+                self._side_after_compute()  # the fresh blocks' previous readers are queued there
+                self.kvb.swap_in(self.k, self.v, blocks, slots, self.pool, stream=self.side)
+                ev = torch.cuda.Event()
+                ev.record(self.side)
+                self.swapins[r] = ev
                 self.free_slots.extend(reversed(slots))
                 self.n.swap_in_blocks += len(blocks)
             else:
@@ -329,10 +368,12 @@ class DataPlane:
         elif op == TRACE_CACHE_PREFIX:
             if int(row[2]) in self.pending:  # the owner's newest row must be in place before blocks are shared
                 self._flush_attention()
+            self._wait_swapin(int(row[2]))
             _expect(int(mgr.cache_prefix(int(row[1]), int(row[2]), int(row[3]))), res, row, "cache_prefix")
         elif op == TRACE_FORK:
             if int(row[2]) in self.pending:
                 self._flush_attention()
+            self._wait_swapin(int(row[2]))
             _expect(int(mgr.fork(int(row[1]), int(row[2]))), res, row, "fork")
             if res:
                 self.tokens[int(row[1])] = self.tokens[int(row[2])]
@@ -342,13 +383,21 @@ class DataPlane:
             if r in self.pending:  # it generated this step: attend before its blocks can be reused
                 self._flush_attention()
             if flag == FREE_SWAPPED:
+                import torch
                 blocks = mgr.block_table(r)
                 if len(self.free_slots) < len(blocks):
                     raise RuntimeError("host swap pool exhausted")
                 slots = [self.free_slots.pop() for _ in blocks]
-                self.kvb.swap_out(self.k, self.v, blocks, slots, self.pool, stream=self.stream)
+                self._side_after_compute()  # its rows, and a swap-in of it still in flight, come first
+                self.kvb.swap_out(self.k, self.v, blocks, slots, self.pool, stream=self.side)
+                ev = torch.cuda.Event()
+                ev.record(self.side)
+                self.swapout_ev = ev  # the swap stream is serial: this covers every earlier swap
+                self.swapins.pop(r, None)
                 self.swapped[r] = (slots, int(row[2]))
                 self.n.swap_out_blocks += len(blocks)
+            else:
+                self._wait_swapin(r)  # its blocks may be handed out again
             mgr.free(r)
             del self.tokens[r]
         elif op == TRACE_CLEAR_CACHE:
