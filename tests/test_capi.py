@@ -140,3 +140,71 @@ def test_header_constants_match_the_binding(kvb):
     for name, value in defs.items():
         if name.startswith(("KVP_STATUS_", "KVP_ATTN_", "KVP_E")) or name == "KVP_OK":
             assert getattr(kvb, name) == value, name
+
+
+C_PROGRAM = r"""
+#include "kvp_b200.h"
+#include <stdio.h>
+
+/* A plain-C caller of the host control plane: prefix sharing, a fork, a batched append with copy-on-write,
+   dense tables and statistics, printed for comparison with the Python binding. */
+int main(void) {
+    kvp_mgr* m = kvp_mgr_create(32, 16);
+    if (!m) return 2;
+    printf("admit %d\n", kvp_mgr_admit(m, 1, 40));
+    printf("prefix %d\n", kvp_mgr_admit_with_prefix(m, 2, 1, 36, 50));
+    printf("fork %d\n", kvp_mgr_fork(m, 3, 1));
+    int64_t rids[3] = {1, 2, 3};
+    int32_t slots[3], pairs[6], ncow = 0;
+    const int done = kvp_mgr_append_batch(m, rids, 3, slots, pairs, &ncow);
+    printf("append %d ncow %d\n", done, ncow);
+    printf("slots %d %d %d\n", slots[0], slots[1], slots[2]);
+    for (int k = 0; k < ncow; ++k) printf("pair %d %d\n", pairs[2 * k], pairs[2 * k + 1]);
+    int32_t tables[3 * 4], lens[3];
+    printf("dense %d\n", kvp_mgr_dense_tables(m, rids, 3, 4, -1, tables, lens));
+    for (int i = 0; i < 3; ++i)
+        printf("row %d %d %d %d len %d\n", tables[4 * i], tables[4 * i + 1], tables[4 * i + 2], tables[4 * i + 3],
+               lens[i]);
+    int64_t st[10];
+    kvp_mgr_stats(m, st);
+    for (int i = 0; i < 10; ++i) printf("stat %lld\n", (long long)st[i]);
+    char buf[256];
+    printf("validate %d\n", kvp_mgr_validate(m, buf, (int32_t)sizeof buf));
+    printf("dup %d\n", kvp_mgr_admit(m, 1, 5));  /* a duplicate id is rejected with an error code */
+    printf("msg %s\n", kvp_last_error()[0] ? "set" : "empty");
+    kvp_mgr_destroy(m);
+    return 0;
+}
+"""
+
+
+def test_header_is_plain_c_and_drives_the_manager(kvb, tmp_path):
+    """include/kvp_b200.h is a C header (what a cgo / JNI / N-API / ctypes binding would include): a C11
+    program compiled with -pedantic against it and linked to the library drives the KVManager through the
+    C ABI, and its results equal the same calls through the Python binding."""
+    import subprocess
+    src = tmp_path / "caller.c"
+    src.write_text(C_PROGRAM)
+    exe = tmp_path / "caller"
+    lib_dir = os.path.dirname(kvb.LIB_PATH)
+    subprocess.run(["gcc", "-std=c11", "-Wall", "-Wextra", "-pedantic", "-Werror", "-I", os.path.join(ROOT, "include"),
+                    str(src), "-L", lib_dir, "-lkvpage_b200", f"-Wl,-rpath,{lib_dir}", "-o", str(exe)],
+                   check=True, capture_output=True, text=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.splitlines()
+    m = kvb.KVManager(32, 16)
+    want = [f"admit {int(m.admit(1, 40))}", f"prefix {int(m.admit_with_prefix(2, 1, 36, 50))}",
+            f"fork {int(m.fork(3, 1))}"]
+    done, slots, pairs = m.append_batch([1, 2, 3])
+    want += [f"append {done} ncow {len(pairs)}", "slots " + " ".join(str(int(x)) for x in slots)]
+    want += [f"pair {int(a)} {int(b)}" for a, b in pairs]
+    tables, lens = m.dense_tables([1, 2, 3], 4, pad=-1)
+    want += ["dense 0"] + [f"row {' '.join(str(int(x)) for x in tables[i])} len {int(lens[i])}" for i in range(3)]
+    s = m.stats()
+    want += [f"stat {int(s[k])}" for k in ("requests", "used_tokens", "allocated_blocks", "allocated_slots",
+                                           "internal_waste", "logical_blocks", "blocks_saved", "cow_copies",
+                                           "cached_blocks", "cache_evictions")]
+    want += ["validate 0"]
+    assert out[:len(want)] == want
+    assert out[len(want)].startswith("dup ") and int(out[len(want)].split()[1]) < 0
+    assert out[len(want) + 1] == "msg set"
+    assert len(pairs) == 1  # the fork's first append copied the shared partial block
