@@ -151,7 +151,8 @@ class DataPlane:
     on the swap stream: a swap-out starts after everything queued before it and the compute stream waits for
     it before its next write (the freed blocks may be handed out again at once); a swap-in (into fresh
     blocks) overlaps all work that does not touch its request, and the compute stream waits for it only
-    before attending that request, sharing its blocks (fork, prefix, prefix cache) or freeing it."""
+    before writing that request's new token, attending it, sharing its blocks (fork, prefix, prefix cache) or
+    freeing it."""
 
     def __init__(self, num_blocks: int, block_size: int, *, layers: int, num_heads: int, kv_heads: int,
                  head_dim: int, source: Callable, queries: Callable, dtype=None, device="cuda",
@@ -228,6 +229,8 @@ class DataPlane:
     def _flush_copies(self):
         if self.pending_cow or self.pending_tokens:
             self._wait_swapouts()
+        for r, _, _ in self.pending_tokens:  # a token lands in its request's (maybe just swapped-in) last block
+            self._wait_swapin(r)
         if self.pending_cow:
             self.kvb.cow_copy(self.k, self.v, self._to_dev(np.asarray(self.pending_cow, dtype=np.int32)),
                               status=self.status, stream=self.stream)
