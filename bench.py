@@ -324,7 +324,8 @@ def run_ours(args, cfg, rank, world, dev):
     # context schedule: 0 = balanced persistent (stream-K) grid; > 0 = fixed splits of that many tiles
     split = args.split
     a0 = kvb.attention_args(q[0], kc[0], vc[0], d_tables, d_lens[0], out[0], nh, kvh, num_blocks=nb,
-                            split_tiles=split, warps_per_kv_head=args.wph, stages=args.stages)
+                            split_tiles=split, warps_per_kv_head=args.wph, stages=args.stages,
+                            seq_start_tiles=args.seq_start_tiles)
     ws = torch.zeros(max(kvb.workspace_bytes(a0), 256), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
@@ -336,7 +337,7 @@ def run_ours(args, cfg, rank, world, dev):
     for l in range(L):
         a = kvb.attention_args(q[l], kc[l], vc[l], d_tables, d_lens[0], out[l], nh, kvh, num_blocks=nb,
                                split_tiles=split, status=status, warps_per_kv_head=args.wph, stages=args.stages,
-                               k_new=knew[l], v_new=vnew[l])
+                               seq_start_tiles=args.seq_start_tiles, k_new=knew[l], v_new=vnew[l])
         a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
         # zero-filled once, every call leaves the counters zero; lengths and tables are never written by a kernel
         # and a layer's kernel writes only its own pool, so each layer's launch may start and load K/V during
@@ -841,6 +842,9 @@ def main():
     ap.add_argument("--split", type=int, default=0, help="tiles per context split (0: balanced persistent grid)")
     ap.add_argument("--wph", type=int, default=0, help="tuning: consumer warps per kv head (0: automatic)")
     ap.add_argument("--stages", type=int, default=0, help="tuning: pipeline stages (0: automatic)")
+    ap.add_argument("--seq-start-tiles", type=int, default=0,
+                    help="tuning: start cost charged per sequence in the balanced partition, in tiles (0: automatic, "
+                         "<0: none)")
     ap.add_argument("--no-e2e", action="store_true", help="tuning runs: skip the end-to-end leg")
     ap.add_argument("--eager", action="store_true", help="launch every layer from Python instead of a CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -260,8 +260,9 @@ int plan_attention(const kvp_attn_args& a, bool have_workspace, AttnPlan* out) {
             if (plan_attention(b, have_workspace, &p16) == KVP_OK && p16.streamk) pl.G = p16.G;
         }
         // A sequence switch (query load, state reset, segment epilogue, and with two warps per kv head their
-        // state combine) costs a CTA about 3.8 us, 5.3 us with two warps per head (the optima of start-cost
-        // sweeps on B200 for the Qwen2.5-0.5B, TinyLlama and Llama-3-8B shapes); charge it in tiles: a tile's
+        // state combine) costs a CTA about 3.8 us, 6.8 us with two warps per head (the optima of start-cost
+        // sweeps on B200 for the Qwen2.5-0.5B, TinyLlama and Llama-3-8B shapes, with each launch's successor
+        // scheduled from its start); charge it in tiles: a tile's
         // time at the full bandwidth shared by the CTAs of one SM.  Only quantities independent of the block
         // size enter (the tile's K/V bytes, one CTA per SM for 48 KB tiles or more, else two), so every block
         // size and placement of the same contexts gets the same partition -- and bit-identical results.
@@ -270,7 +271,7 @@ int plan_attention(const kvp_attn_args& a, bool have_workspace, AttnPlan* out) {
         } else if (a.seq_start_tiles == 0) {
             const double tile_bytes = 16.0 * kc * D * 2 * 2;
             const double ctas = static_cast<double>(sm_count()) * (tile_bytes >= (48 << 10) ? 1 : 2);
-            const double switch_us = pl.wph > 1 ? 5.3 : 3.8;
+            const double switch_us = pl.wph > 1 ? 6.8 : 3.8;
             const double tile_us = tile_bytes * ctas / 6.4e6;
             pl.seq_units = static_cast<int>(std::min(32.0, std::max(0.0, std::round(switch_us / tile_us))));
         }
