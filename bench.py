@@ -124,30 +124,46 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- CPU baseline
-def cpu_baseline(cfg, lens, target_s=12.0, kind_pref="reference"):
-    """Times the reference's paged_attention_cpu (the reference library built here, else the oracle's
-    restatement) on a bounded sample of this workload: a few sequences of one layer, drawn from the same
-    length distribution, K/V as fp32 copies of bf16/fp16 N(0,1) values; all host cores.  Returns the rate
-    scaled to the workload's decode tok/s."""
-    import oracle
-    kind = "reference" if (kind_pref == "reference" and oracle.have_ref()) else "port"
+def _random_sample(cfg, sl, seed, pool_blocks=None):
+    """A CPU-side sample of the workload: requests of context lengths `sl`, N(0,1) fp32 K/V/Q.  Without
+    `pool_blocks` each request's blocks are a random permutation of a pool of exactly their blocks; with it,
+    tables draw ids from a smaller shared pool (filled by tiling a 64 MB random chunk), which keeps host memory
+    and set-up time bounded while every request still reads blocks scattered over DRAM."""
     nh, kvh, D, B = cfg["nh"], cfg["kvh"], cfg["D"], cfg["B"]
-    cores = os.cpu_count() or 1
-    rng = np.random.default_rng(77)
-    ns = max(cores, 8)
-    sl = rng.choice(lens, size=ns, replace=True).astype(np.int32)
+    rng = np.random.default_rng(seed)
+    sl = np.asarray(sl, np.int32)
+    ns = len(sl)
     nblk = (sl + B - 1) // B
-    pool = int(nblk.sum())
-    K = rng.standard_normal((pool, B, kvh, D), dtype=np.float32)
-    V = rng.standard_normal((pool, B, kvh, D), dtype=np.float32)
-    Q = rng.standard_normal((ns, nh, D), dtype=np.float32)
-    perm = rng.permutation(pool).astype(np.int32)
     T = np.zeros((ns, int(nblk.max())), np.int32)
-    o = 0
-    for i in range(ns):
-        T[i, : nblk[i]] = perm[o: o + nblk[i]]
-        o += int(nblk[i])
-    impl = "ref" if kind == "reference" else "c"
+    if pool_blocks is None:
+        pool = int(nblk.sum())
+        K = rng.standard_normal((pool, B, kvh, D), dtype=np.float32)
+        V = rng.standard_normal((pool, B, kvh, D), dtype=np.float32)
+        perm = rng.permutation(pool).astype(np.int32)
+        o = 0
+        for i in range(ns):
+            T[i, : nblk[i]] = perm[o: o + nblk[i]]
+            o += int(nblk[i])
+    else:
+        pool = int(pool_blocks)
+        K = np.empty((pool, B, kvh, D), np.float32)
+        V = np.empty((pool, B, kvh, D), np.float32)
+        for t in (K, V):
+            chunk = rng.standard_normal(min(t.size, 16 << 20), dtype=np.float32)
+            flat = t.reshape(-1)
+            for o in range(0, flat.size, chunk.size):
+                m = min(chunk.size, flat.size - o)
+                flat[o:o + m] = chunk[:m]
+        for i in range(ns):
+            T[i, : nblk[i]] = rng.integers(0, pool, size=nblk[i], dtype=np.int32)
+    Q = rng.standard_normal((ns, nh, D), dtype=np.float32)
+    return Q, K, V, T, sl
+
+
+def _time_cpu(cfg, Q, K, V, T, sl, target_s, impl, cores):
+    """Seconds per paged_attention_cpu call (partitions 1, `cores` threads) over about target_s."""
+    import oracle
+    nh, kvh, D, B = cfg["nh"], cfg["kvh"], cfg["D"], cfg["B"]
     oracle.paged_attention_cpu(nh, kvh, D, B, Q, K, V, T, sl, partitions=1, nthreads=cores, impl=impl)  # warm
     reps, t0 = 0, time.perf_counter()
     while True:
@@ -156,7 +172,61 @@ def cpu_baseline(cfg, lens, target_s=12.0, kind_pref="reference"):
         el = time.perf_counter() - t0
         if el >= target_s or reps >= 1000:
             break
-    per_call = el / reps
+    return el / reps, reps, el
+
+
+def check_parity(cfg, sample):
+    """The GPU's outputs of the timed step's last launch for the sampled requests against the fp64
+    reference_attention (the reference library's own function when it is built, else the oracle's C
+    restatement) on the same K/V, queries and tables; and the rows the fused append wrote.  Tolerance:
+    |got - ref| <= 2e-3 + (2e-3 + half an ulp of the output dtype) |ref|."""
+    import oracle
+    nh, kvh, D, B = cfg["nh"], cfg["kvh"], cfg["D"], cfg["B"]
+    impl = "ref" if oracle.have_ref() else "c"
+    half_ulp = {"bf16": 2.0 ** -8, "f16": 2.0 ** -11}[cfg["dtype"]]
+    worst_abs, worst_excess, appended = 0.0, -1.0, True
+    for l, d in sample["layers"].items():
+        ref = oracle.reference_attention(nh, kvh, D, B, d["q"], d["k"], d["v"], sample["tables"], sample["lens"],
+                                         impl=impl)
+        got = d["out"]
+        finite = bool(np.isfinite(got).all())
+        err = np.abs(got - ref)
+        worst_abs = max(worst_abs, float(err.max()) if finite else float("inf"))
+        worst_excess = max(worst_excess, float((err - (2e-3 + (2e-3 + half_ulp) * np.abs(ref))).max())
+                           if finite else float("inf"))
+        appended &= d["appended_ok"]
+    n = len(sample["lens"])
+    return {"checked": n * len(sample["layers"]), "requests": n, "layers": sorted(sample["layers"]),
+            "context_tokens": [int(sample["lens"].min()), int(sample["lens"].max())],
+            "max_abs_err": worst_abs, "max_excess_over_tolerance": worst_excess, "appended_rows_ok": appended,
+            "ok": bool(worst_excess <= 0 and appended),
+            "oracle": "reference_attention (fp64) of the " + ("reference library" if impl == "ref" else
+                                                               "oracle's C restatement"),
+            "tolerance": "2e-3 abs + (2e-3 + half an ulp of the output dtype) rel"}
+
+
+def cpu_baseline(cfg, lens, target_s=12.0, kind_pref="reference", sample=None):
+    """Times the reference's paged_attention_cpu (the reference library built here, else the oracle's
+    restatement) on a bounded sample of this workload on all host cores, scaled to the workload's decode tok/s.
+    With `sample` (DecodeStep.parity_sample of the last timed step: 16 of its requests, the first and last
+    layer, copied off the device after the timed region) the timed sample is that step's first-layer data, and
+    this leg also checks the GPU's outputs for those requests (check_parity).  Returns (baseline, parity)."""
+    import oracle
+    kind = "reference" if (kind_pref == "reference" and oracle.have_ref()) else "port"
+    impl = "ref" if kind == "reference" else "c"
+    kvh, D = cfg["kvh"], cfg["D"]
+    cores = os.cpu_count() or 1
+    parity = None
+    if sample is not None:
+        first = sample["layers"][min(sample["layers"])]
+        Q, K, V, T, sl = first["q"], first["k"], first["v"], sample["tables"], sample["lens"]
+        what = "the timed step's own data: 16 of its requests (longest, shortest, 14 random), first layer"
+        parity = check_parity(cfg, sample)
+    else:
+        pick = np.random.default_rng(76).choice(lens, size=max(cores, 8), replace=True)
+        Q, K, V, T, sl = _random_sample(cfg, pick, seed=77)
+        what = f"{len(sl)} requests drawn from the workload's lengths, N(0,1) data, one layer"
+    per_call, reps, el = _time_cpu(cfg, Q, K, V, T, sl, target_s, impl, cores)
     elem = 2
     sample_bytes = float(sl.sum()) * kvh * D * 2 * elem  # same byte formula as the GPU (one layer)
     gbs = sample_bytes / per_call / 1e9
@@ -164,8 +234,8 @@ def cpu_baseline(cfg, lens, target_s=12.0, kind_pref="reference"):
     step_s = step_bytes / (gbs * 1e9)
     return {"value": len(lens) / step_s, "unit": "tok/s", "cores": cores, "kind": kind,
             "gb_s": round(gbs, 3),
-            "sample": f"{ns} sequences x 1 layer ({int(sl.sum())} tokens, lengths drawn from the workload), "
-                      f"{reps} timed calls over {el:.1f}s, scaled to {len(lens)} requests x {cfg['L']} layers"}
+            "sample": f"{what} ({int(sl.sum())} tokens), {reps} timed calls over {el:.1f}s, scaled to "
+                      f"{len(lens)} requests x {cfg['L']} layers by its GB/s"}, parity
 
 
 def reference_gpu_kernel(cfg, lens, nseq=32):
@@ -282,7 +352,148 @@ def setup_shard(kvb, cfg, lens, steps_total, dev, seed):
     return mgr, kc, vc, nb
 
 
+class DecodeStep:
+    """The timed decode step of one GPU shard, built once and reused by the benchmark and by the full-batch
+    tests (so both run the same launch plan): the host KVManager is advanced `n_steps` steps up front (one
+    append per request per step, lengths recorded per step; the table after the last step serves every step,
+    as entries past a sequence are never read), and step s is one kvp_paged_attention launch per layer with the
+    fused append of the layer's new K/V at position len - 1, the balanced schedule over one zero-filled
+    workspace (KVP_ATTN_WORKSPACE_CLEAN) and early load (each layer's launch may start and load K/V during the
+    previous one).  `rows_per_step`: the new K/V rows differ from step to step (else one set serves all)."""
+
+    def __init__(self, kvb, cfg, mgr, kc, vc, nb, ns, n_steps, dev, seed, split=0, wph=0, stages=0,
+                 seq_start_tiles=0, rows_per_step=False):
+        import ctypes
+        import torch
+        nh, kvh, D, L, B = cfg["nh"], cfg["kvh"], cfg["D"], cfg["L"], cfg["B"]
+        self.kvb, self.cfg, self.kc, self.vc, self.nb, self.dev, self.ns = kvb, cfg, kc, vc, nb, dev, ns
+        rids = list(range(ns))
+        self.lens_all = np.empty((n_steps, ns), np.int32)
+        for s in range(n_steps):
+            done, _, pairs = mgr.append_batch(rids)
+            assert done == ns and len(pairs) == 0
+            self.lens_all[s] = [mgr.num_tokens(r) for r in rids]
+        self.max_blocks = (int(self.lens_all[-1].max()) + B - 1) // B + 1
+        self.tables, _ = mgr.dense_tables(rids, self.max_blocks, pad=0)
+        self.d_tables = torch.from_numpy(self.tables).to(dev)
+        self.d_lens = torch.from_numpy(self.lens_all).to(dev)
+        tdt = kc.dtype
+        g = torch.Generator(device=dev).manual_seed(seed)
+        self.q = torch.randn((L, ns, nh, D), generator=g, device=dev).to(tdt)
+        nrows = n_steps if rows_per_step else 1
+        self.knew = torch.randn((nrows, L, ns, kvh, D), generator=g, device=dev).to(tdt)
+        self.vnew = torch.randn((nrows, L, ns, kvh, D), generator=g, device=dev).to(tdt)
+        self.out = torch.empty((L, ns, nh, D), device=dev, dtype=tdt)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.split = split
+        a0 = kvb.attention_args(self.q[0], kc[0], vc[0], self.d_tables, self.d_lens[0], self.out[0], nh, kvh,
+                                num_blocks=nb, split_tiles=split, warps_per_kv_head=wph, stages=stages,
+                                seq_start_tiles=seq_start_tiles)
+        self.ws = torch.zeros(max(kvb.workspace_bytes(a0), 256), dtype=torch.uint8, device=dev)
+        # Launch arguments are built once; a step only repoints the lengths and new rows, so the timed loop
+        # measures the kernels, not Python.
+        self.args = []
+        for l in range(L):
+            a = kvb.attention_args(self.q[l], kc[l], vc[l], self.d_tables, self.d_lens[0], self.out[l], nh, kvh,
+                                   num_blocks=nb, split_tiles=split, status=self.status, warps_per_kv_head=wph,
+                                   stages=stages, seq_start_tiles=seq_start_tiles, k_new=self.knew[0, l],
+                                   v_new=self.vnew[0, l])
+            a.workspace, a.workspace_bytes = self.ws.data_ptr(), self.ws.numel()
+            # zero-filled once, every call leaves the counters zero; lengths and tables are never written by a
+            # kernel and a layer's kernel writes only its own pool, so each layer's launch may start and load K/V
+            # during the previous one
+            a.flags = kvb.KVP_ATTN_WORKSPACE_CLEAN | kvb.KVP_ATTN_EARLY_LOAD
+            self.args.append(a)
+        self.lib = kvb.lib()
+        self._ct = ctypes
+        self.lens_row = self.d_lens.stride(0) * 4
+        # launches per layer: one (balanced schedule, or unsplit contexts), two with fixed splits (+ merge)
+        self.per_layer = 1 if split == 0 or split >= (self.max_blocks * B + 15) // 16 or split < 0 else 2
+
+    def launch(self, s, stream_ptr, ev=None, stream=None):
+        """Step s's per-layer launches on a stream (events around each launch when `ev` is given)."""
+        lp = self.d_lens.data_ptr() + s * self.lens_row
+        row = s if self.knew.shape[0] > 1 else 0
+        for l, a in enumerate(self.args):
+            a.seq_lens = lp
+            a.k_new, a.v_new = self.knew[row, l].data_ptr(), self.vnew[row, l].data_ptr()
+            if ev is not None:
+                ev[l][0].record(stream)
+            rc = self.lib.kvp_paged_attention(self._ct.byref(a), stream_ptr)
+            assert rc == 0, self.kvb.last_error()
+            if ev is not None:
+                ev[l][1].record(stream)
+
+    def capture(self, steps):
+        """One CUDA graph per step (its lengths row and new rows are baked into the launches)."""
+        import torch
+        graphs = []
+        cap = torch.cuda.Stream(self.dev)
+        for s in steps:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap, capture_error_mode="thread_local"):
+                self.launch(s, self._ct.c_void_p(torch.cuda.current_stream(self.dev).cuda_stream))
+            graphs.append(g)
+        return graphs
+
+    def sample_rows(self, s, n=16, seed=0):
+        """Requests whose outputs a parity check reads after step s: the longest and the shortest context,
+        the rest drawn at random (seeded)."""
+        lens = self.lens_all[s]
+        pick = [int(np.argmax(lens)), int(np.argmin(lens))]
+        rest = [i for i in np.random.default_rng(seed).permutation(self.ns).tolist() if i not in pick]
+        return pick + rest[:max(0, n - 2)]
+
+    def parity_sample(self, s, layers, idx):
+        """What a CPU check of step s needs, copied out of the device after it ran (no checking here): per
+        layer, the sampled requests' queries and outputs (fp32), their K/V blocks gathered into a compact pool
+        (fp32, exact) with the tables renumbered into it, and whether the pool holds the step's new K/V rows at
+        each sampled request's position len - 1 (the fused append's writes)."""
+        import torch
+        B = self.cfg["B"]
+        lens = self.lens_all[s][idx].astype(np.int32)
+        nblk = (lens + B - 1) // B
+        T = np.zeros((len(idx), int(nblk.max())), np.int32)
+        blocks, off = [], 0
+        for j, i in enumerate(idx):
+            blocks.extend(self.tables[i, :nblk[j]].tolist())
+            T[j, :nblk[j]] = np.arange(off, off + nblk[j])
+            off += int(nblk[j])
+        bidx = torch.tensor(blocks, dtype=torch.long, device=self.dev)
+        ridx = torch.tensor(idx, dtype=torch.long, device=self.dev)
+        pos = lens - 1
+        slot_blk = torch.tensor([int(self.tables[i, p // B]) for i, p in zip(idx, pos)], dtype=torch.long,
+                                device=self.dev)
+        slot_off = torch.tensor((pos % B).tolist(), dtype=torch.long, device=self.dev)
+        row = s if self.knew.shape[0] > 1 else 0
+        out = {"lens": lens, "tables": T, "layers": {}}
+        for l in layers:
+            kc, vc = self.kc[l], self.vc[l]
+            out["layers"][l] = {
+                "q": self.q[l].index_select(0, ridx).float().cpu().numpy(),
+                "out": self.out[l].index_select(0, ridx).float().cpu().numpy(),
+                "k": kc.index_select(0, bidx).float().cpu().numpy(),
+                "v": vc.index_select(0, bidx).float().cpu().numpy(),
+                "appended_ok": bool(torch.equal(kc[slot_blk, slot_off], self.knew[row, l].index_select(0, ridx)) and
+                                    torch.equal(vc[slot_blk, slot_off], self.vnew[row, l].index_select(0, ridx))),
+            }
+        return out
+
+
+def _per_rank_ms(ms, world, dev):
+    """Every rank's device-timed milliseconds (one entry per rank, in rank order)."""
+    if world == 1:
+        return [ms]
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    out = [torch.zeros_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [float(x.item()) for x in out]
+
+
 def run_ours(args, cfg, rank, world, dev):
+    import ctypes
     import torch
     import torch.distributed as dist
     kvb = importlib.import_module("paged-kv-cache-manager_b200")
@@ -302,82 +513,21 @@ def run_ours(args, cfg, rank, world, dev):
     rids = list(range(ns))
     max_len = int(lens.max()) + steps_total + 1
     max_blocks = (max_len + B - 1) // B
-
-    # Device-resident inputs for the value run: per-step lengths precomputed by the host manager (the table
-    # after all steps serves every step: entries past a sequence are never read).  Each step's attention
-    # launch writes the new token of its layer into the slot at position len - 1 (fused append).
-    n_value = W + K
-    lens_all = np.empty((n_value, ns), np.int32)
-    for s in range(n_value):
-        done, _, pairs = mgr.append_batch(rids)
-        assert done == ns and len(pairs) == 0
-        lens_all[s] = [mgr.num_tokens(r) for r in rids]
-    tables, _ = mgr.dense_tables(rids, max_blocks, pad=0)
-    d_tables = torch.from_numpy(tables).to(dev)
-    d_lens = torch.from_numpy(lens_all).to(dev)
-    g = torch.Generator(device=dev).manual_seed(99 + rank)
-    q = torch.randn((L, ns, nh, D), generator=g, device=dev).to(tdt)
-    knew = torch.randn((L, ns, kvh, D), generator=g, device=dev).to(tdt)
-    vnew = torch.randn((L, ns, kvh, D), generator=g, device=dev).to(tdt)
-    out = torch.empty((L, ns, nh, D), device=dev, dtype=tdt)
-    status = torch.zeros(1, dtype=torch.int32, device=dev)
-    # context schedule: 0 = balanced persistent (stream-K) grid; > 0 = fixed splits of that many tiles
-    split = args.split
-    a0 = kvb.attention_args(q[0], kc[0], vc[0], d_tables, d_lens[0], out[0], nh, kvh, num_blocks=nb,
-                            split_tiles=split, warps_per_kv_head=args.wph, stages=args.stages,
-                            seq_start_tiles=args.seq_start_tiles)
-    ws = torch.zeros(max(kvb.workspace_bytes(a0), 256), dtype=torch.uint8, device=dev)
+    # Device-resident inputs for the value run; each step's attention launch writes the new token of its layer
+    # into the slot at position len - 1 (fused append).
+    stepper = DecodeStep(kvb, cfg, mgr, kc, vc, nb, ns, W + K, dev, seed=99 + rank, split=args.split,
+                         wph=args.wph, stages=args.stages, seq_start_tiles=args.seq_start_tiles)
+    lens_all, split, per_layer, status = stepper.lens_all, stepper.split, stepper.per_layer, stepper.status
     stream = torch.cuda.current_stream(dev)
-
-    # Launch arguments are built once; a step only repoints the lengths (so the timed loop measures the
-    # kernels, not Python).
-    import ctypes
-    L_lib = kvb.lib()
-    attn_args = []
-    for l in range(L):
-        a = kvb.attention_args(q[l], kc[l], vc[l], d_tables, d_lens[0], out[l], nh, kvh, num_blocks=nb,
-                               split_tiles=split, status=status, warps_per_kv_head=args.wph, stages=args.stages,
-                               seq_start_tiles=args.seq_start_tiles, k_new=knew[l], v_new=vnew[l])
-        a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
-        # zero-filled once, every call leaves the counters zero; lengths and tables are never written by a kernel
-        # and a layer's kernel writes only its own pool, so each layer's launch may start and load K/V during
-        # the previous one
-        a.flags = kvb.KVP_ATTN_WORKSPACE_CLEAN | kvb.KVP_ATTN_EARLY_LOAD
-        attn_args.append(a)
     sptr = ctypes.c_void_p(stream.cuda_stream)
-    lens_row = d_lens.stride(0) * 4
-    # launches per layer: one (balanced schedule, or unsplit contexts), two with fixed splits (+ merge)
-    per_layer = 1 if split == 0 or split >= (max_blocks * B + 15) // 16 or split < 0 else 2
-
-    def step_device(s, ev=None):
-        lp = d_lens.data_ptr() + s * lens_row
-        for l in range(L):
-            a = attn_args[l]
-            a.seq_lens = lp
-            if ev is not None:
-                ev[l][0].record(stream)
-            assert L_lib.kvp_paged_attention(ctypes.byref(a), sptr) == 0
-            if ev is not None:
-                ev[l][1].record(stream)
-
     for s in range(W):
-        step_device(s)
+        stepper.launch(s, sptr)
     torch.cuda.synchronize(dev)
-    # A step's per-layer launches are replayed from a CUDA graph (one per step: its lengths row is baked into
-    # the launches), so launch-bound small steps are not timed at the host's launch rate.
+    # A step's per-layer launches are replayed from a CUDA graph (one per step), so launch-bound small steps are
+    # not timed at the host's launch rate.
     graphs = []
     if not args.eager:
-        cap = torch.cuda.Stream(dev)
-        for s in range(W + K):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=cap, capture_error_mode="thread_local"):
-                lp = d_lens.data_ptr() + s * lens_row
-                csp = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
-                for l in range(L):
-                    a = attn_args[l]
-                    a.seq_lens = lp
-                    assert L_lib.kvp_paged_attention(ctypes.byref(a), csp) == 0
-            graphs.append(g)
+        graphs = stepper.capture(range(W + K))
         for s in range(W):
             graphs[s].replay()
         torch.cuda.synchronize(dev)
@@ -390,7 +540,7 @@ def run_ours(args, cfg, rank, world, dev):
         t_start.record(stream)
         for s in range(K):
             if args.eager:
-                step_device(W + s, evs[s])
+                stepper.launch(W + s, sptr, evs[s], stream)
             else:
                 graphs[W + s].replay()
         t_end.record(stream)
@@ -403,6 +553,13 @@ def run_ours(args, cfg, rank, world, dev):
     # algorithmic bytes per attention launch: unique K/V bytes of every context, averaged over the steps
     elem = 2
     bytes_per_launch = float(lens_all[W:].astype(np.float64).sum(axis=1).mean()) * kvh * D * 2 * elem
+    # What the CPU-baseline leg checks the last timed step against (copied out after the timed region, before
+    # the end-to-end leg moves the pools on): 16 requests, the first and the last layer.
+    sample = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        last = W + K - 1
+        sample = stepper.parity_sample(last, sorted({0, L - 1}), stepper.sample_rows(last))
+    per_rank = _per_rank_ms(ms_total, world, dev)
 
     if args.no_e2e:
         vals = torch.tensor([ms_total, ms_total, float(np.mean(attn_ms))], dtype=torch.float64, device=dev)
@@ -412,7 +569,7 @@ def run_ours(args, cfg, rank, world, dev):
         gpu_launches = K * L * per_layer
         return dict(ms_total=ms_total, e2e_ms=e2e_ms, attn_avg_ms=attn_avg, bytes_per_launch=bytes_per_launch,
                     clocks=clk.summary(), ns=ns, nb=nb, split=split, gpu_launches=gpu_launches, h2d=0, d2h=0,
-                    lens_mean=float(lens.mean())), lens
+                    lens_mean=float(lens.mean()), per_rank_ms=per_rank, sample=sample), lens
 
     # ---------------------------------------------------------------- e2e through the C ABI, host buffers
     # One kvp_decoder_step per decode step: host KVManager appends, metadata upload, new K/V and per-layer
@@ -422,7 +579,7 @@ def run_ours(args, cfg, rank, world, dev):
     h_k = torch.randn((L, ns, kvh, D), generator=torch.Generator().manual_seed(6)).to(tdt).pin_memory()
     h_v = torch.randn((L, ns, kvh, D), generator=torch.Generator().manual_seed(7)).to(tdt).pin_memory()
     h_out = torch.empty((L, ns, nh, D), dtype=tdt).pin_memory()
-    del q, knew, vnew, out, ws
+    del stepper
     torch.cuda.empty_cache()
     dec = kvb.Decoder(mgr, kc, vc, nh, max_seqs=ns, max_blocks_per_seq=max_blocks)
     for _ in range(W):
@@ -453,7 +610,8 @@ def run_ours(args, cfg, rank, world, dev):
     gpu_launches = K * L * per_layer  # the device-timed value region
     res = dict(ms_total=ms_total, e2e_ms=e2e_ms, attn_avg_ms=attn_avg, bytes_per_launch=bytes_per_launch,
                clocks=clocks, ns=ns, nb=nb, split=split, gpu_launches=gpu_launches,
-               h2d=h2d, d2h=int(h_out.numel() * 2), lens_mean=float(lens.mean()))
+               h2d=h2d, d2h=int(h_out.numel() * 2), lens_mean=float(lens.mean()), per_rank_ms=per_rank,
+               sample=sample)
     return res, lens
 
 
@@ -762,7 +920,7 @@ def run_block_mover(args, cfg):
     kvb = importlib.import_module("paged-kv-cache-manager_b200")
     L, B, kvh, D = cfg["L"], cfg["B"], cfg["kvh"], cfg["D"]
     tdt = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float16
-    nblk = 2048
+    nblk = args.pairs
     nb = 2 * nblk
     two = args.op == "migrate" and torch.cuda.device_count() >= 2
     dst_dev = torch.device("cuda", 0)
@@ -831,6 +989,128 @@ def run_block_mover(args, cfg):
     print(json.dumps(line))
 
 
+def reference_arm(args, cfg, config, metric):
+    """The reference's own CPU implementation of the path (paged_attention_cpu from the reference library built
+    here, else the oracle's C restatement) on all host cores.  A timed step is one layer of every request of
+    the shard (the same length distribution; tables draw their blocks from a shared pool of up to 16,384
+    blocks, N(0,1) fp32 data): 1/L of a decode step, so `ms_per_step` x `steps` is what actually ran, and the
+    decode rate is requests / (L x seconds per step)."""
+    import oracle
+    kind = "reference" if oracle.have_ref() else "port"
+    impl = "ref" if kind == "reference" else "c"
+    cores = os.cpu_count() or 1
+    lens = sample_lens(cfg, cfg["ns"], seed=1000)
+    pool = min(int(((lens + cfg["B"] - 1) // cfg["B"]).sum()), 16384)
+    Q, K, V, T, sl = _random_sample(cfg, lens, seed=77, pool_blocks=pool)
+    nh, kvh, D, B = cfg["nh"], cfg["kvh"], cfg["D"], cfg["B"]
+
+    def one():
+        t0 = time.perf_counter()
+        oracle.paged_attention_cpu(nh, kvh, D, B, Q, K, V, T, sl, partitions=1, nthreads=cores, impl=impl)
+        return time.perf_counter() - t0
+
+    for _ in range(args.warmup):
+        one()
+    t_run = time.perf_counter()
+    secs = [one() for _ in range(args.steps)]
+    wall = time.perf_counter() - t_run
+    per_step = float(np.mean(secs))
+    v = len(sl) / (cfg["L"] * per_step)
+    gbs = float(sl.sum()) * kvh * D * 2 * 2 / per_step / 1e9
+    cb = {"value": v, "unit": "tok/s", "cores": cores, "kind": kind, "gb_s": round(gbs, 3),
+          "sample": f"one layer of all {len(sl)} requests per step ({int(sl.sum())} context tokens; tables over a "
+                    f"shared pool of {pool} blocks), {args.steps} timed steps over {wall:.1f}s"}
+    line = {"metric": metric, "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(1e3 * per_step, 2), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1)", "config": config,
+            "impl": "reference", "cpu_baseline": cb,
+            "step": {"what": f"one layer of the decode step (1/{cfg['L']} of it) for every request, all host cores",
+                     "layers_per_decode_step": cfg["L"], "timed_wall_s": round(wall, 2),
+                     "ms_per_decode_step": round(1e3 * per_step * cfg["L"], 1)},
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    ref_gpu = reference_gpu_kernel(cfg, lens)
+    if ref_gpu is not None:
+        line["reference_gpu_kernel"] = ref_gpu
+    return line
+
+
+def run_scatter(args, cfg):
+    """The append scatter alone (kvp_append_scatter: every layer's K and V row of each new token into its
+    slot), device timed with CUDA events around each launch and L2 flushed before it (a 256 MB buffer written
+    outside the events), at two shapes of this config: `decode` -- one new token for each of the shard's
+    requests (a random slot in each of `requests` distinct random blocks) -- and `prompt` -- `prompt_rows`
+    consecutive positions of one request (its blocks a random permutation of pool ids), the prefill write.
+    Bytes: read + write of 2 (K, V) x layers x rows x kv_heads x head_dim x 2.  The line's value is the prompt
+    shape's GB/s; both shapes are checked bit-exact on a sample of rows."""
+    import torch
+    kvb = importlib.import_module("paged-kv-cache-manager_b200")
+    L, B, kvh, D = cfg["L"], cfg["B"], cfg["kvh"], cfg["D"]
+    tdt = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float16
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    prompt_rows = args.prompt_rows
+    ns = cfg["ns"]
+    nb = 2 * max(ns, (prompt_rows + B - 1) // B) + 16
+    k = torch.zeros((L, nb, B, kvh, D), dtype=tdt, device=dev)
+    v = torch.zeros_like(k)
+    rng = np.random.default_rng(3)
+    shapes = {}
+    blocks = rng.permutation(nb)[:ns]
+    shapes["decode"] = (blocks * B + rng.integers(0, B, size=ns)).astype(np.int32)
+    pos = np.arange(prompt_rows)
+    table = rng.permutation(nb)[:(prompt_rows + B - 1) // B]
+    shapes["prompt"] = (table[pos // B] * B + pos % B).astype(np.int32)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    st = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+    res = {}
+    with ClockSampler(0) as clk:
+        for name, slots in shapes.items():
+            n = len(slots)
+            g = torch.Generator(device=dev).manual_seed(5)
+            kn = torch.randn((L, n, kvh, D), generator=g, device=dev).to(tdt)
+            vn = torch.randn((L, n, kvh, D), generator=g, device=dev).to(tdt)
+            d_slots = torch.from_numpy(slots).to(dev)
+            ms = []
+            for i in range(args.warmup + args.steps):
+                flush.fill_(i & 0xff)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                kvb.append_scatter(kn, vn, k, v, d_slots, status=st, stream=stream)
+                e1.record(stream)
+                if i >= args.warmup:
+                    ms.append((e0, e1))
+            torch.cuda.synchronize(dev)
+            assert int(st.item()) == 0
+            pick = torch.from_numpy(rng.permutation(n)[:64]).to(dev)
+            sl = d_slots[pick].long()
+            assert torch.equal(k[:, sl // B, sl % B], kn[:, pick]) and torch.equal(v[:, sl // B, sl % B], vn[:, pick])
+            t = float(np.mean([a.elapsed_time(b) for a, b in ms]))
+            moved = 2 * 2 * L * n * kvh * D * 2  # read + write, K and V
+            res[name] = {"rows": n, "us_per_launch": round(t * 1e3, 2), "bytes": moved,
+                         "gb_s": round(moved / (t / 1e3) / 1e9, 1), "frac": round(moved / (t / 1e3) / 1e9 / peak, 4)}
+    line = {"metric": "append scatter bandwidth (read + write)", "value": res["prompt"]["gb_s"], "unit": "GB/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(res["prompt"]["us_per_launch"] / 1e3, 5),
+            "higher_is_better": True, "op": "scatter", "dtype": cfg["dtype"], "data": "synthetic N(0,1), seeded",
+            "config": {"workload": f"{args.config}-shaped rows ({kvh} kv heads x {D}, {L} layers, K and V): a prompt "
+                                   f"of {prompt_rows} consecutive positions (value) and a decode step of one row for "
+                                   f"each of {ns} requests",
+                       "l2": "flushed before every launch (256 MB write outside the events)"},
+            "shapes": res,
+            "roofline": {"bound": "hbm", "achieved": res["prompt"]["gb_s"], "peak": peak, "unit": "GB/s",
+                         "frac": res["prompt"]["frac"], "kernel": "append_scatter_kernel<4>",
+                         "peak_source": "measured" if "hbm_gbs" in peaks else "fallback"},
+            "gpu_launches": 2 * args.steps, "clocks": clk.summary()}
+    print(json.dumps(line))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -850,7 +1130,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--requests", type=int, default=0, help="profiling: requests per GPU (pool sized to need)")
     ap.add_argument("--layers", type=int, default=0, help="profiling: number of layers (pool sized to need)")
-    ap.add_argument("--op", default="decode", choices=["decode", "migrate", "cow", "swap", "sim", "latency"],
+    ap.add_argument("--prompt-rows", type=int, default=4096, help="scatter: positions of the prompt shape")
+    ap.add_argument("--pairs", type=int, default=2048, help="cow / migrate: block pairs per step")
+    ap.add_argument("--op", default="decode", choices=["decode", "migrate", "cow", "swap", "sim", "latency", "scatter"],
                     help="decode step (default), a whole-block mover measured alone, the scheduler-driven "
                          "data plane (sim), or the small 8-sequence case's per-call latency (latency)")
     ap.add_argument("--sim-replays", type=int, default=2, help="sim: timed replays of the decision stream")
@@ -878,23 +1160,7 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        lens = sample_lens(cfg, cfg["ns"], seed=1000)
-        for _ in range(args.warmup):
-            cpu_baseline(cfg, lens, target_s=0.5)
-        vals = [cpu_baseline(cfg, lens, target_s=max(0.5, args.cpu_seconds / max(1, args.steps)))
-                for _ in range(args.steps)]
-        v = float(np.mean([x["value"] for x in vals]))
-        cb = dict(vals[-1])
-        cb["value"] = v
-        ref_gpu = reference_gpu_kernel(cfg, lens)
-        line = {"metric": metric, "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": 1000.0 * cfg["ns"] / v, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1)",
-                "config": config, "impl": "reference", "cpu_baseline": cb,
-                "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-        if ref_gpu is not None:
-            line["reference_gpu_kernel"] = ref_gpu
-        print(json.dumps(line))
+        print(json.dumps(reference_arm(args, cfg, config, metric)))
         return
 
     if args.op == "swap":
@@ -905,6 +1171,9 @@ def main():
         return
     if args.op == "latency":
         run_latency(args)
+        return
+    if args.op == "scatter":
+        run_scatter(args, cfg)
         return
     if args.op != "decode":
         run_block_mover(args, cfg)
@@ -952,13 +1221,24 @@ def main():
                     "h2d_bytes_per_step": res["h2d"], "d2h_bytes_per_step": res["d2h"]},
             "gpu_launches": res["gpu_launches"], "clocks": res["clocks"],
             "shard": {"pool_blocks": res["nb"], "split_tiles": res["split"], "mean_context": res["lens_mean"]}}
+    if world > 1:
+        tok = [cfg["ns"] / (ms / args.steps / 1e3) for ms in res["per_rank_ms"]]
+        line["per_rank"] = {"tok_s": [round(x, 1) for x in tok],
+                            "ms_per_step": [round(ms / args.steps, 4) for ms in res["per_rank_ms"]],
+                            "imbalance_max_over_mean": round(max(res["per_rank_ms"]) /
+                                                             float(np.mean(res["per_rank_ms"])), 4)}
+    parity_ok = True
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(cfg, lens, target_s=args.cpu_seconds)
+        line["cpu_baseline"], parity = cpu_baseline(cfg, lens, target_s=args.cpu_seconds, sample=res["sample"])
+        line["parity"] = parity
+        parity_ok = parity is None or parity["ok"]
     if rank == 0:
         print(json.dumps(line))
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    if not parity_ok:
+        sys.exit("parity check of the timed step failed")
 
 
 if __name__ == "__main__":

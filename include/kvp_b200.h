@@ -119,6 +119,20 @@ typedef struct kvp_attn_args {
 KVP_API size_t kvp_attention_workspace_size(const kvp_attn_args* a);
 KVP_API int kvp_paged_attention(const kvp_attn_args* a, void* stream);
 
+/* Failure-detection test hook (no counterpart in the reference, whose nearest analogue is the simulator's
+ * livelock guard, src/simulator.cpp:136).  Every pipeline wait of the attention kernel is bounded; no valid
+ * input makes one run out, so this entry point exists to test that path without a GPU fault: it is
+ * kvp_paged_attention with each wait limited to wait_limit_cycles clock cycles (1 .. 2e9; the normal entry
+ * point uses 2e9, about a second) and, with stall_first_stage == 1, the first CTA's first pipeline stage armed
+ * for 16 bytes of a copy that is never issued -- a flag nothing sets.  That CTA's consumers give up after the
+ * limit, its producer stops issuing and waits (bounded) for the copies it did issue, the kernel ORs
+ * KVP_STATUS_TIMEOUT into `status` and returns; no copy is left in flight and the context stays usable.
+ * After KVP_STATUS_TIMEOUT from any entry point the outputs of the affected sequences are undefined and the
+ * workspace's merge counters may be nonzero: the next call on that workspace must not pass
+ * KVP_ATTN_WORKSPACE_CLEAN (without it the call clears them). */
+KVP_API int kvp_attention_wait_test(const kvp_attn_args* a, void* stream, int64_t wait_limit_cycles,
+                                    int32_t stall_first_stage);
+
 /* The same attention for callers that cannot allocate device memory -- e.g. a serving engine whose memory
  * manager reserves nearly all HBM for the KV pool and gives libraries no allocation hook, or a plugin whose
  * enqueue callback must not allocate.  This entry point has no counterpart in the reference.  It ignores

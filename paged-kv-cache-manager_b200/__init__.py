@@ -96,6 +96,7 @@ _SIGNATURES = [
     ("kvp_attention_workspace_size", _sz, [C.POINTER(AttnArgs)]),
     ("kvp_paged_attention", C.c_int, [C.POINTER(AttnArgs), _vp]),
     ("kvp_paged_attention_noalloc", C.c_int, [C.POINTER(AttnArgs), _vp]),
+    ("kvp_attention_wait_test", C.c_int, [C.POINTER(AttnArgs), _vp, _i64, _i32]),
     ("kvp_append_scatter", C.c_int, [C.POINTER(AppendArgs), _vp]),
     ("kvp_cow_copy", C.c_int, [C.POINTER(CowArgs), _vp]),
     ("kvp_migrate_blocks", C.c_int, [C.POINTER(MigrateArgs), _vp]),

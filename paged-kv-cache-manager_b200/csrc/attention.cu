@@ -13,6 +13,7 @@
 #include <vector>
 
 #include "attention_common.h"
+#include "kvp_device.cuh"
 
 // ============================================================================ host side
 namespace kvpi {
@@ -312,7 +313,11 @@ extern "C" KVP_API size_t kvp_attention_workspace_size(const kvp_attn_args* a) {
     return pl.ws_bytes;
 }
 
-extern "C" KVP_API int kvp_paged_attention(const kvp_attn_args* a, void* stream) {
+namespace {
+
+// kvp_paged_attention with every pipeline wait limited to `wait_limit` clock cycles; `stall` arms the first
+// CTA's first stage for a copy that is never issued (kvp_attention_wait_test only).
+int attention_call(const kvp_attn_args* a, void* stream, long long wait_limit, int stall) {
     using namespace kvpi;
     clear_error();
     if (!a) return fail(KVP_EINVAL, "null arguments");
@@ -410,6 +415,8 @@ extern "C" KVP_API int kvp_paged_attention(const kvp_attn_args* a, void* stream)
     prm.kvh = a->kv_heads;
     prm.early_load = (a->flags & KVP_ATTN_EARLY_LOAD) ? 1 : 0;
     prm.seq_units = pl.seq_units;
+    prm.wait_limit = wait_limit;
+    prm.stall_first_stage = stall;
     const float scale = a->scale > 0.f ? a->scale : 1.0f / std::sqrt(static_cast<float>(a->head_dim));
     prm.sl2 = scale * 1.4426950408889634f;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -417,4 +424,20 @@ extern "C" KVP_API int kvp_paged_attention(const kvp_attn_args* a, void* stream)
     if (a->kv_dtype == KVP_DTYPE_F16)
         return qres ? kvpd::launch_f16_qres(*a, pl, prm, km, vm, s) : kvpd::launch_f16(*a, pl, prm, km, vm, s);
     return qres ? kvpd::launch_bf16_qres(*a, pl, prm, km, vm, s) : kvpd::launch_bf16(*a, pl, prm, km, vm, s);
+}
+
+}  // namespace
+
+extern "C" KVP_API int kvp_paged_attention(const kvp_attn_args* a, void* stream) {
+    return attention_call(a, stream, kvpd::kWaitLimitCycles, 0);
+}
+
+extern "C" KVP_API int kvp_attention_wait_test(const kvp_attn_args* a, void* stream, int64_t wait_limit_cycles,
+                                               int32_t stall_first_stage) {
+    if (wait_limit_cycles < 1 || wait_limit_cycles > kvpd::kWaitLimitCycles || stall_first_stage < 0 ||
+        stall_first_stage > 1) {
+        kvpi::clear_error();
+        return kvpi::fail(KVP_EINVAL, "wait limit must be in [1, 2e9] cycles and stall_first_stage 0 or 1");
+    }
+    return attention_call(a, stream, wait_limit_cycles, stall_first_stage);
 }

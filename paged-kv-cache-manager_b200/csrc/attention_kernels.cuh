@@ -63,15 +63,16 @@ struct Geo {
 
 // ---------------------------------------------------------------- producer: one tile into one stage
 // All 32 lanes call this (the table cache is a warp-wide register array); lane 0 issues the copies.
-// Returns the transaction bytes the tile adds to the stage's barrier.
+// `phantom` (failure-detection test only): lane 0 arms the stage for 16 bytes and issues nothing, so the
+// stage never completes and nothing is in flight for it.
 template <int D>
 __device__ __forceinline__ void produce_tile(const AttnParams& p, const CUtensorMap* km, const CUtensorMap* vm,
                                              uint32_t kst, uint32_t vst, uint32_t fb, int tb, int len,
                                              const int32_t* trow, int kvh0, int lane, int& cache_lo,
-                                             int32_t& cached, uint32_t extra_tx) {
+                                             int32_t& cached, bool phantom) {
     using G_ = Geo<D>;
     const int nr = min(p.nruns, (len - tb + p.R - 1) / p.R);
-    if (lane == 0) mbar_arrive_expect_tx(fb, static_cast<uint32_t>(nr) * G_::NCH * 2u * p.box_tx + extra_tx);
+    if (lane == 0) mbar_arrive_expect_tx(fb, phantom ? 16u : static_cast<uint32_t>(nr) * G_::NCH * 2u * p.box_tx);
     for (int j = 0; j < nr; ++j) {
         const int tok = tb + j * p.R;
         const int bi = blk_of(p, tok);
@@ -85,7 +86,7 @@ __device__ __forceinline__ void produce_tile(const AttnParams& p, const CUtensor
             if (lane == 0) report(p.status, KVP_STATUS_BAD_BLOCK);
             row = p.oob_row;
         }
-        if (lane == 0) {
+        if (lane == 0 && !phantom) {
 #pragma unroll
             for (int c = 0; c < G_::NCH; ++c) {
                 const uint32_t off = static_cast<uint32_t>(j * G_::NCH + c) * p.box_slot;
@@ -136,13 +137,14 @@ __device__ __forceinline__ void append_new_token(const AttnParams& p, int seq, i
 // Up to 8 consecutive tiles of one sequence at once, lane k producing tile `tile + k` into stage
 // (i + k) % S: each lane waits for its own stage, arms its own barrier and issues its own copies, so the
 // per-tile issue cost is paid in parallel.  Only for one run per tile (block_size a multiple of 16).  The
-// tile counter i is passed as (st0, r0) = (i % S, i / S); nb <= S.  Returns false (after reporting) if a wait
-// gave up.
+// tile counter i is passed as (st0, r0) = (i % S, i / S); nb <= S.  Each issuing lane records its stage's round
+// in ps->issued.  Returns false (after reporting) if a wait gave up.  `phantom`: the lane of tile counter 0
+// arms its stage for 16 bytes and issues nothing (failure-detection test only).
 template <int D>
 __device__ __forceinline__ bool produce_batch(const AttnParams& p, const CUtensorMap* km, const CUtensorMap* vm,
                                               uint32_t smem_base, uint64_t* full_bar, uint64_t* empty_bar, int st0,
                                               int r0, int tile, int nb, int len, const int32_t* trow, int kvh0,
-                                              int lane, int& cache_lo, int32_t& cached) {
+                                              int lane, int& cache_lo, int32_t& cached, PipeState* ps, bool phantom) {
     using G_ = Geo<D>;
     const int S = p.stages;
     const int bi_first = blk_of(p, tile * 16);
@@ -167,15 +169,18 @@ __device__ __forceinline__ bool produce_batch(const AttnParams& p, const CUtenso
             st -= S;
             ++r;
         }
-        if (r >= 1 && !mbar_wait(smem_u32(&empty_bar[st]), static_cast<uint32_t>((r - 1) & 1))) {
+        if (r >= 1 && !mbar_wait(smem_u32(&empty_bar[st]), static_cast<uint32_t>((r - 1) & 1), p.wait_limit)) {
             report(p.status, KVP_STATUS_TIMEOUT);
             ok = false;
         }
-        if (ok) {
+        if (ok && phantom && st == 0 && r == 0) {
+            mbar_arrive_expect_tx(smem_u32(&full_bar[st]), 16u);
+        } else if (ok) {
             const uint32_t fb = smem_u32(&full_bar[st]);
             const uint32_t kst = smem_base + static_cast<uint32_t>(st) * p.stage_bytes;
             const uint32_t vst = kst + p.stage_half;
             mbar_arrive_expect_tx(fb, static_cast<uint32_t>(G_::NCH) * 2u * p.box_tx);
+            reinterpret_cast<volatile int*>(ps->issued)[st] = r + 1;
 #pragma unroll
             for (int c = 0; c < G_::NCH; ++c) {
                 const uint32_t off = static_cast<uint32_t>(c) * p.box_slot;
@@ -574,8 +579,10 @@ struct StreamSegments {
 };
 
 __device__ __forceinline__ void init_barriers(const AttnParams& p, uint64_t* full_bar, uint64_t* empty_bar,
-                                              uint64_t* qfull, uint64_t* qempty) {
+                                              uint64_t* qfull, uint64_t* qempty, PipeState* ps) {
     if (threadIdx.x == 0) {
+        ps->abort = 0;
+        for (int s = 0; s < kMaxStages + 2; ++s) ps->issued[s] = 0;
         for (int s = 0; s < p.stages; ++s) {
             mbar_init(smem_u32(&full_bar[s]), 1);
             mbar_init(smem_u32(&empty_bar[s]), static_cast<uint32_t>(p.kvh_cta));
@@ -594,8 +601,11 @@ __device__ __forceinline__ void init_barriers(const AttnParams& p, uint64_t* ful
 // is a multiple of wph, so each stage always has the same kvh_cta consumers).  At the end of a segment the
 // wph warps of a head combine their (m, l, O) lane by lane through shared memory.
 //
-// Every wait is bounded: a warp that gives up reports KVP_STATUS_TIMEOUT and then runs through the rest of
-// its control flow without waiting (so the named barriers of its partner warps are still reached).
+// Every wait is bounded: a warp that gives up reports KVP_STATUS_TIMEOUT, raises ps->abort and then runs
+// through the rest of its control flow without waiting (so the named barriers of its partner warps are still
+// reached).  The producer stops issuing once a wait gave up and, before it returns, waits (bounded) for every
+// copy it issued that no consumer waited for, so the CTA never exits with a bulk copy in flight into its
+// shared memory.
 template <int D>
 __device__ __forceinline__ void merge_rows(const AttnParams& p, size_t row0, size_t stride, int n, size_t out_off,
                                            int lane);
@@ -614,10 +624,28 @@ struct MergeShape {
     static constexpr int U = (D <= 64 && NT == 1) ? 4 : 2;
 };
 
+// After a wait gave up: lane 0 of the producer waits (bounded) for the last copy issued into each stage and
+// query slot; a stage whose last round a consumer already waited for completes at once.
+__device__ __forceinline__ void drain_copies(const AttnParams& p, PipeState* ps, uint64_t* full_bar, uint64_t* qfull,
+                                             int lane) {
+    __syncwarp();
+    if (lane == 0) {
+        const volatile int* issued = ps->issued;
+        for (int st = 0; st < p.stages + 2; ++st) {
+            const int n = issued[st < p.stages ? st : kMaxStages + (st - p.stages)];
+            if (n == 0) continue;
+            const uint32_t bar = smem_u32(st < p.stages ? &full_bar[st] : &qfull[st - p.stages]);
+            if (!mbar_wait(bar, static_cast<uint32_t>((n - 1) & 1), p.wait_limit)) report(p.status, KVP_STATUS_TIMEOUT);
+        }
+    }
+    __syncwarp();
+}
+
 template <int D, int NT, class KV, bool QLO, class Segs>
 __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap* km, const CUtensorMap* vm, Segs segs,
                                          uint8_t* dyn, uint32_t smem_base, uint64_t* full_bar, uint64_t* empty_bar,
-                                         uint64_t* qfull, uint64_t* qempty, int grp, int* pend, bool waited) {
+                                         uint64_t* qfull, uint64_t* qempty, int grp, int* pend, bool waited,
+                                         PipeState* ps) {
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int NC = p.kvh_cta * p.wph;
@@ -634,6 +662,9 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
         }
         bool ok = true;
         int pst = 0, pr = 0, j = 0;  // stage and round (i % S, i / S) of the running tile counter i
+        // failure-detection test only: this CTA's first stage is armed for a copy that is never issued
+        const bool stall = p.stall_first_stage && blockIdx.x == 0 && blockIdx.y == 0;
+        const volatile int* abort = &ps->abort;
         while (segs.next(sg)) {
             const int len = sg.len;
             const int32_t* trow = p.tables + static_cast<size_t>(sg.seq) * p.max_blocks;
@@ -644,19 +675,23 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
             auto produce_range = [&](int from, int to) {
                 for (int tile = from; tile < to;) {
                     const int nb = min(nb_max, to - tile);
+                    if (ok && *abort) ok = false;  // a consumer gave up: issue nothing more
                     if (ok) {
+                        const bool phantom = stall && pst == 0 && pr == 0;
                         if (nb_max > 1) {
                             ok = produce_batch<D>(p, km, vm, smem_base, full_bar, empty_bar, pst, pr, tile, nb, len, trow,
-                                                  kvh0, lane, cache_lo, cached);
+                                                  kvh0, lane, cache_lo, cached, ps, phantom);
                         } else {
                             const int st = pst;
-                            if (pr >= 1 && !mbar_wait(smem_u32(&empty_bar[st]), static_cast<uint32_t>((pr - 1) & 1))) {
+                            if (pr >= 1 && !mbar_wait(smem_u32(&empty_bar[st]), static_cast<uint32_t>((pr - 1) & 1),
+                                                      p.wait_limit)) {
                                 if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
                                 ok = false;
                             } else {
                                 const uint32_t kst = smem_base + static_cast<uint32_t>(st) * p.stage_bytes;
                                 produce_tile<D>(p, km, vm, kst, kst + p.stage_half, smem_u32(&full_bar[st]), tile * 16,
-                                                len, trow, kvh0, lane, cache_lo, cached, 0u);
+                                                len, trow, kvh0, lane, cache_lo, cached, phantom);
+                                if (lane == 0 && !phantom) reinterpret_cast<volatile int*>(ps->issued)[st] = pr + 1;
                             }
                         }
                         __syncwarp();
@@ -682,12 +717,15 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
             }
             if (p.q_area != 0) {
                 const int slot = j & 1;
-                if (ok && j >= 2 && !mbar_wait(smem_u32(&qempty[slot]), static_cast<uint32_t>(((j >> 1) - 1) & 1))) {
+                if (ok && *abort) ok = false;
+                if (ok && j >= 2 &&
+                    !mbar_wait(smem_u32(&qempty[slot]), static_cast<uint32_t>(((j >> 1) - 1) & 1), p.wait_limit)) {
                     if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
                     ok = false;
                 }
                 if (ok && lane == 0) {
                     const uint32_t qb = smem_u32(&qfull[slot]);
+                    reinterpret_cast<volatile int*>(ps->issued)[kMaxStages + slot] = (j >> 1) + 1;
                     mbar_arrive_expect_tx(qb, q_bytes);
                     const char* src = static_cast<const char*>(p.q) +
                                       (static_cast<size_t>(sg.seq) * p.nh + static_cast<size_t>(kvh0) * p.g) * D * qelem;
@@ -698,6 +736,7 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
             produce_range(first, sg.tile1);
             ++j;
         }
+        if (!ok || *abort) drain_copies(p, ps, full_bar, qfull, lane);
         return;
     }
     if (warp > NC) return;
@@ -720,8 +759,11 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
         const int len = sg.len;
         if (p.q_area != 0) {
             const int slot = j & 1;
-            if (ok && !mbar_wait(smem_u32(&qfull[slot]), static_cast<uint32_t>((j >> 1) & 1))) {
-                if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
+            if (ok && !mbar_wait(smem_u32(&qfull[slot]), static_cast<uint32_t>((j >> 1) & 1), p.wait_limit)) {
+                if (lane == 0) {
+                    report(p.status, KVP_STATUS_TIMEOUT);
+                    *reinterpret_cast<volatile int*>(&ps->abort) = 1;
+                }
                 ok = false;
             }
             if (ok) cs.load_q_smem(p, dyn + p.q_off + static_cast<size_t>(slot) * p.q_area, head, lane);
@@ -740,8 +782,11 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
             }
             if (++turn == p.wph) turn = 0;
             if (!ok || !mine) continue;
-            if (!mbar_wait(smem_u32(&full_bar[st]), static_cast<uint32_t>(ph))) {
-                if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
+            if (!mbar_wait(smem_u32(&full_bar[st]), static_cast<uint32_t>(ph), p.wait_limit)) {
+                if (lane == 0) {
+                    report(p.status, KVP_STATUS_TIMEOUT);
+                    *reinterpret_cast<volatile int*>(&ps->abort) = 1;
+                }
                 ok = false;
                 continue;
             }
@@ -822,6 +867,7 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
     __shared__ __align__(8) uint64_t full_bar[kMaxStages];
     __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
     __shared__ __align__(8) uint64_t qfull[2], qempty[2];
+    __shared__ PipeState ps;
     extern __shared__ uint8_t dyn_smem[];
 
     const int seq = blockIdx.x / p.groups;
@@ -844,7 +890,7 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
     }
     if (split >= nsplit) return;
     const uint32_t base_off = ((smem_u32(dyn_smem) + 1023u) & ~1023u) - smem_u32(dyn_smem);
-    init_barriers(p, full_bar, empty_bar, qfull, qempty);
+    init_barriers(p, full_bar, empty_bar, qfull, qempty, &ps);
     SplitSegments segs;
     segs.seg.seq = seq;
     segs.seg.len = len;
@@ -856,7 +902,7 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
     segs.seg.nseg = 0;
     segs.done = false;
     cta_body<D, NT, KV, QLO>(p, &kmap, &vmap, segs, dyn_smem + base_off, smem_u32(dyn_smem) + base_off, full_bar,
-                        empty_bar, qfull, qempty, grp, nullptr, true);
+                        empty_bar, qfull, qempty, grp, nullptr, true, &ps);
 }
 
 // ---------------------------------------------------------------- stream-K schedule
@@ -922,6 +968,7 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
     __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
     __shared__ __align__(8) uint64_t qfull[2], qempty[2];
     __shared__ int32_t warp_tot[32];
+    __shared__ PipeState ps;
     extern __shared__ uint8_t dyn_smem[];
 
     // Let the next kernel on the stream (a programmatic dependent launch) be scheduled now: its CTAs then take
@@ -950,7 +997,7 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
     segs.nh = p.nh;
     __shared__ int pend[8];  // merge flags and coordinates of the CTA's split segments
     if (threadIdx.x < 2) pend[threadIdx.x] = 0;
-    init_barriers(p, full_bar, empty_bar, qfull, qempty);  // (its barrier also publishes pend)
+    init_barriers(p, full_bar, empty_bar, qfull, qempty, &ps);  // (its barrier also publishes pend)
     // Everything above reads only seq_lens and shared memory; with an early start (programmatic dependent
     // launch) it overlaps the previous kernel's tail.  What follows may read what that kernel wrote or write
     // what it reads, so it waits for it -- with an early load, the producer warps first issue their CTA's
@@ -974,7 +1021,7 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
     }
     if (c >= Ge) return;
     cta_body<D, NT, KV, QLO>(p, &kmap, &vmap, segs, dyn_smem + base_off, smem_u32(dyn_smem) + base_off, full_bar,
-                        empty_bar, qfull, qempty, grp, pend, waited);
+                        empty_bar, qfull, qempty, grp, pend, waited, &ps);
 }
 
 // ---------------------------------------------------------------- merges

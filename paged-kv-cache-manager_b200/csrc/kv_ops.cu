@@ -15,7 +15,12 @@
 namespace kvpd {
 
 // ---------------------------------------------------------------- append scatter
-// One 16-byte unit per thread-iteration: unit u of (layer, seq, K|V).  Row of a token = kv_heads*D elems.
+// A group of 2^lpr_shift lanes copies one token row (kv_heads * head_dim elements, row_u 16-byte units) of K
+// and of V for one (layer, sequence): the slot is loaded once per row, every lane keeps up to U units of K and
+// U of V in flight before it stores them, and no index needs an integer division.  Grid: x strides over row
+// groups, y over layers.  Rows are copied whole, so for a decode step (one row per sequence, 2 KB at the
+// Llama-3-8B head shape) and for a prompt (consecutive positions: rows contiguous within a block) every store
+// fills whole 128-byte lines.
 struct AppendParams {
     const uint4* k_new;
     const uint4* v_new;
@@ -26,28 +31,52 @@ struct AppendParams {
     long long layer_stride_u;  // 16-byte units between layer pools
     long long num_slots;       // num_blocks * block_size (0: unchecked)
     int num_layers, num_seqs, row_u;  // row_u: 16-byte units per token row
+    int lpr_shift;                    // log2(lanes per row), at most 5
 };
 
+template <int U>
 __global__ void __launch_bounds__(256) append_scatter_kernel(const AppendParams p) {
-    const long long per_layer = static_cast<long long>(p.num_seqs) * p.row_u;
-    const long long total = per_layer * p.num_layers;
-    for (long long u = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; u < total;
-         u += static_cast<long long>(gridDim.x) * blockDim.x) {
-        const int layer = static_cast<int>(u / per_layer);
-        const long long r = u - layer * per_layer;
-        const int seq = static_cast<int>(r / p.row_u);
-        const int e = static_cast<int>(r - static_cast<long long>(seq) * p.row_u);
-        const int slot = __ldg(p.slots + seq);
-        if (slot < 0) continue;
-        if (p.num_slots > 0 && slot >= p.num_slots) {
-            if (e == 0 && layer == 0) report(p.status, KVP_STATUS_BAD_BLOCK);
-            continue;
+    const int lane = threadIdx.x & 31;
+    const int lpr = 1 << p.lpr_shift;
+    const int el = lane & (lpr - 1);
+    const int rows_per_warp = 32 >> p.lpr_shift;
+    const int warps = blockDim.x >> 5;
+    const int first = (blockIdx.x * warps + (threadIdx.x >> 5)) * rows_per_warp + (lane >> p.lpr_shift);
+    const int stride = gridDim.x * warps * rows_per_warp;
+    for (int layer = blockIdx.y; layer < p.num_layers; layer += gridDim.y) {
+        const long long src_layer = static_cast<long long>(layer) * p.num_seqs * p.row_u;
+        const long long dst_layer = static_cast<long long>(layer) * p.layer_stride_u;
+        for (int seq = first; seq < p.num_seqs; seq += stride) {
+            const int slot = __ldg(p.slots + seq);
+            if (slot < 0) continue;
+            if (p.num_slots > 0 && slot >= p.num_slots) {
+                if (el == 0 && layer == 0) report(p.status, KVP_STATUS_BAD_BLOCK);
+                continue;
+            }
+            const uint4* ks = p.k_new + src_layer + static_cast<long long>(seq) * p.row_u;
+            const uint4* vs = p.v_new + src_layer + static_cast<long long>(seq) * p.row_u;
+            uint4* kd = p.k_cache + dst_layer + static_cast<long long>(slot) * p.row_u;
+            uint4* vd = p.v_cache + dst_layer + static_cast<long long>(slot) * p.row_u;
+            for (int e0 = el; e0 < p.row_u; e0 += lpr * U) {
+                uint4 kb[U], vb[U];
+#pragma unroll
+                for (int k = 0; k < U; ++k) {
+                    const int e = e0 + k * lpr;
+                    if (e < p.row_u) {
+                        kb[k] = __ldcs(ks + e);  // read once: do not keep the new rows in L2
+                        vb[k] = __ldcs(vs + e);
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < U; ++k) {
+                    const int e = e0 + k * lpr;
+                    if (e < p.row_u) {
+                        kd[e] = kb[k];  // default policy: the attention that follows may find the row in L2
+                        vd[e] = vb[k];
+                    }
+                }
+            }
         }
-        const long long dst = layer * p.layer_stride_u + static_cast<long long>(slot) * p.row_u + e;
-        const uint4 kx = __ldg(p.k_new + u);
-        const uint4 vx = __ldg(p.v_new + u);
-        p.k_cache[dst] = kx;
-        p.v_cache[dst] = vx;
     }
 }
 
@@ -108,12 +137,6 @@ long long resolve_layer_stride(long long given, long long num_blocks, int block_
     return given > 0 ? given : num_blocks * block_size * kvh * static_cast<long long>(D);
 }
 
-int grid_for(long long work_units, int threads) {
-    const long long want = (work_units + threads - 1) / threads;
-    const long long cap = static_cast<long long>(sm_count()) * 16;
-    return static_cast<int>(std::max<long long>(1, std::min(want, cap)));
-}
-
 }  // namespace
 }  // namespace kvpi
 
@@ -147,8 +170,15 @@ extern "C" KVP_API int kvp_append_scatter(const kvp_append_args* a, void* stream
     p.num_layers = a->num_layers;
     p.num_seqs = a->num_seqs;
     p.row_u = static_cast<int>(row_bytes / 16);
-    const long long units = static_cast<long long>(a->num_layers) * a->num_seqs * p.row_u;
-    kvpd::append_scatter_kernel<<<grid_for(units, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+    // lanes per row: the largest power of two <= min(32, row_u)
+    p.lpr_shift = 0;
+    while (p.lpr_shift < 5 && (2 << p.lpr_shift) <= p.row_u) ++p.lpr_shift;
+    const int threads = 256, rows_per_block = (threads / 32) * (32 >> p.lpr_shift);
+    const int gy = std::min(a->num_layers, 65535);
+    const long long want_x = (static_cast<long long>(a->num_seqs) + rows_per_block - 1) / rows_per_block;
+    const long long cap_x = std::max<long long>(1, (static_cast<long long>(sm_count()) * 32 + gy - 1) / gy);
+    const dim3 grid(static_cast<unsigned>(std::min(want_x, cap_x)), static_cast<unsigned>(gy));
+    kvpd::append_scatter_kernel<4><<<grid, threads, 0, static_cast<cudaStream_t>(stream)>>>(p);
     return cuda_status(cudaGetLastError(), "append scatter launch");
 }
 

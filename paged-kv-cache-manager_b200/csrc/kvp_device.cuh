@@ -128,16 +128,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 // Waits for phase `parity` of the barrier to complete.  Gives up after about `limit` clock cycles
-// (roughly a second at B200 clocks) and returns false, so a broken pipeline ends the kernel with an error
-// status instead of hanging the GPU.
+// (kWaitLimitCycles: roughly a second at B200 clocks) and returns false, so a broken pipeline ends the kernel
+// with an error status instead of hanging the GPU.
 constexpr long long kWaitLimitCycles = 2000000000LL;
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, long long limit) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     while (true) {
         for (int i = 0; i < 64; ++i)
             if (mbar_try_wait(bar, parity)) return true;
-        if (clock64() - t0 > kWaitLimitCycles) return false;
+        if (clock64() - t0 > limit) return false;
     }
 }
 
