@@ -59,9 +59,12 @@ KVP_API const char* kvp_version(void);
  * Replaces the reference's GPU entry point launch_paged_attention (cuda/paged_attention.cuh:16-19) and is
  * the device form of paged_attention_cpu / reference_attention (include/kvpage/paged_attention.h:25-35,
  * src/paged_attention.cpp:25-114): one query token per sequence, softmax(q.K^T * scale) V over the
- * sequence's context, read in place through its block table.  fp32 accumulation; K/V fp16 or bf16;
- * q and out fp32, fp16 or bf16.  Requirements: head_dim in {32, 64, 96, 128, 256}; num_heads % kv_heads
- * == 0; num_heads / kv_heads <= 16; block_size >= 1; 16-byte aligned pools. */
+ * sequence's context, read in place through its block table.  fp32 accumulation; q and out fp32, fp16 or
+ * bf16.  K/V fp16 or bf16 (16-byte aligned pools): the tensor-core kernel, with the split schedules below.
+ * K/V fp32 (the reference's own float layout; 4-byte aligned pools): a CUDA-core kernel in fp32 arithmetic,
+ * one CTA per (sequence, kv head), no workspace, no fused append, the tuning fields ignored.
+ * Requirements: head_dim in {32, 64, 96, 128, 256}; num_heads % kv_heads == 0; num_heads / kv_heads <= 16
+ * (<= 8 at head_dim 256); block_size >= 1. */
 typedef struct kvp_attn_args {
     const void* q;
     int32_t q_dtype;
@@ -118,6 +121,23 @@ typedef struct kvp_attn_args {
  * kernel. */
 KVP_API size_t kvp_attention_workspace_size(const kvp_attn_args* a);
 KVP_API int kvp_paged_attention(const kvp_attn_args* a, void* stream);
+
+/* Host-buffer attention with the parameter list of the reference's CPU entry points, reference_attention and
+ * paged_attention_cpu (include/kvpage/paged_attention.h:25-35 of the reference; their callers are
+ * tests/test_attention.cpp and the Python binding python/kvpage_py.cpp:43-66).  Host pointers: fp32 q and out
+ * [num_seqs][num_heads][head_dim]; fp32 k_cache / v_cache [num_blocks][block_size][kv_heads][head_dim], of which
+ * the blocks up to the largest id the sequences' table entries use are read; int32 block_tables
+ * [num_seqs][max_blocks] and seq_lens [num_seqs].  The reference's checks give KVP_EINVAL with its messages
+ * (num_heads % kv_heads != 0; a seq_len < 1 or longer than max_blocks blocks; partitions < 1), a negative
+ * block id KVP_EBOUNDS.  The computation runs on the current device -- the fp32 CUDA-core kernel, no CPU
+ * path: the inputs are copied in, the outputs copied back, and the call returns once `out` is written
+ * (synchronous, like the reference).  Unlike the device entry points it allocates the device buffers it
+ * needs and frees them before returning.  `partitions` is the reference's parameter (checked >= 1); the
+ * kernel's own split of the context does not depend on it. */
+KVP_API int kvp_paged_attention_host(int32_t num_heads, int32_t kv_heads, int32_t head_dim, int32_t block_size,
+                                     int32_t num_seqs, int32_t max_blocks, const float* q, const float* k_cache,
+                                     const float* v_cache, const int32_t* block_tables, const int32_t* seq_lens,
+                                     float* out, int32_t partitions);
 
 /* Failure-detection test hook (no counterpart in the reference, whose nearest analogue is the simulator's
  * livelock guard, src/simulator.cpp:136).  Every pipeline wait of the attention kernel is bounded; no valid

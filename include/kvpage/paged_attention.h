@@ -3,7 +3,7 @@
 // The reference declares its CPU implementations here (include/kvpage/paged_attention.h:8-35:
 // AttnShape, reference_attention, paged_attention_cpu).  This library keeps AttnShape and the layout
 // contract unchanged and provides the device implementation behind the same shape description; it runs
-// only on the GPU (there is no CPU fallback) and forwards to kvp_paged_attention in kvp_b200.h.
+// only on the GPU (there is no CPU fallback) and forwards to the C ABI in kvp_b200.h.
 //
 // Layouts (row-major, contiguous), unchanged from the reference:
 //   q, out        [num_seqs][num_heads][head_dim]
@@ -37,5 +37,19 @@ KVPAGE_EXPORT void paged_attention(const AttnShape& s, int num_seqs, int max_blo
                      const void* k_cache, const void* v_cache, DType kv_dtype, int64_t num_blocks,
                      const int32_t* block_tables, const int32_t* seq_lens, void* out, DType out_dtype,
                      void* workspace = nullptr, size_t workspace_bytes = 0, void* stream = nullptr);
+
+// The reference's two entry points with their exact parameter lists (include/kvpage/paged_attention.h:25-35 of
+// the reference), so its callers -- tests/test_attention.cpp, python/kvpage_py.cpp -- link unchanged.  Host
+// buffers, fp32 throughout; both run the same device path (kvp_paged_attention_host: copy in, the fp32
+// CUDA-core kernel, copy out) and return once `out` is written.  The reference's checks throw
+// std::invalid_argument with its messages ("num_heads % kv_heads != 0", "bad seq_len", "partitions < 1"), as
+// does a negative block id; a CUDA failure throws std::runtime_error.  `partitions` is checked (>= 1) but does
+// not change the result beyond float rounding: the kernel splits the context its own way.
+KVPAGE_EXPORT void reference_attention(const AttnShape& s, int num_seqs, int max_blocks, const float* q,
+                                       const float* k_cache, const float* v_cache, const int32_t* block_tables,
+                                       const int32_t* seq_lens, float* out);
+KVPAGE_EXPORT void paged_attention_cpu(const AttnShape& s, int num_seqs, int max_blocks, const float* q,
+                                       const float* k_cache, const float* v_cache, const int32_t* block_tables,
+                                       const int32_t* seq_lens, float* out, int partitions);
 
 }  // namespace kvp

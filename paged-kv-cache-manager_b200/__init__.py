@@ -97,6 +97,7 @@ _SIGNATURES = [
     ("kvp_paged_attention", C.c_int, [C.POINTER(AttnArgs), _vp]),
     ("kvp_paged_attention_noalloc", C.c_int, [C.POINTER(AttnArgs), _vp]),
     ("kvp_attention_wait_test", C.c_int, [C.POINTER(AttnArgs), _vp, _i64, _i32]),
+    ("kvp_paged_attention_host", C.c_int, [_i32] * 6 + [_vp] * 6 + [_i32]),
     ("kvp_append_scatter", C.c_int, [C.POINTER(AppendArgs), _vp]),
     ("kvp_cow_copy", C.c_int, [C.POINTER(CowArgs), _vp]),
     ("kvp_migrate_blocks", C.c_int, [C.POINTER(MigrateArgs), _vp]),
@@ -460,6 +461,28 @@ def paged_attention(q, k_cache, v_cache, block_tables, seq_lens, num_heads: int,
     if early_load:
         a.flags |= KVP_ATTN_EARLY_LOAD
     _launch(dev, lib().kvp_paged_attention, a, stream)
+    return out
+
+
+def paged_attention_host(num_heads: int, kv_heads: int, head_dim: int, block_size: int, q, k_cache, v_cache,
+                         block_tables, seq_lens, partitions: int = 1):
+    """kvp_paged_attention_host: the reference's CPU attention signature (host arrays, fp32) on the device path
+    of the current CUDA device -- copy in, the fp32 CUDA-core kernel, copy out.  q [ns][nh][D], k/v
+    [num_blocks][B][kvh][D], tables [ns][max_blocks] int32, lens [ns] int32; returns out [ns][nh][D] (numpy,
+    fp32).  The reference's argument checks raise ValueError, as its binding's std::invalid_argument does."""
+    import numpy as np
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    k = np.ascontiguousarray(k_cache, dtype=np.float32)
+    v = np.ascontiguousarray(v_cache, dtype=np.float32)
+    t = np.ascontiguousarray(block_tables, dtype=np.int32)
+    n = np.ascontiguousarray(seq_lens, dtype=np.int32)
+    out = np.empty(q.shape, dtype=np.float32)
+    rc = lib().kvp_paged_attention_host(num_heads, kv_heads, head_dim, block_size, q.shape[0],
+                                        t.shape[1] if t.ndim == 2 else 0, q.ctypes.data, k.ctypes.data,
+                                        v.ctypes.data, t.ctypes.data, n.ctypes.data, out.ctypes.data, partitions)
+    if rc in (KVP_EINVAL, KVP_EBOUNDS):
+        raise ValueError(last_error())
+    _check(rc)
     return out
 
 

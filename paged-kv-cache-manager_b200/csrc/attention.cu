@@ -307,7 +307,7 @@ int plan_attention(const kvp_attn_args& a, bool have_workspace, AttnPlan* out) {
 }  // namespace kvpi
 
 extern "C" KVP_API size_t kvp_attention_workspace_size(const kvp_attn_args* a) {
-    if (!a) return 0;
+    if (!a || a->kv_dtype == KVP_DTYPE_F32) return 0;
     kvpi::AttnPlan pl;
     if (kvpi::plan_attention(*a, true, &pl) != KVP_OK) return 0;
     return pl.ws_bytes;
@@ -321,11 +321,11 @@ int attention_call(const kvp_attn_args* a, void* stream, long long wait_limit, i
     using namespace kvpi;
     clear_error();
     if (!a) return fail(KVP_EINVAL, "null arguments");
-    if (!valid_dtype(a->q_dtype) || !valid_dtype(a->out_dtype) ||
-        !(a->kv_dtype == KVP_DTYPE_F16 || a->kv_dtype == KVP_DTYPE_BF16))
-        return fail(KVP_EINVAL, "unsupported dtype (K/V must be fp16 or bf16)");
+    if (!valid_dtype(a->q_dtype) || !valid_dtype(a->out_dtype) || !valid_dtype(a->kv_dtype))
+        return fail(KVP_EINVAL, "unsupported dtype");
     if (a->num_seqs > 0 && (!a->q || !a->k_cache || !a->v_cache || !a->block_tables || !a->seq_lens || !a->out))
         return fail(KVP_EINVAL, "null buffer");
+    if (a->kv_dtype == KVP_DTYPE_F32) return launch_attention_f32(*a, static_cast<cudaStream_t>(stream));
     if (!aligned16(a->k_cache) || !aligned16(a->v_cache)) return fail(KVP_EINVAL, "K/V pools must be 16-byte aligned");
     if ((a->k_new == nullptr) != (a->v_new == nullptr)) return fail(KVP_EINVAL, "k_new and v_new go together");
     if (a->k_new) {

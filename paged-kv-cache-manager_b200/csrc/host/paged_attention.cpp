@@ -1,6 +1,8 @@
-// C++ entry points of the device attention path; both forward to the C ABI (kvp_paged_attention).
+// C++ entry points of the device attention path; all forward to the C ABI.
 //   kvp::paged_attention  -- device form of the reference's paged_attention entry points
 //                            (include/kvpage/paged_attention.h:25-35 of the reference)
+//   kvp::reference_attention / kvp::paged_attention_cpu -- the reference's host-buffer signatures, on the
+//                            device path (kvp_paged_attention_host)
 //   launch_paged_attention -- same signature and error behaviour as the reference's GPU entry point
 //                            (cuda/paged_attention.cuh:16-19, cuda/paged_attention.cu:100-115)
 #include "kvpage/paged_attention.h"
@@ -44,6 +46,30 @@ void paged_attention(const AttnShape& s, int num_seqs, int max_blocks, const voi
     const int rc = kvp_paged_attention(&a, stream);
     if (rc == KVP_EINVAL || rc == KVP_ENOSPACE) throw std::invalid_argument(kvp_last_error());
     if (rc != KVP_OK) throw std::runtime_error(kvp_last_error());
+}
+
+namespace {
+
+void host_attention(const AttnShape& s, int num_seqs, int max_blocks, const float* q, const float* k_cache,
+                    const float* v_cache, const int32_t* block_tables, const int32_t* seq_lens, float* out,
+                    int partitions) {
+    const int rc = kvp_paged_attention_host(s.num_heads, s.kv_heads, s.head_dim, s.block_size, num_seqs, max_blocks,
+                                            q, k_cache, v_cache, block_tables, seq_lens, out, partitions);
+    if (rc == KVP_EINVAL || rc == KVP_EBOUNDS) throw std::invalid_argument(kvp_last_error());
+    if (rc != KVP_OK) throw std::runtime_error(kvp_last_error());
+}
+
+}  // namespace
+
+void reference_attention(const AttnShape& s, int num_seqs, int max_blocks, const float* q, const float* k_cache,
+                         const float* v_cache, const int32_t* block_tables, const int32_t* seq_lens, float* out) {
+    host_attention(s, num_seqs, max_blocks, q, k_cache, v_cache, block_tables, seq_lens, out, 1);
+}
+
+void paged_attention_cpu(const AttnShape& s, int num_seqs, int max_blocks, const float* q, const float* k_cache,
+                         const float* v_cache, const int32_t* block_tables, const int32_t* seq_lens, float* out,
+                         int partitions) {
+    host_attention(s, num_seqs, max_blocks, q, k_cache, v_cache, block_tables, seq_lens, out, partitions);
 }
 
 }  // namespace kvp

@@ -57,5 +57,7 @@ struct AttnPlan {
     size_t ws_cnt_off = 0;  // stream-K: byte offset of the per-sequence segment counters (a fixed-size region)
 };
 int plan_attention(const kvp_attn_args& a, bool have_workspace, AttnPlan* plan);
+// fp32 K/V pools: the CUDA-core kernel (attention_f32.cu); needs no workspace.
+int launch_attention_f32(const kvp_attn_args& a, cudaStream_t s);
 
 }  // namespace kvpi

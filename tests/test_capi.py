@@ -29,7 +29,12 @@ def test_cxx_drop_in_symbols_exported(kvb):
     for sym in ("kvp::KVManager::append_token(long)", "kvp::KVManager::admit_with_prefix(long, long, int, int)",
                 "kvp::KVManager::fork(long, long)", "kvp::KVManager::free(long)",
                 "kvp::BlockAllocator::allocate()", "launch_paged_attention(",
-                "kvp::paged_attention(kvp::AttnShape const&"):
+                "kvp::paged_attention(kvp::AttnShape const&",
+                # the reference's host-buffer attention signatures (include/kvpage/paged_attention.h:25-35)
+                "kvp::reference_attention(kvp::AttnShape const&, int, int, float const*, float const*, float const*, "
+                "int const*, int const*, float*)",
+                "kvp::paged_attention_cpu(kvp::AttnShape const&, int, int, float const*, float const*, float const*, "
+                "int const*, int const*, float*, int)"):
         assert sym in out, sym
     # nothing from the statically linked CUDA runtime leaks out of the library
     assert " cudaMalloc" not in out
@@ -52,7 +57,9 @@ def _args(kvb, **kw):
 
 
 @pytest.mark.parametrize("bad", [dict(head_dim=48), dict(kv_heads=3), dict(num_heads=40, kv_heads=2),
-                                 dict(kv_dtype=0), dict(q_dtype=7), dict(block_size=0), dict(k_cache=(1 << 20) + 2)])
+                                 dict(kv_dtype=9), dict(q_dtype=7), dict(block_size=0), dict(k_cache=(1 << 20) + 2),
+                                 dict(kv_dtype=0, k_new=1 << 20, v_new=1 << 20), dict(kv_dtype=0, head_dim=48),
+                                 dict(kv_dtype=0, k_cache=(1 << 20) + 2)])
 def test_attention_rejects_invalid_arguments(kvb, bad):
     L = kvb.lib()
     rc = L.kvp_paged_attention(C.byref(_args(kvb, **bad)), None)
@@ -208,3 +215,4 @@ def test_header_is_plain_c_and_drives_the_manager(kvb, tmp_path):
     assert out[len(want)].startswith("dup ") and int(out[len(want)].split()[1]) < 0
     assert out[len(want) + 1] == "msg set"
     assert len(pairs) == 1  # the fork's first append copied the shared partial block
+
