@@ -158,9 +158,13 @@ KVP_API int kvp_attention_wait_test(const kvp_attn_args* a, void* stream, int64_
  * enqueue callback must not allocate.  This entry point has no counterpart in the reference.  It ignores
  * a->workspace and keeps the split partials in a fixed KVP_NOALLOC_SCRATCH_BYTES device array built into the
  * library (held by every GPU that loads it, until exit); it calls no allocator.  The array's device address
- * is looked up on the first call made on each device, so make that first call before any stream capture.
- * With split_tiles == 0 the splits are coarsened until the partials fit; an explicit split_tiles whose
- * partials exceed the array returns KVP_ENOSPACE.  KVP_ATTN_WORKSPACE_CLEAN is ignored: every call clears the
+ * is looked up on the first call made in each CUDA context (the first call on a device, and again after a
+ * cudaDeviceReset gives the device a new context), so make that first call before any stream capture.
+ * With split_tiles == 0 the balanced schedule is used while its partials fit -- they need
+ * 8192 * (kv_heads / kv_heads_per_cta) * 4 B of counters plus (SMs * CTAs per SM + num_seqs) * num_heads *
+ * (head_dim + 2) * 4 B, rounded up to 256 B each -- and beyond that the call switches to fixed splits of 16,
+ * 32, 64, ... tiles until their partials fit (at the Llama-3-8B head shape, 32/8 heads of 128, from about
+ * 1,900 sequences per call); an explicit split_tiles whose partials exceed the array returns KVP_ENOSPACE.  KVP_ATTN_WORKSPACE_CLEAN is ignored: every call clears the
  * merge counters it uses.  All calls share the array: calls that overlap on the GPU race and must be
  * serialised by the caller. */
 #define KVP_NOALLOC_SCRATCH_BYTES (32u << 20)

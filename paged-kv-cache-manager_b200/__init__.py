@@ -25,6 +25,7 @@ KVP_STATUS_BAD_BLOCK, KVP_STATUS_BAD_LEN, KVP_STATUS_TIMEOUT = 1, 2, 4
 KVP_ATTN_WORKSPACE_CLEAN = 1
 KVP_ATTN_EARLY_START = 2
 KVP_ATTN_EARLY_LOAD = 4
+KVP_NOALLOC_SCRATCH_BYTES = 32 << 20  # the no-allocation entry point's fixed scratch array
 F32, F16, BF16 = 0, 1, 2
 NO_REQUEST = -1
 STATS_FIELDS = ("requests", "used_tokens", "allocated_blocks", "allocated_slots", "internal_waste",

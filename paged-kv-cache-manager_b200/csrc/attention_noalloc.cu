@@ -9,12 +9,15 @@
 // library, so the call itself allocates nothing.
 //
 // The array is KVP_NOALLOC_SCRATCH_BYTES (32 MiB) of device memory that every GPU which loads the library
-// holds until the process exits.  Its device address is looked up once per device, on the first call made
-// with that device current, so that first call should come before any stream capture.  All calls share the
+// holds until the process exits.  Its device address is looked up on the first call made in each CUDA context
+// (the first call on a device, and again after cudaDeviceReset or a re-created primary context gives the
+// device a new context, where the module -- and the array -- may sit at a new address), so that first call
+// should come before any stream capture.  All calls share the
 // array and it keeps whatever the last call left there: the only words that must start at zero, the merge
 // counters of the balanced schedule, are cleared on the stream by every call (every split writes its partials
 // before the merge reads them), and two calls that overlap on the GPU -- on different streams, or from
 // different threads -- race on it and must be serialised by the caller.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -33,23 +36,56 @@ constexpr int kMaxDevices = 64;
 // cudaGetSymbolAddress below.
 static __device__ __align__(256) unsigned char g_split_scratch[kScratchBytes];
 
-void* g_scratch_addr[kMaxDevices] = {};
+// The scratch address found for a device, and the unique id of the context it was found in.
+struct ScratchEntry {
+    unsigned long long ctx_id = 0;
+    void* addr = nullptr;
+};
+ScratchEntry g_scratch[kMaxDevices];
 std::mutex g_scratch_mu;
 
-// Device address of the scratch array on the current device, looked up on first use per device.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+// Unique id of the current context (0 when there is none yet, or the driver cannot say).
+unsigned long long current_context_id() {
+    static CtxGetCurrentFn get_current = nullptr;
+    static CtxGetIdFn get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<CtxGetCurrentFn>(f);
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<CtxGetIdFn>(f);
+    });
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (get_current && get_id && get_current(&ctx) == CUDA_SUCCESS && ctx && get_id(ctx, &id) == CUDA_SUCCESS) return id;
+    return 0;
+}
+
+// Device address of the scratch array in the current context: looked up on the first call in each context
+// (without a context id from the driver, on every call).
 int scratch_address(void** out) {
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return kvpi::cuda_status(e, "cudaGetDevice");
     if (dev < 0 || dev >= kMaxDevices) return kvpi::fail(KVP_EINVAL, "device index outside the supported range");
     std::lock_guard<std::mutex> lock(g_scratch_mu);
-    if (!g_scratch_addr[dev]) {
+    unsigned long long id = current_context_id();
+    if (id == 0 || g_scratch[dev].ctx_id != id || !g_scratch[dev].addr) {
         void* p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_split_scratch);
+        e = cudaGetSymbolAddress(&p, g_split_scratch);  // also makes the device's primary context current
         if (e != cudaSuccess) return kvpi::cuda_status(e, "cudaGetSymbolAddress(split scratch)");
-        g_scratch_addr[dev] = p;
+        if (id == 0) id = current_context_id();
+        g_scratch[dev].ctx_id = id;
+        g_scratch[dev].addr = p;
     }
-    *out = g_scratch_addr[dev];
+    *out = g_scratch[dev].addr;
     return KVP_OK;
 }
 

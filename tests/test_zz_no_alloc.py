@@ -76,7 +76,7 @@ def test_no_alloc_automatic_split_fits_and_oversize_is_rejected(kvb, cuda):
     import torch
     args = _inputs(3, [5000] * 40)
     want = _with_workspace(kvb, *args, 1)
-    got = _no_alloc(kvb, *args, 0)  # automatic: coarsened to fit the fixed scratch
+    got = _no_alloc(kvb, *args, 0)  # automatic: the balanced schedule's partials fit the fixed scratch
     _close(got, want)
     # one tile per split: 40 x 313 splits x 32 heads x (D + 2) floats is beyond the 32 MiB array
     q, k, v, t, l, nh, kvh = args
@@ -103,3 +103,22 @@ def test_no_alloc_balanced_call_after_fixed_splits(kvb, cuda):
     assert rc == 0, kvb.last_error()
     torch.cuda.synchronize()
     _close(out, want)
+
+
+def test_no_alloc_coarsens_when_balanced_partials_do_not_fit(kvb, cuda):
+    # 2,500 short sequences at the Llama-3-8B head shape: the balanced schedule would need about 44 MB of partials,
+    # more than the 32 MiB array, so the automatic call switches to fixed splits coarse enough to fit.
+    import torch
+    lens = np.random.default_rng(6).integers(200, 400, size=2500).tolist()
+    args = _inputs(6, lens)
+    q, k, v, t, l, nh, kvh = args
+    probe = kvb.attention_args(q, k, v, t, l, torch.empty(q.shape, dtype=torch.float32, device=q.device), nh, kvh)
+    assert kvb.workspace_bytes(probe) > kvb.KVP_NOALLOC_SCRATCH_BYTES
+    fits = []
+    for split in (16, 32, 64, 128):
+        probe.split_tiles = split
+        fits.append(kvb.workspace_bytes(probe) <= kvb.KVP_NOALLOC_SCRATCH_BYTES)
+    assert any(fits)
+    want = _with_workspace(kvb, *args, 0)
+    for _ in range(2):
+        _close(_no_alloc(kvb, *args, 0), want)
