@@ -911,6 +911,325 @@ def run_latency(args):
     print(json.dumps(line))
 
 
+class OpMix:
+    """The KV-management op mix on one GPU (BASELINE config 5 at its stated scale by default): a shared
+    `prefix`-token prompt admitted once (the parent), `requests` requests admitted with admit_with_prefix on it
+    (prompt = prefix + a seeded suffix of 1..255 tokens, never block-aligned, so the request's last block is
+    partial), each forked into `samples` samples (the request plus samples - 1 forks); then decode steps: every
+    live sample appends one token (KVManager.append_batch on the host), the copy-on-write pairs those appends
+    decided are copied (kvp_cow_copy; the first append of all but one of the samples sharing a partial block),
+    and every sample's new K/V row of every layer is written to its slot (kvp_append_scatter).  After every
+    `swap_every`-th step, samples drawn at random (seeded) until their tables hold `swap_frac` of the allocated
+    blocks are swapped out to a pinned host pool (kvp_swap_out on a side stream, then freed, as the reference's
+    simulator preempts, src/simulator.cpp:117-133); they sit out the next step, whose allocations reuse the freed
+    blocks, and are swapped back in after it (admitted with fresh ids and no sharing, kvp_swap_in;
+    src/simulator.cpp:193, 231-241).
+
+    Content model: the K (V) row of position p written on behalf of `origin` is row key(origin, p) of a seeded
+    N(0,1) bank, where origin is the parent for the prefix, the request for its suffix and the sample for its
+    decode tokens -- so the context any live sample must see through its table is known, and check() compares
+    it on the device bit for bit.  `on_op(name, args, result)` sees every KVManager call in order (a test replays
+    them on the reference's KVManager)."""
+
+    BANK = 8192
+
+    def __init__(self, kvb, cfg, dev, requests=512, samples=8, prefix=2048, steps=64, swap_every=16,
+                 swap_frac=0.1, seed=5, on_op=None):
+        import torch
+        self.kvb, self.cfg, self.dev = kvb, cfg, dev
+        self.L, self.B, self.kvh, self.D = cfg["L"], cfg["B"], cfg["kvh"], cfg["D"]
+        self.tdt = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float16
+        self.requests, self.samples, self.prefix = requests, samples, prefix
+        self.swap_every, self.swap_frac, self.on_op = swap_every, swap_frac, on_op
+        self.rng = np.random.default_rng(seed)
+        B = self.B
+        self.suffix = self.rng.integers(1, 256, size=requests)
+        self.suffix[(prefix + self.suffix) % B == 0] += 1  # keep every request's last block partial
+        # pool: prefix + suffix blocks, one copy-on-write block per sample, the decode growth, the swap-in copies
+        n_s = requests * samples
+        grow = n_s * (steps // B + 2)
+        need = prefix // B + int(((self.suffix + B - 1) // B).sum()) + n_s + grow
+        swap_cap = int(swap_frac * need) + (prefix + 256 + steps) // B + 8
+        rounds = steps // swap_every + 1
+        self.nb = need + rounds * swap_cap + 64
+        self.swap_cap = swap_cap
+        self.k = torch.empty((self.L, self.nb, B, self.kvh, self.D), dtype=self.tdt, device=dev)
+        self.v = torch.empty_like(self.k)
+        g = torch.Generator(device=dev).manual_seed(seed)
+        self.bank_k = torch.randn((self.L, self.BANK, self.kvh, self.D), generator=g, device=dev).to(self.tdt)
+        self.bank_v = torch.randn((self.L, self.BANK, self.kvh, self.D), generator=g, device=dev).to(self.tdt)
+        self.mgr = kvb.KVManager(self.nb, B)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.compute = torch.cuda.current_stream(dev)
+        self.side = torch.cuda.Stream(dev)
+        self.slot_bytes = kvb.host_slot_bytes(self.L, B, self.kvh, self.D, self.k.element_size())
+        self.host = torch.empty(self.slot_bytes * swap_cap, dtype=torch.uint8, pin_memory=True)
+        self.parent = -1
+        # Sample identities are 0 .. requests * samples - 1 (request r's are r * samples + s); a sample keeps its
+        # identity (and so its content) when a swap gives it a new manager id.
+        self.mid = {}
+        self.tokens = np.zeros(n_s, np.int64)
+        self.live = []        # identities decoding this step
+        self.away = []        # identities swapped out: (identity, tokens, host slots)
+        self.next_id = 10 ** 7
+        self.counters = dict(cow_pairs=0, cow_bytes=0, cow_ms=0.0, scatter_rows=0, scatter_bytes=0, scatter_ms=0.0,
+                             swap_out_blocks=0, swap_in_blocks=0, swap_out_ms=0.0, swap_in_ms=0.0, swap_rounds=0,
+                             steps=0)
+        self._events = []
+
+    # ---------------------------------------------------------------- helpers
+    def _op(self, name, *args):
+        res = getattr(self.mgr, name)(*args)
+        if self.on_op is not None:
+            self.on_op(name, args, res)
+        return res
+
+    def _key(self, origin, pos):
+        return (np.asarray(origin, np.int64) * 1000003 + np.asarray(pos, np.int64) * 7919) % self.BANK
+
+    def _origin(self, ident, pos):
+        """Who wrote position pos of sample ident (arrays broadcast): the parent, the request, or the sample."""
+        ident, pos = np.asarray(ident, np.int64), np.asarray(pos, np.int64)
+        req = ident // self.samples
+        prompt = self.prefix + self.suffix[req]
+        return np.where(pos < self.prefix, self.parent, np.where(pos < prompt, req * self.samples, ident))
+
+    def _write(self, keys, slots, timed=False):
+        """Bank rows `keys` into `slots` (every layer, K and V) with kvp_append_scatter on the compute stream."""
+        import torch
+        idx = torch.from_numpy(np.asarray(keys, np.int64)).to(self.dev)
+        kn = self.bank_k.index_select(1, idx)
+        vn = self.bank_v.index_select(1, idx)
+        d_slots = torch.from_numpy(np.asarray(slots, np.int32)).to(self.dev)
+        if timed:
+            e = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            e[0].record(self.compute)
+        self.kvb.append_scatter(kn, vn, self.k, self.v, d_slots, status=self.status, stream=self.compute)
+        if timed:
+            e[1].record(self.compute)
+            self._events.append(("scatter", e, len(slots)))
+
+    def _prompt_rows(self, ident, start, end):
+        tbl = self.mgr.block_table(self.mid[ident])
+        pos = np.arange(start, end)
+        slots = np.asarray(tbl, np.int64)[pos // self.B] * self.B + pos % self.B
+        self._write(self._key(self._origin(ident, pos), pos), slots)
+
+    # ---------------------------------------------------------------- workload
+    def setup(self):
+        """Parent prefix, the requests' prompts (their suffix rows written), the forks."""
+        self.parent = self.next_id
+        self.next_id += 1
+        assert self._op("admit", self.parent, self.prefix)
+        pos = np.arange(self.prefix)
+        tbl = np.asarray(self.mgr.block_table(self.parent), np.int64)
+        self._write(self._key(np.full(self.prefix, self.parent), pos), tbl[pos // self.B] * self.B + pos % self.B)
+        for r in range(self.requests):
+            lead = r * self.samples
+            prompt = self.prefix + int(self.suffix[r])
+            self.mid[lead] = lead
+            assert self._op("admit_with_prefix", lead, self.parent, self.prefix, prompt)
+            self._prompt_rows(lead, self.prefix, prompt)
+            self.live.append(lead)
+            for s in range(1, self.samples):
+                ident = lead + s
+                self.mid[ident] = ident
+                assert self._op("fork", ident, lead)
+                self.live.append(ident)
+            self.tokens[lead:lead + self.samples] = prompt
+        self.compute.synchronize()
+
+    def step(self):
+        """One decode step of every live sample; then, on swap steps, the swap-in of the previous round's
+        samples and the swap-out of this round's."""
+        import torch
+        live = self.live
+        rids = [self.mid[i] for i in live]
+        done, slots, pairs = self._op("append_batch", rids)
+        assert done == len(rids), "the pool ran out of blocks"
+        if len(pairs):
+            e = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            e[0].record(self.compute)
+            self.kvb.cow_copy(self.k, self.v, torch.from_numpy(np.ascontiguousarray(pairs)).to(self.dev),
+                              status=self.status, stream=self.compute)
+            e[1].record(self.compute)
+            self._events.append(("cow", e, len(pairs)))
+        ids = np.asarray(live, np.int64)
+        pos = self.tokens[ids]  # the new token's position
+        self.tokens[ids] += 1
+        self._write(self._key(self._origin(ids, pos), pos), slots, timed=True)
+        self.counters["steps"] += 1
+        if self.away:
+            self._swap_in()
+        if self.counters["steps"] % self.swap_every == 0:
+            self._swap_out()
+
+    def _swap_out(self):
+        import torch
+        allocated = self.mgr.total_blocks() - self.mgr.free_blocks()
+        order = self.rng.permutation(len(self.live))
+        victims, blocks, held = [], [], 0
+        for j in order:
+            ident = self.live[int(j)]
+            tbl = self.mgr.block_table(self.mid[ident])
+            if held + len(tbl) > self.swap_cap:
+                continue
+            victims.append(ident)
+            blocks.append(tbl)
+            held += len(tbl)
+            if held >= self.swap_frac * allocated:
+                break
+        flat = [b for t in blocks for b in t]
+        self.side.wait_stream(self.compute)  # the rows written so far go out with the blocks
+        e = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        e[0].record(self.side)
+        self.kvb.swap_out(self.k, self.v, flat, list(range(len(flat))), self.host, stream=self.side)
+        e[1].record(self.side)
+        self._events.append(("swap_out", e, len(flat)))
+        self.compute.wait_stream(self.side)  # freed blocks are rewritten only after they went out
+        o = 0
+        for ident, tbl in zip(victims, blocks):
+            tokens = int(self.tokens[ident])
+            self._op("free", self.mid[ident])
+            self.away.append((ident, tokens, list(range(o, o + len(tbl)))))
+            o += len(tbl)
+        gone = set(victims)
+        self.live = [i for i in self.live if i not in gone]
+        self.counters["swap_rounds"] += 1
+
+    def _swap_in(self):
+        import torch
+        fresh, slots = [], []
+        for ident, tokens, hs in self.away:
+            new = self.next_id
+            self.next_id += 1
+            assert self._op("admit", new, tokens), "no room to swap back in"
+            self.mid[ident] = new
+            tbl = self.mgr.block_table(new)
+            assert len(tbl) == len(hs)
+            fresh.extend(tbl)
+            slots.extend(hs)
+            self.live.append(ident)
+        e = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        e[0].record(self.side)
+        self.kvb.swap_in(self.k, self.v, fresh, slots, self.host, stream=self.side)
+        e[1].record(self.side)
+        self._events.append(("swap_in", e, len(fresh)))
+        self.compute.wait_stream(self.side)  # the next step appends into the fresh blocks
+        self.away = []
+
+    def settle(self):
+        """Waits for the device, folds the op events into the counters; returns the status word."""
+        import torch
+        torch.cuda.synchronize(self.dev)
+        blk = 2 * self.L * self.B * self.kvh * self.D * self.k.element_size()
+        row = 2 * self.L * self.kvh * self.D * self.k.element_size()
+        c = self.counters
+        for kind, (e0, e1), n in self._events:
+            ms = e0.elapsed_time(e1)
+            if kind == "cow":
+                c["cow_pairs"] += n
+                c["cow_bytes"] += 2 * n * blk
+                c["cow_ms"] += ms
+            elif kind == "scatter":
+                c["scatter_rows"] += n
+                c["scatter_bytes"] += 2 * n * row
+                c["scatter_ms"] += ms
+            elif kind == "swap_out":
+                c["swap_out_blocks"] += n
+                c["swap_out_ms"] += ms
+            else:
+                c["swap_in_blocks"] += n
+                c["swap_in_ms"] += ms
+        self._events = []
+        return int(self.status.item())
+
+    def check(self, idents=None):
+        """Every given live sample's context, gathered from the device through its table, equals the content
+        model bit for bit (K and V, every layer).  Returns the number of rows checked."""
+        import torch
+        torch.cuda.synchronize(self.dev)
+        rows = 0
+        for ident in (self.live if idents is None else idents):
+            mid = self.mid[ident]
+            n = self.mgr.num_tokens(mid)
+            tbl = np.asarray(self.mgr.block_table(mid), np.int64)
+            pos = np.arange(n)
+            blk = torch.from_numpy(tbl[pos // self.B]).to(self.dev)
+            off = torch.from_numpy(pos % self.B).to(self.dev)
+            key = torch.from_numpy(self._key(self._origin(ident, pos), pos)).to(self.dev)
+            for pool, bank in ((self.k, self.bank_k), (self.v, self.bank_v)):
+                got = pool[:, blk, off]
+                assert torch.equal(got, bank.index_select(1, key)), f"sample {ident}: context differs"
+            rows += n
+        return rows
+
+
+def run_mix(args, cfg):
+    """The KV-management op mix (OpMix) at its stated scale: 512 requests x 8 samples on a 2048-token shared
+    prefix, Llama-3-8B-shaped blocks (32 layers, 8 kv heads x 128, bf16, 16 tokens: 2 MiB per block), a swap
+    round every 16 steps.  `--warmup` steps run first (the copy-on-write burst of the first append is among
+    them), then `--steps` timed steps; steps/s is the host + device wall time per timed step.  Reported beside
+    it: copy-on-write, append-scatter and swap bandwidths from CUDA events around each of those launches over the
+    whole run.  Verified after the run: every live sample's context equals the content model (a sample of 256
+    with --mix-check-all not given)."""
+    import torch
+    kvb = importlib.import_module("paged-kv-cache-manager_b200")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    total = args.warmup + args.steps
+    mix = OpMix(kvb, cfg, dev, requests=args.mix_requests, steps=total, seed=5)
+    mix.setup()
+    for _ in range(args.warmup):
+        mix.step()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(0) as clk:
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            mix.step()
+        torch.cuda.synchronize(dev)
+        wall = time.perf_counter() - t0
+    assert mix.settle() == 0
+    assert mix.mgr.validate() == ""
+    live = list(mix.live)
+    pick = live if args.mix_check_all else [live[int(i)] for i in np.random.default_rng(9).permutation(len(live))[:256]]
+    rows = mix.check(pick)
+    c = mix.counters
+    blk = 2 * mix.L * mix.B * mix.kvh * mix.D * 2
+    st = mix.mgr.stats()
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+
+    def rate(b, ms):
+        return round(b / (ms / 1e3) / 1e9, 1) if ms > 0 else None
+
+    line = {"metric": "KV-op mix decode steps per second", "value": round(args.steps / wall, 2), "unit": "steps/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * wall / args.steps, 3),
+            "higher_is_better": True, "op": "mix", "dtype": cfg["dtype"], "data": "synthetic N(0,1) bank rows, seeded",
+            "config": {"workload": f"KV-op mix: {args.mix_requests} requests x {mix.samples} samples on a {mix.prefix}-token "
+                                   f"shared prefix (admit_with_prefix + fork), {mix.L} layers x {mix.kvh} kv heads x "
+                                   f"{mix.D}, bf16, block {mix.B}; copy-on-write on the first append; every "
+                                   f"{mix.swap_every} steps {int(100 * mix.swap_frac)}% of the allocated blocks swapped "
+                                   f"out to pinned host memory and back in after one step",
+                       "step": "host append_batch of every live sample + copy-on-write + append scatter (+ swaps)"},
+            "cow": {"pairs": c["cow_pairs"], "gb_s": rate(c["cow_bytes"], c["cow_ms"]),
+                    "frac_of_hbm_peak": round(c["cow_bytes"] / (c["cow_ms"] / 1e3) / 1e9 / peak, 4) if c["cow_ms"] else None,
+                    "bytes": "read + write of 2 MiB per pair"},
+            "scatter": {"rows": c["scatter_rows"], "gb_s": rate(c["scatter_bytes"], c["scatter_ms"]),
+                        "frac_of_hbm_peak": round(c["scatter_bytes"] / (c["scatter_ms"] / 1e3) / 1e9 / peak, 4)},
+            "swap": {"rounds": c["swap_rounds"], "out_blocks": c["swap_out_blocks"], "in_blocks": c["swap_in_blocks"],
+                     "out_gb_s": rate(c["swap_out_blocks"] * blk, c["swap_out_ms"]),
+                     "in_gb_s": rate(c["swap_in_blocks"] * blk, c["swap_in_ms"])},
+            "kv_stats": dict(st), "pool_blocks": mix.nb,
+            "verified": {"samples": len(pick), "rows": rows, "bit_exact": True},
+            "gpu_launches": args.steps * 2 + c["swap_rounds"], "clocks": clk.summary()}
+    print(json.dumps(line))
+
+
 def run_block_mover(args, cfg):
     """Whole-block movers of the data plane, device timed: `migrate` copies blocks from a second GPU's pool into
     this GPU's pool (kvp_migrate_blocks, peer loads over NVLink; two pools on one GPU when only one is
@@ -1132,7 +1451,10 @@ def main():
     ap.add_argument("--layers", type=int, default=0, help="profiling: number of layers (pool sized to need)")
     ap.add_argument("--prompt-rows", type=int, default=4096, help="scatter: positions of the prompt shape")
     ap.add_argument("--pairs", type=int, default=2048, help="cow / migrate: block pairs per step")
-    ap.add_argument("--op", default="decode", choices=["decode", "migrate", "cow", "swap", "sim", "latency", "scatter"],
+    ap.add_argument("--mix-requests", type=int, default=512, help="mix: requests (8 samples each)")
+    ap.add_argument("--mix-check-all", action="store_true", help="mix: verify every live sample, not 256")
+    ap.add_argument("--op", default="decode",
+                    choices=["decode", "migrate", "cow", "swap", "sim", "latency", "scatter", "mix"],
                     help="decode step (default), a whole-block mover measured alone, the scheduler-driven "
                          "data plane (sim), or the small 8-sequence case's per-call latency (latency)")
     ap.add_argument("--sim-replays", type=int, default=2, help="sim: timed replays of the decision stream")
@@ -1174,6 +1496,9 @@ def main():
         return
     if args.op == "scatter":
         run_scatter(args, cfg)
+        return
+    if args.op == "mix":
+        run_mix(args, cfg)
         return
     if args.op != "decode":
         run_block_mover(args, cfg)
