@@ -3,9 +3,10 @@ with libkvpage_b200.so instead of the reference's library: the allocator, KV-man
 feature (prefix cache), random-trace and scheduler tests (tests/test_*.cpp of
 prathameshpranjale/paged-kv-cache-manager), the last three driving the reference's own simulator
 (src/simulator.cpp, workload.cpp, metrics.cpp) on top of this library's KVManager.  This checks the drop-in
-claim directly: the reference's callers compile unchanged and see identical behaviour.  The reference's CPU
-attention tests are not part of it (this library has no CPU attention path).  Runs where the reference
-sources are present (the development container); skipped elsewhere."""
+claim directly: the reference's callers compile unchanged and see identical behaviour.  The reference's attention
+test (tests/test_attention.cpp) needs a GPU here -- this library serves paged_attention_cpu on the device -- so it
+is built by oracle/Makefile and run by tests/test_host_attention_gpu.py.  Runs where the reference sources are
+present (the development container); skipped elsewhere."""
 import os
 import subprocess
 
