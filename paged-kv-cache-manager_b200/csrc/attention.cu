@@ -315,8 +315,8 @@ extern "C" KVP_API size_t kvp_attention_workspace_size(const kvp_attn_args* a) {
 
 namespace {
 
-// kvp_paged_attention with every pipeline wait limited to `wait_limit` clock cycles; `stall` arms the first
-// CTA's first stage for a copy that is never issued (kvp_attention_wait_test only).
+// kvp_paged_attention with every pipeline wait limited to `wait_limit` clock cycles; `stall` arms the first stage
+// of the CTAs in the grid's first row for a copy that is never issued (kvp_attention_wait_test only).
 int attention_call(const kvp_attn_args* a, void* stream, long long wait_limit, int stall) {
     using namespace kvpi;
     clear_error();

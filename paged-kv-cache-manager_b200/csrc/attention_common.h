@@ -54,8 +54,9 @@ struct AttnParams {
     int early_load;  // the producer may load the first K/V tiles before waiting for the previous kernel
     int seq_units;   // stream-K: start-cost units charged ahead of each sequence's tiles
     long long wait_limit;  // clock cycles after which a pipeline wait gives up (KVP_STATUS_TIMEOUT)
-    // Failure-detection test (kvp_attention_wait_test): the producer of CTA (0, 0) arms its first stage for 16
-    // bytes of a copy it never issues, so that stage's wait runs out; nothing is ever in flight for it.
+    // Failure-detection test (kvp_attention_wait_test): the producer of every CTA with blockIdx.y == 0 arms its
+    // first stage for 16 bytes of a copy it never issues, so that stage's wait runs out; nothing is ever in flight
+    // for it.
     int stall_first_stage;
 };
 

@@ -662,8 +662,10 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
         }
         bool ok = true;
         int pst = 0, pr = 0, j = 0;  // stage and round (i % S, i / S) of the running tile counter i
-        // failure-detection test only: this CTA's first stage is armed for a copy that is never issued
-        const bool stall = p.stall_first_stage && blockIdx.x == 0 && blockIdx.y == 0;
+        // failure-detection test only: the first stage of every CTA in the grid's first row (kv-head group 0 of the
+        // balanced schedule, split 0 of the fixed splits -- rows that always hold CTAs with tiles) is armed for a
+        // copy that is never issued
+        const bool stall = p.stall_first_stage && blockIdx.y == 0;
         const volatile int* abort = &ps->abort;
         while (segs.next(sg)) {
             const int len = sg.len;
