@@ -205,37 +205,34 @@ def check_parity(cfg, sample):
             "tolerance": "2e-3 abs + (2e-3 + half an ulp of the output dtype) rel"}
 
 
+def cpu_layer_workload(cfg, lens):
+    """What the reference's CPU code is timed on: one layer of every request of the shard, its own context
+    length, N(0,1) fp32 data, tables drawing their blocks from a shared pool of at most 16,384 blocks (so host
+    memory and set-up stay bounded while every request still reads blocks scattered over DRAM).  One call is
+    1/L of a decode step, and every host thread has many requests to work through."""
+    pool = min(int(((lens + cfg["B"] - 1) // cfg["B"]).sum()), 16384)
+    return _random_sample(cfg, lens, seed=77, pool_blocks=pool), pool
+
+
 def cpu_baseline(cfg, lens, target_s=12.0, kind_pref="reference", sample=None):
     """Times the reference's paged_attention_cpu (the reference library built here, else the oracle's
-    restatement) on a bounded sample of this workload on all host cores, scaled to the workload's decode tok/s.
-    With `sample` (DecodeStep.parity_sample of the last timed step: 16 of its requests, the first and last
-    layer, copied off the device after the timed region) the timed sample is that step's first-layer data, and
-    this leg also checks the GPU's outputs for those requests (check_parity).  Returns (baseline, parity)."""
+    restatement) on all host cores over cpu_layer_workload() for about target_s (at least one call), and scales
+    it to decode tok/s = requests / (L x seconds per call).  With `sample` (DecodeStep.parity_sample of the last
+    timed step: 16 of its requests, the first and last layer, copied off the device after the timed region) this
+    leg also checks the GPU's outputs for those requests (check_parity).  Returns (baseline, parity)."""
     import oracle
     kind = "reference" if (kind_pref == "reference" and oracle.have_ref()) else "port"
     impl = "ref" if kind == "reference" else "c"
     kvh, D = cfg["kvh"], cfg["D"]
     cores = os.cpu_count() or 1
-    parity = None
-    if sample is not None:
-        first = sample["layers"][min(sample["layers"])]
-        Q, K, V, T, sl = first["q"], first["k"], first["v"], sample["tables"], sample["lens"]
-        what = "the timed step's own data: 16 of its requests (longest, shortest, 14 random), first layer"
-        parity = check_parity(cfg, sample)
-    else:
-        pick = np.random.default_rng(76).choice(lens, size=max(cores, 8), replace=True)
-        Q, K, V, T, sl = _random_sample(cfg, pick, seed=77)
-        what = f"{len(sl)} requests drawn from the workload's lengths, N(0,1) data, one layer"
+    parity = check_parity(cfg, sample) if sample is not None else None
+    (Q, K, V, T, sl), pool = cpu_layer_workload(cfg, lens)
     per_call, reps, el = _time_cpu(cfg, Q, K, V, T, sl, target_s, impl, cores)
-    elem = 2
-    sample_bytes = float(sl.sum()) * kvh * D * 2 * elem  # same byte formula as the GPU (one layer)
-    gbs = sample_bytes / per_call / 1e9
-    step_bytes = float(lens.sum()) * kvh * D * 2 * elem * cfg["L"]
-    step_s = step_bytes / (gbs * 1e9)
-    return {"value": len(lens) / step_s, "unit": "tok/s", "cores": cores, "kind": kind,
+    gbs = float(sl.sum()) * kvh * D * 2 * 2 / per_call / 1e9  # the GPU's byte formula
+    return {"value": len(lens) / (cfg["L"] * per_call), "unit": "tok/s", "cores": cores, "kind": kind,
             "gb_s": round(gbs, 3),
-            "sample": f"{what} ({int(sl.sum())} tokens), {reps} timed calls over {el:.1f}s, scaled to "
-                      f"{len(lens)} requests x {cfg['L']} layers by its GB/s"}, parity
+            "sample": f"one layer of all {len(sl)} requests per call ({int(sl.sum())} context tokens; tables over a "
+                      f"shared pool of {pool} blocks), {reps} timed calls over {el:.1f}s, x {cfg['L']} layers"}, parity
 
 
 def reference_gpu_kernel(cfg, lens, nseq=32):
@@ -1319,8 +1316,7 @@ def reference_arm(args, cfg, config, metric):
     impl = "ref" if kind == "reference" else "c"
     cores = os.cpu_count() or 1
     lens = sample_lens(cfg, cfg["ns"], seed=1000)
-    pool = min(int(((lens + cfg["B"] - 1) // cfg["B"]).sum()), 16384)
-    Q, K, V, T, sl = _random_sample(cfg, lens, seed=77, pool_blocks=pool)
+    (Q, K, V, T, sl), pool = cpu_layer_workload(cfg, lens)
     nh, kvh, D, B = cfg["nh"], cfg["kvh"], cfg["D"], cfg["B"]
 
     def one():
