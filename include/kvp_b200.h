@@ -143,9 +143,10 @@ KVP_API int kvp_paged_attention_host(int32_t num_heads, int32_t kv_heads, int32_
  * livelock guard, src/simulator.cpp:136).  Every pipeline wait of the attention kernel is bounded; no valid
  * input makes one run out, so this entry point exists to test that path without a GPU fault: it is
  * kvp_paged_attention with each wait limited to wait_limit_cycles clock cycles (1 .. 2e9; the normal entry
- * point uses 2e9, about a second) and, with stall_first_stage == 1, the first pipeline stage of every CTA of the
- * grid's first row (kv-head group 0 of the balanced schedule, split 0 of the fixed splits) armed for 16 bytes of
- * a copy that is never issued -- a flag nothing sets.  Those CTAs' consumers give up after the limit, their
+ * point uses 2e9, about a second) and, with stall_first_stage == 1, in every CTA of the grid's first row (kv-head
+ * group 0 of the balanced schedule, split 0 of the fixed splits) pipeline stage 0 armed for 16 bytes of a copy
+ * that is never issued -- a flag nothing sets -- and the tiles issued from stage 1 on.  Those CTAs' consumers,
+ * which expect the first tile in stage 0, give up after the limit, their
  * producers stop issuing and wait (bounded) for the copies they did issue, the kernel ORs KVP_STATUS_TIMEOUT
  * into `status` and returns; no copy is left in flight and the context stays usable.
  * After KVP_STATUS_TIMEOUT from any entry point the outputs of the affected sequences are undefined and the

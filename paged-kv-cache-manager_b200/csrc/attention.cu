@@ -276,6 +276,21 @@ int plan_attention(const kvp_attn_args& a, bool have_workspace, AttnPlan* out) {
             const double tile_us = tile_bytes * ctas / 6.4e6;
             pl.seq_units = static_cast<int>(std::min(32.0, std::max(0.0, std::round(switch_us / tile_us))));
         }
+        // Back-to-back launches (a step's layers) see their last-dispatched CTAs start late: they get the SM slots
+        // the previous grid frees last and run their whole prologue after it ends.  A per-CTA timeline of
+        // graph-replayed steps on B200 (Qwen2.5-0.5B and TinyLlama shapes, 296 CTAs) put the CTAs from about the
+        // last sixth of the index range behind, by 1 to 5 us at their first tile.  Those CTAs get about 3 us worth
+        // of tiles fewer each (tile time as for the start cost above), spread over all CTAs; linear ramps from
+        // 3 to 8 us and over a tenth to a quarter of the grid measured the same.  Applied to every balanced
+        // launch, so the partition -- and the result, bit for bit -- depends only on the lengths and the head
+        // shape, not on how the launch is ordered against its neighbours.
+        {
+            const double tile_bytes = 16.0 * kc * D * 2 * 2;
+            const double ctas = static_cast<double>(sm_count()) * (tile_bytes >= (48 << 10) ? 1 : 2);
+            const double tile_us = tile_bytes * ctas / 6.4e6;
+            pl.taper_m = std::max(1, static_cast<int>(std::lround(pl.G / 6.0)));
+            pl.taper_d = static_cast<int>(std::lround(3.0 / tile_us));
+        }
         pl.split_tiles = pl.max_tiles;
         pl.max_splits = 1;
         // The merge counters come first, in a region sized for the most sequences a call may have, so their
@@ -415,6 +430,8 @@ int attention_call(const kvp_attn_args* a, void* stream, long long wait_limit, i
     prm.kvh = a->kv_heads;
     prm.early_load = (a->flags & KVP_ATTN_EARLY_LOAD) ? 1 : 0;
     prm.seq_units = pl.seq_units;
+    prm.taper_m = pl.taper_m;
+    prm.taper_d = pl.taper_d;
     prm.wait_limit = wait_limit;
     prm.stall_first_stage = stall;
     const float scale = a->scale > 0.f ? a->scale : 1.0f / std::sqrt(static_cast<float>(a->head_dim));

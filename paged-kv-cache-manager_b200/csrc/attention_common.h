@@ -53,20 +53,21 @@ struct AttnParams {
     int kvh;
     int early_load;  // the producer may load the first K/V tiles before waiting for the previous kernel
     int seq_units;   // stream-K: start-cost units charged ahead of each sequence's tiles
+    // Stream-K taper: the last taper_m CTAs -- dispatched last, into the SM slots the previous grid frees last
+    // when launches run back to back -- get taper_d fewer units each; 0: even split.
+    int taper_m;
+    int taper_d;
     long long wait_limit;  // clock cycles after which a pipeline wait gives up (KVP_STATUS_TIMEOUT)
-    // Failure-detection test (kvp_attention_wait_test): the producer of every CTA with blockIdx.y == 0 arms its
-    // first stage for 16 bytes of a copy it never issues, so that stage's wait runs out; nothing is ever in flight
-    // for it.
+    // Failure-detection test (kvp_attention_wait_test): the producer of every CTA with blockIdx.y == 0 arms stage 0
+    // for 16 bytes of a copy it never issues and starts its tiles at stage 1, so the consumers' first wait runs
+    // out; nothing is ever in flight for stage 0.
     int stall_first_stage;
 };
 
-// Per-CTA pipeline bookkeeping in shared memory that lets a CTA whose waits gave up leave without a bulk copy
-// in flight: `abort` tells the producer to stop issuing, and issued[] holds 1 + the round of the last copy
-// issued into each stage (the two query slots after the kMaxStages stage entries), so the producer can wait
-// for exactly those copies before it returns.
+// Per-CTA pipeline state in shared memory: `abort` is raised by a consumer warp whose wait gave up, so the
+// producer drains its copies before it returns even when its own waits all succeeded.
 struct PipeState {
     int abort;
-    int issued[kMaxStages + 2];
 };
 
 // Per-variant entry points: K/V dtype x whether the query needs a low-half residual MMA (its dtype differs

@@ -63,16 +63,14 @@ struct Geo {
 
 // ---------------------------------------------------------------- producer: one tile into one stage
 // All 32 lanes call this (the table cache is a warp-wide register array); lane 0 issues the copies.
-// `phantom` (failure-detection test only): lane 0 arms the stage for 16 bytes and issues nothing, so the
-// stage never completes and nothing is in flight for it.
 template <int D>
 __device__ __forceinline__ void produce_tile(const AttnParams& p, const CUtensorMap* km, const CUtensorMap* vm,
                                              uint32_t kst, uint32_t vst, uint32_t fb, int tb, int len,
                                              const int32_t* trow, int kvh0, int lane, int& cache_lo,
-                                             int32_t& cached, bool phantom) {
+                                             int32_t& cached) {
     using G_ = Geo<D>;
     const int nr = min(p.nruns, (len - tb + p.R - 1) / p.R);
-    if (lane == 0) mbar_arrive_expect_tx(fb, phantom ? 16u : static_cast<uint32_t>(nr) * G_::NCH * 2u * p.box_tx);
+    if (lane == 0) mbar_arrive_expect_tx(fb, static_cast<uint32_t>(nr) * G_::NCH * 2u * p.box_tx);
     for (int j = 0; j < nr; ++j) {
         const int tok = tb + j * p.R;
         const int bi = blk_of(p, tok);
@@ -86,7 +84,7 @@ __device__ __forceinline__ void produce_tile(const AttnParams& p, const CUtensor
             if (lane == 0) report(p.status, KVP_STATUS_BAD_BLOCK);
             row = p.oob_row;
         }
-        if (lane == 0 && !phantom) {
+        if (lane == 0) {
 #pragma unroll
             for (int c = 0; c < G_::NCH; ++c) {
                 const uint32_t off = static_cast<uint32_t>(j * G_::NCH + c) * p.box_slot;
@@ -137,14 +135,13 @@ __device__ __forceinline__ void append_new_token(const AttnParams& p, int seq, i
 // Up to 8 consecutive tiles of one sequence at once, lane k producing tile `tile + k` into stage
 // (i + k) % S: each lane waits for its own stage, arms its own barrier and issues its own copies, so the
 // per-tile issue cost is paid in parallel.  Only for one run per tile (block_size a multiple of 16).  The
-// tile counter i is passed as (st0, r0) = (i % S, i / S); nb <= S.  Each issuing lane records its stage's round
-// in ps->issued.  Returns false (after reporting) if a wait gave up.  `phantom`: the lane of tile counter 0
-// arms its stage for 16 bytes and issues nothing (failure-detection test only).
+// tile counter i is passed as (st0, r0) = (i % S, i / S); nb <= S.  Returns false (after reporting) if a wait
+// gave up; `issued` is then the mask of the lanes that did issue their copies.
 template <int D>
 __device__ __forceinline__ bool produce_batch(const AttnParams& p, const CUtensorMap* km, const CUtensorMap* vm,
                                               uint32_t smem_base, uint64_t* full_bar, uint64_t* empty_bar, int st0,
                                               int r0, int tile, int nb, int len, const int32_t* trow, int kvh0,
-                                              int lane, int& cache_lo, int32_t& cached, PipeState* ps, bool phantom) {
+                                              int lane, int& cache_lo, int32_t& cached, unsigned& issued) {
     using G_ = Geo<D>;
     const int S = p.stages;
     const int bi_first = blk_of(p, tile * 16);
@@ -173,14 +170,11 @@ __device__ __forceinline__ bool produce_batch(const AttnParams& p, const CUtenso
             report(p.status, KVP_STATUS_TIMEOUT);
             ok = false;
         }
-        if (ok && phantom && st == 0 && r == 0) {
-            mbar_arrive_expect_tx(smem_u32(&full_bar[st]), 16u);
-        } else if (ok) {
+        if (ok) {
             const uint32_t fb = smem_u32(&full_bar[st]);
             const uint32_t kst = smem_base + static_cast<uint32_t>(st) * p.stage_bytes;
             const uint32_t vst = kst + p.stage_half;
             mbar_arrive_expect_tx(fb, static_cast<uint32_t>(G_::NCH) * 2u * p.box_tx);
-            reinterpret_cast<volatile int*>(ps->issued)[st] = r + 1;
 #pragma unroll
             for (int c = 0; c < G_::NCH; ++c) {
                 const uint32_t off = static_cast<uint32_t>(c) * p.box_slot;
@@ -197,7 +191,9 @@ __device__ __forceinline__ bool produce_batch(const AttnParams& p, const CUtenso
             }
         }
     }
-    return __all_sync(0xffffffffu, ok);
+    const unsigned failed = __ballot_sync(0xffffffffu, !ok);
+    issued = ((nb >= 32 ? 0u : (1u << nb)) - 1u) & ~failed;
+    return failed == 0;
 }
 
 // ---------------------------------------------------------------- consumer: one warp, one kv head
@@ -509,11 +505,13 @@ struct Segment {
     int len;  // the sequence's context length
     bool single;
     size_t part_row;
-    int c0, nseg;  // stream-K: first CTA holding part of the sequence and how many do (0: merged elsewhere)
+    int c0, nseg;  // stream-K: first CTA holding part of the sequence and how many do (0: merged elsewhere;
+                   // -1: split, Segs::span() gives them)
 };
 
 // Fixed splits: the CTA's one segment.
 struct SplitSegments {
+    static constexpr bool lazy_span = false;
     Segment seg;
     bool done;
     __device__ __forceinline__ bool next(Segment& s) {
@@ -535,7 +533,6 @@ __device__ __forceinline__ long long muldiv_floor(long long a, long long b, long
 }
 
 // CTA c of Ge owns tiles [c*T/Ge, (c+1)*T/Ge) of the concatenation of all sequences' tiles (T in total).
-__device__ __forceinline__ long long cta_begin(long long c, long long T, int G) { return muldiv_floor(c, T, G); }
 // The owner of tile t: the c with c*T < (t+1)*G <= (c+1)*T, i.e. floor(((t+1)*G - 1) / T).  The quotient is
 // below 2^16, so a single-precision estimate is off by at most one and one integer step corrects it.
 __device__ __forceinline__ int cta_of_tile(long long t, long long T, int G) {
@@ -546,16 +543,59 @@ __device__ __forceinline__ int cta_of_tile(long long t, long long T, int G) {
     return static_cast<int>(c);
 }
 
+// The division of the step's T units between Ge CTAs.  Even: CTA c owns [c*T/Ge, (c+1)*T/Ge).  Tapered: CTAs
+// are dispatched in index order into the SM slots the previous grid frees, so when launches run back to back
+// the last ones start late -- by up to the length of a prologue; the last m CTAs each give up D units, spread
+// evenly over all CTAs:
+//   begin(c) = floor(c * (T + D m) / Ge) - D * max(0, c - (Ge - m)).
+// D is dropped when the even share is below D + 2 units, so every CTA keeps at least one unit (the merge counts
+// assume it).  Integer arithmetic throughout; begin() is the one function a CTA's own range and the owner of a
+// unit both come from.
+struct Partition {
+    int T;         // units (the prefix sums are 32-bit)
+    int Ge, m, D;  // D == 0: even split
+    Partition() = default;
+    __device__ __forceinline__ Partition(long long T_, int Ge_, int taper_m, int taper_d) : T(static_cast<int>(T_)), Ge(Ge_) {
+        m = min(taper_m, Ge);
+        D = (m > 0 && Ge > 0 && T >= static_cast<long long>(Ge) * (taper_d + 2)) ? taper_d : 0;
+    }
+    __device__ __forceinline__ long long begin(long long c) const {
+        if (D == 0) return muldiv_floor(c, T, Ge);
+        return muldiv_floor(c, static_cast<long long>(T) + static_cast<long long>(D) * m, Ge) -
+               static_cast<long long>(D) * max(0LL, c - (Ge - m));
+    }
+    // The CTA whose range holds unit t (the last c with begin(c) <= t).
+    __device__ __forceinline__ int owner(long long t) const {
+        if (D == 0) return cta_of_tile(t, T, Ge);
+        const long long Tp = static_cast<long long>(T) + static_cast<long long>(D) * m;
+        const int cr = Ge - m;
+        if (t < muldiv_floor(cr, Tp, Ge)) return cta_of_tile(t, Tp, Ge);  // before the taper: an even split of Tp
+        // in the taper begin(c) ~ c (Tp / Ge - D) + D cr: estimate, then step to the exact owner
+        long long c = cr + static_cast<long long>(static_cast<double>(t - muldiv_floor(cr, Tp, Ge)) /
+                                                  (static_cast<double>(Tp) / Ge - D));
+        c = min(max(c, static_cast<long long>(cr)), static_cast<long long>(Ge - 1));
+        while (c > cr && begin(c) > t) --c;
+        while (c + 1 < Ge && begin(c + 1) <= t) ++c;
+        return static_cast<int>(c);
+    }
+};
+
 // Stream-K: the CTA's tile range [t, end) of the concatenated sequences, cut at sequence boundaries.
 // The concatenated space is counted in units: each valid sequence spans X start-cost units (the time a CTA
 // spends switching to a new sequence, in tiles) followed by its tiles, so the balanced split charges that
 // cost to the CTA that starts the sequence.  A CTA whose range holds only a sequence's start-cost units does
-// no work for it; the CTAs holding its tiles are c0 .. c0 + nseg - 1.
+// no work for it; the CTAs holding its tiles are c0 .. c0 + nseg - 1.  Lazy: a split segment's span is not
+// found here but by the one thread that records it (span()), with the partition rebuilt from the launch
+// parameters -- for the register-heavy instantiations, where keeping it in every warp costs spills; the others
+// find it here, in every warp at once (faster: Qwen2.5-0.5B-shaped steps 137.0k against 133.1k tok/s on B200).
+template <bool Lazy>
 struct StreamSegments {
+    static constexpr bool lazy_span = Lazy;
     const int32_t* P;  // unit prefix sums in shared memory
     const uint8_t* R;  // tokens in each sequence's last tile, in shared memory
-    long long t, end, T;
-    int s, cta, nh, Ge, X;
+    long long t, end;
+    Partition part;    // (not read when Lazy)
+    int s, cta, nh, X;
     __device__ __forceinline__ bool next(Segment& sg) {
         while (t < end) {
             while (P[s + 1] <= t) ++s;
@@ -570,11 +610,26 @@ struct StreamSegments {
             sg.tile1 = static_cast<int>(e - first);
             sg.single = (a == first) && (e == P[s + 1]);
             sg.part_row = static_cast<size_t>(cta + s) * nh;
-            sg.c0 = sg.single ? cta : cta_of_tile(first, T, Ge);
-            sg.nseg = sg.single ? 1 : cta_of_tile(P[s + 1] - 1, T, Ge) - sg.c0 + 1;
+            if (sg.single) {
+                sg.c0 = cta;
+                sg.nseg = 1;
+            } else if constexpr (Lazy) {
+                sg.c0 = cta;
+                sg.nseg = -1;
+            } else {
+                sg.c0 = part.owner(first);
+                sg.nseg = part.owner(P[s + 1] - 1) - sg.c0 + 1;
+            }
             return true;
         }
         return false;
+    }
+    // The CTAs holding parts of sequence s (Lazy only), from the launch parameters and the prefix sums.
+    __device__ __forceinline__ void span(const AttnParams& p, int s, int& c0, int& nseg) const {
+        const int T = P[p.num_seqs];
+        const Partition pt(T, min(p.G, T), p.taper_m, p.taper_d);
+        c0 = pt.owner(static_cast<long long>(P[s]) + X);
+        nseg = pt.owner(static_cast<long long>(P[s + 1]) - 1) - c0 + 1;
     }
 };
 
@@ -582,7 +637,6 @@ __device__ __forceinline__ void init_barriers(const AttnParams& p, uint64_t* ful
                                               uint64_t* qfull, uint64_t* qempty, PipeState* ps) {
     if (threadIdx.x == 0) {
         ps->abort = 0;
-        for (int s = 0; s < kMaxStages + 2; ++s) ps->issued[s] = 0;
         for (int s = 0; s < p.stages; ++s) {
             mbar_init(smem_u32(&full_bar[s]), 1);
             mbar_init(smem_u32(&empty_bar[s]), static_cast<uint32_t>(p.kvh_cta));
@@ -603,9 +657,11 @@ __device__ __forceinline__ void init_barriers(const AttnParams& p, uint64_t* ful
 //
 // Every wait is bounded: a warp that gives up reports KVP_STATUS_TIMEOUT, raises ps->abort and then runs
 // through the rest of its control flow without waiting (so the named barriers of its partner warps are still
-// reached).  The producer stops issuing once a wait gave up and, before it returns, waits (bounded) for every
+// reached).  The producer stops issuing once one of its own waits gave up (a consumer that gave up stops
+// freeing stages, so the producer's next wait gives up too) and, before it returns, waits (bounded) for every
 // copy it issued that no consumer waited for, so the CTA never exits with a bulk copy in flight into its
-// shared memory.
+// shared memory.  What it issued is known from registers: every tile before the counter (okst, okr) after its
+// last fully issued batch, plus the lanes `fmask` of the batch at (fst0, fr0) that failed; query loads: jq.
 template <int D>
 __device__ __forceinline__ void merge_rows(const AttnParams& p, size_t row0, size_t stride, int n, size_t out_off,
                                            int lane);
@@ -625,18 +681,29 @@ struct MergeShape {
 };
 
 // After a wait gave up: lane 0 of the producer waits (bounded) for the last copy issued into each stage and
-// query slot; a stage whose last round a consumer already waited for completes at once.
-__device__ __forceinline__ void drain_copies(const AttnParams& p, PipeState* ps, uint64_t* full_bar, uint64_t* qfull,
-                                             int lane) {
+// query slot; a stage whose last round a consumer already waited for completes at once.  `stall`: stage 0's
+// round 0 was the failure-detection test's phantom (nothing in flight), skipped.
+__device__ __forceinline__ void drain_copies(const AttnParams& p, uint64_t* full_bar, uint64_t* qfull, int lane, int okst,
+                                             int okr, int fst0, int fr0, unsigned fmask, int jq, bool stall) {
     __syncwarp();
     if (lane == 0) {
-        const volatile int* issued = ps->issued;
-        for (int st = 0; st < p.stages + 2; ++st) {
-            const int n = issued[st < p.stages ? st : kMaxStages + (st - p.stages)];
-            if (n == 0) continue;
-            const uint32_t bar = smem_u32(st < p.stages ? &full_bar[st] : &qfull[st - p.stages]);
-            if (!mbar_wait(bar, static_cast<uint32_t>((n - 1) & 1), p.wait_limit)) report(p.status, KVP_STATUS_TIMEOUT);
+        auto wait = [&](uint32_t bar, int round) {
+            if (!mbar_wait(bar, static_cast<uint32_t>(round & 1), p.wait_limit)) report(p.status, KVP_STATUS_TIMEOUT);
+        };
+        for (int st = 0; st < p.stages; ++st) {
+            const int n = okr + (st < okst ? 1 : 0);  // rounds issued into stage st before the failed batch
+            if (n > 0 && !(stall && st == 0 && n == 1)) wait(smem_u32(&full_bar[st]), n - 1);
         }
+        for (int k = 0; k < 32; ++k) {
+            if (!((fmask >> k) & 1u)) continue;
+            int st = fst0 + k, r = fr0;
+            if (st >= p.stages) {
+                st -= p.stages;
+                ++r;
+            }
+            wait(smem_u32(&full_bar[st]), r);
+        }
+        for (int k = max(0, jq - 2); k < jq; ++k) wait(smem_u32(&qfull[k & 1]), k >> 1);
     }
     __syncwarp();
 }
@@ -662,11 +729,18 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
         }
         bool ok = true;
         int pst = 0, pr = 0, j = 0;  // stage and round (i % S, i / S) of the running tile counter i
-        // failure-detection test only: the first stage of every CTA in the grid's first row (kv-head group 0 of the
-        // balanced schedule, split 0 of the fixed splits -- rows that always hold CTAs with tiles) is armed for a
-        // copy that is never issued
+        int okst = 0, okr = 0, fst0 = 0, fr0 = 0, jq = 0;  // what was issued (see above)
+        unsigned fmask = 0;
+        // Failure-detection test only (kvp_attention_wait_test): in every CTA of the grid's first row (kv-head group
+        // 0 of the balanced schedule, split 0 of the fixed splits -- rows that always hold CTAs with tiles) stage 0
+        // is armed for 16 bytes of a copy that is never issued and the tiles start at stage 1, so the consumers,
+        // which expect the first tile in stage 0, wait until their limit.  Nothing is ever in flight for stage 0.
         const bool stall = p.stall_first_stage && blockIdx.y == 0;
-        const volatile int* abort = &ps->abort;
+        if (stall) {
+            if (lane == 0) mbar_arrive_expect_tx(smem_u32(&full_bar[0]), 16u);
+            __syncwarp();
+            pst = okst = 1;  // the stage count is at least 2
+        }
         while (segs.next(sg)) {
             const int len = sg.len;
             const int32_t* trow = p.tables + static_cast<size_t>(sg.seq) * p.max_blocks;
@@ -677,12 +751,18 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
             auto produce_range = [&](int from, int to) {
                 for (int tile = from; tile < to;) {
                     const int nb = min(nb_max, to - tile);
-                    if (ok && *abort) ok = false;  // a consumer gave up: issue nothing more
+                    bool sent_all = false;
                     if (ok) {
-                        const bool phantom = stall && pst == 0 && pr == 0;
                         if (nb_max > 1) {
+                            unsigned issued = 0;
                             ok = produce_batch<D>(p, km, vm, smem_base, full_bar, empty_bar, pst, pr, tile, nb, len, trow,
-                                                  kvh0, lane, cache_lo, cached, ps, phantom);
+                                                  kvh0, lane, cache_lo, cached, issued);
+                            if (!ok) {
+                                fst0 = pst;
+                                fr0 = pr;
+                                fmask = issued;
+                            }
+                            sent_all = ok;
                         } else {
                             const int st = pst;
                             if (pr >= 1 && !mbar_wait(smem_u32(&empty_bar[st]), static_cast<uint32_t>((pr - 1) & 1),
@@ -692,8 +772,8 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
                             } else {
                                 const uint32_t kst = smem_base + static_cast<uint32_t>(st) * p.stage_bytes;
                                 produce_tile<D>(p, km, vm, kst, kst + p.stage_half, smem_u32(&full_bar[st]), tile * 16,
-                                                len, trow, kvh0, lane, cache_lo, cached, phantom);
-                                if (lane == 0 && !phantom) reinterpret_cast<volatile int*>(ps->issued)[st] = pr + 1;
+                                                len, trow, kvh0, lane, cache_lo, cached);
+                                sent_all = true;
                             }
                         }
                         __syncwarp();
@@ -703,6 +783,10 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
                     if (pst >= S) {
                         pst -= S;
                         ++pr;
+                    }
+                    if (sent_all) {
+                        okst = pst;
+                        okr = pr;
                     }
                 }
             };
@@ -719,7 +803,6 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
             }
             if (p.q_area != 0) {
                 const int slot = j & 1;
-                if (ok && *abort) ok = false;
                 if (ok && j >= 2 &&
                     !mbar_wait(smem_u32(&qempty[slot]), static_cast<uint32_t>(((j >> 1) - 1) & 1), p.wait_limit)) {
                     if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
@@ -727,18 +810,19 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
                 }
                 if (ok && lane == 0) {
                     const uint32_t qb = smem_u32(&qfull[slot]);
-                    reinterpret_cast<volatile int*>(ps->issued)[kMaxStages + slot] = (j >> 1) + 1;
                     mbar_arrive_expect_tx(qb, q_bytes);
                     const char* src = static_cast<const char*>(p.q) +
                                       (static_cast<size_t>(sg.seq) * p.nh + static_cast<size_t>(kvh0) * p.g) * D * qelem;
                     bulk_load(smem_base + p.q_off + static_cast<uint32_t>(slot) * p.q_area, src, q_bytes, qb);
                 }
             }
+            if (p.q_area != 0 && ok) jq = j + 1;  // query loads 0 .. j issued
             if (appends) append_new_token<D>(p, sg.seq, len, trow, kvh0, lane);
             produce_range(first, sg.tile1);
             ++j;
         }
-        if (!ok || *abort) drain_copies(p, ps, full_bar, qfull, lane);
+        if (!ok || *reinterpret_cast<volatile int*>(&ps->abort))
+            drain_copies(p, full_bar, qfull, lane, okst, okr, fst0, fr0, fmask, jq, stall);
         return;
     }
     if (warp > NC) return;
@@ -812,7 +896,7 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
         // every writer warp of every CTA holding part of it has added (nseg * kvh_cta).  The add's old value
         // is only examined after the CTA's last segment, so no warp waits for its round trip or for another
         // warp here.
-        if (!sg.single && sg.nseg > 0) {
+        if (!sg.single && sg.nseg != 0) {
             if (sub == 0) {
                 __syncwarp();
                 if (lane == 0 && ok) {
@@ -821,9 +905,13 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
                 }
             }
             if (warp == 0 && lane == 0) {
+                int c0 = sg.c0, nseg = sg.nseg;
+                if constexpr (Segs::lazy_span) {
+                    if (nseg < 0) segs.span(p, sg.seq, c0, nseg);
+                }
                 pend[2 + 3 * np] = sg.seq;
-                pend[3 + 3 * np] = sg.c0;
-                pend[4 + 3 * np] = sg.nseg;
+                pend[3 + 3 * np] = c0;
+                pend[4 + 3 * np] = nseg;
             }
             ++np;
         }
@@ -986,14 +1074,14 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
     const long long T = P[ns];
     // With fewer tiles than CTAs only the first T CTAs work, so every working CTA owns >= 1 tile.
     const int Ge = static_cast<int>(min(static_cast<long long>(p.G), T));
-    StreamSegments segs;
+    StreamSegments<MergeShape<D, NT>::per_warp> segs;
     segs.P = P;
     segs.R = R;
-    segs.T = T;
-    segs.Ge = Ge;
+    const Partition part(T, Ge, p.taper_m, p.taper_d);
+    segs.part = part;
     segs.X = p.seq_units;
-    segs.t = Ge > 0 ? cta_begin(c, T, Ge) : 0;
-    segs.end = Ge > 0 ? cta_begin(c + 1, T, Ge) : 0;
+    segs.t = Ge > 0 ? part.begin(c) : 0;
+    segs.end = Ge > 0 ? part.begin(c + 1) : 0;
     segs.s = seq_of_tile(P, ns, segs.t);
     segs.cta = c;
     segs.nh = p.nh;

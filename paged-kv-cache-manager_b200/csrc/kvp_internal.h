@@ -51,6 +51,8 @@ struct AttnPlan {
     uint32_t q_off = 0, comb_off = 0;  // offsets of the query slots and of the warp-combine area
     uint32_t pre_off = 0;   // stream-K: offset of the prefix sums
     int seq_units = 0;      // stream-K: start-cost units charged ahead of each sequence's tiles
+    int taper_m = 0;        // stream-K: the last CTAs, which get fewer units (0: even split)
+    int taper_d = 0;        // units each of them gives up
     size_t smem = 0, ws_bytes = 0;
     size_t ws_ml_off = 0;   // byte offset of the partial (m, l) pairs in the workspace
     size_t ws_o_off = 0;    // byte offset of the partial outputs in the workspace
