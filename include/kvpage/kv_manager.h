@@ -77,6 +77,10 @@ public:
     // When on, every mutating call validates and throws std::logic_error on a violation.  Default: on in
     // builds without NDEBUG.
     void set_check_each_op(bool on) { check_each_op_ = on; }
+    // Calls so far that created, changed or removed a block table (admissions, forks, appends, frees): a caller
+    // mirroring tables elsewhere (the decode-step runtime's staged rows) can tell whether any table changed since
+    // it last looked.  Not part of the reference's interface.
+    uint64_t table_changes() const { return table_changes_; }
 
 private:
     struct PrefixEntry {
@@ -105,6 +109,7 @@ private:
     int64_t cow_events_ = 0;
     int64_t evictions_ = 0;
     int64_t clock_ = 0;
+    uint64_t table_changes_ = 0;
 #ifdef NDEBUG
     bool check_each_op_ = false;
 #else

@@ -105,6 +105,11 @@ struct kvp_decoder {
     Layout lay;
     char* ws = nullptr;
     int32_t* h_meta = nullptr;  // pinned staging with the same layout as the device meta region
+    // What the staging's table rows hold: the rows of `staged_rids` as of the manager's table_changes() count
+    // `staged_changes` (valid: a step completed its bookkeeping since the rows were last fully written).
+    bool staged_valid = false;
+    uint64_t staged_changes = 0;
+    std::vector<int64_t> staged_rids;
     size_t meta_bytes = 0;
     int64_t layer_stride = 0;   // elements
     cudaStream_t s_in = nullptr, s_comp = nullptr, s_out = nullptr;
@@ -138,18 +143,26 @@ struct kvp_decoder {
 namespace {
 
 // Host bookkeeping of a step: appends, copy-on-write pairs, table rows and lengths into the pinned staging
-// (the fused append derives each written slot from the table row and the length).  Returns KVP_OK or
-// KVP_ENOSPACE (an append found no block).
+// (the fused append derives each written slot from the table row and the length).  When the batch is the
+// previous step's, in the same order, and no table changed in between (the manager's change count), the staged
+// rows are still current except for what this step's appends change -- only the last entry of a row -- so
+// only those entries are written (a full row rewrite cost about 40 us per step for 256 requests of 1,100
+// tokens, 190 us at 4,400).  Returns KVP_OK or KVP_ENOSPACE (an append found no block).
 int host_step(kvp_decoder* d, const int64_t* rids, int n) {
     kvp::KVManager& m = d->mgr->m;
     const kvp_decoder_config& c = d->cfg;
     const int B = c.block_size, MB = c.max_blocks_per_seq;
     int32_t* tables = d->h_meta;
     int32_t* lens = tables + static_cast<size_t>(n) * MB;
+    const bool incremental = d->staged_valid && d->staged_changes == m.table_changes() &&
+                             d->staged_rids.size() == static_cast<size_t>(n) &&
+                             std::memcmp(d->staged_rids.data(), rids, sizeof(int64_t) * static_cast<size_t>(n)) == 0;
+    d->staged_valid = false;  // until this step's bookkeeping completes
     d->pairs.clear();
     for (int i = 0; i < n; ++i) {
         const kvp::BlockTable& t = m.table(rids[i]);
         const int pos = t.tokens;
+        const size_t size_before = t.blocks.size();
         const kvp::BlockId old_last = t.blocks.empty() ? kvp::kNoBlock : t.blocks.back();
         if (!m.append_token(rids[i])) return kvpi::fail(KVP_ENOSPACE, "no free block for request " + std::to_string(rids[i]));
         if (pos % B != 0 && t.blocks.back() != old_last) {
@@ -159,9 +172,16 @@ int host_step(kvp_decoder* d, const int64_t* rids, int n) {
         if (static_cast<int>(t.blocks.size()) > MB)
             return kvpi::fail(KVP_EBOUNDS, "request " + std::to_string(rids[i]) + " outgrew max_blocks_per_seq");
         lens[i] = t.tokens;
-        std::memcpy(tables + static_cast<size_t>(i) * MB, t.blocks.data(), sizeof(int32_t) * t.blocks.size());
+        int32_t* row = tables + static_cast<size_t>(i) * MB;
+        if (!incremental)
+            std::memcpy(row, t.blocks.data(), sizeof(int32_t) * t.blocks.size());
+        else if (t.blocks.size() != size_before || t.blocks.back() != old_last)
+            row[t.blocks.size() - 1] = t.blocks.back();
     }
     std::memcpy(lens + n, d->pairs.data(), sizeof(int32_t) * d->pairs.size());
+    d->staged_rids.assign(rids, rids + n);
+    d->staged_changes = m.table_changes();
+    d->staged_valid = true;
     return KVP_OK;
 }
 
@@ -253,7 +273,7 @@ int enqueue_layers(kvp_decoder* d, int n, const void* q, const void* knew, const
 }
 
 // Layers per output copy: enough consecutive layers that each copy moves at least ~512 KB (small copies pay a
-// fixed cost each on the copy engines), while the last group -- whose copy nothing overlaps -- stays small.
+// fixed cost each on the copy engines); the last layer is copied on its own (nothing overlaps that copy).
 int layers_per_copy(const kvp_decoder_config& c, int n) {
     const size_t q_layer = static_cast<size_t>(n) * c.num_heads * c.head_dim * elem(c.q_dtype);
     const size_t want = size_t(512) << 10;
@@ -304,7 +324,8 @@ int enqueue_host_body(kvp_decoder* d, int n, const char* hq, const char* hk, con
         }
         const int rc = launch_layer(d, n, l, dq, dk, dv, dout, d->s_comp);
         if (rc != KVP_OK) return rc;
-        if (l + 1 - out0 == per || l + 1 == L) {  // an output group is complete
+        // An output group is complete -- the last layer always gets its own, since nothing overlaps its copy.
+        if (l + 1 - out0 == per || l + 1 == L || l + 2 == L) {
             const size_t L0 = static_cast<size_t>(out0), G = static_cast<size_t>(l + 1 - out0);
             e = cudaEventRecord(d->ev_att[oi], d->s_comp);
             if (e == cudaSuccess) e = cudaStreamWaitEvent(d->s_out, d->ev_att[oi], 0);

@@ -173,6 +173,7 @@ bool KVManager::admit_shared(RequestId r, const std::vector<BlockId>& shared, in
     }
     table_entries_ += static_cast<int64_t>(t.blocks.size());
     requests_.emplace(r, std::move(t));
+    ++table_changes_;
     checkpoint();
     return true;
 }
@@ -209,6 +210,7 @@ bool KVManager::fork(RequestId r, RequestId parent) {
     for (BlockId b : child.blocks) pool_.retain(b);
     table_entries_ += static_cast<int64_t>(child.blocks.size());
     requests_.emplace(r, std::move(child));
+    ++table_changes_;
     checkpoint();
     return true;
 }
@@ -238,6 +240,7 @@ bool KVManager::append_token(RequestId r) {
         filled_slots_ += 1;
     }
     t.tokens += 1;
+    ++table_changes_;
     checkpoint();
     return true;
 }
@@ -248,6 +251,7 @@ void KVManager::free(RequestId r) {
     for (BlockId b : it->second.blocks) drop_ref(b);
     table_entries_ -= static_cast<int64_t>(it->second.blocks.size());
     requests_.erase(it);
+    ++table_changes_;
     checkpoint();
 }
 

@@ -114,3 +114,51 @@ def test_decoder_reports_exhaustion(kvb, cuda):
         dec.step([0, 1], z, zk, zk, z.clone())  # both need a new block; only one is free
     assert e.value.code == kvb.KVP_ENOSPACE
     assert m.num_tokens(0) == 33 and m.num_tokens(1) == 16  # the first append happened, the second did not
+
+
+@pytest.mark.parametrize("path", ["host", "device"])
+def test_decoder_staging_follows_external_table_changes(kvb, cuda, path):
+    """The same batch in the same order step after step (the decoder then rewrites only the table entries its own
+    appends changed), with the tables changed behind its back between steps: a request freed and re-admitted
+    under the same id with another length, and an append made through the manager directly.  Every step must
+    still equal the hand-driven path bit for bit."""
+    import torch
+    nh, kvh, D, L, MB = 8, 2, 64, 4, 40
+    k1, v1, m1 = _setup(kvb, 7)
+    k2, v2 = k1.clone(), v1.clone()
+    _, _, m2 = _setup(kvb, 7)
+    dec = kvb.Decoder(m1, k1, v1, nh, max_seqs=8, max_blocks_per_seq=MB)
+    order = [3, 0, 4, 1, 2]
+    n = len(order)
+    side = torch.cuda.Stream()
+    hbufs = [torch.empty(s, dtype=torch.bfloat16).pin_memory() for s in ((L, n, nh, D), (L, n, kvh, D), (L, n, kvh, D),
+                                                                        (L, n, nh, D))]
+    dbufs = [b.cuda() for b in hbufs]
+    for step in range(9):
+        if step == 3:  # request 1 freed and re-admitted under its id with a different length, on both managers
+            for m in (m1, m2):
+                m.free(1)
+                assert m.admit(1, 90)
+        if step == 6:  # an append made outside the decoder
+            for m in (m1, m2):
+                assert m.append_token(4)
+        q = torch.randn((L, n, nh, D)).to(torch.bfloat16)
+        kn = torch.randn((L, n, kvh, D)).to(torch.bfloat16)
+        vn = torch.randn((L, n, kvh, D)).to(torch.bfloat16)
+        if path == "host":
+            hq, hk, hv, ho = hbufs
+            hq.copy_(q), hk.copy_(kn), hv.copy_(vn)
+            dec.step(order, hq, hk, hv, ho)
+            out1 = ho.clone()
+        else:
+            dq, dk, dv, do = dbufs
+            dq.copy_(q), dk.copy_(kn), dv.copy_(vn)
+            side.wait_stream(torch.cuda.current_stream())
+            dec.step_device(np.asarray(order, dtype=np.int64), dq, dk, dv, do, stream=side)
+            torch.cuda.synchronize()
+            out1 = do.cpu()
+        out2 = _manual_step(kvb, m2, k2, v2, order, q.cuda(), kn.cuda(), vn.cuda(), 0, MB, nh, kvh)
+        torch.cuda.synchronize()
+        assert torch.equal(out1, out2.cpu()), step
+        assert torch.equal(k1, k2) and torch.equal(v1, v2), step
+    assert dec.status() == 0
