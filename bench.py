@@ -579,6 +579,7 @@ def run_ours(args, cfg, rank, world, dev):
     del stepper
     torch.cuda.empty_cache()
     dec = kvb.Decoder(mgr, kc, vc, nh, max_seqs=ns, max_blocks_per_seq=max_blocks)
+    rids = np.arange(ns, dtype=np.int64)  # the batch as the C ABI takes it (no per-step conversion)
     for _ in range(W):
         dec.step(rids, h_q, h_k, h_v, h_out)
     if world > 1:

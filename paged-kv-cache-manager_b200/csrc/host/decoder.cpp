@@ -115,6 +115,7 @@ struct kvp_decoder {
     cudaStream_t s_in = nullptr, s_comp = nullptr, s_out = nullptr;
     cudaEvent_t ev_staged = nullptr;  // after the latest metadata upload (the pinned staging is reusable)
     cudaEvent_t ev_fork = nullptr, ev_join_in = nullptr, ev_join_out = nullptr;
+    cudaEvent_t ev_first = nullptr;  // after the copy of layer 0's inputs, issued before the step's bookkeeping
     std::vector<cudaEvent_t> ev_q, ev_att;
     std::vector<int32_t> pairs;
     int device = 0;
@@ -130,7 +131,7 @@ struct kvp_decoder {
         if (h_meta) cudaFreeHost(h_meta);
         for (auto e : ev_q) cudaEventDestroy(e);
         for (auto e : ev_att) cudaEventDestroy(e);
-        for (auto e : {ev_staged, ev_fork, ev_join_in, ev_join_out})
+        for (auto e : {ev_staged, ev_fork, ev_join_in, ev_join_out, ev_first})
             if (e) cudaEventDestroy(e);
         for (auto s : {s_in, s_comp, s_out})
             if (s) cudaStreamDestroy(s);
@@ -280,14 +281,27 @@ int layers_per_copy(const kvp_decoder_config& c, int n) {
     return static_cast<int>(std::min<size_t>(static_cast<size_t>(c.num_layers), std::max<size_t>(1, (want + q_layer - 1) / q_layer)));
 }
 
+// Layer 0's inputs, copied up on the copy-in stream before the step's bookkeeping (they do not depend on it), so
+// the copy overlaps the host work; ev_first follows it.
+int copy_first_layer(kvp_decoder* d, int n, const char* hq, const char* hk, const char* hv) {
+    const kvp_decoder_config& c = d->cfg;
+    const size_t q_layer = static_cast<size_t>(n) * c.num_heads * c.head_dim * elem(c.q_dtype);
+    const size_t kv_layer = static_cast<size_t>(n) * c.kv_heads * c.head_dim * elem(c.kv_dtype);
+    cudaError_t e = cudaMemcpyAsync(d->ws + d->lay.q, hq, q_layer, cudaMemcpyHostToDevice, d->s_in);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d->ws + d->lay.k, hk, kv_layer, cudaMemcpyHostToDevice, d->s_in);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d->ws + d->lay.v, hv, kv_layer, cudaMemcpyHostToDevice, d->s_in);
+    if (e == cudaSuccess) e = cudaEventRecord(d->ev_first, d->s_in);
+    return kvpi::cuda_status(e, "decoder first-layer copy");
+}
+
 // The host-buffer step's device work after the metadata upload and the copy-on-write copies, forked from and
-// joined back into the compute stream.  Inputs go up on the copy-in stream in groups of 1, 2, 4, ... layers:
-// the first layer can start after one layer's copy, and the doubling groups land while earlier layers compute
-// with few copies and few waits (per-layer copies of a few hundred KB each fell behind the attention at the
-// TinyLlama shape: 1.49 ms per step against 1.34 ms with doubling groups on B200).  Each layer's attention
-// waits for its group on the compute stream; outputs go back on the copy-out stream in groups of
-// layers_per_copy() layers once their last launch is done.  The same calls are captured into one graph when a
-// step's key repeats.
+// joined back into the compute stream.  Layer 0's inputs are already on their way (copy_first_layer, ev_first:
+// an external event, so a captured graph waits for that step's copy, made outside it); the rest go up on the
+// copy-in stream in groups of 2, 4, ... layers, which land while earlier layers compute with few copies and few
+// waits (per-layer copies of a few hundred KB each fell behind the attention at the TinyLlama shape: 1.49 ms per
+// step against 1.34 ms with doubling groups on B200).  Each layer's attention waits for its group on the compute
+// stream; outputs go back on the copy-out stream in groups of layers_per_copy() layers once their last launch is
+// done.  The same calls are captured into one graph when a step's key repeats.
 int enqueue_host_body(kvp_decoder* d, int n, const char* hq, const char* hk, const char* hv, char* hout) {
     const kvp_decoder_config& c = d->cfg;
     const size_t q_layer = static_cast<size_t>(n) * c.num_heads * c.head_dim * elem(c.q_dtype);
@@ -302,9 +316,10 @@ int enqueue_host_body(kvp_decoder* d, int n, const char* hq, const char* hk, con
     cudaError_t e = cudaEventRecord(d->ev_fork, d->s_comp);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(d->s_in, d->ev_fork, 0);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(d->s_out, d->ev_fork, 0);
-    // copy-in groups [in0, in0 + g) with g = 1, 2, 4, ... (at most L groups: ev_q has one event per layer)
-    size_t gi = 0;
-    for (int in0 = 0, g = 1; e == cudaSuccess && in0 < L; in0 += g, g *= 2, ++gi) {
+    // copy-in groups [in0, in0 + g) with g = 1, 2, 4, ... (at most L groups: ev_q has one event per layer); the
+    // first (layer 0) was issued before the bookkeeping
+    size_t gi = 1;
+    for (int in0 = 1, g = 2; e == cudaSuccess && in0 < L; in0 += g, g *= 2, ++gi) {
         const size_t L0 = static_cast<size_t>(in0), G = static_cast<size_t>(std::min(g, L - in0));
         e = cudaMemcpyAsync(dq + q_layer * L0, hq + q_layer * L0, q_layer * G, cudaMemcpyHostToDevice, d->s_in);
         if (e == cudaSuccess)
@@ -317,7 +332,9 @@ int enqueue_host_body(kvp_decoder* d, int n, const char* hq, const char* hk, con
     size_t oi = 0;
     for (int l = 0, next_in = 0, g = 1, out0 = 0; e == cudaSuccess && l < L; ++l) {
         if (l == next_in) {  // the first layer of a copy-in group waits for the group
-            e = cudaStreamWaitEvent(d->s_comp, d->ev_q[gi++], 0);
+            e = gi == 0 ? cudaStreamWaitEvent(d->s_comp, d->ev_first, cudaEventWaitExternal)
+                        : cudaStreamWaitEvent(d->s_comp, d->ev_q[gi], 0);
+            ++gi;
             next_in += g;
             g *= 2;
             if (e != cudaSuccess) break;
@@ -517,6 +534,7 @@ KVP_API kvp_decoder* kvp_decoder_create(const kvp_decoder_config* c, kvp_mgr* mg
     ok = ok && cudaEventCreateWithFlags(&d->ev_fork, cudaEventDisableTiming) == cudaSuccess;
     ok = ok && cudaEventCreateWithFlags(&d->ev_join_in, cudaEventDisableTiming) == cudaSuccess;
     ok = ok && cudaEventCreateWithFlags(&d->ev_join_out, cudaEventDisableTiming) == cudaSuccess;
+    ok = ok && cudaEventCreateWithFlags(&d->ev_first, cudaEventDisableTiming) == cudaSuccess;
     d->ev_q.resize(static_cast<size_t>(c->num_layers));
     d->ev_att.resize(static_cast<size_t>(c->num_layers));
     for (int l = 0; ok && l < c->num_layers; ++l) {
@@ -573,6 +591,9 @@ KVP_API int kvp_decoder_step(kvp_decoder* d, const int64_t* rids, int32_t n, con
         DeviceScope scope(d->device);
         const kvp_decoder_config& c = d->cfg;
         int rc = wait_staging(d);
+        if (rc != KVP_OK) return rc;
+        rc = copy_first_layer(d, n, static_cast<const char*>(q), static_cast<const char*>(k_new),
+                              static_cast<const char*>(v_new));
         if (rc != KVP_OK) return rc;
         rc = host_step(d, rids, n);
         if (rc != KVP_OK) return rc;
