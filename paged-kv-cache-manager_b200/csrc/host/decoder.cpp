@@ -295,9 +295,9 @@ int copy_first_layer(kvp_decoder* d, int n, const char* hq, const char* hk, cons
 }
 
 // The host-buffer step's device work after the metadata upload and the copy-on-write copies, forked from and
-// joined back into the compute stream.  Layer 0's inputs are already on their way (copy_first_layer, ev_first:
-// an external event, so a captured graph waits for that step's copy, made outside it); the rest go up on the
-// copy-in stream in groups of 2, 4, ... layers, which land while earlier layers compute with few copies and few
+// joined back into the compute stream.  Layer 0's inputs are already up (copy_first_layer; the compute stream
+// waits for ev_first before this body is enqueued or replayed, so a captured graph holds no wait on a copy made
+// outside it); the rest go up on the copy-in stream in groups of 2, 4, ... layers, which land while earlier layers compute with few copies and few
 // waits (per-layer copies of a few hundred KB each fell behind the attention at the TinyLlama shape: 1.49 ms per
 // step against 1.34 ms with doubling groups on B200).  Each layer's attention waits for its group on the compute
 // stream; outputs go back on the copy-out stream in groups of layers_per_copy() layers once their last launch is
@@ -317,7 +317,7 @@ int enqueue_host_body(kvp_decoder* d, int n, const char* hq, const char* hk, con
     if (e == cudaSuccess) e = cudaStreamWaitEvent(d->s_in, d->ev_fork, 0);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(d->s_out, d->ev_fork, 0);
     // copy-in groups [in0, in0 + g) with g = 1, 2, 4, ... (at most L groups: ev_q has one event per layer); the
-    // first (layer 0) was issued before the bookkeeping
+    // first (layer 0) was issued before the bookkeeping and has been waited for
     size_t gi = 1;
     for (int in0 = 1, g = 2; e == cudaSuccess && in0 < L; in0 += g, g *= 2, ++gi) {
         const size_t L0 = static_cast<size_t>(in0), G = static_cast<size_t>(std::min(g, L - in0));
@@ -331,9 +331,8 @@ int enqueue_host_body(kvp_decoder* d, int n, const char* hq, const char* hk, con
     gi = 0;
     size_t oi = 0;
     for (int l = 0, next_in = 0, g = 1, out0 = 0; e == cudaSuccess && l < L; ++l) {
-        if (l == next_in) {  // the first layer of a copy-in group waits for the group
-            e = gi == 0 ? cudaStreamWaitEvent(d->s_comp, d->ev_first, cudaEventWaitExternal)
-                        : cudaStreamWaitEvent(d->s_comp, d->ev_q[gi], 0);
+        if (l == next_in) {  // the first layer of a copy-in group (after layer 0's) waits for the group
+            if (gi > 0) e = cudaStreamWaitEvent(d->s_comp, d->ev_q[gi], 0);
             ++gi;
             next_in += g;
             g *= 2;
@@ -602,6 +601,8 @@ KVP_API int kvp_decoder_step(kvp_decoder* d, const int64_t* rids, int32_t n, con
         if (rc != KVP_OK) return rc;
         const int32_t* d_pairs = d->d_meta() + static_cast<size_t>(n) * c.max_blocks_per_seq + n;
         rc = launch_cow(d, d_pairs, d->s_comp);
+        if (rc != KVP_OK) return rc;
+        rc = kvpi::cuda_status(cudaStreamWaitEvent(d->s_comp, d->ev_first, 0), "decoder first-layer wait");
         if (rc != KVP_OK) return rc;
         bool launched = false;
         if (c.graph && !d->graph_off) {
