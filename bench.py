@@ -330,13 +330,18 @@ def setup_shard(kvb, cfg, lens, steps_total, dev, seed):
             flat[o: o + n].copy_(chunk[:n])
     del chunk
     torch.cuda.empty_cache()
-    # Manager: requests admitted empty, then grown block by block in a random interleaving, so tables are
-    # fragmented the way a long-running server's are.
     mgr = kvb.KVManager(nb, B)
-    for r in range(ns):
+    grow_requests(mgr, lens, B, seed + 1)
+    return mgr, kc, vc, nb
+
+
+def grow_requests(mgr, lens, B, seed):
+    """Requests 0 .. len(lens)-1 admitted empty, then grown block by block in a random interleaving to their
+    lengths, so tables are fragmented the way a long-running server's are."""
+    for r in range(len(lens)):
         assert mgr.admit(r, 0)
-    rng = np.random.default_rng(seed + 1)
-    remaining = lens.copy()
+    rng = np.random.default_rng(seed)
+    remaining = np.asarray(lens).copy()
     while remaining.max() > 0:
         order = rng.permutation(np.nonzero(remaining > 0)[0])
         rids = []
@@ -346,7 +351,6 @@ def setup_shard(kvb, cfg, lens, steps_total, dev, seed):
             remaining[r] -= k
         done, _, _ = mgr.append_batch(rids)
         assert done == len(rids)
-    return mgr, kc, vc, nb
 
 
 class DecodeStep:
@@ -504,7 +508,7 @@ def run_ours(args, cfg, rank, world, dev):
     lens = all_lens[sh.shard_of(rank_of, rank)]
     ns = len(lens)
     W, K = args.warmup, args.steps
-    steps_total = W + K + 2 * (W + K)  # value run, then e2e run
+    steps_total = W + K + 2  # the value run's steps; the e2e run regrows the requests and takes as many
     mgr, kc, vc, nb = setup_shard(kvb, cfg, lens, steps_total, dev, seed=rank * 7 + 1)
     tdt = kc.dtype
     rids = list(range(ns))
@@ -578,6 +582,11 @@ def run_ours(args, cfg, rank, world, dev):
     h_out = torch.empty((L, ns, nh, D), dtype=tdt).pin_memory()
     del stepper
     torch.cuda.empty_cache()
+    # The requests are freed and regrown to their starting lengths (new fragmented tables over the same pool),
+    # so the e2e run's W + K steps attend over the same context lengths as the value run's.
+    for r in rids:
+        mgr.free(r)
+    grow_requests(mgr, lens, B, seed=rank * 7 + 3)
     dec = kvb.Decoder(mgr, kc, vc, nh, max_seqs=ns, max_blocks_per_seq=max_blocks)
     rids = np.arange(ns, dtype=np.int64)  # the batch as the C ABI takes it (no per-step conversion)
     for _ in range(W):
