@@ -11,6 +11,8 @@ Inputs are synthetic, seeded N(0,1).
           per-layer launches replayed from a CUDA graph, or launched from Python with --eager)
   e2e   : the same step through the C ABI with host buffers: per-layer queries and new K/V copied from pinned
           host memory, the host KVManager step, and the attention output copied back, inside the timed region
+          (the requests regrown to the value run's starting lengths; each step's bookkeeping planned while the
+          previous step runs)
   roofline : the attention kernel's algorithmic bytes (unique K/V bytes of the contexts) per launch / its
           average duration (CUDA events around each launch with --eager; otherwise the replayed steps' CUDA-event
           time over their launches, gaps between launches included), against the measured HBM copy peak
@@ -508,7 +510,7 @@ def run_ours(args, cfg, rank, world, dev):
     lens = all_lens[sh.shard_of(rank_of, rank)]
     ns = len(lens)
     W, K = args.warmup, args.steps
-    steps_total = W + K + 2  # the value run's steps; the e2e run regrows the requests and takes as many
+    steps_total = W + K + 2  # the value run's steps; the e2e run regrows the requests and takes W + K + 1
     mgr, kc, vc, nb = setup_shard(kvb, cfg, lens, steps_total, dev, seed=rank * 7 + 1)
     tdt = kc.dtype
     rids = list(range(ns))
@@ -573,9 +575,10 @@ def run_ours(args, cfg, rank, world, dev):
                     lens_mean=float(lens.mean()), per_rank_ms=per_rank, sample=sample), lens
 
     # ---------------------------------------------------------------- e2e through the C ABI, host buffers
-    # One kvp_decoder_step per decode step: host KVManager appends, metadata upload, new K/V and per-layer
+    # Per decode step through the decoder's C ABI: host KVManager appends, metadata upload, new K/V and per-layer
     # queries copied in from pinned host memory, copy-on-write + fused append/attention for every layer, and
-    # each layer's output copied back, with the copies overlapping the attention of other layers.
+    # each layer's output copied back, with the copies overlapping the attention of other layers; the next
+    # step's appends are planned while the step runs (kvp_decoder_submit / plan / wait).
     h_q = torch.randn((L, ns, nh, D), generator=torch.Generator().manual_seed(5)).to(tdt).pin_memory()
     h_k = torch.randn((L, ns, kvh, D), generator=torch.Generator().manual_seed(6)).to(tdt).pin_memory()
     h_v = torch.randn((L, ns, kvh, D), generator=torch.Generator().manual_seed(7)).to(tdt).pin_memory()
@@ -589,8 +592,17 @@ def run_ours(args, cfg, rank, world, dev):
     grow_requests(mgr, lens, B, seed=rank * 7 + 3)
     dec = kvb.Decoder(mgr, kc, vc, nh, max_seqs=ns, max_blocks_per_seq=max_blocks)
     rids = np.arange(ns, dtype=np.int64)  # the batch as the C ABI takes it (no per-step conversion)
+
+    def e2e_step():
+        # a serving loop's step: submit it (inputs copied up, launches), plan the next step's bookkeeping while
+        # it runs, then wait for its outputs to reach the host
+        dec.submit(rids, h_q, h_k, h_v, h_out)
+        dec.plan(rids)
+        dec.wait()
+
+    dec.plan(rids)
     for _ in range(W):
-        dec.step(rids, h_q, h_k, h_v, h_out)
+        e2e_step()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
@@ -598,7 +610,7 @@ def run_ours(args, cfg, rank, world, dev):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(K):
-        dec.step(rids, h_q, h_k, h_v, h_out)
+        e2e_step()
     e1.record(stream)
     torch.cuda.synchronize(dev)
     wall_ms = (time.perf_counter() - t0) * 1e3

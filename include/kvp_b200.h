@@ -97,6 +97,17 @@ typedef struct kvp_attn_args {
     /* tuning (balanced schedule), 0: automatic: a sequence's start cost, in 16-token tiles, charged to the CTA
      * that starts it when the step's tiles are divided between CTAs; < 0: none */
     int32_t seq_start_tiles;
+    /* Inputs written by a copy on another stream (null: none; fp16/bf16 pools): the kernel reads q, k_new and
+     * v_new only once this device word is non-zero -- the copy stream writes it after the data -- so the
+     * launch needs no stream wait on that copy, which would keep it from starting during the previous kernel
+     * (KVP_ATTN_EARLY_START / EARLY_LOAD).  The inputs are then the copy's, not the previous kernel's: with
+     * KVP_ATTN_EARLY_LOAD the queries are loaded, and the first ring of tiles attended, before the kernel waits
+     * for the previous one (every global write still waits for it).  With inputs_epoch (a device word, set before the launch) the
+     * condition is instead (*inputs_ready - *inputs_epoch) >= 0 as a signed 32-bit difference, so a flag
+     * that a copy sets to each step's epoch needs no reset between steps.  The wait is bounded
+     * (KVP_STATUS_TIMEOUT).  Both 4-byte aligned. */
+    const int32_t* inputs_ready;
+    const int32_t* inputs_epoch;
 } kvp_attn_args;
 
 /* The caller guarantees the workspace's counter words are zero, so the call skips resetting them: true for
@@ -346,6 +357,19 @@ KVP_API int kvp_decoder_step(kvp_decoder* d, const int64_t* rids, int32_t n, con
  * bookkeeping and the small table upload are done before returning). */
 KVP_API int kvp_decoder_step_device(kvp_decoder* d, const int64_t* rids, int32_t n, const void* q,
                                     const void* k_new, const void* v_new, void* out, void* stream);
+/* Pipelined steps.  kvp_decoder_submit() is kvp_decoder_step() without the wait: it issues the step's copies
+ * and launches and returns; kvp_decoder_wait() returns once the submitted step's outputs are in host memory
+ * (a submit, step or step_device call waits for a submitted step first).  kvp_decoder_plan() does the NEXT
+ * step's bookkeeping now -- its KVManager appends (the manager reflects them at once), copy-on-write pairs and
+ * staged tables, in the staging buffer the submitted step does not use -- so that it overlaps the submitted
+ * step on the device.  The next submit / step / step_device must then be for the same requests in the same
+ * order (else KVP_EINVAL, and the planned appends stay in the manager); if the caller changed any table
+ * between the plan and that call, the planned tables are re-read from the manager.  A second plan before that
+ * call is KVP_ESTATE.  A serving loop: plan(batch); per step: submit(batch) -> plan(next batch) -> wait(). */
+KVP_API int kvp_decoder_submit(kvp_decoder* d, const int64_t* rids, int32_t n, const void* q, const void* k_new,
+                               const void* v_new, void* out);
+KVP_API int kvp_decoder_plan(kvp_decoder* d, const int64_t* rids, int32_t n);
+KVP_API int kvp_decoder_wait(kvp_decoder* d);
 /* OR of the KVP_STATUS_* bits the decoder's kernels reported so far (synchronises the decoder's streams). */
 KVP_API int kvp_decoder_status(kvp_decoder* d);
 

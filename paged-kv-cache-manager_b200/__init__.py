@@ -53,7 +53,7 @@ class AttnArgs(C.Structure):
                 ("block_size", _i32), ("max_blocks", _i32), ("scale", _f32), ("split_tiles", _i32),
                 ("kv_heads_per_cta", _i32), ("stages", _i32), ("workspace", _vp), ("workspace_bytes", _sz),
                 ("status", _vp), ("warps_per_kv_head", _i32), ("flags", _i32), ("k_new", _vp), ("v_new", _vp),
-                ("seq_start_tiles", _i32)]
+                ("seq_start_tiles", _i32), ("inputs_ready", _vp), ("inputs_epoch", _vp)]
 
 
 class AppendArgs(C.Structure):
@@ -140,6 +140,9 @@ _SIGNATURES = [
     ("kvp_decoder_destroy", None, [_vp]),
     ("kvp_decoder_step", C.c_int, [_vp, _pi64, _i32, _vp, _vp, _vp, _vp]),
     ("kvp_decoder_step_device", C.c_int, [_vp, _pi64, _i32, _vp, _vp, _vp, _vp, _vp]),
+    ("kvp_decoder_submit", C.c_int, [_vp, _pi64, _i32, _vp, _vp, _vp, _vp]),
+    ("kvp_decoder_plan", C.c_int, [_vp, _pi64, _i32]),
+    ("kvp_decoder_wait", C.c_int, [_vp]),
     ("kvp_decoder_status", C.c_int, [_vp]),
 ]
 
@@ -398,9 +401,10 @@ def _stream_ptr(stream):
 
 def attention_args(q, k_cache, v_cache, block_tables, seq_lens, out, num_heads, kv_heads, *, num_blocks=None,
                    workspace=None, split_tiles=0, kv_heads_per_cta=0, stages=0, status=None, scale=0.0,
-                   warps_per_kv_head=0, k_new=None, v_new=None, seq_start_tiles=0) -> AttnArgs:
+                   warps_per_kv_head=0, k_new=None, v_new=None, seq_start_tiles=0, inputs_ready=None) -> AttnArgs:
     """AttnArgs for one layer; k_cache/v_cache are [num_blocks][B][kv_heads][D] (or views of them).  With
-    k_new/v_new ([num_seqs][kv_heads][D], pool dtype) the kernel first writes each sequence's newest token."""
+    k_new/v_new ([num_seqs][kv_heads][D], pool dtype) the kernel first writes each sequence's newest token.
+    inputs_ready: an int32 device word the kernel waits for (non-zero) before it reads q / k_new / v_new."""
     nb, B, kvh, D = k_cache.shape[-4:]
     assert kvh == kv_heads
     a = AttnArgs()
@@ -424,6 +428,8 @@ def attention_args(q, k_cache, v_cache, block_tables, seq_lens, out, num_heads, 
             if tuple(t.shape) != (q.shape[0], kv_heads, D) or t.dtype != k_cache.dtype or not t.is_contiguous():
                 raise ValueError(f"{name} must be a contiguous [num_seqs][kv_heads][head_dim] tensor in the pool dtype")
         a.k_new, a.v_new = _dev(k_new, "k_new"), _dev(v_new, "v_new")
+    if inputs_ready is not None:
+        a.inputs_ready = _dev(inputs_ready, "inputs_ready")
     return a
 
 
@@ -647,6 +653,26 @@ class Decoder:
                 raise ValueError("decoder.step takes contiguous host tensors")
         _check(self._L.kvp_decoder_step(self._h, r.ctypes.data_as(_pi64), len(r), q.data_ptr(), k_new.data_ptr(),
                                          v_new.data_ptr(), out.data_ptr()))
+
+    def submit(self, rids, q, k_new, v_new, out):
+        """step() without the wait: issues the step's copies and launches and returns; `out` is complete after
+        wait()."""
+        r = self._rids(rids)
+        for t in (q, k_new, v_new, out):
+            if t.is_cuda or not t.is_contiguous():
+                raise ValueError("decoder.submit takes contiguous host tensors")
+        _check(self._L.kvp_decoder_submit(self._h, r.ctypes.data_as(_pi64), len(r), q.data_ptr(),
+                                           k_new.data_ptr(), v_new.data_ptr(), out.data_ptr()))
+
+    def plan(self, rids):
+        """The next step's bookkeeping now (its KVManager appends happen at once), overlapping a submitted step;
+        the next submit / step / step_device must be for the same requests in the same order."""
+        r = self._rids(rids)
+        _check(self._L.kvp_decoder_plan(self._h, r.ctypes.data_as(_pi64), len(r)))
+
+    def wait(self):
+        """Returns once the submitted step's outputs are in host memory."""
+        _check(self._L.kvp_decoder_wait(self._h))
 
     def step_device(self, rids, q, k_new, v_new, out, stream=None):
         r = self._rids(rids)

@@ -347,6 +347,8 @@ int attention_call(const kvp_attn_args* a, void* stream, long long wait_limit, i
         if (!aligned16(a->k_new) || !aligned16(a->v_new)) return fail(KVP_EINVAL, "k_new / v_new must be 16-byte aligned");
         if (a->num_blocks <= 0) return fail(KVP_EINVAL, "the fused append needs num_blocks (it bounds the written slot)");
     }
+    if ((reinterpret_cast<uintptr_t>(a->inputs_ready) | reinterpret_cast<uintptr_t>(a->inputs_epoch)) & 3u)
+        return fail(KVP_EINVAL, "inputs_ready / inputs_epoch must be 4-byte aligned");
     AttnPlan pl;
     int rc = plan_attention(*a, a->workspace != nullptr, &pl);
     if (rc != KVP_OK) return rc;
@@ -434,6 +436,8 @@ int attention_call(const kvp_attn_args* a, void* stream, long long wait_limit, i
     prm.taper_d = pl.taper_d;
     prm.wait_limit = wait_limit;
     prm.stall_first_stage = stall;
+    prm.inputs_ready = a->inputs_ready;
+    prm.inputs_epoch = a->inputs_ready ? a->inputs_epoch : nullptr;
     const float scale = a->scale > 0.f ? a->scale : 1.0f / std::sqrt(static_cast<float>(a->head_dim));
     prm.sl2 = scale * 1.4426950408889634f;
     cudaStream_t s = static_cast<cudaStream_t>(stream);

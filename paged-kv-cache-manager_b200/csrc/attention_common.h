@@ -62,6 +62,11 @@ struct AttnParams {
     // for 16 bytes of a copy it never issues and starts its tiles at stage 1, so the consumers' first wait runs
     // out; nothing is ever in flight for stage 0.
     int stall_first_stage;
+    // Inputs produced by copies on another stream (null: none): the queries and the fused append's new K/V are
+    // read only once this word is non-zero -- or, with inputs_epoch, once (word - *inputs_epoch) >= 0 as a
+    // 32-bit signed difference (bounded wait, KVP_STATUS_TIMEOUT).
+    const int32_t* inputs_ready;
+    const int32_t* inputs_epoch;
 };
 
 // Per-CTA pipeline state in shared memory: `abort` is raised by a consumer warp whose wait gave up, so the

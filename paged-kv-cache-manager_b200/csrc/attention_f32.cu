@@ -162,6 +162,7 @@ int launch_attention_f32(const kvp_attn_args& a, cudaStream_t s) {
     if (g > 8 && D > 128) return fail(KVP_EINVAL, "head_dim 256 supports at most 8 query heads per kv head");
     if (a.block_size < 1 || a.max_blocks < 1 || a.num_seqs < 0) return fail(KVP_EINVAL, "bad block_size / max_blocks / num_seqs");
     if (a.k_new || a.v_new) return fail(KVP_EINVAL, "the fused append needs fp16 or bf16 pools");
+    if (a.inputs_ready) return fail(KVP_EINVAL, "inputs_ready needs fp16 or bf16 pools");
     if ((reinterpret_cast<uintptr_t>(a.k_cache) | reinterpret_cast<uintptr_t>(a.v_cache)) & 3u)
         return fail(KVP_EINVAL, "fp32 pools must be 4-byte aligned");
     if (static_cast<long long>(a.num_seqs) * a.kv_heads > 0x7fffffffLL) return fail(KVP_EINVAL, "too many sequences");

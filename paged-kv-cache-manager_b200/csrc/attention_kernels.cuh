@@ -123,9 +123,9 @@ __device__ __forceinline__ void append_new_token(const AttnParams& p, int seq, i
         uint4* kd = static_cast<uint4*>(p.k_pool) + dst;
         uint4* vd = static_cast<uint4*>(p.v_pool) + dst;
         const int chunks = p.kvh_cta * D / 8;
-        for (int c = lane; c < chunks; c += 32) {
-            kd[c] = __ldg(ks + c);
-            vd[c] = __ldg(vs + c);
+        for (int c = lane; c < chunks; c += 32) {  // coherent loads: another stream's copy may have written them
+            kd[c] = __ldcg(ks + c);
+            vd[c] = __ldcg(vs + c);
         }
     }
     fence_proxy_async_global();
@@ -791,15 +791,41 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
                 }
             };
             const bool appends = p.k_new != nullptr && sg.tile1 == ((len + 15) >> 4);
+            // L2 prefetches of the rows a segment start reads after the wait (its queries and, for the segment
+            // holding the newest token, the new K/V): a prefetch is only a hint, safe before the wait even for
+            // rows the previous kernel writes, and the loads after it then come from L2 instead of DRAM.  Left
+            // out of the register-heavy instantiations (their spills would grow).
+            auto prefetch_rows = [&](int seq, bool with_new) {
+                if constexpr (MergeShape<D, NT>::per_warp) return;
+                if (seq >= p.num_seqs) return;
+                const char* qs = static_cast<const char*>(p.q) +
+                                 (static_cast<size_t>(seq) * p.nh + static_cast<size_t>(kvh0) * p.g) * D * qelem;
+                for (uint32_t o = static_cast<uint32_t>(lane) * 128u; o < q_bytes; o += 32u * 128u) prefetch_l2(qs + o);
+                if (with_new && lane < 2) {
+                    const size_t off = (static_cast<size_t>(seq) * p.kvh + kvh0) * D * 2;
+                    const char* src = static_cast<const char*>(lane ? p.v_new : p.k_new) + off;
+                    for (int o = 0; o < p.kvh_cta * D * 2; o += 128) prefetch_l2(src + o);
+                }
+            };
             int first = sg.tile0;
             if (!waited) {
                 // Early load: the first tiles of the CTA's range -- one ring at most, so no stage has to be freed
                 // by the consumers, and short of the tile the fused append writes into -- before waiting for the
-                // previous kernel; queries, the append and every write come after the wait.
+                // previous kernel; queries, the append and every write come after the wait.  Queries that a copy
+                // on another stream produces (inputs_ready) are not the previous kernel's: they are loaded before
+                // the wait too, so the consumers may work through the first ring during the previous kernel
+                // (they wait for it before their first global write).
                 first = min(sg.tile1 - (appends ? 1 : 0), sg.tile0 + S);
                 produce_range(sg.tile0, first);
-                griddep_wait();
-                waited = true;
+                if (p.inputs_ready == nullptr) prefetch_rows(sg.seq, appends);
+                if (p.inputs_ready == nullptr) {
+                    griddep_wait();
+                    waited = true;
+                }
+            }
+            if (j == 0 && p.inputs_ready != nullptr && ok && !warp_wait_flag(p.inputs_ready, p.inputs_epoch, p.wait_limit)) {
+                if (lane == 0) report(p.status, KVP_STATUS_TIMEOUT);
+                ok = false;
             }
             if (p.q_area != 0) {
                 const int slot = j & 1;
@@ -817,7 +843,12 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
                 }
             }
             if (p.q_area != 0 && ok) jq = j + 1;  // query loads 0 .. j issued
-            if (appends) append_new_token<D>(p, sg.seq, len, trow, kvh0, lane);
+            if (!waited) {
+                griddep_wait();
+                waited = true;
+            }
+            if (appends && ok) append_new_token<D>(p, sg.seq, len, trow, kvh0, lane);
+            prefetch_rows(sg.seq + 1, p.k_new != nullptr);  // the next segment of the range, if any, starts it
             produce_range(first, sg.tile1);
             ++j;
         }
@@ -841,6 +872,9 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
     // parts of a longer sequence); pend[k] flags a merge, pend[2 + 3k ..] holds (seq, c0, nseg); old0 / old1
     // hold a writer warp's counter values from before its adds.
     int np = 0, old0 = -1, old1 = -1;
+    // Consumers can only run ahead of the producer's wait for the previous kernel when the queries came from
+    // another stream's copy (see the producer); then their first global write waits for that kernel itself.
+    bool cwaited = waited || p.inputs_ready == nullptr;
     while (segs.next(sg)) {
         const int len = sg.len;
         if (p.q_area != 0) {
@@ -856,6 +890,13 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
             __syncwarp();
             if (ok && lane == 0) mbar_arrive(smem_u32(&qempty[slot]));
         } else {
+            if (j == 0 && p.inputs_ready != nullptr && ok && !warp_wait_flag(p.inputs_ready, p.inputs_epoch, p.wait_limit)) {
+                if (lane == 0) {
+                    report(p.status, KVP_STATUS_TIMEOUT);
+                    *reinterpret_cast<volatile int*>(&ps->abort) = 1;
+                }
+                ok = false;
+            }
             cs.load_q_global(p, sg.seq, kvh_global, lane);
         }
         cs.reset();
@@ -889,6 +930,10 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
             if (sub == 0)
                 for (int k = 1; k < p.wph; ++k) cs.merge_state(area + (k - 1) * stride, lane);
             named_barrier(1 + head, p.wph * 32);  // the area is rewritten by the next segment
+        }
+        if (!cwaited) {
+            griddep_wait();
+            cwaited = true;
         }
         if (sub == 0 && ok) cs.finish(p, lane, sg.seq, kvh_global, sg.single, sg.part_row);
         // Stream-K, sequence split across CTAs: each head's writer warp counts its partial rows as done with

@@ -28,8 +28,13 @@ constexpr int kMaxSplitsCap = 64;  // most fixed splits per sequence the decoder
 size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 int elem(int dt) { return dt == KVP_DTYPE_F32 ? 4 : 2; }
 
+// Int32 words at the head of the meta region: the step's epoch (host-buffer steps count 1, 2, ...; the kernels
+// of a step compare the input-ready flags against it), padded to 16 bytes.
+constexpr int kHeadWords = 4;
+
 struct Layout {
-    size_t meta = 0;        // [tables max_seqs*max_blocks][lens][pairs 2*max_seqs] int32
+    size_t meta = 0;        // [epoch + pad][tables max_seqs*max_blocks][lens][pairs 2*max_seqs] int32
+    size_t flags = 0;       // int32 per layer: input-ready flags, set to the step's epoch by the copy-in stream
     size_t status = 0;      // int32
     size_t attn = 0;        // split partials
     size_t q = 0, k = 0, v = 0, out = 0;  // host-path staging
@@ -42,7 +47,9 @@ Layout layout_of(const kvp_decoder_config& c) {
     const size_t ns = static_cast<size_t>(c.max_seqs);
     size_t o = 0;
     L.meta = o;
-    o = align256(o + sizeof(int32_t) * (ns * static_cast<size_t>(c.max_blocks_per_seq) + 3 * ns));
+    o = align256(o + sizeof(int32_t) * (kHeadWords + ns * static_cast<size_t>(c.max_blocks_per_seq) + 3 * ns));
+    L.flags = o;
+    o = align256(o + sizeof(int32_t) * static_cast<size_t>(c.num_layers));
     L.status = o;
     o = align256(o + sizeof(int32_t));
     L.attn = o;
@@ -99,25 +106,43 @@ struct GraphKey {
     bool operator==(const GraphKey& o) const { return n == o.n && q == o.q && k == o.k && v == o.v && out == o.out; }
 };
 
+// One of the two pinned staging buffers of step metadata (same layout as the device meta region), and what its
+// table rows hold: row i is request rids[i]'s table with sizes[i] entries, as of the manager's table_changes()
+// count `changes`, when the decoder's own appends had reached `ours` (valid: a step's bookkeeping completed
+// since the rows were last fully written).
+struct Staging {
+    int32_t* base = nullptr;  // pinned: the epoch word and its padding, then `h`
+    int32_t* h = nullptr;     // tables, lengths, pairs
+    cudaEvent_t ev = nullptr;  // after the latest upload from `h` (it is writable again)
+    std::vector<int32_t> pairs;  // the copy-on-write pairs of the step staged here (src, dst, ...)
+    bool valid = false;
+    uint64_t changes = 0, ours = 0;
+    std::vector<int64_t> rids;
+    std::vector<int32_t> sizes;
+};
+
 struct kvp_decoder {
     kvp_decoder_config cfg{};
     kvp_mgr* mgr = nullptr;
     Layout lay;
     char* ws = nullptr;
-    int32_t* h_meta = nullptr;  // pinned staging with the same layout as the device meta region
-    // What the staging's table rows hold: the rows of `staged_rids` as of the manager's table_changes() count
-    // `staged_changes` (valid: a step completed its bookkeeping since the rows were last fully written).
-    bool staged_valid = false;
-    uint64_t staged_changes = 0;
-    std::vector<int64_t> staged_rids;
+    // Double-buffered staging: a step's bookkeeping (or the next step's, planned while this one runs) writes
+    // one buffer while the other may still be read by an upload in flight.
+    Staging stg[2];
+    int next = 0;                // the buffer the next step's bookkeeping writes
+    uint64_t our_appends = 0;    // appends this decoder made through the manager
+    // A planned step (kvp_decoder_plan): its bookkeeping is done and staged in stg[plan_buf].
+    bool planned = false;
+    int plan_buf = 0;
+    uint64_t plan_changes = 0;
+    bool submitted = false;      // a host-buffer step was submitted and not yet waited for
+    int32_t* h_epoch = nullptr;  // pinned: the current host-buffer step's epoch, the source of the flags' copies
+    int32_t epoch = 0;
     size_t meta_bytes = 0;
     int64_t layer_stride = 0;   // elements
     cudaStream_t s_in = nullptr, s_comp = nullptr, s_out = nullptr;
-    cudaEvent_t ev_staged = nullptr;  // after the latest metadata upload (the pinned staging is reusable)
     cudaEvent_t ev_fork = nullptr, ev_join_in = nullptr, ev_join_out = nullptr;
-    cudaEvent_t ev_first = nullptr;  // after the copy of layer 0's inputs, issued before the step's bookkeeping
-    std::vector<cudaEvent_t> ev_q, ev_att;
-    std::vector<int32_t> pairs;
+    std::vector<cudaEvent_t> ev_att;
     int device = 0;
     GraphKey last_key, exec_key;  // the previous step's key; the key the instantiated graph was captured for
     cudaGraphExec_t exec = nullptr;
@@ -128,70 +153,103 @@ struct kvp_decoder {
     ~kvp_decoder() {
         if (exec) cudaGraphExecDestroy(exec);
         if (exec_full) cudaGraphExecDestroy(exec_full);
-        if (h_meta) cudaFreeHost(h_meta);
-        for (auto e : ev_q) cudaEventDestroy(e);
+        if (h_epoch) cudaFreeHost(h_epoch);
+        for (Staging& b : stg) {
+            if (b.base) cudaFreeHost(b.base);
+            if (b.ev) cudaEventDestroy(b.ev);
+        }
         for (auto e : ev_att) cudaEventDestroy(e);
-        for (auto e : {ev_staged, ev_fork, ev_join_in, ev_join_out, ev_first})
+        for (auto e : {ev_fork, ev_join_in, ev_join_out})
             if (e) cudaEventDestroy(e);
         for (auto s : {s_in, s_comp, s_out})
             if (s) cudaStreamDestroy(s);
     }
 
-    int32_t* d_meta() const { return reinterpret_cast<int32_t*>(ws + lay.meta); }
+    int32_t* d_epoch() const { return reinterpret_cast<int32_t*>(ws + lay.meta); }
+    int32_t* d_meta() const { return d_epoch() + kHeadWords; }
+    int32_t* d_flags() const { return reinterpret_cast<int32_t*>(ws + lay.flags); }
     int32_t* d_status() const { return reinterpret_cast<int32_t*>(ws + lay.status); }
 };
 
 namespace {
 
-// Host bookkeeping of a step: appends, copy-on-write pairs, table rows and lengths into the pinned staging
-// (the fused append derives each written slot from the table row and the length).  When the batch is the
-// previous step's, in the same order, and no table changed in between (the manager's change count), the staged
-// rows are still current except for what this step's appends change -- only the last entry of a row -- so
-// only those entries are written (a full row rewrite cost about 40 us per step for 256 requests of 1,100
-// tokens, 190 us at 4,400).  Returns KVP_OK or KVP_ENOSPACE (an append found no block).
-int host_step(kvp_decoder* d, const int64_t* rids, int n) {
+// Host bookkeeping of a step into staging buffer `buf`: appends, copy-on-write pairs, table rows and lengths
+// (the fused append derives each written slot from the table row and the length).  When the buffer last
+// staged the same batch, in the same order, and every table change since then was one of this decoder's own
+// appends (the manager's change count against the decoder's append count), a row can only have changed from
+// its last staged entry on -- appends add entries and copy-on-write replaces the last one -- so only those
+// entries are written (a full row rewrite cost about 40 us per step for 256 requests of 1,100 tokens, 190 us
+// at 4,400).  Returns KVP_OK or KVP_ENOSPACE (an append found no block).
+int host_step(kvp_decoder* d, const int64_t* rids, int n, int buf) {
     kvp::KVManager& m = d->mgr->m;
     const kvp_decoder_config& c = d->cfg;
     const int B = c.block_size, MB = c.max_blocks_per_seq;
-    int32_t* tables = d->h_meta;
+    Staging& st = d->stg[buf];
+    int32_t* tables = st.h;
     int32_t* lens = tables + static_cast<size_t>(n) * MB;
-    const bool incremental = d->staged_valid && d->staged_changes == m.table_changes() &&
-                             d->staged_rids.size() == static_cast<size_t>(n) &&
-                             std::memcmp(d->staged_rids.data(), rids, sizeof(int64_t) * static_cast<size_t>(n)) == 0;
-    d->staged_valid = false;  // until this step's bookkeeping completes
-    d->pairs.clear();
+    const bool incremental = st.valid && m.table_changes() - st.changes == d->our_appends - st.ours &&
+                             st.rids.size() == static_cast<size_t>(n) &&
+                             std::memcmp(st.rids.data(), rids, sizeof(int64_t) * static_cast<size_t>(n)) == 0;
+    st.valid = false;  // until this step's bookkeeping completes
+    st.pairs.clear();
+    st.sizes.resize(static_cast<size_t>(n));
     for (int i = 0; i < n; ++i) {
         const kvp::BlockTable& t = m.table(rids[i]);
         const int pos = t.tokens;
-        const size_t size_before = t.blocks.size();
         const kvp::BlockId old_last = t.blocks.empty() ? kvp::kNoBlock : t.blocks.back();
         if (!m.append_token(rids[i])) return kvpi::fail(KVP_ENOSPACE, "no free block for request " + std::to_string(rids[i]));
+        ++d->our_appends;
         if (pos % B != 0 && t.blocks.back() != old_last) {
-            d->pairs.push_back(old_last);
-            d->pairs.push_back(t.blocks.back());
+            st.pairs.push_back(old_last);
+            st.pairs.push_back(t.blocks.back());
         }
-        if (static_cast<int>(t.blocks.size()) > MB)
+        const int size = static_cast<int>(t.blocks.size());
+        if (size > MB)
             return kvpi::fail(KVP_EBOUNDS, "request " + std::to_string(rids[i]) + " outgrew max_blocks_per_seq");
         lens[i] = t.tokens;
         int32_t* row = tables + static_cast<size_t>(i) * MB;
-        if (!incremental)
-            std::memcpy(row, t.blocks.data(), sizeof(int32_t) * t.blocks.size());
-        else if (t.blocks.size() != size_before || t.blocks.back() != old_last)
-            row[t.blocks.size() - 1] = t.blocks.back();
+        const int from = incremental ? std::max(0, std::min(st.sizes[static_cast<size_t>(i)], size) - 1) : 0;
+        std::memcpy(row + from, t.blocks.data() + from, sizeof(int32_t) * static_cast<size_t>(size - from));
+        st.sizes[static_cast<size_t>(i)] = size;
     }
-    std::memcpy(lens + n, d->pairs.data(), sizeof(int32_t) * d->pairs.size());
-    d->staged_rids.assign(rids, rids + n);
-    d->staged_changes = m.table_changes();
-    d->staged_valid = true;
+    std::memcpy(lens + n, st.pairs.data(), sizeof(int32_t) * st.pairs.size());
+    st.rids.assign(rids, rids + n);
+    st.changes = m.table_changes();
+    st.ours = d->our_appends;
+    st.valid = true;
+    return KVP_OK;
+}
+
+// Rewrites the rows and lengths of staging buffer `buf` from the manager (no appends): a planned step whose
+// tables the caller changed between the plan and the submit.  Its copy-on-write pairs stay as planned.
+int restage(kvp_decoder* d, const int64_t* rids, int n, int buf) {
+    kvp::KVManager& m = d->mgr->m;
+    const int MB = d->cfg.max_blocks_per_seq;
+    Staging& st = d->stg[buf];
+    int32_t* lens = st.h + static_cast<size_t>(n) * MB;
+    st.valid = false;
+    for (int i = 0; i < n; ++i) {
+        const kvp::BlockTable& t = m.table(rids[i]);
+        const int size = static_cast<int>(t.blocks.size());
+        if (size > MB)
+            return kvpi::fail(KVP_EBOUNDS, "request " + std::to_string(rids[i]) + " outgrew max_blocks_per_seq");
+        std::memcpy(st.h + static_cast<size_t>(i) * MB, t.blocks.data(), sizeof(int32_t) * static_cast<size_t>(size));
+        st.sizes[static_cast<size_t>(i)] = size;
+        lens[i] = t.tokens;
+    }
+    st.changes = m.table_changes();
+    st.ours = d->our_appends;
+    st.valid = true;
     return KVP_OK;
 }
 
 
 // Copy-on-write launches in order-preserving chunks: a pair whose destination is the source of an earlier
 // pair of the chunk starts a new chunk, so every block is read before it is overwritten.
-int launch_cow(kvp_decoder* d, const int32_t* d_pairs, cudaStream_t s) {
+int launch_cow(kvp_decoder* d, const int32_t* d_pairs, cudaStream_t s, int buf) {
     const kvp_decoder_config& c = d->cfg;
-    const int npairs = static_cast<int>(d->pairs.size() / 2);
+    const std::vector<int32_t>& pairs = d->stg[buf].pairs;
+    const int npairs = static_cast<int>(pairs.size() / 2);
     int start = 0;
     std::unordered_set<int32_t> srcs;
     auto flush = [&](int end) {
@@ -212,21 +270,22 @@ int launch_cow(kvp_decoder* d, const int32_t* d_pairs, cudaStream_t s) {
         return kvp_cow_copy(&a, s);
     };
     for (int k = 0; k < npairs; ++k) {
-        if (srcs.count(d->pairs[2 * k + 1])) {
+        if (srcs.count(pairs[2 * k + 1])) {
             int rc = flush(k);
             if (rc != KVP_OK) return rc;
             start = k;
             srcs.clear();
         }
-        srcs.insert(d->pairs[2 * k]);
+        srcs.insert(pairs[2 * k]);
     }
     return flush(npairs);
 }
 
 // Layer l's attention launch (fused append of its new token) on stream s; q / knew / vnew / out are the
-// device arrays of all layers.
+// device arrays of all layers; `ready`: the input-ready flag of the layer's copy-in group (null: its inputs
+// are in place before the launch).
 int launch_layer(kvp_decoder* d, int n, int l, const void* q, const void* knew, const void* vnew, void* out,
-                 cudaStream_t s) {
+                 cudaStream_t s, const int32_t* ready = nullptr) {
     const kvp_decoder_config& c = d->cfg;
     const int32_t* meta = d->d_meta();
     const size_t L = static_cast<size_t>(l);
@@ -260,6 +319,8 @@ int launch_layer(kvp_decoder* d, int n, int l, const void* q, const void* knew, 
     a.flags = KVP_ATTN_WORKSPACE_CLEAN | (l > 0 ? KVP_ATTN_EARLY_LOAD : KVP_ATTN_EARLY_START);
     a.k_new = static_cast<const char*>(knew) + kv_layer * L;  // fused append of this layer's new token
     a.v_new = static_cast<const char*>(vnew) + kv_layer * L;
+    a.inputs_ready = ready;
+    a.inputs_epoch = ready ? d->d_epoch() : nullptr;
     return kvp_paged_attention(&a, s);
 }
 
@@ -282,7 +343,7 @@ int layers_per_copy(const kvp_decoder_config& c, int n) {
 }
 
 // Layer 0's inputs, copied up on the copy-in stream before the step's bookkeeping (they do not depend on it), so
-// the copy overlaps the host work; ev_first follows it.
+// the copy overlaps the host work, then layer 0's input-ready flag.
 int copy_first_layer(kvp_decoder* d, int n, const char* hq, const char* hk, const char* hv) {
     const kvp_decoder_config& c = d->cfg;
     const size_t q_layer = static_cast<size_t>(n) * c.num_heads * c.head_dim * elem(c.q_dtype);
@@ -290,18 +351,22 @@ int copy_first_layer(kvp_decoder* d, int n, const char* hq, const char* hk, cons
     cudaError_t e = cudaMemcpyAsync(d->ws + d->lay.q, hq, q_layer, cudaMemcpyHostToDevice, d->s_in);
     if (e == cudaSuccess) e = cudaMemcpyAsync(d->ws + d->lay.k, hk, kv_layer, cudaMemcpyHostToDevice, d->s_in);
     if (e == cudaSuccess) e = cudaMemcpyAsync(d->ws + d->lay.v, hv, kv_layer, cudaMemcpyHostToDevice, d->s_in);
-    if (e == cudaSuccess) e = cudaEventRecord(d->ev_first, d->s_in);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d->d_flags(), d->h_epoch, sizeof(int32_t), cudaMemcpyHostToDevice, d->s_in);
     return kvpi::cuda_status(e, "decoder first-layer copy");
 }
 
 // The host-buffer step's device work after the metadata upload and the copy-on-write copies, forked from and
-// joined back into the compute stream.  Layer 0's inputs are already up (copy_first_layer; the compute stream
-// waits for ev_first before this body is enqueued or replayed, so a captured graph holds no wait on a copy made
-// outside it); the rest go up on the copy-in stream in groups of 2, 4, ... layers, which land while earlier layers compute with few copies and few
-// waits (per-layer copies of a few hundred KB each fell behind the attention at the TinyLlama shape: 1.49 ms per
-// step against 1.34 ms with doubling groups on B200).  Each layer's attention waits for its group on the compute
-// stream; outputs go back on the copy-out stream in groups of layers_per_copy() layers once their last launch is
-// done.  The same calls are captured into one graph when a step's key repeats.
+// joined back into the compute stream.  Layer 0's inputs are already on their way (copy_first_layer); the rest
+// go up on the copy-in stream in groups of 2, 4, ... layers, which land while earlier layers compute with few
+// copies (per-layer copies of a few hundred KB each fell behind the attention at the TinyLlama shape: 1.49 ms
+// per step against 1.34 ms with doubling groups on B200).  After each group the copy-in stream copies the
+// step's epoch into the group's input-ready flag, and the group's layers wait for it inside the kernel
+// (kvp_attn_args.inputs_ready / inputs_epoch: flag - epoch >= 0) rather than on the stream: a stream wait on
+// another stream's copy ends the early start of the launch after it, which cost 13-27 us per group on B200
+// (Qwen2.5-0.5B / TinyLlama shapes), and the epoch makes a step's flags current without a reset between steps.
+// Outputs go back on the copy-out stream in groups of layers_per_copy() layers once their last launch is done.
+// The same calls are captured into one graph when a step's key repeats (the flags' source is a pinned word the
+// host sets to the epoch before each step's copies).
 int enqueue_host_body(kvp_decoder* d, int n, const char* hq, const char* hk, const char* hv, char* hout) {
     const kvp_decoder_config& c = d->cfg;
     const size_t q_layer = static_cast<size_t>(n) * c.num_heads * c.head_dim * elem(c.q_dtype);
@@ -316,8 +381,8 @@ int enqueue_host_body(kvp_decoder* d, int n, const char* hq, const char* hk, con
     cudaError_t e = cudaEventRecord(d->ev_fork, d->s_comp);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(d->s_in, d->ev_fork, 0);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(d->s_out, d->ev_fork, 0);
-    // copy-in groups [in0, in0 + g) with g = 1, 2, 4, ... (at most L groups: ev_q has one event per layer); the
-    // first (layer 0) was issued before the bookkeeping and has been waited for
+    // copy-in groups [in0, in0 + g) with g = 1, 2, 4, ..., group gi's flag in word gi (fewer groups than layers);
+    // the first (layer 0) was issued before the bookkeeping and has been waited for
     size_t gi = 1;
     for (int in0 = 1, g = 2; e == cudaSuccess && in0 < L; in0 += g, g *= 2, ++gi) {
         const size_t L0 = static_cast<size_t>(in0), G = static_cast<size_t>(std::min(g, L - in0));
@@ -326,19 +391,18 @@ int enqueue_host_body(kvp_decoder* d, int n, const char* hq, const char* hk, con
             e = cudaMemcpyAsync(dk + kv_layer * L0, hk + kv_layer * L0, kv_layer * G, cudaMemcpyHostToDevice, d->s_in);
         if (e == cudaSuccess)
             e = cudaMemcpyAsync(dv + kv_layer * L0, hv + kv_layer * L0, kv_layer * G, cudaMemcpyHostToDevice, d->s_in);
-        if (e == cudaSuccess) e = cudaEventRecord(d->ev_q[gi], d->s_in);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(d->d_flags() + gi, d->h_epoch, sizeof(int32_t), cudaMemcpyHostToDevice, d->s_in);
     }
     gi = 0;
     size_t oi = 0;
     for (int l = 0, next_in = 0, g = 1, out0 = 0; e == cudaSuccess && l < L; ++l) {
-        if (l == next_in) {  // the first layer of a copy-in group (after layer 0's) waits for the group
-            if (gi > 0) e = cudaStreamWaitEvent(d->s_comp, d->ev_q[gi], 0);
+        if (l == next_in) {  // the first layer of the next copy-in group
             ++gi;
             next_in += g;
             g *= 2;
-            if (e != cudaSuccess) break;
         }
-        const int rc = launch_layer(d, n, l, dq, dk, dv, dout, d->s_comp);
+        const int rc = launch_layer(d, n, l, dq, dk, dv, dout, d->s_comp, d->d_flags() + (gi - 1));
         if (rc != KVP_OK) return rc;
         // An output group is complete -- the last layer always gets its own, since nothing overlaps its copy.
         if (l + 1 - out0 == per || l + 1 == L || l + 2 == L) {
@@ -407,10 +471,10 @@ bool capture_host_body(kvp_decoder* d, const GraphKey& key) {
 // Device-buffer step after the metadata upload: copy-on-write copies, then the layer launches (replayed from
 // a graph once the key repeats, unless the caller is capturing the stream itself).
 int enqueue_device(kvp_decoder* d, int n, const void* q, const void* knew, const void* vnew, void* out,
-                   cudaStream_t s_comp) {
+                   cudaStream_t s_comp, int buf) {
     const kvp_decoder_config& c = d->cfg;
     const int32_t* d_pairs = d->d_meta() + static_cast<size_t>(n) * c.max_blocks_per_seq + n;
-    int rc = launch_cow(d, d_pairs, s_comp);
+    int rc = launch_cow(d, d_pairs, s_comp, buf);
     if (rc != KVP_OK) return rc;
     if (c.graph && !d->graph_off) {
         GraphKey key;
@@ -434,16 +498,40 @@ int enqueue_device(kvp_decoder* d, int n, const void* q, const void* knew, const
     return enqueue_layers(d, n, q, knew, vnew, out, s_comp);
 }
 
-int upload_meta(kvp_decoder* d, int n, cudaStream_t s) {
-    const size_t ints = static_cast<size_t>(n) * d->cfg.max_blocks_per_seq + static_cast<size_t>(n) + d->pairs.size();
-    cudaError_t e = cudaMemcpyAsync(d->d_meta(), d->h_meta, ints * sizeof(int32_t), cudaMemcpyHostToDevice, s);
+// Uploads staging buffer `buf` into the device meta region on stream s; the buffer is the next one's to write.
+int upload_meta(kvp_decoder* d, int n, cudaStream_t s, int buf) {
+    Staging& st = d->stg[buf];
+    const size_t ints = static_cast<size_t>(kHeadWords) + static_cast<size_t>(n) * d->cfg.max_blocks_per_seq +
+                        static_cast<size_t>(n) + st.pairs.size();
+    st.base[0] = d->epoch;
+    cudaError_t e = cudaMemcpyAsync(d->d_epoch(), st.base, ints * sizeof(int32_t), cudaMemcpyHostToDevice, s);
     if (e != cudaSuccess) return kvpi::cuda_status(e, "decoder metadata upload");
-    e = cudaEventRecord(d->ev_staged, s);
+    e = cudaEventRecord(st.ev, s);
+    d->next = 1 - buf;
     return kvpi::cuda_status(e, "decoder record");
 }
 
-// The pinned staging may still be read by the previous step's upload.
-int wait_staging(kvp_decoder* d) { return kvpi::cuda_status(cudaEventSynchronize(d->ev_staged), "decoder staging wait"); }
+// Staging buffer `buf` may still be read by an earlier step's upload.
+int wait_staging(kvp_decoder* d, int buf) {
+    return kvpi::cuda_status(cudaEventSynchronize(d->stg[buf].ev), "decoder staging wait");
+}
+
+// The staged metadata of a step over `rids`: the planned step's (which must be this batch), re-read from the
+// manager if the caller changed any table since the plan, or else this step's bookkeeping now.  Sets *buf.
+int stage_step(kvp_decoder* d, const int64_t* rids, int n, int* buf) {
+    if (d->planned) {
+        d->planned = false;
+        const Staging& st = d->stg[d->plan_buf];
+        if (st.rids.size() != static_cast<size_t>(n) ||
+            std::memcmp(st.rids.data(), rids, sizeof(int64_t) * static_cast<size_t>(n)) != 0)
+            return kvpi::fail(KVP_EINVAL, "the step's batch differs from the planned batch (same requests, same order)");
+        *buf = d->plan_buf;
+        return d->mgr->m.table_changes() == d->plan_changes ? KVP_OK : restage(d, rids, n, *buf);
+    }
+    *buf = d->next;
+    const int rc = wait_staging(d, *buf);
+    return rc != KVP_OK ? rc : host_step(d, rids, n, *buf);
+}
 
 // Makes the decoder's device current for the scope of a call (its streams, events and launches belong to it).
 struct DeviceScope {
@@ -525,25 +613,31 @@ KVP_API kvp_decoder* kvp_decoder_create(const kvp_decoder_config* c, kvp_mgr* mg
                                           : c->num_blocks * c->block_size * static_cast<int64_t>(c->kv_heads) * c->head_dim;
     d->meta_bytes = lay.status - lay.meta;
     cudaGetDevice(&d->device);
-    bool ok = cudaHostAlloc(reinterpret_cast<void**>(&d->h_meta), d->meta_bytes, cudaHostAllocDefault) == cudaSuccess;
+    bool ok = true;
+    for (Staging& b : d->stg) {
+        ok = ok && cudaHostAlloc(reinterpret_cast<void**>(&b.base), d->meta_bytes, cudaHostAllocDefault) == cudaSuccess;
+        ok = ok && cudaEventCreateWithFlags(&b.ev, cudaEventDisableTiming) == cudaSuccess;
+        if (ok) {
+            std::memset(b.base, 0, sizeof(int32_t) * kHeadWords);
+            b.h = b.base + kHeadWords;
+        }
+    }
+    ok = ok && cudaHostAlloc(reinterpret_cast<void**>(&d->h_epoch), sizeof(int32_t), cudaHostAllocDefault) == cudaSuccess;
+    if (ok) *d->h_epoch = 0;
     ok = ok && cudaStreamCreateWithFlags(&d->s_in, cudaStreamNonBlocking) == cudaSuccess;
     ok = ok && cudaStreamCreateWithFlags(&d->s_comp, cudaStreamNonBlocking) == cudaSuccess;
     ok = ok && cudaStreamCreateWithFlags(&d->s_out, cudaStreamNonBlocking) == cudaSuccess;
-    ok = ok && cudaEventCreateWithFlags(&d->ev_staged, cudaEventDisableTiming) == cudaSuccess;
     ok = ok && cudaEventCreateWithFlags(&d->ev_fork, cudaEventDisableTiming) == cudaSuccess;
     ok = ok && cudaEventCreateWithFlags(&d->ev_join_in, cudaEventDisableTiming) == cudaSuccess;
     ok = ok && cudaEventCreateWithFlags(&d->ev_join_out, cudaEventDisableTiming) == cudaSuccess;
-    ok = ok && cudaEventCreateWithFlags(&d->ev_first, cudaEventDisableTiming) == cudaSuccess;
-    d->ev_q.resize(static_cast<size_t>(c->num_layers));
     d->ev_att.resize(static_cast<size_t>(c->num_layers));
-    for (int l = 0; ok && l < c->num_layers; ++l) {
-        ok = cudaEventCreateWithFlags(&d->ev_q[static_cast<size_t>(l)], cudaEventDisableTiming) == cudaSuccess &&
-             cudaEventCreateWithFlags(&d->ev_att[static_cast<size_t>(l)], cudaEventDisableTiming) == cudaSuccess;
-    }
+    for (int l = 0; ok && l < c->num_layers; ++l)
+        ok = cudaEventCreateWithFlags(&d->ev_att[static_cast<size_t>(l)], cudaEventDisableTiming) == cudaSuccess;
     ok = ok && cudaMemsetAsync(d->d_status(), 0, sizeof(int32_t), d->s_comp) == cudaSuccess;
+    ok = ok && cudaMemsetAsync(d->d_flags(), 0, sizeof(int32_t) * static_cast<size_t>(c->num_layers), d->s_comp) == cudaSuccess;
     // The attention workspace's merge counters start at zero and every completed call leaves them zero.
     if (lay.attn_bytes) ok = ok && cudaMemsetAsync(d->ws + lay.attn, 0, lay.attn_bytes, d->s_comp) == cudaSuccess;
-    ok = ok && cudaEventRecord(d->ev_staged, d->s_in) == cudaSuccess;
+    for (Staging& b : d->stg) ok = ok && cudaEventRecord(b.ev, d->s_in) == cudaSuccess;
     ok = ok && cudaStreamSynchronize(d->s_comp) == cudaSuccess;
     if (!ok) {
         kvpi::fail(KVP_ECUDA, std::string("decoder setup: ") + cudaGetErrorString(cudaGetLastError()));
@@ -570,39 +664,80 @@ KVP_API int kvp_decoder_step_device(kvp_decoder* d, const int64_t* rids, int32_t
         if (n == 0) return KVP_OK;
         DeviceScope scope(d->device);
         if (!kvpi::aligned16(k_new) || !kvpi::aligned16(v_new)) return kvpi::fail(KVP_EINVAL, "k_new / v_new must be 16-byte aligned");
-        int rc = wait_staging(d);
-        if (rc != KVP_OK) return rc;
-        rc = host_step(d, rids, n);
+        if (d->submitted) {  // a host-buffer step in flight on the decoder's streams reads the same meta region
+            const int rw = kvp_decoder_wait(d);
+            if (rw != KVP_OK) return rw;
+        }
+        int buf = 0;
+        int rc = stage_step(d, rids, n, &buf);
         if (rc != KVP_OK) return rc;
         cudaStream_t s = static_cast<cudaStream_t>(stream);
-        rc = upload_meta(d, n, s);
+        rc = upload_meta(d, n, s, buf);
         if (rc != KVP_OK) return rc;
-        return enqueue_device(d, n, q, k_new, v_new, out, s);
+        return enqueue_device(d, n, q, k_new, v_new, out, s, buf);
     });
 }
 
-KVP_API int kvp_decoder_step(kvp_decoder* d, const int64_t* rids, int32_t n, const void* q, const void* k_new,
-                             const void* v_new, void* out) {
+KVP_API int kvp_decoder_plan(kvp_decoder* d, const int64_t* rids, int32_t n) {
+    return guarded([&] {
+        if (!d || (n > 0 && !rids)) return kvpi::fail(KVP_EINVAL, "null argument");
+        if (n < 0 || n > d->cfg.max_seqs) return kvpi::fail(KVP_EINVAL, "n outside [0, max_seqs]");
+        if (d->planned) return kvpi::fail(KVP_ESTATE, "a step is already planned (submit it first)");
+        if (n == 0) return KVP_OK;
+        DeviceScope scope(d->device);
+        // The buffer the submitted step uploaded from may still be in flight; the other one is free once the
+        // upload before it completed (a step ago).
+        const int buf = d->next;
+        int rc = wait_staging(d, buf);
+        if (rc != KVP_OK) return rc;
+        rc = host_step(d, rids, n, buf);
+        if (rc != KVP_OK) return rc;
+        d->planned = true;
+        d->plan_buf = buf;
+        d->plan_changes = d->mgr->m.table_changes();
+        return KVP_OK;
+    });
+}
+
+KVP_API int kvp_decoder_wait(kvp_decoder* d) {
+    if (!d) return kvpi::fail(KVP_EINVAL, "null argument");
+    kvpi::clear_error();
+    DeviceScope scope(d->device);
+    d->submitted = false;
+    return kvpi::cuda_status(cudaStreamSynchronize(d->s_comp), "decoder step");  // outputs are in host memory
+}
+
+KVP_API int kvp_decoder_submit(kvp_decoder* d, const int64_t* rids, int32_t n, const void* q, const void* k_new,
+                               const void* v_new, void* out) {
     return guarded([&] {
         if (!d || (n > 0 && (!rids || !q || !k_new || !v_new || !out))) return kvpi::fail(KVP_EINVAL, "null argument");
         if (n < 0 || n > d->cfg.max_seqs) return kvpi::fail(KVP_EINVAL, "n outside [0, max_seqs]");
         if (n == 0) return KVP_OK;
         DeviceScope scope(d->device);
         const kvp_decoder_config& c = d->cfg;
-        int rc = wait_staging(d);
+        // The device staging of a step's inputs is single: a step still in flight finishes first.
+        if (d->submitted) {
+            const int rw = kvp_decoder_wait(d);
+            if (rw != KVP_OK) return rw;
+        }
+        // This step's epoch: the value its copies write into the input-ready flags (no copy of an earlier step
+        // is still pending, so the pinned source word is free), compared modulo 2^32.
+        d->epoch = static_cast<int32_t>(static_cast<uint32_t>(d->epoch) + 1u);
+        *d->h_epoch = d->epoch;
+        int rc = copy_first_layer(d, n, static_cast<const char*>(q), static_cast<const char*>(k_new),
+                                  static_cast<const char*>(v_new));
         if (rc != KVP_OK) return rc;
-        rc = copy_first_layer(d, n, static_cast<const char*>(q), static_cast<const char*>(k_new),
-                              static_cast<const char*>(v_new));
-        if (rc != KVP_OK) return rc;
-        rc = host_step(d, rids, n);
-        if (rc != KVP_OK) return rc;
+        int buf = 0;
+        rc = stage_step(d, rids, n, &buf);
+        if (rc != KVP_OK) {
+            cudaStreamSynchronize(d->s_in);  // the first layer's copy reads the caller's buffers
+            return rc;
+        }
         // compute stream: metadata, copy-on-write copies, then the step body (copies in, launches, copies out)
-        rc = upload_meta(d, n, d->s_comp);
+        rc = upload_meta(d, n, d->s_comp, buf);
         if (rc != KVP_OK) return rc;
         const int32_t* d_pairs = d->d_meta() + static_cast<size_t>(n) * c.max_blocks_per_seq + n;
-        rc = launch_cow(d, d_pairs, d->s_comp);
-        if (rc != KVP_OK) return rc;
-        rc = kvpi::cuda_status(cudaStreamWaitEvent(d->s_comp, d->ev_first, 0), "decoder first-layer wait");
+        rc = launch_cow(d, d_pairs, d->s_comp, buf);
         if (rc != KVP_OK) return rc;
         bool launched = false;
         if (c.graph && !d->graph_off) {
@@ -626,8 +761,15 @@ KVP_API int kvp_decoder_step(kvp_decoder* d, const int64_t* rids, int32_t n, con
                                    static_cast<const char*>(v_new), static_cast<char*>(out));
             if (rc != KVP_OK) return rc;
         }
-        return kvpi::cuda_status(cudaStreamSynchronize(d->s_comp), "decoder step");  // outputs are in host memory
+        d->submitted = true;
+        return KVP_OK;
     });
+}
+
+KVP_API int kvp_decoder_step(kvp_decoder* d, const int64_t* rids, int32_t n, const void* q, const void* k_new,
+                             const void* v_new, void* out) {
+    const int rc = kvp_decoder_submit(d, rids, n, q, k_new, v_new, out);
+    return rc != KVP_OK || !d || n == 0 ? rc : kvp_decoder_wait(d);
 }
 
 KVP_API int kvp_decoder_status(kvp_decoder* d) {

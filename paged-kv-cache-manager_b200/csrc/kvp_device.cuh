@@ -103,6 +103,27 @@ __device__ __forceinline__ void griddep_launch_dependents() { asm volatile("grid
 __device__ __forceinline__ void fence_proxy_async_global() {
     asm volatile("fence.proxy.async.global;" ::: "memory");
 }
+// Bounded wait of a whole warp until *flag != 0 -- or, with `epoch`, until *flag - *epoch >= 0 as a signed
+// 32-bit difference -- a word a copy on another stream writes after the data it guards: every lane's acquire
+// load at GPU scope orders its own later reads, and the proxy fence the bulk copies issued next.  False when
+// `limit` clock cycles passed first.
+__device__ __forceinline__ bool warp_wait_flag(const int32_t* flag, const int32_t* epoch, long long limit) {
+    const long long t0 = clock64();
+    const uint32_t e = epoch ? static_cast<uint32_t>(__ldcg(epoch)) : 0u;
+    for (unsigned ns = 32;; ns = ns < 1024 ? 2 * ns : ns) {
+        int v;
+        asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+        const bool ready = epoch ? static_cast<int32_t>(static_cast<uint32_t>(v) - e) >= 0 : v != 0;
+        if (__all_sync(0xffffffffu, ready)) break;
+        if (__any_sync(0xffffffffu, clock64() - t0 > limit)) return false;
+        __nanosleep(ns);
+    }
+    fence_proxy_async_global();
+    return true;
+}
+
+__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile(
         "{\n\t.reg .b64 st;\n\t"

@@ -162,3 +162,81 @@ def test_decoder_staging_follows_external_table_changes(kvb, cuda, path):
         assert torch.equal(out1, out2.cpu()), step
         assert torch.equal(k1, k2) and torch.equal(v1, v2), step
     assert dec.status() == 0
+
+
+@pytest.mark.parametrize("path", ["host", "device"])
+def test_decoder_pipelined_steps_match_manual_path(kvb, cuda, path):
+    """Pipelined steps: each step is submitted (host buffers) or enqueued (device buffers), the NEXT step's
+    bookkeeping is planned while it runs, and only then is it waited for.  Nine steps with the batch changing
+    once (the plan is made for the next step's batch) and, between one plan and its submit, an append made
+    through the manager directly (the planned tables are then re-read).  Outputs and pools equal the
+    hand-driven path bit for bit at every step."""
+    import torch
+    nh, kvh, D, L, MB = 8, 2, 64, 4, 40
+    k1, v1, m1 = _setup(kvb, 9)
+    k2, v2 = k1.clone(), v1.clone()
+    _, _, m2 = _setup(kvb, 9)
+    dec = kvb.Decoder(m1, k1, v1, nh, max_seqs=8, max_blocks_per_seq=MB)
+    rng = np.random.default_rng(4)
+    orders = [[int(x) for x in rng.permutation([0, 1, 2, 3, 4] if s < 5 else [0, 2, 4])] for s in range(9)]
+    side = torch.cuda.Stream()
+    bufs = {}
+    dec.plan(orders[0])
+    for step, order in enumerate(orders):
+        n = len(order)
+        if step == 6:  # an append made outside the decoder, between the plan of this step and its submit
+            for m in (m1, m2):
+                assert m.append_token(order[0])
+        q = torch.randn((L, n, nh, D)).to(torch.bfloat16)
+        kn = torch.randn((L, n, kvh, D)).to(torch.bfloat16)
+        vn = torch.randn((L, n, kvh, D)).to(torch.bfloat16)
+        if n not in bufs:
+            bufs[n] = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in (q, kn, vn, q)]
+            bufs[n] += [t.cuda() for t in bufs[n]]
+        hq, hk, hv, ho, dq, dk, dv, do = bufs[n]
+        if path == "host":
+            hq.copy_(q), hk.copy_(kn), hv.copy_(vn)
+            dec.submit(order, hq, hk, hv, ho)
+        else:
+            dq.copy_(q), dk.copy_(kn), dv.copy_(vn)
+            side.wait_stream(torch.cuda.current_stream())
+            dec.step_device(order, dq, dk, dv, do, stream=side)
+        if step + 1 < len(orders):
+            dec.plan(orders[step + 1])
+        if path == "host":
+            dec.wait()
+            out1 = ho.clone()
+        else:
+            torch.cuda.synchronize()
+            out1 = do.cpu()
+        out2 = _manual_step(kvb, m2, k2, v2, order, q.cuda(), kn.cuda(), vn.cuda(), 0, MB, nh, kvh)
+        torch.cuda.synchronize()
+        assert torch.equal(out1, out2.cpu()), step
+        assert torch.equal(k1, k2) and torch.equal(v1, v2), step
+    assert dec.status() == 0
+    assert m1.stats() == m2.stats()
+
+
+def test_decoder_plan_misuse(kvb, cuda):
+    """A second plan before the planned step is an error (KVP_ESTATE); a step over another batch than the
+    planned one is rejected (ValueError) and leaves the planned appends in the manager; a plan over an empty
+    batch is a no-op."""
+    import torch
+    nh, kvh, D, L, MB = 8, 2, 64, 4, 40
+    k, v, m = _setup(kvb, 11)
+    dec = kvb.Decoder(m, k, v, nh, max_seqs=8, max_blocks_per_seq=MB)
+    before = [m.num_tokens(r) for r in range(5)]
+    dec.plan([])
+    dec.plan([0, 1])
+    assert [m.num_tokens(r) for r in range(5)] == [before[0] + 1, before[1] + 1] + before[2:]
+    with pytest.raises(kvb.KVPError) as e:
+        dec.plan([0, 1])
+    assert e.value.code == kvb.KVP_ESTATE
+    z = torch.zeros((L, 2, nh, D), dtype=torch.bfloat16).pin_memory()
+    zk = torch.zeros((L, 2, kvh, D), dtype=torch.bfloat16).pin_memory()
+    with pytest.raises(ValueError, match="planned batch"):
+        dec.submit([1, 0], z, zk, zk, z.clone())
+    assert [m.num_tokens(r) for r in range(5)] == [before[0] + 1, before[1] + 1] + before[2:]
+    dec.step([1, 0], z, zk, zk, z.clone())  # no plan pending: a normal step
+    assert [m.num_tokens(r) for r in range(5)] == [before[0] + 2, before[1] + 2] + before[2:]
+    assert dec.status() == 0

@@ -1,8 +1,8 @@
 """kvp_paged_attention_noalloc: the attention entry point for callers that cannot allocate device memory
 (a serving engine whose memory manager has reserved the HBM for the KV pool, or a plugin whose enqueue
 callback may not allocate).  It keeps the split partials in a fixed array inside the library instead of a
-caller-provided workspace.  Checked through the C ABI against kvp_paged_attention with a workspace, on two
-calls in a row (the second sees whatever the first left in the shared array).  This file is collected
+caller-provided workspace.  Checked through the C ABI against the fp64 oracle and against kvp_paged_attention
+with a workspace, on two calls in a row (the second sees whatever the first left in the shared array).  This file is collected
 last so that a run stopping at its first failure has already run every other test."""
 import ctypes as C
 
@@ -62,13 +62,19 @@ def _close(got, want):
     assert (np.abs(g - w) <= ATOL + RTOL * np.abs(w)).all(), float(np.abs(g - w).max())
 
 
-def test_no_alloc_matches_workspace_entry_point_twice(kvb, cuda):
-    # Two consecutive calls with different inputs and split sizes, both compared with the entry point that
-    # takes a caller-allocated workspace.
-    for seed, lens, split in ((1, [700, 3000, 17, 1500, 64], 4), (2, [33, 4096, 2048, 1], 3)):
+def test_no_alloc_matches_workspace_entry_point_twice(kvb, ora, cuda):
+    # Two consecutive calls with different inputs and split sizes (and one with the balanced schedule), each
+    # checked against the fp64 oracle and against the entry point that takes a caller-allocated workspace.
+    from test_attention_gpu import check_close
+    for seed, lens, split in ((1, [700, 3000, 17, 1500, 64], 4), (2, [33, 4096, 2048, 1], 3), (3, [900, 5, 2500], 0)):
         args = _inputs(seed, lens)
-        want = _with_workspace(kvb, *args, split)
         got = _no_alloc(kvb, *args, split)
+        q, k, v, t, l, nh, kvh = args
+        ref = ora.reference_attention(nh, kvh, q.shape[2], k.shape[1], q.float().cpu().numpy(),
+                                      k.float().cpu().numpy(), v.float().cpu().numpy(), t.cpu().numpy(),
+                                      l.cpu().numpy())
+        check_close(got.cpu().numpy(), ref, what=f"no-alloc call (split {split})")
+        want = _with_workspace(kvb, *args, split)
         _close(got, want)
 
 
