@@ -791,22 +791,6 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
                 }
             };
             const bool appends = p.k_new != nullptr && sg.tile1 == ((len + 15) >> 4);
-            // L2 prefetches of the rows a segment start reads after the wait (its queries and, for the segment
-            // holding the newest token, the new K/V): a prefetch is only a hint, safe before the wait even for
-            // rows the previous kernel writes, and the loads after it then come from L2 instead of DRAM.  Left
-            // out of the register-heavy instantiations (their spills would grow).
-            auto prefetch_rows = [&](int seq, bool with_new) {
-                if constexpr (MergeShape<D, NT>::per_warp) return;
-                if (seq >= p.num_seqs) return;
-                const char* qs = static_cast<const char*>(p.q) +
-                                 (static_cast<size_t>(seq) * p.nh + static_cast<size_t>(kvh0) * p.g) * D * qelem;
-                for (uint32_t o = static_cast<uint32_t>(lane) * 128u; o < q_bytes; o += 32u * 128u) prefetch_l2(qs + o);
-                if (with_new && lane < 2) {
-                    const size_t off = (static_cast<size_t>(seq) * p.kvh + kvh0) * D * 2;
-                    const char* src = static_cast<const char*>(lane ? p.v_new : p.k_new) + off;
-                    for (int o = 0; o < p.kvh_cta * D * 2; o += 128) prefetch_l2(src + o);
-                }
-            };
             int first = sg.tile0;
             if (!waited) {
                 // Early load: the first tiles of the CTA's range -- one ring at most, so no stage has to be freed
@@ -817,7 +801,6 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
                 // (they wait for it before their first global write).
                 first = min(sg.tile1 - (appends ? 1 : 0), sg.tile0 + S);
                 produce_range(sg.tile0, first);
-                if (p.inputs_ready == nullptr) prefetch_rows(sg.seq, appends);
                 if (p.inputs_ready == nullptr) {
                     griddep_wait();
                     waited = true;
@@ -848,7 +831,6 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
                 waited = true;
             }
             if (appends && ok) append_new_token<D>(p, sg.seq, len, trow, kvh0, lane);
-            prefetch_rows(sg.seq + 1, p.k_new != nullptr);  // the next segment of the range, if any, starts it
             produce_range(first, sg.tile1);
             ++j;
         }

@@ -122,8 +122,6 @@ __device__ __forceinline__ bool warp_wait_flag(const int32_t* flag, const int32_
     return true;
 }
 
-__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
-
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile(
         "{\n\t.reg .b64 st;\n\t"
