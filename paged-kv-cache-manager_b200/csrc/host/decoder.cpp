@@ -9,6 +9,7 @@
 // its attention finishes, so transfers overlap the attention of other layers.  Once a step's key (batch size
 // and buffers) repeats, that whole body -- copies and launches on the three streams -- is replayed from one
 // CUDA graph, so a step costs the host a handful of runtime calls.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -28,13 +29,9 @@ constexpr int kMaxSplitsCap = 64;  // most fixed splits per sequence the decoder
 size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 int elem(int dt) { return dt == KVP_DTYPE_F32 ? 4 : 2; }
 
-// Int32 words at the head of the meta region: the step's epoch (host-buffer steps count 1, 2, ...; the kernels
-// of a step compare the input-ready flags against it), padded to 16 bytes.
-constexpr int kHeadWords = 4;
-
 struct Layout {
-    size_t meta = 0;        // [epoch + pad][tables max_seqs*max_blocks][lens][pairs 2*max_seqs] int32
-    size_t flags = 0;       // int32 per layer: input-ready flags, set to the step's epoch by the copy-in stream
+    size_t meta = 0;        // [tables max_seqs*max_blocks][lens][pairs 2*max_seqs] int32
+    size_t flags = 0;       // int32 per layer: input-ready flags (one per copy-in group), 1 while the group is up
     size_t status = 0;      // int32
     size_t attn = 0;        // split partials
     size_t q = 0, k = 0, v = 0, out = 0;  // host-path staging
@@ -47,7 +44,7 @@ Layout layout_of(const kvp_decoder_config& c) {
     const size_t ns = static_cast<size_t>(c.max_seqs);
     size_t o = 0;
     L.meta = o;
-    o = align256(o + sizeof(int32_t) * (kHeadWords + ns * static_cast<size_t>(c.max_blocks_per_seq) + 3 * ns));
+    o = align256(o + sizeof(int32_t) * (ns * static_cast<size_t>(c.max_blocks_per_seq) + 3 * ns));
     L.flags = o;
     o = align256(o + sizeof(int32_t) * static_cast<size_t>(c.num_layers));
     L.status = o;
@@ -111,8 +108,7 @@ struct GraphKey {
 // count `changes`, when the decoder's own appends had reached `ours` (valid: a step's bookkeeping completed
 // since the rows were last fully written).
 struct Staging {
-    int32_t* base = nullptr;  // pinned: the epoch word and its padding, then `h`
-    int32_t* h = nullptr;     // tables, lengths, pairs
+    int32_t* h = nullptr;  // pinned: tables, lengths, pairs
     cudaEvent_t ev = nullptr;  // after the latest upload from `h` (it is writable again)
     std::vector<int32_t> pairs;  // the copy-on-write pairs of the step staged here (src, dst, ...)
     bool valid = false;
@@ -136,8 +132,11 @@ struct kvp_decoder {
     int plan_buf = 0;
     uint64_t plan_changes = 0;
     bool submitted = false;      // a host-buffer step was submitted and not yet waited for
-    int32_t* h_epoch = nullptr;  // pinned: the current host-buffer step's epoch, the source of the flags' copies
-    int32_t epoch = 0;
+    // Input-ready flags are set by a stream memory operation (cuStreamWriteValue32: no copy-engine work) where the
+    // driver offers it inside graphs, else by a 4-byte copy from the pinned word h_one.
+    using WriteValueFn = CUresult (*)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
+    WriteValueFn write_value = nullptr;
+    int32_t* h_one = nullptr;
     size_t meta_bytes = 0;
     int64_t layer_stride = 0;   // elements
     cudaStream_t s_in = nullptr, s_comp = nullptr, s_out = nullptr;
@@ -153,9 +152,9 @@ struct kvp_decoder {
     ~kvp_decoder() {
         if (exec) cudaGraphExecDestroy(exec);
         if (exec_full) cudaGraphExecDestroy(exec_full);
-        if (h_epoch) cudaFreeHost(h_epoch);
+        if (h_one) cudaFreeHost(h_one);
         for (Staging& b : stg) {
-            if (b.base) cudaFreeHost(b.base);
+            if (b.h) cudaFreeHost(b.h);
             if (b.ev) cudaEventDestroy(b.ev);
         }
         for (auto e : ev_att) cudaEventDestroy(e);
@@ -165,8 +164,7 @@ struct kvp_decoder {
             if (s) cudaStreamDestroy(s);
     }
 
-    int32_t* d_epoch() const { return reinterpret_cast<int32_t*>(ws + lay.meta); }
-    int32_t* d_meta() const { return d_epoch() + kHeadWords; }
+    int32_t* d_meta() const { return reinterpret_cast<int32_t*>(ws + lay.meta); }
     int32_t* d_flags() const { return reinterpret_cast<int32_t*>(ws + lay.flags); }
     int32_t* d_status() const { return reinterpret_cast<int32_t*>(ws + lay.status); }
 };
@@ -320,7 +318,6 @@ int launch_layer(kvp_decoder* d, int n, int l, const void* q, const void* knew, 
     a.k_new = static_cast<const char*>(knew) + kv_layer * L;  // fused append of this layer's new token
     a.v_new = static_cast<const char*>(vnew) + kv_layer * L;
     a.inputs_ready = ready;
-    a.inputs_epoch = ready ? d->d_epoch() : nullptr;
     return kvp_paged_attention(&a, s);
 }
 
@@ -342,6 +339,14 @@ int layers_per_copy(const kvp_decoder_config& c, int n) {
     return static_cast<int>(std::min<size_t>(static_cast<size_t>(c.num_layers), std::max<size_t>(1, (want + q_layer - 1) / q_layer)));
 }
 
+// Sets an input-ready flag to 1 on stream s once the work before it in s is done.
+cudaError_t set_flag(kvp_decoder* d, int32_t* flag, cudaStream_t s) {
+    if (d->write_value)
+        return d->write_value(s, reinterpret_cast<CUdeviceptr>(flag), 1u, 0u) == CUDA_SUCCESS ? cudaSuccess
+                                                                                              : cudaErrorUnknown;
+    return cudaMemcpyAsync(flag, d->h_one, sizeof(int32_t), cudaMemcpyHostToDevice, s);
+}
+
 // Layer 0's inputs, copied up on the copy-in stream before the step's bookkeeping (they do not depend on it), so
 // the copy overlaps the host work, then layer 0's input-ready flag.
 int copy_first_layer(kvp_decoder* d, int n, const char* hq, const char* hk, const char* hv) {
@@ -351,7 +356,7 @@ int copy_first_layer(kvp_decoder* d, int n, const char* hq, const char* hk, cons
     cudaError_t e = cudaMemcpyAsync(d->ws + d->lay.q, hq, q_layer, cudaMemcpyHostToDevice, d->s_in);
     if (e == cudaSuccess) e = cudaMemcpyAsync(d->ws + d->lay.k, hk, kv_layer, cudaMemcpyHostToDevice, d->s_in);
     if (e == cudaSuccess) e = cudaMemcpyAsync(d->ws + d->lay.v, hv, kv_layer, cudaMemcpyHostToDevice, d->s_in);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(d->d_flags(), d->h_epoch, sizeof(int32_t), cudaMemcpyHostToDevice, d->s_in);
+    if (e == cudaSuccess) e = set_flag(d, d->d_flags(), d->s_in);
     return kvpi::cuda_status(e, "decoder first-layer copy");
 }
 
@@ -360,13 +365,13 @@ int copy_first_layer(kvp_decoder* d, int n, const char* hq, const char* hk, cons
 // go up on the copy-in stream in groups of 2, 4, ... layers, which land while earlier layers compute with few
 // copies (per-layer copies of a few hundred KB each fell behind the attention at the TinyLlama shape: 1.49 ms
 // per step against 1.34 ms with doubling groups on B200).  After each group the copy-in stream copies the
-// step's epoch into the group's input-ready flag, and the group's layers wait for it inside the kernel
-// (kvp_attn_args.inputs_ready / inputs_epoch: flag - epoch >= 0) rather than on the stream: a stream wait on
-// another stream's copy ends the early start of the launch after it, which cost 13-27 us per group on B200
-// (Qwen2.5-0.5B / TinyLlama shapes), and the epoch makes a step's flags current without a reset between steps.
-// Outputs go back on the copy-out stream in groups of layers_per_copy() layers once their last launch is done.
-// The same calls are captured into one graph when a step's key repeats (the flags' source is a pinned word the
-// host sets to the epoch before each step's copies).
+// group's input-ready flag to 1, and the group's layers wait for it inside the kernel (kvp_attn_args.inputs_ready)
+// rather than on the stream: a stream wait on another stream's copy ends the early start of the launch after it,
+// which cost 13-27 us per group on B200 (Qwen2.5-0.5B / TinyLlama shapes).  The flags are set by stream memory
+// operations where the driver allows them in graphs: a copy engine spends ~7 us on even a 4-byte copy (B200),
+// time the step's input copies wait for.  Once the last layer is done, the copy-in stream clears the flags for
+// the next step.  Outputs go back on the copy-out stream in groups of layers_per_copy() layers once their last
+// launch is done.  The same calls are captured into one graph when a step's key repeats.
 int enqueue_host_body(kvp_decoder* d, int n, const char* hq, const char* hk, const char* hv, char* hout) {
     const kvp_decoder_config& c = d->cfg;
     const size_t q_layer = static_cast<size_t>(n) * c.num_heads * c.head_dim * elem(c.q_dtype);
@@ -392,7 +397,7 @@ int enqueue_host_body(kvp_decoder* d, int n, const char* hq, const char* hk, con
         if (e == cudaSuccess)
             e = cudaMemcpyAsync(dv + kv_layer * L0, hv + kv_layer * L0, kv_layer * G, cudaMemcpyHostToDevice, d->s_in);
         if (e == cudaSuccess)
-            e = cudaMemcpyAsync(d->d_flags() + gi, d->h_epoch, sizeof(int32_t), cudaMemcpyHostToDevice, d->s_in);
+            e = set_flag(d, d->d_flags() + gi, d->s_in);
     }
     gi = 0;
     size_t oi = 0;
@@ -416,6 +421,9 @@ int enqueue_host_body(kvp_decoder* d, int n, const char* hq, const char* hk, con
             out0 = l + 1;
         }
     }
+    // every layer is done with the flags: clear them for the next step (beside the last output copy)
+    if (e == cudaSuccess && oi > 0) e = cudaStreamWaitEvent(d->s_in, d->ev_att[oi - 1], 0);
+    if (e == cudaSuccess) e = cudaMemsetAsync(d->d_flags(), 0, sizeof(int32_t) * gi, d->s_in);
     if (e == cudaSuccess) e = cudaEventRecord(d->ev_join_in, d->s_in);
     if (e == cudaSuccess) e = cudaEventRecord(d->ev_join_out, d->s_out);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(d->s_comp, d->ev_join_in, 0);
@@ -501,10 +509,8 @@ int enqueue_device(kvp_decoder* d, int n, const void* q, const void* knew, const
 // Uploads staging buffer `buf` into the device meta region on stream s; the buffer is the next one's to write.
 int upload_meta(kvp_decoder* d, int n, cudaStream_t s, int buf) {
     Staging& st = d->stg[buf];
-    const size_t ints = static_cast<size_t>(kHeadWords) + static_cast<size_t>(n) * d->cfg.max_blocks_per_seq +
-                        static_cast<size_t>(n) + st.pairs.size();
-    st.base[0] = d->epoch;
-    cudaError_t e = cudaMemcpyAsync(d->d_epoch(), st.base, ints * sizeof(int32_t), cudaMemcpyHostToDevice, s);
+    const size_t ints = static_cast<size_t>(n) * d->cfg.max_blocks_per_seq + static_cast<size_t>(n) + st.pairs.size();
+    cudaError_t e = cudaMemcpyAsync(d->d_meta(), st.h, ints * sizeof(int32_t), cudaMemcpyHostToDevice, s);
     if (e != cudaSuccess) return kvpi::cuda_status(e, "decoder metadata upload");
     e = cudaEventRecord(st.ev, s);
     d->next = 1 - buf;
@@ -555,6 +561,43 @@ int guarded(F&& f) {
     } catch (const std::exception& e) {
         return kvpi::fail(KVP_ESTATE, e.what());
     }
+}
+
+// Uses stream memory operations for the input-ready flags if the driver has cuStreamWriteValue32 and it works
+// both directly and captured in a graph (probed once on the decoder's first flag word, left zero); otherwise the
+// flags are set by copies.
+void probe_write_value(kvp_decoder* d) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuStreamWriteValue32", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !f) {
+        cudaGetLastError();
+        return;
+    }
+    const auto fn = reinterpret_cast<kvp_decoder::WriteValueFn>(f);
+    const CUdeviceptr flag = reinterpret_cast<CUdeviceptr>(d->d_flags());
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t ex = nullptr;
+    int32_t v = 0;
+    bool ok = cudaStreamBeginCapture(d->s_comp, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+    if (ok) {
+        const bool wrote = fn(d->s_comp, flag, 1u, 0u) == CUDA_SUCCESS;
+        ok = cudaStreamEndCapture(d->s_comp, &g) == cudaSuccess && wrote && g;
+    }
+    ok = ok && cudaGraphInstantiate(&ex, g, 0) == cudaSuccess && cudaGraphLaunch(ex, d->s_comp) == cudaSuccess &&
+         cudaMemcpyAsync(&v, d->d_flags(), sizeof(v), cudaMemcpyDeviceToHost, d->s_comp) == cudaSuccess &&
+         cudaStreamSynchronize(d->s_comp) == cudaSuccess && v == 1;
+    ok = ok && cudaMemsetAsync(d->d_flags(), 0, sizeof(int32_t), d->s_comp) == cudaSuccess &&
+         fn(d->s_comp, flag, 1u, 0u) == CUDA_SUCCESS &&
+         cudaMemcpyAsync(&v, d->d_flags(), sizeof(v), cudaMemcpyDeviceToHost, d->s_comp) == cudaSuccess &&
+         cudaStreamSynchronize(d->s_comp) == cudaSuccess && v == 1;
+    if (ex) cudaGraphExecDestroy(ex);
+    if (g) cudaGraphDestroy(g);
+    cudaGetLastError();
+    cudaMemsetAsync(d->d_flags(), 0, sizeof(int32_t), d->s_comp);
+    cudaStreamSynchronize(d->s_comp);
+    cudaGetLastError();
+    if (ok) d->write_value = fn;
 }
 
 }  // namespace
@@ -615,15 +658,11 @@ KVP_API kvp_decoder* kvp_decoder_create(const kvp_decoder_config* c, kvp_mgr* mg
     cudaGetDevice(&d->device);
     bool ok = true;
     for (Staging& b : d->stg) {
-        ok = ok && cudaHostAlloc(reinterpret_cast<void**>(&b.base), d->meta_bytes, cudaHostAllocDefault) == cudaSuccess;
+        ok = ok && cudaHostAlloc(reinterpret_cast<void**>(&b.h), d->meta_bytes, cudaHostAllocDefault) == cudaSuccess;
         ok = ok && cudaEventCreateWithFlags(&b.ev, cudaEventDisableTiming) == cudaSuccess;
-        if (ok) {
-            std::memset(b.base, 0, sizeof(int32_t) * kHeadWords);
-            b.h = b.base + kHeadWords;
-        }
     }
-    ok = ok && cudaHostAlloc(reinterpret_cast<void**>(&d->h_epoch), sizeof(int32_t), cudaHostAllocDefault) == cudaSuccess;
-    if (ok) *d->h_epoch = 0;
+    ok = ok && cudaHostAlloc(reinterpret_cast<void**>(&d->h_one), sizeof(int32_t), cudaHostAllocDefault) == cudaSuccess;
+    if (ok) *d->h_one = 1;
     ok = ok && cudaStreamCreateWithFlags(&d->s_in, cudaStreamNonBlocking) == cudaSuccess;
     ok = ok && cudaStreamCreateWithFlags(&d->s_comp, cudaStreamNonBlocking) == cudaSuccess;
     ok = ok && cudaStreamCreateWithFlags(&d->s_out, cudaStreamNonBlocking) == cudaSuccess;
@@ -639,6 +678,7 @@ KVP_API kvp_decoder* kvp_decoder_create(const kvp_decoder_config* c, kvp_mgr* mg
     if (lay.attn_bytes) ok = ok && cudaMemsetAsync(d->ws + lay.attn, 0, lay.attn_bytes, d->s_comp) == cudaSuccess;
     for (Staging& b : d->stg) ok = ok && cudaEventRecord(b.ev, d->s_in) == cudaSuccess;
     ok = ok && cudaStreamSynchronize(d->s_comp) == cudaSuccess;
+    if (ok) probe_write_value(d);
     if (!ok) {
         kvpi::fail(KVP_ECUDA, std::string("decoder setup: ") + cudaGetErrorString(cudaGetLastError()));
         delete d;
@@ -720,46 +760,52 @@ KVP_API int kvp_decoder_submit(kvp_decoder* d, const int64_t* rids, int32_t n, c
             const int rw = kvp_decoder_wait(d);
             if (rw != KVP_OK) return rw;
         }
-        // This step's epoch: the value its copies write into the input-ready flags (no copy of an earlier step
-        // is still pending, so the pinned source word is free), compared modulo 2^32.
-        d->epoch = static_cast<int32_t>(static_cast<uint32_t>(d->epoch) + 1u);
-        *d->h_epoch = d->epoch;
-        int rc = copy_first_layer(d, n, static_cast<const char*>(q), static_cast<const char*>(k_new),
-                                  static_cast<const char*>(v_new));
-        if (rc != KVP_OK) return rc;
-        int buf = 0;
-        rc = stage_step(d, rids, n, &buf);
-        if (rc != KVP_OK) {
-            cudaStreamSynchronize(d->s_in);  // the first layer's copy reads the caller's buffers
-            return rc;
-        }
-        // compute stream: metadata, copy-on-write copies, then the step body (copies in, launches, copies out)
-        rc = upload_meta(d, n, d->s_comp, buf);
-        if (rc != KVP_OK) return rc;
-        const int32_t* d_pairs = d->d_meta() + static_cast<size_t>(n) * c.max_blocks_per_seq + n;
-        rc = launch_cow(d, d_pairs, d->s_comp, buf);
-        if (rc != KVP_OK) return rc;
-        bool launched = false;
-        if (c.graph && !d->graph_off) {
-            GraphKey key;
-            key.n = n;
-            key.q = q;
-            key.k = k_new;
-            key.v = v_new;
-            key.out = out;
-            const bool repeat = key == d->last_full;
-            d->last_full = key;
-            if (!(d->exec_full && d->full_key == key) && repeat && !capture_host_body(d, key)) d->graph_off = true;
-            if (d->exec_full && d->full_key == key) {
-                const cudaError_t e = cudaGraphLaunch(d->exec_full, d->s_comp);
-                if (e != cudaSuccess) return kvpi::cuda_status(e, "decoder graph launch");
-                launched = true;
-            }
-        }
-        if (!launched) {
-            rc = enqueue_host_body(d, n, static_cast<const char*>(q), static_cast<const char*>(k_new),
-                                   static_cast<const char*>(v_new), static_cast<char*>(out));
+        const int rc = [&]() -> int {
+            int rc = copy_first_layer(d, n, static_cast<const char*>(q), static_cast<const char*>(k_new),
+                                      static_cast<const char*>(v_new));
             if (rc != KVP_OK) return rc;
+            int buf = 0;
+            rc = stage_step(d, rids, n, &buf);
+            if (rc != KVP_OK) return rc;
+            // compute stream: metadata, copy-on-write copies, then the step body (copies in, launches, copies out)
+            rc = upload_meta(d, n, d->s_comp, buf);
+            if (rc != KVP_OK) return rc;
+            const int32_t* d_pairs = d->d_meta() + static_cast<size_t>(n) * c.max_blocks_per_seq + n;
+            rc = launch_cow(d, d_pairs, d->s_comp, buf);
+            if (rc != KVP_OK) return rc;
+            bool launched = false;
+            if (c.graph && !d->graph_off) {
+                GraphKey key;
+                key.n = n;
+                key.q = q;
+                key.k = k_new;
+                key.v = v_new;
+                key.out = out;
+                const bool repeat = key == d->last_full;
+                d->last_full = key;
+                if (!(d->exec_full && d->full_key == key) && repeat && !capture_host_body(d, key)) d->graph_off = true;
+                if (d->exec_full && d->full_key == key) {
+                    const cudaError_t e = cudaGraphLaunch(d->exec_full, d->s_comp);
+                    if (e != cudaSuccess) return kvpi::cuda_status(e, "decoder graph launch");
+                    launched = true;
+                }
+            }
+            if (!launched) {
+                rc = enqueue_host_body(d, n, static_cast<const char*>(q), static_cast<const char*>(k_new),
+                                       static_cast<const char*>(v_new), static_cast<char*>(out));
+                if (rc != KVP_OK) return rc;
+            }
+            return KVP_OK;
+        }();
+        if (rc != KVP_OK) {
+            // The step's copies read the caller's buffers and may have set input-ready flags: let them finish and
+            // clear the flags before any later step.
+            cudaStreamSynchronize(d->s_in);
+            cudaStreamSynchronize(d->s_out);
+            cudaStreamSynchronize(d->s_comp);
+            cudaMemsetAsync(d->d_flags(), 0, sizeof(int32_t) * static_cast<size_t>(c.num_layers), d->s_comp);
+            cudaStreamSynchronize(d->s_comp);
+            return rc;
         }
         d->submitted = true;
         return KVP_OK;

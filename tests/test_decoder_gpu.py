@@ -114,6 +114,21 @@ def test_decoder_reports_exhaustion(kvb, cuda):
         dec.step([0, 1], z, zk, zk, z.clone())  # both need a new block; only one is free
     assert e.value.code == kvb.KVP_ENOSPACE
     assert m.num_tokens(0) == 33 and m.num_tokens(1) == 16  # the first append happened, the second did not
+    # The failed step had already started its first layer's copy (and set that layer's input-ready flag): the
+    # next step must still wait for its own inputs.  Its fused append and attention must match a direct launch.
+    m.free(1)
+    g = torch.Generator().manual_seed(4)
+    q = torch.randn((L, 1, nh, D), generator=g).to(torch.bfloat16).pin_memory()
+    kn = torch.randn((L, 1, kvh, D), generator=g).to(torch.bfloat16).pin_memory()
+    vn = torch.randn((L, 1, kvh, D), generator=g).to(torch.bfloat16).pin_memory()
+    out = torch.empty((L, 1, nh, D), dtype=torch.bfloat16).pin_memory()
+    dec.step([0], q, kn, vn, out)
+    assert dec.status() == 0
+    tables, lens = m.dense_tables([0], 4)
+    t, ln = torch.from_numpy(tables).cuda(), torch.from_numpy(lens).cuda()
+    for layer in range(L):
+        want = kvb.paged_attention(q[layer].cuda(), k[layer], v[layer], t, ln, nh, kvh)
+        assert torch.equal(out[layer], want.cpu()), layer
 
 
 @pytest.mark.parametrize("path", ["host", "device"])
