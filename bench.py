@@ -592,11 +592,15 @@ def run_ours(args, cfg, rank, world, dev):
     grow_requests(mgr, lens, B, seed=rank * 7 + 3)
     dec = kvb.Decoder(mgr, kc, vc, nh, max_seqs=ns, max_blocks_per_seq=max_blocks)
     rids = np.arange(ns, dtype=np.int64)  # the batch as the C ABI takes it (no per-step conversion)
+    # the step's inputs produced in place in the decoder's pinned input buffers (a layer's queries and new K/V
+    # adjacent, so each group of layers goes up in one copy)
+    p_q, p_k, p_v = dec.host_inputs(ns)
+    p_q.copy_(h_q), p_k.copy_(h_k), p_v.copy_(h_v)
 
     def e2e_step():
         # a serving loop's step: submit it (inputs copied up, launches), plan the next step's bookkeeping while
         # it runs, then wait for its outputs to reach the host
-        dec.submit(rids, h_q, h_k, h_v, h_out)
+        dec.submit(rids, p_q, p_k, p_v, h_out)
         dec.plan(rids)
         dec.wait()
 

@@ -368,6 +368,13 @@ KVP_API int kvp_decoder_step_device(kvp_decoder* d, const int64_t* rids, int32_t
  * call is KVP_ESTATE.  A serving loop: plan(batch); per step: submit(batch) -> plan(next batch) -> wait(). */
 KVP_API int kvp_decoder_submit(kvp_decoder* d, const int64_t* rids, int32_t n, const void* q, const void* k_new,
                                const void* v_new, void* out);
+/* Pinned host input buffers owned by the decoder, for callers that produce each step's inputs in place: for a
+ * step of n requests, layer l's queries are at q + l * layer_stride bytes, its new K at k_new + l * layer_stride
+ * and its new V at v_new + l * layer_stride (each [n][heads][head_dim] in the config's dtypes), so a layer's
+ * three inputs are adjacent and a run of layers goes up in one copy instead of three.  A step given exactly
+ * these pointers (same n) uses that layout; the buffer is shared by all n and lives as long as the decoder. */
+KVP_API int kvp_decoder_host_inputs(kvp_decoder* d, int32_t n, void** q, void** k_new, void** v_new,
+                                    size_t* layer_stride);
 KVP_API int kvp_decoder_plan(kvp_decoder* d, const int64_t* rids, int32_t n);
 KVP_API int kvp_decoder_wait(kvp_decoder* d);
 /* OR of the KVP_STATUS_* bits the decoder's kernels reported so far (synchronises the decoder's streams). */

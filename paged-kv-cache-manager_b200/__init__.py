@@ -141,6 +141,7 @@ _SIGNATURES = [
     ("kvp_decoder_step", C.c_int, [_vp, _pi64, _i32, _vp, _vp, _vp, _vp]),
     ("kvp_decoder_step_device", C.c_int, [_vp, _pi64, _i32, _vp, _vp, _vp, _vp, _vp]),
     ("kvp_decoder_submit", C.c_int, [_vp, _pi64, _i32, _vp, _vp, _vp, _vp]),
+    ("kvp_decoder_host_inputs", C.c_int, [_vp, _i32, C.POINTER(_vp), C.POINTER(_vp), C.POINTER(_vp), C.POINTER(_sz)]),
     ("kvp_decoder_plan", C.c_int, [_vp, _pi64, _i32]),
     ("kvp_decoder_wait", C.c_int, [_vp]),
     ("kvp_decoder_status", C.c_int, [_vp]),
@@ -648,19 +649,60 @@ class Decoder:
         """Host tensors (pinned for overlap): q/out [L][n][nh][D], k_new/v_new [L][n][kvh][D].  Returns once
         `out` holds the step's attention outputs."""
         r = self._rids(rids)
-        for t in (q, k_new, v_new, out):
-            if t.is_cuda or not t.is_contiguous():
-                raise ValueError("decoder.step takes contiguous host tensors")
+        for t in (q, k_new, v_new):
+            if not self._host_tensor_ok(t):
+                raise ValueError("decoder.step takes host tensors: contiguous, or the host_inputs() views")
+        if out.is_cuda or not out.is_contiguous():
+            raise ValueError("decoder.step takes a contiguous host output tensor")
         _check(self._L.kvp_decoder_step(self._h, r.ctypes.data_as(_pi64), len(r), q.data_ptr(), k_new.data_ptr(),
                                          v_new.data_ptr(), out.data_ptr()))
+
+    def host_inputs(self, n: int):
+        """The decoder's own pinned input buffers for a step of n requests (kvp_decoder_host_inputs): q, k_new,
+        v_new as [L][n][heads][D] host tensors whose layers interleave in one allocation, so a step given them
+        copies each group of layers up in one transfer.  Write a step's inputs into them and pass them to
+        submit() / step()."""
+        import numpy as np
+        import torch
+        c = self.cfg
+        ptrs = [C.c_void_p() for _ in range(3)]
+        stride = _sz()
+        _check(self._L.kvp_decoder_host_inputs(self._h, n, C.byref(ptrs[0]), C.byref(ptrs[1]), C.byref(ptrs[2]),
+                                                C.byref(stride)))
+        dt = {F32: (np.float32, torch.float32), F16: (np.uint16, torch.float16), BF16: (np.uint16, torch.bfloat16)}
+        total = c.num_layers * stride.value
+        base = ptrs[0].value
+        buf = np.ctypeslib.as_array((C.c_uint8 * total).from_address(base))
+        out = []
+        for p, heads, code in ((ptrs[0], c.num_heads, c.q_dtype), (ptrs[1], c.kv_heads, c.kv_dtype),
+                               (ptrs[2], c.kv_heads, c.kv_dtype)):
+            npt, tt = dt[code]
+            item = np.dtype(npt).itemsize
+            view = np.lib.stride_tricks.as_strided(
+                buf[p.value - base:].view(npt), shape=(c.num_layers, n, heads, c.head_dim),
+                strides=(stride.value, heads * c.head_dim * item, c.head_dim * item, item))
+            out.append(torch.from_numpy(view).view(tt))
+        self._host_in = (out, buf)  # keeps the views' memory referenced while they are in use
+        return out
+
+    def _host_tensor_ok(self, t):
+        if t.is_cuda:
+            return False
+        if t.is_contiguous():
+            return True
+        views = getattr(self, "_host_in", None)
+        return views is not None and any(t.data_ptr() == v.data_ptr() and t.shape == v.shape and
+                                         t.stride() == v.stride() for v in views[0])
 
     def submit(self, rids, q, k_new, v_new, out):
         """step() without the wait: issues the step's copies and launches and returns; `out` is complete after
         wait()."""
         r = self._rids(rids)
-        for t in (q, k_new, v_new, out):
-            if t.is_cuda or not t.is_contiguous():
-                raise ValueError("decoder.submit takes contiguous host tensors")
+        for t in (q, k_new, v_new):
+            if not self._host_tensor_ok(t):
+                raise ValueError("decoder.submit takes host tensors: contiguous, or the host_inputs() views")
+        if out.is_cuda or not out.is_contiguous():
+            raise ValueError("decoder.submit takes a contiguous host output tensor")
         _check(self._L.kvp_decoder_submit(self._h, r.ctypes.data_as(_pi64), len(r), q.data_ptr(),
                                            k_new.data_ptr(), v_new.data_ptr(), out.data_ptr()))
 

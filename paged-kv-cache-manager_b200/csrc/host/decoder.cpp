@@ -137,6 +137,7 @@ struct kvp_decoder {
     using WriteValueFn = CUresult (*)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
     WriteValueFn write_value = nullptr;
     int32_t* h_one = nullptr;
+    char* h_in = nullptr;  // pinned packed input buffer (kvp_decoder_host_inputs), allocated on first use
     size_t meta_bytes = 0;
     int64_t layer_stride = 0;   // elements
     cudaStream_t s_in = nullptr, s_comp = nullptr, s_out = nullptr;
@@ -153,6 +154,7 @@ struct kvp_decoder {
         if (exec) cudaGraphExecDestroy(exec);
         if (exec_full) cudaGraphExecDestroy(exec_full);
         if (h_one) cudaFreeHost(h_one);
+        if (h_in) cudaFreeHost(h_in);
         for (Staging& b : stg) {
             if (b.h) cudaFreeHost(b.h);
             if (b.ev) cudaEventDestroy(b.ev);
@@ -279,19 +281,55 @@ int launch_cow(kvp_decoder* d, const int32_t* d_pairs, cudaStream_t s, int buf) 
     return flush(npairs);
 }
 
-// Layer l's attention launch (fused append of its new token) on stream s; q / knew / vnew / out are the
-// device arrays of all layers; `ready`: the input-ready flag of the layer's copy-in group (null: its inputs
-// are in place before the launch).
-int launch_layer(kvp_decoder* d, int n, int l, const void* q, const void* knew, const void* vnew, void* out,
-                 cudaStream_t s, const int32_t* ready = nullptr) {
+// Where a step's inputs are: layer l's queries at q + l * q_stride bytes, its new K at k + l * kv_stride and its
+// new V at v + l * kv_stride.  Separate arrays [L][n][...]: each stride is one layer of that array.  Packed (the
+// decoder's own pinned input buffer and its device mirror): a layer's queries, new K and new V are adjacent and
+// both strides are their sum, so a run of layers is one contiguous range -- one copy.
+struct Inputs {
+    const char *q = nullptr, *k = nullptr, *v = nullptr;
+    size_t q_stride = 0, kv_stride = 0;
+    bool packed = false;
+};
+
+size_t q_layer_bytes(const kvp_decoder_config& c, int n) {
+    return static_cast<size_t>(n) * c.num_heads * c.head_dim * elem(c.q_dtype);
+}
+size_t kv_layer_bytes(const kvp_decoder_config& c, int n) {
+    return static_cast<size_t>(n) * c.kv_heads * c.head_dim * elem(c.kv_dtype);
+}
+
+Inputs separate_inputs(const kvp_decoder_config& c, int n, const void* q, const void* k, const void* v) {
+    Inputs in;
+    in.q = static_cast<const char*>(q);
+    in.k = static_cast<const char*>(k);
+    in.v = static_cast<const char*>(v);
+    in.q_stride = q_layer_bytes(c, n);
+    in.kv_stride = kv_layer_bytes(c, n);
+    return in;
+}
+
+Inputs packed_inputs(const kvp_decoder_config& c, int n, const void* base) {
+    Inputs in;
+    in.q = static_cast<const char*>(base);
+    in.k = in.q + q_layer_bytes(c, n);
+    in.v = in.k + kv_layer_bytes(c, n);
+    in.q_stride = in.kv_stride = q_layer_bytes(c, n) + 2 * kv_layer_bytes(c, n);
+    in.packed = true;
+    return in;
+}
+
+// Layer l's attention launch (fused append of its new token) on stream s, its inputs as `in` places them (device
+// memory) and its output at out + l * one layer's output; `ready`: the input-ready flag of the layer's copy-in
+// group (null: its inputs are in place before the launch).
+int launch_layer(kvp_decoder* d, int n, int l, const Inputs& in, void* out, cudaStream_t s,
+                 const int32_t* ready = nullptr) {
     const kvp_decoder_config& c = d->cfg;
     const int32_t* meta = d->d_meta();
     const size_t L = static_cast<size_t>(l);
     const size_t kv_layer_bytes = static_cast<size_t>(d->layer_stride) * 2;
     const size_t q_layer = static_cast<size_t>(n) * c.num_heads * c.head_dim;
-    const size_t kv_layer = static_cast<size_t>(n) * c.kv_heads * c.head_dim * elem(c.kv_dtype);
     kvp_attn_args a{};
-    a.q = static_cast<const char*>(q) + q_layer * elem(c.q_dtype) * L;
+    a.q = in.q + in.q_stride * L;
     a.q_dtype = c.q_dtype;
     a.k_cache = static_cast<const char*>(c.k_cache) + kv_layer_bytes * L;
     a.v_cache = static_cast<const char*>(c.v_cache) + kv_layer_bytes * L;
@@ -315,8 +353,8 @@ int launch_layer(kvp_decoder* d, int n, int l, const void* q, const void* knew, 
     // launch may start during the previous one, and from the second layer on (the previous kernel then writes
     // only its own layer's pool) also load K/V before it ends
     a.flags = KVP_ATTN_WORKSPACE_CLEAN | (l > 0 ? KVP_ATTN_EARLY_LOAD : KVP_ATTN_EARLY_START);
-    a.k_new = static_cast<const char*>(knew) + kv_layer * L;  // fused append of this layer's new token
-    a.v_new = static_cast<const char*>(vnew) + kv_layer * L;
+    a.k_new = in.k + in.kv_stride * L;  // fused append of this layer's new token
+    a.v_new = in.v + in.kv_stride * L;
     a.inputs_ready = ready;
     return kvp_paged_attention(&a, s);
 }
@@ -324,8 +362,9 @@ int launch_layer(kvp_decoder* d, int n, int l, const void* q, const void* knew, 
 // Every layer's launch, in order on stream s (device buffers).
 int enqueue_layers(kvp_decoder* d, int n, const void* q, const void* knew, const void* vnew, void* out,
                    cudaStream_t s) {
+    const Inputs in = separate_inputs(d->cfg, n, q, knew, vnew);
     for (int l = 0; l < d->cfg.num_layers; ++l) {
-        const int rc = launch_layer(d, n, l, q, knew, vnew, out, s);
+        const int rc = launch_layer(d, n, l, in, out, s);
         if (rc != KVP_OK) return rc;
     }
     return KVP_OK;
@@ -347,15 +386,41 @@ cudaError_t set_flag(kvp_decoder* d, int32_t* flag, cudaStream_t s) {
     return cudaMemcpyAsync(flag, d->h_one, sizeof(int32_t), cudaMemcpyHostToDevice, s);
 }
 
+// The device copy of a step's host inputs: the workspace's input region, laid out as the host inputs are.
+Inputs device_inputs(kvp_decoder* d, int n, const Inputs& host) {
+    char* base = d->ws + d->lay.q;  // the q, k and v regions follow one another: room for either layout
+    return host.packed ? packed_inputs(d->cfg, n, base)
+                       : separate_inputs(d->cfg, n, base, d->ws + d->lay.k, d->ws + d->lay.v);
+}
+
+// The step's host inputs as the caller passed them: the decoder's own packed buffer (kvp_decoder_host_inputs) or
+// separate arrays.
+Inputs host_inputs_of(kvp_decoder* d, int n, const void* q, const void* k, const void* v) {
+    if (d->h_in && q == d->h_in) {
+        const Inputs p = packed_inputs(d->cfg, n, d->h_in);
+        if (k == p.k && v == p.v) return p;
+    }
+    return separate_inputs(d->cfg, n, q, k, v);
+}
+
+// Layers [l0, l0 + G) of the step's inputs up on stream s: one copy when packed, else one per array.
+cudaError_t copy_layers(const Inputs& dev, const Inputs& host, int l0, int G, cudaStream_t s) {
+    const size_t L0 = static_cast<size_t>(l0), n = static_cast<size_t>(G);
+    const auto up = [&](const char* dst, const char* src, size_t stride) {
+        return cudaMemcpyAsync(const_cast<char*>(dst) + stride * L0, src + stride * L0, stride * n,
+                               cudaMemcpyHostToDevice, s);
+    };
+    if (host.packed) return up(dev.q, host.q, host.q_stride);
+    cudaError_t e = up(dev.q, host.q, host.q_stride);
+    if (e == cudaSuccess) e = up(dev.k, host.k, host.kv_stride);
+    if (e == cudaSuccess) e = up(dev.v, host.v, host.kv_stride);
+    return e;
+}
+
 // Layer 0's inputs, copied up on the copy-in stream before the step's bookkeeping (they do not depend on it), so
 // the copy overlaps the host work, then layer 0's input-ready flag.
-int copy_first_layer(kvp_decoder* d, int n, const char* hq, const char* hk, const char* hv) {
-    const kvp_decoder_config& c = d->cfg;
-    const size_t q_layer = static_cast<size_t>(n) * c.num_heads * c.head_dim * elem(c.q_dtype);
-    const size_t kv_layer = static_cast<size_t>(n) * c.kv_heads * c.head_dim * elem(c.kv_dtype);
-    cudaError_t e = cudaMemcpyAsync(d->ws + d->lay.q, hq, q_layer, cudaMemcpyHostToDevice, d->s_in);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(d->ws + d->lay.k, hk, kv_layer, cudaMemcpyHostToDevice, d->s_in);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(d->ws + d->lay.v, hv, kv_layer, cudaMemcpyHostToDevice, d->s_in);
+int copy_first_layer(kvp_decoder* d, int n, const Inputs& host) {
+    cudaError_t e = copy_layers(device_inputs(d, n, host), host, 0, 1, d->s_in);
     if (e == cudaSuccess) e = set_flag(d, d->d_flags(), d->s_in);
     return kvpi::cuda_status(e, "decoder first-layer copy");
 }
@@ -372,14 +437,10 @@ int copy_first_layer(kvp_decoder* d, int n, const char* hq, const char* hk, cons
 // time the step's input copies wait for.  Once the last layer is done, the copy-in stream clears the flags for
 // the next step.  Outputs go back on the copy-out stream in groups of layers_per_copy() layers once their last
 // launch is done.  The same calls are captured into one graph when a step's key repeats.
-int enqueue_host_body(kvp_decoder* d, int n, const char* hq, const char* hk, const char* hv, char* hout) {
+int enqueue_host_body(kvp_decoder* d, int n, const Inputs& host, char* hout) {
     const kvp_decoder_config& c = d->cfg;
-    const size_t q_layer = static_cast<size_t>(n) * c.num_heads * c.head_dim * elem(c.q_dtype);
     const size_t o_layer = static_cast<size_t>(n) * c.num_heads * c.head_dim * elem(c.out_dtype);
-    const size_t kv_layer = static_cast<size_t>(n) * c.kv_heads * c.head_dim * elem(c.kv_dtype);
-    char* dq = d->ws + d->lay.q;
-    char* dk = d->ws + d->lay.k;
-    char* dv = d->ws + d->lay.v;
+    const Inputs dev = device_inputs(d, n, host);
     char* dout = d->ws + d->lay.out;
     const int L = c.num_layers;
     const int per = layers_per_copy(c, n);
@@ -390,14 +451,8 @@ int enqueue_host_body(kvp_decoder* d, int n, const char* hq, const char* hk, con
     // the first (layer 0) was issued before the bookkeeping and has been waited for
     size_t gi = 1;
     for (int in0 = 1, g = 2; e == cudaSuccess && in0 < L; in0 += g, g *= 2, ++gi) {
-        const size_t L0 = static_cast<size_t>(in0), G = static_cast<size_t>(std::min(g, L - in0));
-        e = cudaMemcpyAsync(dq + q_layer * L0, hq + q_layer * L0, q_layer * G, cudaMemcpyHostToDevice, d->s_in);
-        if (e == cudaSuccess)
-            e = cudaMemcpyAsync(dk + kv_layer * L0, hk + kv_layer * L0, kv_layer * G, cudaMemcpyHostToDevice, d->s_in);
-        if (e == cudaSuccess)
-            e = cudaMemcpyAsync(dv + kv_layer * L0, hv + kv_layer * L0, kv_layer * G, cudaMemcpyHostToDevice, d->s_in);
-        if (e == cudaSuccess)
-            e = set_flag(d, d->d_flags() + gi, d->s_in);
+        e = copy_layers(dev, host, in0, std::min(g, L - in0), d->s_in);
+        if (e == cudaSuccess) e = set_flag(d, d->d_flags() + gi, d->s_in);
     }
     gi = 0;
     size_t oi = 0;
@@ -407,7 +462,7 @@ int enqueue_host_body(kvp_decoder* d, int n, const char* hq, const char* hk, con
             next_in += g;
             g *= 2;
         }
-        const int rc = launch_layer(d, n, l, dq, dk, dv, dout, d->s_comp, d->d_flags() + (gi - 1));
+        const int rc = launch_layer(d, n, l, dev, dout, d->s_comp, d->d_flags() + (gi - 1));
         if (rc != KVP_OK) return rc;
         // An output group is complete -- the last layer always gets its own, since nothing overlaps its copy.
         if (l + 1 - out0 == per || l + 1 == L || l + 2 == L) {
@@ -469,8 +524,8 @@ bool capture_host_body(kvp_decoder* d, const GraphKey& key) {
         cudaGetLastError();
         return false;
     }
-    const int rc = enqueue_host_body(d, key.n, static_cast<const char*>(key.q), static_cast<const char*>(key.k),
-                                     static_cast<const char*>(key.v), static_cast<char*>(const_cast<void*>(key.out)));
+    const int rc = enqueue_host_body(d, key.n, host_inputs_of(d, key.n, key.q, key.k, key.v),
+                                     static_cast<char*>(const_cast<void*>(key.out)));
     if (!finish_capture(d->s_comp, rc, &d->exec_full)) return false;
     d->full_key = key;
     return true;
@@ -718,6 +773,32 @@ KVP_API int kvp_decoder_step_device(kvp_decoder* d, const int64_t* rids, int32_t
     });
 }
 
+KVP_API int kvp_decoder_host_inputs(kvp_decoder* d, int32_t n, void** q, void** k_new, void** v_new,
+                                    size_t* layer_stride) {
+    return guarded([&] {
+        if (!d || !q || !k_new || !v_new || !layer_stride) return kvpi::fail(KVP_EINVAL, "null argument");
+        if (n < 1 || n > d->cfg.max_seqs) return kvpi::fail(KVP_EINVAL, "n outside [1, max_seqs]");
+        const kvp_decoder_config& c = d->cfg;
+        if ((q_layer_bytes(c, n) | kv_layer_bytes(c, n)) & 15u)
+            return kvpi::fail(KVP_EINVAL, "packed inputs need rows of a multiple of 16 bytes");
+        if (!d->h_in) {
+            DeviceScope scope(d->device);
+            const size_t bytes = static_cast<size_t>(c.num_layers) *
+                                 (q_layer_bytes(c, c.max_seqs) + 2 * kv_layer_bytes(c, c.max_seqs));
+            if (cudaHostAlloc(reinterpret_cast<void**>(&d->h_in), bytes, cudaHostAllocDefault) != cudaSuccess) {
+                d->h_in = nullptr;
+                return kvpi::cuda_status(cudaGetLastError(), "pinned input buffer");
+            }
+        }
+        const Inputs in = packed_inputs(c, n, d->h_in);
+        *q = const_cast<char*>(in.q);
+        *k_new = const_cast<char*>(in.k);
+        *v_new = const_cast<char*>(in.v);
+        *layer_stride = in.q_stride;
+        return KVP_OK;
+    });
+}
+
 KVP_API int kvp_decoder_plan(kvp_decoder* d, const int64_t* rids, int32_t n) {
     return guarded([&] {
         if (!d || (n > 0 && !rids)) return kvpi::fail(KVP_EINVAL, "null argument");
@@ -760,9 +841,9 @@ KVP_API int kvp_decoder_submit(kvp_decoder* d, const int64_t* rids, int32_t n, c
             const int rw = kvp_decoder_wait(d);
             if (rw != KVP_OK) return rw;
         }
+        const Inputs host = host_inputs_of(d, n, q, k_new, v_new);
         const int rc = [&]() -> int {
-            int rc = copy_first_layer(d, n, static_cast<const char*>(q), static_cast<const char*>(k_new),
-                                      static_cast<const char*>(v_new));
+            int rc = copy_first_layer(d, n, host);
             if (rc != KVP_OK) return rc;
             int buf = 0;
             rc = stage_step(d, rids, n, &buf);
@@ -791,8 +872,7 @@ KVP_API int kvp_decoder_submit(kvp_decoder* d, const int64_t* rids, int32_t n, c
                 }
             }
             if (!launched) {
-                rc = enqueue_host_body(d, n, static_cast<const char*>(q), static_cast<const char*>(k_new),
-                                       static_cast<const char*>(v_new), static_cast<char*>(out));
+                rc = enqueue_host_body(d, n, host, static_cast<char*>(out));
                 if (rc != KVP_OK) return rc;
             }
             return KVP_OK;

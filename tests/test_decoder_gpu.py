@@ -179,7 +179,7 @@ def test_decoder_staging_follows_external_table_changes(kvb, cuda, path):
     assert dec.status() == 0
 
 
-@pytest.mark.parametrize("path", ["host", "device"])
+@pytest.mark.parametrize("path", ["host", "packed", "device"])
 def test_decoder_pipelined_steps_match_manual_path(kvb, cuda, path):
     """Pipelined steps: each step is submitted (host buffers) or enqueued (device buffers), the NEXT step's
     bookkeeping is planned while it runs, and only then is it waited for.  Nine steps with the batch changing
@@ -212,13 +212,17 @@ def test_decoder_pipelined_steps_match_manual_path(kvb, cuda, path):
         if path == "host":
             hq.copy_(q), hk.copy_(kn), hv.copy_(vn)
             dec.submit(order, hq, hk, hv, ho)
+        elif path == "packed":  # the decoder's own pinned input buffers (one copy per group of layers)
+            pq, pk, pv = dec.host_inputs(n)
+            pq.copy_(q), pk.copy_(kn), pv.copy_(vn)
+            dec.submit(order, pq, pk, pv, ho)
         else:
             dq.copy_(q), dk.copy_(kn), dv.copy_(vn)
             side.wait_stream(torch.cuda.current_stream())
             dec.step_device(order, dq, dk, dv, do, stream=side)
         if step + 1 < len(orders):
             dec.plan(orders[step + 1])
-        if path == "host":
+        if path in ("host", "packed"):
             dec.wait()
             out1 = ho.clone()
         else:
