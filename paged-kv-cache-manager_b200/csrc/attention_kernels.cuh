@@ -855,8 +855,9 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
     // hold a writer warp's counter values from before its adds.
     int np = 0, old0 = -1, old1 = -1;
     // Consumers can only run ahead of the producer's wait for the previous kernel when the queries came from
-    // another stream's copy (see the producer); then their first global write waits for that kernel itself.
-    bool cwaited = waited || p.inputs_ready == nullptr;
+    // another stream's copy (see the producer); then each segment's global writes wait for that kernel first
+    // (at once after the first time).
+    const bool write_wait = !waited && p.inputs_ready != nullptr;
     while (segs.next(sg)) {
         const int len = sg.len;
         if (p.q_area != 0) {
@@ -913,10 +914,7 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
                 for (int k = 1; k < p.wph; ++k) cs.merge_state(area + (k - 1) * stride, lane);
             named_barrier(1 + head, p.wph * 32);  // the area is rewritten by the next segment
         }
-        if (!cwaited) {
-            griddep_wait();
-            cwaited = true;
-        }
+        if (write_wait) griddep_wait();
         if (sub == 0 && ok) cs.finish(p, lane, sg.seq, kvh_global, sg.single, sg.part_row);
         // Stream-K, sequence split across CTAs: each head's writer warp counts its partial rows as done with
         // one releasing add (the warp barrier orders its lanes' rows before it); a sequence is complete when
