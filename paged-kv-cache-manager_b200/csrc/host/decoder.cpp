@@ -8,7 +8,9 @@
 // stream feeds the new K/V and each layer's queries and a copy-out stream drains each layer's output as soon as
 // its attention finishes, so transfers overlap the attention of other layers.  Once a step's key (batch size
 // and buffers) repeats, that whole body -- copies and launches on the three streams -- is replayed from one
-// CUDA graph, so a step costs the host a handful of runtime calls.
+// CUDA graph, so a step costs the host a handful of runtime calls.  A step can be submitted without waiting for
+// it (kvp_decoder_submit / kvp_decoder_wait) and the next step's bookkeeping planned while it runs
+// (kvp_decoder_plan, into the second of two pinned staging buffers).
 #include <cuda.h>
 #include <cuda_runtime.h>
 
