@@ -96,3 +96,58 @@ def test_tinyllama_shape_128_step_loop(kvb, ora, cuda):
             assert int(st.status.item()) == 0, s
             _check_step(ora, st, s, [0, cfg["L"] - 1], "128-step loop")
     del graphs
+
+
+def test_decoder_pipelined_tinyllama_shape(kvb, ora, cuda):
+    """The end-to-end leg of bench.py at the TinyLlama shape, checked: 256 requests (log-normal lengths, median
+    1024), 22 layers, bf16, through the decoder with its packed pinned inputs and pipelined steps (submit, plan
+    the next step, wait), 6 steps with new inputs each step.  After the last step, 16 sampled requests'
+    outputs of the first and the last layer against the fp64 oracle on the pools and tables as the decoder
+    left them, and their newest K/V rows equal to the last step's inputs."""
+    import torch
+    import bench
+    cfg = _cfg("tinyllama-1.1b", 22)
+    L, nh, kvh, D, B = cfg["L"], cfg["nh"], cfg["kvh"], cfg["D"], cfg["B"]
+    lens = bench.sample_lens(cfg, cfg["ns"], seed=1000)
+    ns, steps = len(lens), 6
+    dev = torch.device("cuda:0")
+    mgr, kc, vc, nb = bench.setup_shard(kvb, cfg, lens, steps + 2, dev, seed=31)
+    max_blocks = (int(lens.max()) + steps + 2 + B) // B
+    dec = kvb.Decoder(mgr, kc, vc, nh, max_seqs=ns, max_blocks_per_seq=max_blocks)
+    rids = np.arange(ns, dtype=np.int64)
+    pq, pk, pv = dec.host_inputs(ns)
+    out = torch.empty((L, ns, nh, D), dtype=torch.bfloat16).pin_memory()
+    g = torch.Generator().manual_seed(5)
+    dec.plan(rids)
+    for s in range(steps):
+        q = torch.randn((L, ns, nh, D), generator=g).to(torch.bfloat16)
+        kn = torch.randn((L, ns, kvh, D), generator=g).to(torch.bfloat16)
+        vn = torch.randn((L, ns, kvh, D), generator=g).to(torch.bfloat16)
+        pq.copy_(q), pk.copy_(kn), pv.copy_(vn)
+        dec.submit(rids, pq, pk, pv, out)
+        if s + 1 < steps:
+            dec.plan(rids)
+        dec.wait()
+    assert dec.status() == 0
+    idx = [int(np.argmax(lens)), int(np.argmin(lens))] + \
+        [int(i) for i in np.random.default_rng(2).choice(ns, 14, replace=False)]
+    tables, got_lens = mgr.dense_tables([int(i) for i in idx], max_blocks)
+    assert (got_lens == lens[idx] + steps).all()
+    nblk = (got_lens + B - 1) // B
+    T = np.zeros((len(idx), int(nblk.max())), np.int32)
+    blocks, off = [], 0
+    for j in range(len(idx)):
+        blocks.extend(tables[j, :nblk[j]].tolist())
+        T[j, :nblk[j]] = np.arange(off, off + nblk[j])
+        off += int(nblk[j])
+    bidx = torch.tensor(blocks, dtype=torch.long, device=dev)
+    for layer in (0, L - 1):
+        k = kc[layer].index_select(0, bidx)
+        v = vc[layer].index_select(0, bidx)
+        for j, i in enumerate(idx):  # the fused append of the last step: position len - 1
+            p = int(got_lens[j]) - 1
+            blk = int(T[j, p // B])
+            assert torch.equal(k[blk, p % B].cpu(), kn[layer, i]) and torch.equal(v[blk, p % B].cpu(), vn[layer, i])
+        ref = ora.reference_attention(nh, kvh, D, B, q[layer, idx].float().numpy(), k.float().cpu().numpy(),
+                                      v.float().cpu().numpy(), T, got_lens)
+        check_close(out[layer, idx].float().numpy(), ref, out_dtype="bf16", what=f"decoder layer {layer}")
