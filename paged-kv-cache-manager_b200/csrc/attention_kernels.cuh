@@ -880,6 +880,9 @@ __device__ __forceinline__ void cta_body(const AttnParams& p, const CUtensorMap*
                 }
                 ok = false;
             }
+            // queries the previous kernel may write: read them once it is done (the producer's wait does not
+            // order these loads; with inputs_ready they come from the flagged copy instead)
+            if (j == 0 && !waited && p.inputs_ready == nullptr) griddep_wait();
             cs.load_q_global(p, sg.seq, kvh_global, lane);
         }
         cs.reset();

@@ -401,11 +401,14 @@ def test_clean_workspace_reuse_across_batch_sizes(kvb, ora, cuda):
     assert int(ws[:8192 * 4].view(torch.int32).abs().sum().item()) == 0
 
 
+@pytest.mark.parametrize("q_misaligned", [False, True], ids=["q16", "q-unaligned"])
 @pytest.mark.parametrize("shape", [(14, 2, 64), (32, 8, 128)], ids=["qwen", "llama"])
-def test_early_start_back_to_back_bit_exact(kvb, cuda, shape):
+def test_early_start_back_to_back_bit_exact(kvb, cuda, shape, q_misaligned):
     """Eight layers launched back to back on one stream with early start (each kernel's prologue overlapping
     the previous kernel's tail) and early load (its first K/V tiles loaded before the previous kernel ends), with
-    the fused append, give outputs and pools bit-identical to plain launches."""
+    the fused append, give outputs and pools bit-identical to plain launches.  With queries off a 16-byte
+    boundary the consumer warps read them with plain loads (no query slot), after waiting for the previous
+    kernel themselves."""
     import torch
     nh, kvh, D = shape
     L, B, ns = 8, 16, 48
@@ -423,6 +426,11 @@ def test_early_start_back_to_back_bit_exact(kvb, cuda, shape):
     K = torch.randn((L, nb, B, kvh, D), generator=g, device="cuda").to(torch.bfloat16)
     V = torch.randn_like(K)
     q = torch.randn((L, ns, nh, D), generator=g, device="cuda").to(torch.bfloat16)
+    if q_misaligned:  # each layer's rows one element past a 16-byte boundary
+        qf = torch.empty((L, ns * nh * D + 1), dtype=torch.bfloat16, device="cuda")
+        qf[:, 1:] = q.reshape(L, -1)
+        q = qf[:, 1:].view(L, ns, nh, D)
+        assert q[0].data_ptr() % 16 == 2
     kn = torch.randn((L, ns, kvh, D), generator=g, device="cuda").to(torch.bfloat16)
     vn = torch.randn_like(kn)
     t = torch.from_numpy(T).cuda()
