@@ -140,6 +140,7 @@ struct kvp_decoder {
     WriteValueFn write_value = nullptr;
     int32_t* h_one = nullptr;
     char* h_in = nullptr;  // pinned packed input buffer (kvp_decoder_host_inputs), allocated on first use
+    size_t h_in_bytes = 0;
     size_t meta_bytes = 0;
     int64_t layer_stride = 0;   // elements
     cudaStream_t s_in = nullptr, s_comp = nullptr, s_out = nullptr;
@@ -791,6 +792,7 @@ KVP_API int kvp_decoder_host_inputs(kvp_decoder* d, int32_t n, void** q, void** 
                 d->h_in = nullptr;
                 return kvpi::cuda_status(cudaGetLastError(), "pinned input buffer");
             }
+            d->h_in_bytes = bytes;
         }
         const Inputs in = packed_inputs(c, n, d->h_in);
         *q = const_cast<char*>(in.q);
@@ -844,6 +846,14 @@ KVP_API int kvp_decoder_submit(kvp_decoder* d, const int64_t* rids, int32_t n, c
             if (rw != KVP_OK) return rw;
         }
         const Inputs host = host_inputs_of(d, n, q, k_new, v_new);
+        if (!host.packed && d->h_in) {  // pointers into the packed buffer, but not its layout for this n
+            const auto inside = [&](const void* x) {
+                return static_cast<const char*>(x) >= d->h_in && static_cast<const char*>(x) < d->h_in + d->h_in_bytes;
+            };
+            if (inside(q) || inside(k_new) || inside(v_new))
+                return kvpi::fail(KVP_EINVAL, "inputs in the decoder's packed buffer must be kvp_decoder_host_inputs()'s "
+                                              "pointers for this step's n");
+        }
         const int rc = [&]() -> int {
             int rc = copy_first_layer(d, n, host);
             if (rc != KVP_OK) return rc;

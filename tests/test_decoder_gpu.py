@@ -259,3 +259,24 @@ def test_decoder_plan_misuse(kvb, cuda):
     dec.step([1, 0], z, zk, zk, z.clone())  # no plan pending: a normal step
     assert [m.num_tokens(r) for r in range(5)] == [before[0] + 2, before[1] + 2] + before[2:]
     assert dec.status() == 0
+
+
+def test_decoder_packed_inputs_for_another_n_rejected(kvb, cuda):
+    """The packed input views of host_inputs(n) lay layers out for that n only: a step over another batch size
+    given them is rejected (KVP_EINVAL, a ValueError) before any bookkeeping, and the manager is unchanged."""
+    import torch
+    nh, kvh, D, L, MB = 8, 2, 64, 4, 40
+    k, v, m = _setup(kvb, 12)
+    dec = kvb.Decoder(m, k, v, nh, max_seqs=8, max_blocks_per_seq=MB)
+    before = [m.num_tokens(r) for r in range(5)]
+    pq, pk, pv = dec.host_inputs(3)
+    out = torch.zeros((L, 2, nh, D), dtype=torch.bfloat16).pin_memory()
+    for call in (dec.submit, dec.step):
+        with pytest.raises(ValueError, match="packed buffer"):
+            call([0, 1], pq, pk, pv, out)
+    assert [m.num_tokens(r) for r in range(5)] == before
+    pq, pk, pv = dec.host_inputs(2)
+    pq.zero_(), pk.zero_(), pv.zero_()
+    dec.step([0, 1], pq, pk, pv, out)
+    assert [m.num_tokens(r) for r in range(5)] == [before[0] + 1, before[1] + 1] + before[2:]
+    assert dec.status() == 0
