@@ -372,7 +372,8 @@ KVP_API int kvp_decoder_submit(kvp_decoder* d, const int64_t* rids, int32_t n, c
  * step of n requests, layer l's queries are at q + l * layer_stride bytes, its new K at k_new + l * layer_stride
  * and its new V at v_new + l * layer_stride (each [n][heads][head_dim] in the config's dtypes), so a layer's
  * three inputs are adjacent and a run of layers goes up in one copy instead of three.  A step given exactly
- * these pointers (same n) uses that layout; the buffer is shared by all n and lives as long as the decoder. */
+ * these pointers (same n) uses that layout; pointers into the buffer from another n are KVP_EINVAL (nothing is
+ * done).  The buffer is shared by all n and lives as long as the decoder. */
 KVP_API int kvp_decoder_host_inputs(kvp_decoder* d, int32_t n, void** q, void** k_new, void** v_new,
                                     size_t* layer_stride);
 KVP_API int kvp_decoder_plan(kvp_decoder* d, const int64_t* rids, int32_t n);
