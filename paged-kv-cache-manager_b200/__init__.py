@@ -138,11 +138,12 @@ _SIGNATURES = [
     ("kvp_decoder_workspace_size", _sz, [C.POINTER(DecoderConfig)]),
     ("kvp_decoder_create", _vp, [C.POINTER(DecoderConfig), _vp]),
     ("kvp_decoder_destroy", None, [_vp]),
-    ("kvp_decoder_step", C.c_int, [_vp, _pi64, _i32, _vp, _vp, _vp, _vp]),
-    ("kvp_decoder_step_device", C.c_int, [_vp, _pi64, _i32, _vp, _vp, _vp, _vp, _vp]),
-    ("kvp_decoder_submit", C.c_int, [_vp, _pi64, _i32, _vp, _vp, _vp, _vp]),
+    # request ids go in as the address of an int64 array (c_void_p: no ctypes pointer object per step)
+    ("kvp_decoder_step", C.c_int, [_vp, _vp, _i32, _vp, _vp, _vp, _vp]),
+    ("kvp_decoder_step_device", C.c_int, [_vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp]),
+    ("kvp_decoder_submit", C.c_int, [_vp, _vp, _i32, _vp, _vp, _vp, _vp]),
     ("kvp_decoder_host_inputs", C.c_int, [_vp, _i32, C.POINTER(_vp), C.POINTER(_vp), C.POINTER(_vp), C.POINTER(_sz)]),
-    ("kvp_decoder_plan", C.c_int, [_vp, _pi64, _i32]),
+    ("kvp_decoder_plan", C.c_int, [_vp, _vp, _i32]),
     ("kvp_decoder_wait", C.c_int, [_vp]),
     ("kvp_decoder_status", C.c_int, [_vp]),
 ]
@@ -626,6 +627,7 @@ class Decoder:
             workspace = torch.empty(need, dtype=torch.uint8, device=k_cache.device)
         c.workspace, c.workspace_bytes = _dev(workspace, "workspace"), workspace.numel() * workspace.element_size()
         self._ws, self._k, self._v, self._mgr, self.cfg = workspace, k_cache, v_cache, mgr, c
+        self._last_args = None  # the previous host step's objects and validated C arguments
         with torch.cuda.device(k_cache.device):
             h = self._L.kvp_decoder_create(C.byref(c), mgr.handle)
         if not h:
@@ -648,14 +650,36 @@ class Decoder:
     def step(self, rids, q, k_new, v_new, out):
         """Host tensors (pinned for overlap): q/out [L][n][nh][D], k_new/v_new [L][n][kvh][D].  Returns once
         `out` holds the step's attention outputs."""
+        _check(self._L.kvp_decoder_step(*self._host_step_args(rids, q, k_new, v_new, out)))
+
+    def _host_step_args(self, rids, q, k_new, v_new, out):
+        """The C arguments of a host-buffer step, validated: shapes [L][n][heads][D] and dtypes of the config,
+        host memory, contiguous (inputs may also be the host_inputs() views).  A serving loop passes the same
+        objects every step (one int64 request-id array, the same tensors): that repeat reuses the validation
+        and re-reads only the data pointers, so the call costs the host a few microseconds, not ~10."""
+        c = self._last_args
+        if c is not None and c[0] is rids and c[1] is q and c[2] is k_new and c[3] is v_new and c[4] is out:
+            ptrs = (q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), out.data_ptr())
+            if ptrs == c[5] and len(rids) == c[6][2]:
+                return c[6]
         r = self._rids(rids)
-        for t in (q, k_new, v_new):
-            if not self._host_tensor_ok(t):
-                raise ValueError("decoder.step takes host tensors: contiguous, or the host_inputs() views")
-        if out.is_cuda or not out.is_contiguous():
-            raise ValueError("decoder.step takes a contiguous host output tensor")
-        _check(self._L.kvp_decoder_step(self._h, r.ctypes.data_as(_pi64), len(r), q.data_ptr(), k_new.data_ptr(),
-                                         v_new.data_ptr(), out.data_ptr()))
+        n = len(r)
+        cfg = self.cfg
+        for t, heads, code, name in ((q, cfg.num_heads, cfg.q_dtype, "q"), (k_new, cfg.kv_heads, cfg.kv_dtype, "k_new"),
+                                     (v_new, cfg.kv_heads, cfg.kv_dtype, "v_new"),
+                                     (out, cfg.num_heads, cfg.out_dtype, "out")):
+            if t.is_cuda:
+                raise ValueError(f"{name}: the decoder's host-buffer steps take host tensors")
+            want = (cfg.num_layers, n, heads, cfg.head_dim)
+            if tuple(t.shape) != want or _dtype_code(t) != code:
+                raise ValueError(f"{name}: expected {want} of the config's dtype, got {tuple(t.shape)} {t.dtype}")
+            if not (t.is_contiguous() or (name != "out" and self._is_host_view(t))):
+                raise ValueError(f"{name}: host tensors must be contiguous (inputs may be the host_inputs() views)")
+        ptrs = (q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), out.data_ptr())
+        args = (self._h, r.ctypes.data, n) + ptrs
+        # only an int64 array the caller owns is remembered: a list converted here could change in place
+        self._last_args = (rids, q, k_new, v_new, out, ptrs, args) if r is rids else None
+        return args
 
     def host_inputs(self, n: int):
         """The decoder's own pinned input buffers for a step of n requests (kvp_decoder_host_inputs): q, k_new,
@@ -685,11 +709,7 @@ class Decoder:
         self._host_in = (out, buf)  # keeps the views' memory referenced while they are in use
         return out
 
-    def _host_tensor_ok(self, t):
-        if t.is_cuda:
-            return False
-        if t.is_contiguous():
-            return True
+    def _is_host_view(self, t):
         views = getattr(self, "_host_in", None)
         return views is not None and any(t.data_ptr() == v.data_ptr() and t.shape == v.shape and
                                          t.stride() == v.stride() for v in views[0])
@@ -697,30 +717,30 @@ class Decoder:
     def submit(self, rids, q, k_new, v_new, out):
         """step() without the wait: issues the step's copies and launches and returns; `out` is complete after
         wait()."""
-        r = self._rids(rids)
-        for t in (q, k_new, v_new):
-            if not self._host_tensor_ok(t):
-                raise ValueError("decoder.submit takes host tensors: contiguous, or the host_inputs() views")
-        if out.is_cuda or not out.is_contiguous():
-            raise ValueError("decoder.submit takes a contiguous host output tensor")
-        _check(self._L.kvp_decoder_submit(self._h, r.ctypes.data_as(_pi64), len(r), q.data_ptr(),
-                                           k_new.data_ptr(), v_new.data_ptr(), out.data_ptr()))
+        _check(self._L.kvp_decoder_submit(*self._host_step_args(rids, q, k_new, v_new, out)))
 
     def plan(self, rids):
         """The next step's bookkeeping now (its KVManager appends happen at once), overlapping a submitted step;
         the next submit / step / step_device must be for the same requests in the same order."""
         r = self._rids(rids)
-        _check(self._L.kvp_decoder_plan(self._h, r.ctypes.data_as(_pi64), len(r)))
+        _check(self._L.kvp_decoder_plan(self._h, r.ctypes.data, len(r)))
 
     def wait(self):
         """Returns once the submitted step's outputs are in host memory."""
         _check(self._L.kvp_decoder_wait(self._h))
 
     def step_device(self, rids, q, k_new, v_new, out, stream=None):
+        """Device tensors of the host step's shapes and dtypes, contiguous; asynchronous on `stream`."""
         r = self._rids(rids)
-        _check(self._L.kvp_decoder_step_device(self._h, r.ctypes.data_as(_pi64), len(r), _dev(q, "q"),
-                                                _dev(k_new, "k_new"), _dev(v_new, "v_new"), _dev(out, "out"),
-                                                _stream_ptr(stream)))
+        n, cfg = len(r), self.cfg
+        for t, heads, code, name in ((q, cfg.num_heads, cfg.q_dtype, "q"), (k_new, cfg.kv_heads, cfg.kv_dtype, "k_new"),
+                                     (v_new, cfg.kv_heads, cfg.kv_dtype, "v_new"),
+                                     (out, cfg.num_heads, cfg.out_dtype, "out")):
+            want = (cfg.num_layers, n, heads, cfg.head_dim)
+            if tuple(t.shape) != want or _dtype_code(t) != code:
+                raise ValueError(f"{name}: expected {want} of the config's dtype, got {tuple(t.shape)} {t.dtype}")
+        _check(self._L.kvp_decoder_step_device(self._h, r.ctypes.data, n, _dev(q, "q"), _dev(k_new, "k_new"),
+                                                _dev(v_new, "v_new"), _dev(out, "out"), _stream_ptr(stream)))
 
     def status(self) -> int:
         return int(self._L.kvp_decoder_status(self._h))

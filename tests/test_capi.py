@@ -216,3 +216,46 @@ def test_header_is_plain_c_and_drives_the_manager(kvb, tmp_path):
     assert out[len(want) + 1] == "msg set"
     assert len(pairs) == 1  # the fork's first append copied the shared partial block
 
+
+
+def test_decoder_host_step_arguments(kvb):
+    """The Python decoder's host-step wrapper: shapes [L][n][heads][D] and the config's dtypes are checked
+    before the C call (a wrong size would make the copies read past the caller's buffers), host tensors only,
+    contiguous or the host_inputs() views; a step that repeats the previous step's objects reuses the checked
+    arguments, and a changed data pointer or a fresh list of request ids is checked again.  No GPU: a decoder
+    object without a C handle."""
+    import numpy as np
+    import torch
+    L, n, nh, kvh, D = 3, 4, 6, 2, 16
+    d = kvb.Decoder.__new__(kvb.Decoder)
+    c = kvb.DecoderConfig()
+    c.num_layers, c.num_heads, c.kv_heads, c.head_dim = L, nh, kvh, D
+    c.q_dtype = c.kv_dtype = c.out_dtype = kvb.BF16
+    d.cfg, d._h, d._last_args = c, C.c_void_p(0), None
+    stride = n * (nh + 2 * kvh) * D
+    buf = torch.zeros(L * stride, dtype=torch.bfloat16)
+    q = buf.as_strided((L, n, nh, D), (stride, nh * D, D, 1))
+    k = buf.as_strided((L, n, kvh, D), (stride, kvh * D, D, 1), n * nh * D)
+    v = buf.as_strided((L, n, kvh, D), (stride, kvh * D, D, 1), n * (nh + kvh) * D)
+    d._host_in = ([q, k, v], None)
+    out = torch.zeros((L, n, nh, D), dtype=torch.bfloat16)
+    rids = np.arange(n, dtype=np.int64)
+    a = d._host_step_args(rids, q, k, v, out)
+    assert a[1:] == (rids.ctypes.data, n, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr())
+    assert d._host_step_args(rids, q, k, v, out) is a  # the repeat reuses the checked arguments
+    out2 = torch.zeros_like(out)
+    assert d._host_step_args(rids, q, k, v, out2)[6] == out2.data_ptr()
+    lst = list(range(n))
+    assert d._host_step_args(lst, q, k, v, out)[2] == n and d._last_args is None  # a list is never remembered
+    bad = [
+        (rids[:3], q, k, v, out),                                       # n disagrees with the tensors
+        (rids, q, k, v, out[:, :3]),                                    # short output
+        (rids, q, k, v, out.float()),                                   # wrong dtype
+        (rids, q, k, v, torch.zeros((L, nh, n, D), dtype=torch.bfloat16).transpose(1, 2)),  # strided output
+        (rids, torch.zeros((L, n, 2 * nh, D), dtype=torch.bfloat16)[:, :, :nh], k, v, out),  # strided, not a view
+    ]
+    for args in bad:
+        with pytest.raises(ValueError):
+            d._host_step_args(*args)
+    d._host_step_args(rids, torch.zeros((L, n, nh, D), dtype=torch.bfloat16), k, v, out)  # contiguous q: fine
+    d._h = None

@@ -262,8 +262,9 @@ def test_decoder_plan_misuse(kvb, cuda):
 
 
 def test_decoder_packed_inputs_for_another_n_rejected(kvb, cuda):
-    """The packed input views of host_inputs(n) lay layers out for that n only: a step over another batch size
-    given them is rejected (KVP_EINVAL, a ValueError) before any bookkeeping, and the manager is unchanged."""
+    """The packed input views of host_inputs(n) lay layers out for that n only.  The Python wrapper rejects
+    them for another batch size by shape; the C ABI, given their raw pointers with another n, rejects the step
+    (KVP_EINVAL) before any bookkeeping, and the manager is unchanged."""
     import torch
     nh, kvh, D, L, MB = 8, 2, 64, 4, 40
     k, v, m = _setup(kvb, 12)
@@ -271,9 +272,13 @@ def test_decoder_packed_inputs_for_another_n_rejected(kvb, cuda):
     before = [m.num_tokens(r) for r in range(5)]
     pq, pk, pv = dec.host_inputs(3)
     out = torch.zeros((L, 2, nh, D), dtype=torch.bfloat16).pin_memory()
-    for call in (dec.submit, dec.step):
-        with pytest.raises(ValueError, match="packed buffer"):
-            call([0, 1], pq, pk, pv, out)
+    with pytest.raises(ValueError, match="expected"):
+        dec.submit([0, 1], pq, pk, pv, out)
+    r = np.array([0, 1], dtype=np.int64)
+    lib = kvb.lib()
+    for fn in (lib.kvp_decoder_submit, lib.kvp_decoder_step):
+        rc = fn(dec._h, r.ctypes.data, 2, pq.data_ptr(), pk.data_ptr(), pv.data_ptr(), out.data_ptr())
+        assert rc == kvb.KVP_EINVAL and "packed buffer" in kvb.last_error()
     assert [m.num_tokens(r) for r in range(5)] == before
     pq, pk, pv = dec.host_inputs(2)
     pq.zero_(), pk.zero_(), pv.zero_()
